@@ -1,0 +1,174 @@
+/*
+ * b2d.h — C ABI of the B200 decode engine (libb2d.so).
+ *
+ * The engine runs the fused 24-layer decode step of the 306M decoder
+ * (embedding -> N x [RMSNorm, QKV, RoPE, GQA attention over the KV cache,
+ * O-proj, RMSNorm, SwiGLU] -> final norm -> tied-embedding logits -> argmax)
+ * as one persistent sm_100a kernel spanning every SM.
+ *
+ * Every entry point takes plain pointers and sizes: device pointers for the
+ * tensors (the caller owns and allocates them, e.g. through PyTorch) and a
+ * CUDA stream passed as `void*` (a `cudaStream_t`, NULL = legacy default
+ * stream).  Calls are stream-ordered and asynchronous unless stated.  Every
+ * call returns a b2d_status; no call aborts the process or traps the GPU.
+ *
+ * Reference interfaces replaced (paths inside zahlmann/transformer):
+ *   b2d_decode_step      <- kernels/multi_sm_decode.py:369-432
+ *                           multi_sm_decode_nlayer(w, config, token_id, pos,
+ *                           kv_packed, kv_splits=1) -> (next_token, logits, kv_out)
+ *                           and the jax_triton.triton_call at :402-430
+ *   b2d_weights_layout   <- kernels/fused_decode_nlayer.py:250-270 pack_weights and
+ *                           :299-321 prepare_decode_weights_nlayer (packed format)
+ *   b2d_kv_layout        <- kernels/fused_decode_nlayer.py:273-296 pack_kv_caches /
+ *                           unpack_kv_caches (KV format; kept identical)
+ *   b2d_sample           <- generate.py:28-65 sample_token (host numpy sampler)
+ *   b2d_model_create / b2d_workspace_create
+ *                        <- the per-call `jnp.zeros(workspace)` at
+ *                           kernels/multi_sm_decode.py:390-400 (allocated once here)
+ */
+#ifndef B2D_H_
+#define B2D_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2D_API __attribute__((visibility("default")))
+#else
+#define B2D_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B2D_OK = 0,
+  B2D_ERR_INVALID_ARG = 1,    /* rejected on the host before any launch */
+  B2D_ERR_UNSUPPORTED = 2,    /* model shape not compiled into this library */
+  B2D_ERR_CUDA = 3,           /* a CUDA runtime call failed (see b2d_cuda_error) */
+  B2D_ERR_NO_MEMORY = 4,
+  B2D_ERR_LAUNCH = 5,         /* cooperative launch refused (grid not co-resident) */
+  B2D_ERR_DEVICE_TIMEOUT = 6, /* a bounded in-kernel wait ran out (status word) */
+  B2D_ERR_DEVICE_INPUT = 7,   /* kernel saw a token/pos out of range (status word) */
+  B2D_ERR_DEVICE_HALTED = 8   /* workspace holds an earlier device error; reset it */
+} b2d_status;
+
+/* Model shape.  Same keys as the reference config dict (model.py:37-47). */
+typedef struct {
+  int32_t vocab_size;
+  int32_t d_model;
+  int32_t n_heads;
+  int32_t n_kv_heads;
+  int32_t n_layers;
+  int32_t d_head;
+  int32_t d_ff;
+  int32_t context_len;
+  float rms_eps;   /* 1e-5, model.py:94 */
+  float rope_base; /* 10000, model.py:101 */
+} b2d_config;
+
+/*
+ * Packed weight buffer layout (bytes from the buffer base; every section is
+ * 256-byte aligned).  All matrices are bf16, stored "output-row major": row r
+ * holds the weights that produce output r, contiguous along the reduction dim,
+ * so a GEMV streams whole rows.  Per layer l, at l * layer_stride:
+ *   qkv  [(H + 2*KVH) * dh][d]   rows: q (head-major), then k, then v
+ *   o    [d][d]
+ *   gu   [d_ff][2][d]            gate row j, then up row j
+ *   down [d][d_ff]
+ * then emb [vocab][d] bf16 (token_emb, read in place as the tied output
+ * projection), then f32 vectors ln1 [L][d], ln2 [L][d], lnf [d], and the RoPE
+ * tables cos/sin [context_len][dh/2] (model.py:101-107, f32).
+ */
+typedef struct {
+  uint64_t layer_stride;
+  uint64_t off_qkv, off_o, off_gu, off_down; /* within a layer */
+  uint64_t off_emb, off_ln1, off_ln2, off_lnf, off_cos, off_sin;
+  uint64_t total_bytes;
+} b2d_weights_layout_t;
+
+/* KV cache layout of one sequence, bf16 elements, identical to the reference
+ * pack_kv_caches: [layer][K|V][kv_head][context_len][d_head], K post-RoPE. */
+typedef struct {
+  uint64_t elems_per_seq;
+  uint64_t layer_elems; /* 2 * kv_heads * context_len * d_head */
+  uint64_t kv_half_elems; /* kv_heads * context_len * d_head */
+} b2d_kv_layout_t;
+
+typedef struct b2d_model b2d_model;
+typedef struct b2d_ws b2d_ws;
+
+/* Sampling parameters, same meaning as generate.py:28-65. */
+typedef struct {
+  double temperature; /* 0 = greedy argmax; applied as float32 (numpy weak scalar) */
+  double top_p;       /* 1 = off; compared in float64 like np.searchsorted */
+  double rep_penalty; /* 1 = off; applied as float32 */
+} b2d_sampling;
+
+B2D_API const char* b2d_status_str(b2d_status s);
+/* Last CUDA error string seen by this thread's failing call ("" if none). */
+B2D_API const char* b2d_cuda_error(void);
+/* 1 if this library was compiled with kernels for `cfg`'s shape. */
+B2D_API int b2d_config_supported(const b2d_config* cfg);
+
+B2D_API b2d_status b2d_weights_layout(const b2d_config* cfg, b2d_weights_layout_t* out);
+B2D_API b2d_status b2d_kv_layout(const b2d_config* cfg, b2d_kv_layout_t* out);
+
+/* Binds a packed weight buffer (device memory on `device`, caller-owned,
+ * must outlive the model).  Nothing is copied. */
+B2D_API b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev,
+                            uint64_t weights_bytes, int device, b2d_model** out);
+B2D_API b2d_status b2d_model_destroy(b2d_model* m);
+/* Number of CTAs the decode kernel launches (one per SM). */
+B2D_API int b2d_model_grid(const b2d_model* m);
+
+/* Workspace: inter-CTA exchange words, control words.  Allocated once here;
+ * nothing is allocated per step.  One workspace per stream; not re-entrant. */
+B2D_API b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out);
+B2D_API b2d_status b2d_workspace_destroy(b2d_ws* ws);
+/* Clears the exchange words and the device status (after a device error). */
+B2D_API b2d_status b2d_workspace_reset(b2d_ws* ws, void* stream);
+/* Synchronises `stream`, reads the device status word.  Returns B2D_OK or
+ * the device error (B2D_ERR_DEVICE_*); *detail gets the raw status word. */
+B2D_API b2d_status b2d_last_error(b2d_ws* ws, void* stream, uint32_t* detail);
+
+/*
+ * One decode step for `batch` sequences.
+ *   tok_dev      int32[batch]  token fed at this step
+ *   pos_dev      int32[batch]  its position (0-based); K/V written there
+ *   kv_dev       bf16 KV caches, b2d_kv_layout per sequence, batch-major
+ *   logits_dev   f32[batch][vocab] or NULL (then only the argmax is produced)
+ *   next_tok_dev int32[batch]  argmax token (first index on ties)
+ * batch == 1 runs the persistent megakernel.
+ */
+B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev,
+                           const int32_t* pos_dev, int batch, void* kv_dev,
+                           float* logits_dev, int32_t* next_tok_dev, void* stream);
+
+/*
+ * Device sampler, one sequence per CTA (generate.py:28-65 semantics).
+ *   logits_dev   f32[batch][vocab]     (read only)
+ *   history_dev  int32[batch][hist_cap] tokens generated so far (prompt excluded)
+ *   hist_len_dev int32[batch]          valid entries in history
+ *   uniforms_dev f32[batch]            one uniform in [0,1) per sequence
+ *   out_tok_dev  int32[batch]
+ */
+B2D_API b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
+                      const int32_t* history_dev, int hist_cap,
+                      const int32_t* hist_len_dev, const float* uniforms_dev,
+                      const b2d_sampling* params, int32_t* out_tok_dev, void* stream);
+
+/*
+ * Test hook, not part of the reference surface: bound every in-kernel wait by
+ * `wait_ns` and split the work over `extra_ctas` more CTAs than are launched,
+ * so the words those phantom CTAs own are never written.  A fault-detection
+ * test uses it to make a wait run out and read B2D_ERR_DEVICE_TIMEOUT back
+ * from b2d_last_error without hanging or faulting the GPU.
+ */
+B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2D_H_ */

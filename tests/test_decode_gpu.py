@@ -1,0 +1,183 @@
+"""GPU parity: the sm_100a decode kernel (through the C ABI) against the
+oracle and the reference fixtures.  Tolerances: see conftest (ATOL/RTOL/MARGIN)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import MARGIN, assert_logits_close, golden
+from oracle import ref_forward as R
+from transformer_b200 import _lib
+from transformer_b200.config import CONFIG_306M, CONFIG_TINY
+from transformer_b200.synth import params_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def _step(eng, tok, pos, kv):
+    t = torch.tensor([tok], dtype=torch.int32, device=eng.device)
+    p = torch.tensor([pos], dtype=torch.int32, device=eng.device)
+    eng.step(t, p, kv, eng.logits, eng.next_tok)
+    return eng.logits[0].cpu().numpy().copy(), int(eng.next_tok[0].item())
+
+
+def test_tiny_teacher_forced_matches_oracle(engine_tiny, params_tiny):
+    eng = engine_tiny
+    P = params_f32(params_tiny)
+    dec = R.CachedDecoder(P, CONFIG_TINY, 1)
+    kv = eng.new_kv()
+    rng = np.random.default_rng(21)
+    toks = rng.integers(0, CONFIG_TINY.vocab_size, CONFIG_TINY.context_len)
+    for p in range(CONFIG_TINY.context_len):  # every position up to the full context
+        got, nxt = _step(eng, int(toks[p]), p, kv)
+        ref = dec.step([toks[p]], [p])[0]
+        assert_logits_close(got, ref, f"pos {p}")
+        i, _, m = R.top2(ref)
+        if m > MARGIN:
+            assert nxt == i, f"pos {p}"
+        assert nxt == int(np.argmax(got))
+    eng.check_device()
+
+
+def test_tiny_kv_cache_written_in_place(engine_tiny, params_tiny):
+    """After prefill the device KV equals the reference prefill's bf16 caches
+    (reference layout), within bf16 rounding of float32 noise."""
+    g = golden("tiny.npz")
+    eng = engine_tiny
+    kv = eng.new_kv()
+    eng.prefill(g["prompt"], kv)
+    torch.cuda.synchronize()
+    from transformer_b200.packing import unpack_kv_caches
+    ks, vs = unpack_kv_caches(kv, CONFIG_TINY.n_layers, CONFIG_TINY.n_kv_heads, CONFIG_TINY.context_len, 64)
+    got = np.concatenate([np.concatenate([k.float().cpu().numpy().reshape(-1), v.float().cpu().numpy().reshape(-1)])
+                          for k, v in zip(ks, vs)])
+    ref = (g["kv_packed_bits"].astype(np.uint32) << 16).view(np.float32)
+    T = len(g["prompt"])
+    mask = np.zeros((CONFIG_TINY.n_layers, 2, CONFIG_TINY.n_kv_heads, CONFIG_TINY.context_len, 64), bool)
+    mask[:, :, :, :T] = True
+    mask = mask.reshape(-1)
+    np.testing.assert_allclose(got[mask], ref[mask], atol=3e-2, rtol=2e-2)
+    assert np.all(got[~mask] == 0)  # positions beyond the prompt untouched
+
+
+def _teacher_forced_306(eng, g, check_steps):
+    prompt, toks = g["prompt"], g["tokens"]
+    kept = dict(zip(g["logits_steps"].tolist(), g["logits"]))
+    kv = eng.new_kv()
+    lg = eng.prefill(prompt, kv).cpu().numpy().copy()
+    errs, mism = [], []
+    for i in range(len(toks)):
+        if i in kept:
+            errs.append(assert_logits_close(lg, kept[i], f"step {i}"))
+        a = int(np.argmax(lg))
+        if g["margin"][i] > MARGIN and a != toks[i]:
+            mism.append(i)
+        if i + 1 < len(toks) and (i + 1) in check_steps | set(kept):
+            pass
+        if i + 1 < len(toks):
+            lg, _ = _step(eng, int(toks[i]), len(prompt) + i, kv)
+    eng.check_device()
+    return errs, mism
+
+
+def test_cfg1_parity_306m(engine306):
+    """Config 1 (16-token prompt, 128 greedy steps): logits at the recorded
+    steps within tolerance; argmax equal to the reference wherever its top-2
+    margin exceeds 0.05 (teacher forced on the reference stream)."""
+    errs, mism = _teacher_forced_306(engine306, golden("cfg1_greedy.npz"), set())
+    assert not mism, f"argmax differs at steps {mism}"
+    print("cfg1 max abs logit err at recorded steps:", errs)
+
+
+def test_cfg2_long_context_parity_306m(engine306):
+    """Config 2 (384-token prompt -> ctx 512): same checks; attention over the
+    full cache dominates the extra bytes."""
+    try:
+        g = golden("cfg2_long.npz")
+    except FileNotFoundError:
+        pytest.skip("cfg2 fixture not generated")
+    errs, mism = _teacher_forced_306(engine306, g, set())
+    assert not mism, f"argmax differs at steps {mism}"
+
+
+def test_free_run_greedy_prefix(engine306):
+    """Free-running greedy decode on the device: report the prefix that matches
+    the reference stream (a near-tie can fork it; teacher-forced parity above
+    is the gate).  The device's own argmax must equal argmax(logits)."""
+    g = golden("cfg1_greedy.npz")
+    eng = engine306
+    kv = eng.new_kv()
+    lg = eng.prefill(g["prompt"], kv)
+    tok = int(torch.argmax(lg).item())
+    out = [tok]
+    for i in range(1, 32):
+        lg_np, nxt = _step(eng, tok, len(g["prompt"]) + i - 1, kv)
+        assert nxt == int(np.argmax(lg_np))
+        tok = nxt
+        out.append(tok)
+    ref = g["tokens"][:32]
+    n = int(np.argmax(np.array(out) != ref)) if np.any(np.array(out) != ref) else 32
+    print("free-run greedy prefix matching the reference:", n, "of 32")
+
+
+def test_deterministic(engine306):
+    """Fixed-order reductions: repeated steps give bit-identical logits."""
+    eng = engine306
+    outs = []
+    for _ in range(3):
+        kv = eng.new_kv()
+        eng.prefill([5, 17, 900], kv)
+        lg, _ = _step(eng, 31, 3, kv)
+        outs.append(lg)
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[1], outs[2])
+
+
+def test_drop_in_api(cuda, engine306):
+    """multi_sm_decode_nlayer keeps the reference call shape and returns
+    (next_token, logits[vocab], kv) with the cache updated in place."""
+    from transformer_b200.multi_sm_decode import multi_sm_decode_nlayer
+    w = engine306.w
+    kv = engine306.new_kv()
+    nt, logits, kv2 = multi_sm_decode_nlayer(w, w["config"].as_dict(), 123, 0, kv)
+    assert kv2 is kv and logits.shape == (CONFIG_306M.vocab_size,)
+    assert int(nt.item()) == int(torch.argmax(logits).item())
+    nt2, _, _ = multi_sm_decode_nlayer(w, w["config"].as_dict(), nt, torch.tensor([1], dtype=torch.int32,
+                                                                                  device=cuda), kv)
+    assert 0 <= int(nt2.item()) < CONFIG_306M.vocab_size
+    with pytest.raises(_lib.B2DError):
+        multi_sm_decode_nlayer(w, w["config"].as_dict(), 123, CONFIG_306M.context_len, kv)
+
+
+def test_bad_device_input_sets_status_and_recovers(engine_tiny):
+    """A token id out of range fed as a device tensor is caught by the kernel:
+    status word set, no fault, later steps halted until reset."""
+    eng = engine_tiny
+    kv = eng.new_kv()
+    _step(eng, CONFIG_TINY.vocab_size + 5, 0, kv)
+    st, word = eng.last_error()
+    assert st == _lib.B2D_ERR_DEVICE_INPUT, (st, hex(word))
+    _step(eng, 3, 0, kv)  # halted: returns immediately
+    assert eng.last_error()[0] == _lib.B2D_ERR_DEVICE_INPUT
+    eng.reset()
+    _step(eng, 3, 0, kv)
+    assert eng.last_error()[0] == _lib.B2D_OK
+
+
+def test_wait_timeout_is_reported_not_hung(engine_tiny):
+    """Failure detection without a GPU fault: the work is split over one CTA
+    more than is launched, so the words that CTA owns are never written; every
+    wait is bounded (50 ms here), the status word reports the timeout, and the
+    context stays usable after a reset."""
+    eng = engine_tiny
+    kv = eng.new_kv()
+    eng.debug_set(50_000_000, extra_ctas=1)
+    _step(eng, 3, 0, kv)
+    st, word = eng.last_error()
+    assert st == _lib.B2D_ERR_DEVICE_TIMEOUT, (st, hex(word))
+    eng.debug_set(2_000_000_000, extra_ctas=0)
+    eng.reset()
+    kv = eng.new_kv()
+    got, _ = _step(eng, 3, 0, kv)
+    assert eng.last_error()[0] == _lib.B2D_OK and np.isfinite(got).all()

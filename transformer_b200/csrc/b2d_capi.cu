@@ -1,0 +1,337 @@
+// b2d_capi.cu — the C ABI declared in include/b2d.h.
+//
+// Host side of the engine: model / workspace lifetime, layout queries, host
+// validation, and the cooperative launch of the shape-specialised kernels.
+// Nothing here allocates per step; workspaces are allocated once.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include "../../include/b2d.h"
+#include "decode_b1.cuh"
+#include "sampler.cuh"
+
+namespace {
+
+thread_local char g_cuda_err[256] = "";
+
+b2d_status cuda_fail(cudaError_t e, const char* what) {
+  std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", what, cudaGetErrorString(e));
+  if (e == cudaErrorMemoryAllocation) return B2D_ERR_NO_MEMORY;
+  if (e == cudaErrorCooperativeLaunchTooLarge) return B2D_ERR_LAUNCH;
+  return B2D_ERR_CUDA;
+}
+
+#define B2D_CUDA(call, what)                         \
+  do {                                               \
+    cudaError_t e_ = (call);                         \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+constexpr uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+using Shape306M = b2d::Shape<1024, 2816, 16, 4>;
+using ShapeTiny = b2d::Shape<256, 768, 4, 2>;
+
+// Shape-specialised entry points.
+struct ShapeOps {
+  int d, dff, nh, nkv;
+  size_t smem;
+  const void* kernel;
+  size_t sampler_smem;
+};
+
+template <class S>
+ShapeOps make_ops() {
+  return ShapeOps{S::D, S::DFF, S::NH, S::NKV, sizeof(b2d::Smem<S>),
+                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S>), 0};
+}
+
+const ShapeOps* find_ops(const b2d_config* c) {
+  static const ShapeOps ops[] = {make_ops<Shape306M>(), make_ops<ShapeTiny>()};
+  if (!c || c->d_head != 64) return nullptr;
+  for (const auto& o : ops)
+    if (o.d == c->d_model && o.dff == c->d_ff && o.nh == c->n_heads && o.nkv == c->n_kv_heads) return &o;
+  return nullptr;
+}
+
+bool config_valid(const b2d_config* c) {
+  return c && c->vocab_size > 0 && c->d_model > 0 && c->n_heads > 0 && c->n_kv_heads > 0 &&
+         c->n_layers > 0 && c->d_head == 64 && c->d_ff > 0 && c->context_len > 0 &&
+         c->n_heads % c->n_kv_heads == 0 && c->rms_eps > 0.f;
+}
+
+void compute_layout(const b2d_config* c, b2d_weights_layout_t* L) {
+  const uint64_t d = c->d_model, f = c->d_ff, qkv = uint64_t(c->n_heads + 2 * c->n_kv_heads) * c->d_head;
+  const uint64_t V = c->vocab_size, nl = c->n_layers, half = c->d_head / 2, ctx = c->context_len;
+  L->off_qkv = 0;
+  L->off_o = L->off_qkv + align256(qkv * d * 2);
+  L->off_gu = L->off_o + align256(d * d * 2);
+  L->off_down = L->off_gu + align256(f * 2 * d * 2);
+  L->layer_stride = L->off_down + align256(d * f * 2);
+  L->off_emb = nl * L->layer_stride;
+  L->off_ln1 = L->off_emb + align256(V * d * 2);
+  L->off_ln2 = L->off_ln1 + align256(nl * d * 4);
+  L->off_lnf = L->off_ln2 + align256(nl * d * 4);
+  L->off_cos = L->off_lnf + align256(d * 4);
+  L->off_sin = L->off_cos + align256(ctx * half * 4);
+  L->total_bytes = L->off_sin + align256(ctx * half * 4);
+}
+
+}  // namespace
+
+struct b2d_model {
+  b2d_config cfg;
+  int device;
+  const uint8_t* w;
+  uint64_t wbytes;
+  b2d_weights_layout_t lay;
+  const ShapeOps* ops;
+  int grid;
+};
+
+struct b2d_ws {
+  b2d_model* m;
+  int max_batch;
+  uint64_t* words;
+  size_t n_words;
+  b2d::Control* ctl;
+  float* am_val;
+  int32_t* am_idx;
+  uint32_t layer_words, w_att, w_hm, w_act;
+  int att_T;
+  uint64_t wait_ns;
+  int grid_part;
+};
+
+extern "C" {
+
+const char* b2d_status_str(b2d_status s) {
+  switch (s) {
+    case B2D_OK: return "ok";
+    case B2D_ERR_INVALID_ARG: return "invalid argument";
+    case B2D_ERR_UNSUPPORTED: return "model shape or batch not supported by this build";
+    case B2D_ERR_CUDA: return "CUDA error";
+    case B2D_ERR_NO_MEMORY: return "out of device memory";
+    case B2D_ERR_LAUNCH: return "cooperative launch refused (grid not co-resident)";
+    case B2D_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case B2D_ERR_DEVICE_INPUT: return "device saw token/pos out of range";
+    case B2D_ERR_DEVICE_HALTED: return "workspace halted by an earlier device error";
+  }
+  return "unknown status";
+}
+
+const char* b2d_cuda_error(void) { return g_cuda_err; }
+
+int b2d_config_supported(const b2d_config* cfg) { return config_valid(cfg) && find_ops(cfg) ? 1 : 0; }
+
+b2d_status b2d_weights_layout(const b2d_config* cfg, b2d_weights_layout_t* out) {
+  if (!config_valid(cfg) || !out) return B2D_ERR_INVALID_ARG;
+  compute_layout(cfg, out);
+  return B2D_OK;
+}
+
+b2d_status b2d_kv_layout(const b2d_config* cfg, b2d_kv_layout_t* out) {
+  if (!config_valid(cfg) || !out) return B2D_ERR_INVALID_ARG;
+  out->kv_half_elems = uint64_t(cfg->n_kv_heads) * cfg->context_len * cfg->d_head;
+  out->layer_elems = 2 * out->kv_half_elems;
+  out->elems_per_seq = uint64_t(cfg->n_layers) * out->layer_elems;
+  return B2D_OK;
+}
+
+b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint64_t weights_bytes,
+                            int device, b2d_model** out) {
+  if (!out) return B2D_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (!config_valid(cfg) || !weights_dev || (reinterpret_cast<uintptr_t>(weights_dev) & 255u))
+    return B2D_ERR_INVALID_ARG;
+  const ShapeOps* ops = find_ops(cfg);
+  if (!ops) return B2D_ERR_UNSUPPORTED;
+  b2d_weights_layout_t lay;
+  compute_layout(cfg, &lay);
+  if (weights_bytes < lay.total_bytes) return B2D_ERR_INVALID_ARG;
+  int ndev = 0;
+  B2D_CUDA(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  int sms = 0, coop = 0;
+  B2D_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+  B2D_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device), "coop attr");
+  if (!coop) return B2D_ERR_LAUNCH;
+  B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(ops->smem)),
+           "cudaFuncSetAttribute(smem)");
+  int per_sm = 0;
+  B2D_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops->kernel, b2d::kThreads, ops->smem),
+           "occupancy");
+  if (per_sm < 1) return B2D_ERR_LAUNCH;
+  b2d_model* m = new (std::nothrow) b2d_model;
+  if (!m) return B2D_ERR_NO_MEMORY;
+  m->cfg = *cfg;
+  m->device = device;
+  m->w = static_cast<const uint8_t*>(weights_dev);
+  m->wbytes = weights_bytes;
+  m->lay = lay;
+  m->ops = ops;
+  m->grid = sms;
+  *out = m;
+  return B2D_OK;
+}
+
+b2d_status b2d_model_destroy(b2d_model* m) {
+  delete m;
+  return B2D_OK;
+}
+
+int b2d_model_grid(const b2d_model* m) { return m ? m->grid : 0; }
+
+b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
+  if (!out) return B2D_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (!m || max_batch < 1) return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  const b2d_config& c = m->cfg;
+  b2d_ws* ws = new (std::nothrow) b2d_ws;
+  if (!ws) return B2D_ERR_NO_MEMORY;
+  std::memset(ws, 0, sizeof(*ws));
+  ws->m = m;
+  ws->max_batch = max_batch;
+  ws->att_T = 64 * ((c.context_len + 511) / 512);
+  const uint32_t qkv = uint32_t(c.n_heads + 2 * c.n_kv_heads) * 64;
+  ws->w_att = uint32_t(c.d_model) + qkv;
+  ws->w_hm = ws->w_att + uint32_t(c.n_heads) * b2d::kMaxSplits * b2d::kAttWords;
+  ws->w_act = ws->w_hm + uint32_t(c.d_model);
+  ws->layer_words = ws->w_act + uint32_t(c.d_ff);
+  ws->layer_words = (ws->layer_words + 1) & ~1u;
+  ws->n_words = size_t(c.n_layers) * ws->layer_words + c.d_model;
+  ws->wait_ns = 2000000000ull;  // 2 s bound on every in-kernel wait
+  ws->grid_part = m->grid;
+  cudaError_t e = cudaMalloc(&ws->words, ws->n_words * sizeof(uint64_t));
+  if (e == cudaSuccess) e = cudaMalloc(&ws->ctl, sizeof(b2d::Control));
+  if (e == cudaSuccess) e = cudaMalloc(&ws->am_val, sizeof(float) * m->grid);
+  if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
+  if (e == cudaSuccess) e = cudaMemset(ws->words, 0, ws->n_words * sizeof(uint64_t));
+  if (e == cudaSuccess) e = cudaMemset(ws->ctl, 0, sizeof(b2d::Control));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    b2d_workspace_destroy(ws);
+    return cuda_fail(e, "workspace allocation");
+  }
+  *out = ws;
+  return B2D_OK;
+}
+
+b2d_status b2d_workspace_destroy(b2d_ws* ws) {
+  if (!ws) return B2D_OK;
+  if (ws->m) cudaSetDevice(ws->m->device);
+  cudaFree(ws->words);
+  cudaFree(ws->ctl);
+  cudaFree(ws->am_val);
+  cudaFree(ws->am_idx);
+  delete ws;
+  return B2D_OK;
+}
+
+b2d_status b2d_workspace_reset(b2d_ws* ws, void* stream) {
+  if (!ws) return B2D_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
+  B2D_CUDA(cudaMemsetAsync(ws->words, 0, ws->n_words * sizeof(uint64_t), st), "reset words");
+  B2D_CUDA(cudaMemsetAsync(ws->ctl, 0, sizeof(b2d::Control), st), "reset control");
+  return B2D_OK;
+}
+
+b2d_status b2d_last_error(b2d_ws* ws, void* stream, uint32_t* detail) {
+  if (!ws) return B2D_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
+  uint32_t s = 0;
+  B2D_CUDA(cudaMemcpyAsync(&s, &ws->ctl->status, sizeof(s), cudaMemcpyDeviceToHost, st), "read status");
+  B2D_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  if (detail) *detail = s;
+  if (s == 0) return B2D_OK;
+  if ((s & 0xF00u) == b2d::ST_TIMEOUT) return B2D_ERR_DEVICE_TIMEOUT;
+  if ((s & 0xF00u) == b2d::ST_BAD_INPUT) return B2D_ERR_DEVICE_INPUT;
+  return B2D_ERR_DEVICE_HALTED;
+}
+
+// Test hook (not part of the product surface): shorten the in-kernel wait
+// bound and/or split the work over more CTAs than are launched, so a test can
+// make a wait run out on a flag nothing sets and check the status word.
+b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas) {
+  if (!ws || wait_ns == 0 || extra_ctas < 0 || extra_ctas > 1024) return B2D_ERR_INVALID_ARG;
+  ws->wait_ns = wait_ns;
+  ws->grid_part = ws->m->grid + extra_ctas;
+  return B2D_OK;
+}
+
+b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                           int batch, void* kv_dev, float* logits_dev, int32_t* next_tok_dev,
+                           void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_dev || !next_tok_dev || batch < 1 ||
+      batch > ws->max_batch)
+    return B2D_ERR_INVALID_ARG;
+  if (batch != 1) return B2D_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  const b2d_config& c = m->cfg;
+  b2d::DecodeArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.wbase = m->w;
+  A.layer_stride = m->lay.layer_stride;
+  A.off_qkv = m->lay.off_qkv;
+  A.off_o = m->lay.off_o;
+  A.off_gu = m->lay.off_gu;
+  A.off_down = m->lay.off_down;
+  A.off_emb = m->lay.off_emb;
+  A.ln1 = reinterpret_cast<const float*>(m->w + m->lay.off_ln1);
+  A.ln2 = reinterpret_cast<const float*>(m->w + m->lay.off_ln2);
+  A.lnf = reinterpret_cast<const float*>(m->w + m->lay.off_lnf);
+  A.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
+  A.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
+  A.tok = tok_dev;
+  A.pos = pos_dev;
+  A.kv = static_cast<__nv_bfloat16*>(kv_dev);
+  A.logits = logits_dev;
+  A.next_tok = next_tok_dev;
+  A.words = ws->words;
+  A.ctl = ws->ctl;
+  A.am_val = ws->am_val;
+  A.am_idx = ws->am_idx;
+  A.layer_words = ws->layer_words;
+  A.w_att = ws->w_att;
+  A.w_hm = ws->w_hm;
+  A.w_act = ws->w_act;
+  A.vocab = c.vocab_size;
+  A.n_layers = c.n_layers;
+  A.ctx = c.context_len;
+  A.att_T = ws->att_T;
+  A.grid_part = ws->grid_part;
+  A.wait_ns = ws->wait_ns;
+  A.eps = c.rms_eps;
+  void* args[] = {&A};
+  B2D_CUDA(cudaLaunchCooperativeKernel(m->ops->kernel, dim3(m->grid), dim3(b2d::kThreads), args,
+                                       m->ops->smem, st),
+           "decode launch");
+  return B2D_OK;
+}
+
+b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab, const int32_t* history_dev,
+                      int hist_cap, const int32_t* hist_len_dev, const float* uniforms_dev,
+                      const b2d_sampling* params, int32_t* out_tok_dev, void* stream) {
+  if (!ws || !logits_dev || batch < 1 || vocab < 1 || vocab > b2d::kSamplerMaxVocab || !params ||
+      !out_tok_dev || hist_cap < 0 || (hist_cap > 0 && (!history_dev || !hist_len_dev)) ||
+      !(params->temperature >= 0.0) || !(params->top_p > 0.0) || !(params->rep_penalty > 0.0))
+    return B2D_ERR_INVALID_ARG;
+  if (params->temperature > 0.0 && !uniforms_dev) return B2D_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
+  B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
+                               params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st),
+           "sampler launch");
+  return B2D_OK;
+}
+
+}  // extern "C"

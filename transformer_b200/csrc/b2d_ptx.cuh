@@ -1,0 +1,135 @@
+// b2d_ptx.cuh — small inline-PTX helpers shared by the decode kernels (sm_100a).
+//
+// Everything here is hand-written PTX for: mbarriers, the bulk (non-tensor)
+// global->shared async copy with an L2 cache-policy hint, relaxed gpu-scope
+// loads/stores used by the inter-CTA exchange words, and the global timer used
+// to bound every wait.  No multicast form of any copy is used.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+namespace b2d {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier ----------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+               ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// True once the phase with the given parity has completed.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// ---- bulk async copy global -> shared (completes on an mbarrier) --------
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy) : "memory");
+}
+
+// ---- exchange words -----------------------------------------------------
+// An exchange word is 8 bytes: low 32 bits payload (float bits), high 32 bits
+// the launch's flag.  A single 64-bit store is single-copy atomic, so a reader
+// that sees the current flag also sees the payload written with it.
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t flag) {
+  const uint64_t w = (static_cast<uint64_t>(flag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// Two adjacent words (16-byte aligned); each 64-bit element is read atomically.
+__device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t word_flag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
+__device__ __forceinline__ float word_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+// ---- named barrier among the consumer warps -----------------------------
+template <int NT>
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+// Barrier + AND-reduction of a predicate over the consumer threads.
+template <int NT>
+__device__ __forceinline__ bool consumer_sync_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"(static_cast<uint32_t>(v)), "n"(NT) : "memory");
+  return r != 0;
+}
+
+// ---- math helpers -------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float round_bf16(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+// acc += dot(8 bf16 weights packed in w, 8 bf16 activations packed in x),
+// products and accumulation in f32 (bf16 -> f32 is exact).
+__device__ __forceinline__ float dot8(const uint4 w, const uint4 x, float acc) {
+  acc = fmaf(bf16_lo(w.x), bf16_lo(x.x), acc);
+  acc = fmaf(bf16_hi(w.x), bf16_hi(x.x), acc);
+  acc = fmaf(bf16_lo(w.y), bf16_lo(x.y), acc);
+  acc = fmaf(bf16_hi(w.y), bf16_hi(x.y), acc);
+  acc = fmaf(bf16_lo(w.z), bf16_lo(x.z), acc);
+  acc = fmaf(bf16_hi(w.z), bf16_hi(x.z), acc);
+  acc = fmaf(bf16_lo(w.w), bf16_lo(x.w), acc);
+  acc = fmaf(bf16_hi(w.w), bf16_hi(x.w), acc);
+  return acc;
+}
+// Pack two f32 (already bf16-representable) into a bf16x2 word.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
+}
+
+}  // namespace b2d

@@ -1,0 +1,184 @@
+"""Decode entry points over the C ABI.
+
+``multi_sm_decode_nlayer`` keeps the reference's call shape
+(``kernels/multi_sm_decode.py:369-432``): ``(w, config, token_id, pos,
+kv_packed, kv_splits=1) -> (next_token, logits, kv)``.  Differences, by design:
+the KV cache is updated in place (the returned ``kv`` is the same tensor; the
+reference returns a fresh copy, :198-208), the workspace is allocated once per
+model instead of zeroed per call (:390-400), and ``token_id`` / ``pos`` may be
+device int32 tensors so a loop can feed the previous step's output without a
+host round trip.
+
+``DecodeEngine`` is the lower-level handle the host loop, tests and bench use:
+one bound model, one workspace, preallocated step buffers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from .config import ModelConfig
+from .packing import kv_elems, new_kv_cache
+
+
+def _ptr(t: torch.Tensor | None):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream_ptr(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class DecodeEngine:
+    """A packed model bound to the C ABI plus one workspace."""
+
+    def __init__(self, w: dict, max_batch: int = 1):
+        self.lib = _lib.load()
+        self.w = w
+        self.cfg: ModelConfig = w["config"]
+        buf = w["packed_w"]
+        self.device = buf.device
+        self._cfg_c = _lib.make_config(self.cfg)
+        if not self.lib.b2d_config_supported(ctypes.byref(self._cfg_c)):
+            raise _lib.B2DError(_lib.B2D_ERR_UNSUPPORTED, "b2d_config_supported", str(self.cfg))
+        model = ctypes.c_void_p()
+        _lib.check(self.lib.b2d_model_create(ctypes.byref(self._cfg_c), _ptr(buf), buf.numel(),
+                                             self.device.index or 0, ctypes.byref(model)),
+                   "b2d_model_create")
+        self.model = model
+        ws = ctypes.c_void_p()
+        try:
+            _lib.check(self.lib.b2d_workspace_create(self.model, max_batch, ctypes.byref(ws)),
+                       "b2d_workspace_create")
+        except Exception:
+            self.lib.b2d_model_destroy(self.model)
+            raise
+        self.ws = ws
+        self.max_batch = max_batch
+        self.grid = self.lib.b2d_model_grid(self.model)
+        dev = self.device
+        self.tok = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.next_tok = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self.logits = torch.zeros(max_batch, self.cfg.vocab_size, dtype=torch.float32, device=dev)
+
+    def close(self):
+        if getattr(self, "ws", None):
+            self.lib.b2d_workspace_destroy(self.ws)
+            self.ws = None
+        if getattr(self, "model", None):
+            self.lib.b2d_model_destroy(self.model)
+            self.model = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- buffers -------------------------------------------------------
+    def new_kv(self, batch: int = 1) -> torch.Tensor:
+        return new_kv_cache(self.cfg, batch, self.device)
+
+    @property
+    def kv_elems(self) -> int:
+        return kv_elems(self.cfg)
+
+    # ---- one step ------------------------------------------------------
+    def step(self, tok: torch.Tensor, pos: torch.Tensor, kv: torch.Tensor,
+             logits: torch.Tensor | None = None, next_tok: torch.Tensor | None = None,
+             stream=None, batch: int = 1) -> None:
+        """Launch one decode step (async, stream-ordered).  All device tensors."""
+        if next_tok is None:
+            next_tok = self.next_tok
+        for t, name in ((tok, "tok"), (pos, "pos"), (next_tok, "next_tok")):
+            if t.dtype != torch.int32 or t.device != self.device or t.numel() < batch:
+                raise ValueError(f"{name} must be an int32 tensor on {self.device} with >= {batch} items")
+        if kv.dtype != torch.bfloat16 or kv.device != self.device or kv.numel() < batch * self.kv_elems:
+            raise ValueError("kv must be a bf16 cache on the model device (see new_kv)")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() < batch * self.cfg.vocab_size):
+            raise ValueError("logits must be float32 [batch, vocab]")
+        st = self.lib.b2d_decode_step(self.model, self.ws, _ptr(tok), _ptr(pos), batch, _ptr(kv),
+                                      _ptr(logits), _ptr(next_tok), _stream_ptr(stream))
+        _lib.check(st, "b2d_decode_step")
+
+    def last_error(self, stream=None):
+        """(status, raw device word); synchronises the stream."""
+        detail = ctypes.c_uint32(0)
+        st = self.lib.b2d_last_error(self.ws, _stream_ptr(stream), ctypes.byref(detail))
+        return st, detail.value
+
+    def check_device(self, stream=None):
+        st, detail = self.last_error(stream)
+        if st != _lib.B2D_OK:
+            raise _lib.B2DError(st, "device status", f"word 0x{detail:x}")
+
+    def reset(self, stream=None):
+        _lib.check(self.lib.b2d_workspace_reset(self.ws, _stream_ptr(stream)), "b2d_workspace_reset")
+
+    def debug_set(self, wait_ns: int, extra_ctas: int = 0):
+        _lib.check(self.lib.b2d_debug_set(self.ws, int(wait_ns), int(extra_ctas)), "b2d_debug_set")
+
+    # ---- prompt ingestion ----------------------------------------------
+    def prefill(self, prompt, kv: torch.Tensor, start: int = 0, stream=None) -> torch.Tensor:
+        """Feed prompt tokens one step at a time (teacher forcing), writing the
+        KV cache; returns the logits of the last prompt position (device)."""
+        prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
+        if prompt.size == 0:
+            raise ValueError("empty prompt")
+        if start + prompt.size > self.cfg.context_len:
+            raise ValueError("prompt longer than the context")
+        toks = torch.from_numpy(prompt).to(self.device)
+        poss = torch.arange(start, start + prompt.size, dtype=torch.int32, device=self.device)
+        for i in range(prompt.size):
+            self.step(toks[i:i + 1], poss[i:i + 1], kv, self.logits, self.next_tok, stream)
+        return self.logits[0]
+
+
+_ENGINES: dict = {}
+
+
+def engine_for(w: dict) -> DecodeEngine:
+    """One engine per packed weight buffer (the workspace is reused)."""
+    key = w["packed_w"].data_ptr()
+    eng = _ENGINES.get(key)
+    if eng is None or eng.w is not w:
+        eng = DecodeEngine(w)
+        _ENGINES[key] = eng
+    return eng
+
+
+def multi_sm_decode_nlayer(w, config, token_id, pos, kv_packed, kv_splits=1):
+    """Reference-compatible single decode step (``multi_sm_decode.py:369-432``).
+
+    Returns ``(next_token, logits, kv_packed)``: a 0-d int32 device tensor, the
+    float32 logits ``[vocab]`` (device) and the KV cache, updated in place.
+    ``token_id`` / ``pos``: Python ints (range-checked here) or int32 device
+    tensors (range-checked by the kernel, which then sets the device status).
+    """
+    eng = engine_for(w)
+    cfg = eng.cfg
+    if isinstance(token_id, torch.Tensor):
+        tok = token_id.reshape(-1)[:1].to(device=eng.device, dtype=torch.int32)
+    else:
+        token_id = int(token_id)
+        if not 0 <= token_id < cfg.vocab_size:
+            raise _lib.B2DError(_lib.B2D_ERR_INVALID_ARG, "multi_sm_decode_nlayer", f"token_id {token_id}")
+        tok = torch.tensor([token_id], dtype=torch.int32).to(eng.device, non_blocking=True)
+    if isinstance(pos, torch.Tensor):
+        p = pos.reshape(-1)[:1].to(device=eng.device, dtype=torch.int32)
+    else:
+        pos = int(pos)
+        if not 0 <= pos < cfg.context_len:
+            raise _lib.B2DError(_lib.B2D_ERR_INVALID_ARG, "multi_sm_decode_nlayer", f"pos {pos}")
+        p = torch.tensor([pos], dtype=torch.int32).to(eng.device, non_blocking=True)
+    logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device=eng.device)
+    nxt = torch.empty(1, dtype=torch.int32, device=eng.device)
+    eng.step(tok, p, kv_packed, logits, nxt)
+    return nxt[0], logits, kv_packed
