@@ -168,6 +168,18 @@ B2D_API b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, in
  */
 B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
 
+/*
+ * Diagnostics (no reference counterpart; the reference only times whole
+ * steps, profile_kernels.py:44-64).  b2d_debug_trace: every CTA records
+ * global-timer stamps (ns) at its phase boundaries into buf_dev
+ * [grid][stamps_per_cta] (slot 0 = start, 13 per layer, 3 final; NULL/0 turns
+ * it off).  b2d_debug_tune: knob 1 = sleep (ns) between failed polls of the
+ * exchange words (0 = spin); knob 2 = weight-stream copies in flight per CTA
+ * (1..12, default 4).
+ */
+B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
+B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);
+
 #ifdef __cplusplus
 }
 #endif

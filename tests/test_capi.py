@@ -84,6 +84,8 @@ def test_host_argument_validation(lib):
     assert lib.b2d_sample(None, None, 1, 32000, None, 0, None, None, ctypes.byref(sp), None,
                           None) == _lib.B2D_ERR_INVALID_ARG
     assert lib.b2d_debug_set(None, 1, 0) == _lib.B2D_ERR_INVALID_ARG
+    assert lib.b2d_debug_tune(None, 1, 0) == _lib.B2D_ERR_INVALID_ARG
+    assert lib.b2d_debug_trace(None, None, 0) == _lib.B2D_ERR_INVALID_ARG
 
 
 def test_product_path_has_no_oracle_import():

@@ -77,6 +77,8 @@ _SIGS = {
     "b2d_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P,
                                   ctypes.POINTER(Sampling), _P, _P]),
     "b2d_debug_set": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int]),
+    "b2d_debug_trace": (ctypes.c_int, [_P, _P, ctypes.c_int]),
+    "b2d_debug_tune": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
 }
 
 _lib = None

@@ -104,6 +104,10 @@ struct b2d_ws {
   int att_T;
   uint64_t wait_ns;
   int grid_part;
+  uint64_t* trace;
+  int trace_stride;
+  uint32_t poll_ns;
+  int max_inflight;
 };
 
 extern "C" {
@@ -163,6 +167,7 @@ b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint
   B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(ops->smem)),
            "cudaFuncSetAttribute(smem)");
+  if (sms < b2d::kMinGrid) return B2D_ERR_UNSUPPORTED;  // phase register budgets assume >= 128 SMs
   int per_sm = 0;
   B2D_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops->kernel, b2d::kThreads, ops->smem),
            "occupancy");
@@ -198,7 +203,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   std::memset(ws, 0, sizeof(*ws));
   ws->m = m;
   ws->max_batch = max_batch;
-  ws->att_T = 64 * ((c.context_len + 511) / 512);
+  ws->att_T = 128 * ((c.context_len + 511) / 512);  // <= kMaxSplits units per head
   const uint32_t qkv = uint32_t(c.n_heads + 2 * c.n_kv_heads) * 64;
   ws->w_att = uint32_t(c.d_model) + qkv;
   ws->w_hm = ws->w_att + uint32_t(c.n_heads) * b2d::kMaxSplits * b2d::kAttWords;
@@ -208,6 +213,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   ws->n_words = size_t(c.n_layers) * ws->layer_words + c.d_model;
   ws->wait_ns = 2000000000ull;  // 2 s bound on every in-kernel wait
   ws->grid_part = m->grid;
+  ws->max_inflight = 4;
   cudaError_t e = cudaMalloc(&ws->words, ws->n_words * sizeof(uint64_t));
   if (e == cudaSuccess) e = cudaMalloc(&ws->ctl, sizeof(b2d::Control));
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_val, sizeof(float) * m->grid);
@@ -267,6 +273,31 @@ b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas) {
   return B2D_OK;
 }
 
+// Diagnostic hooks: per-CTA phase stamps (global timer, ns) into a caller
+// buffer of grid * stamps_per_cta uint64 (NULL disables), and a back-off
+// between failed polls of the exchange words.
+b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta) {
+  if (!ws || stamps_per_cta < 0 || (buf_dev == nullptr) != (stamps_per_cta == 0)) return B2D_ERR_INVALID_ARG;
+  ws->trace = buf_dev;
+  ws->trace_stride = stamps_per_cta;
+  return B2D_OK;
+}
+
+b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
+  if (!ws) return B2D_ERR_INVALID_ARG;
+  switch (knob) {
+    case 1:  // back-off between failed polls, ns
+      if (value < 0 || value > 100000) return B2D_ERR_INVALID_ARG;
+      ws->poll_ns = static_cast<uint32_t>(value);
+      return B2D_OK;
+    case 2:  // bulk copies in flight per CTA
+      if (value < 1 || value > b2d::kStages) return B2D_ERR_INVALID_ARG;
+      ws->max_inflight = static_cast<int>(value);
+      return B2D_OK;
+  }
+  return B2D_ERR_INVALID_ARG;
+}
+
 b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
                            int batch, void* kv_dev, float* logits_dev, int32_t* next_tok_dev,
                            void* stream) {
@@ -311,6 +342,10 @@ b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, con
   A.grid_part = ws->grid_part;
   A.wait_ns = ws->wait_ns;
   A.eps = c.rms_eps;
+  A.trace = ws->trace;
+  A.trace_stride = ws->trace_stride;
+  A.poll_ns = ws->poll_ns;
+  A.max_inflight = ws->max_inflight;
   void* args[] = {&A};
   B2D_CUDA(cudaLaunchCooperativeKernel(m->ops->kernel, dim3(m->grid), dim3(b2d::kThreads), args,
                                        m->ops->smem, st),

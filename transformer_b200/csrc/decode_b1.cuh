@@ -28,6 +28,8 @@
 //  * All reductions run in a fixed order (no float atomics): bit-reproducible.
 #pragma once
 
+#include <cstddef>
+
 #include "b2d_ptx.cuh"
 
 namespace b2d {
@@ -39,7 +41,7 @@ enum : uint32_t {
 };
 enum : uint32_t {
   SITE_H = 1, SITE_QKV = 2, SITE_ATT = 3, SITE_HM = 4, SITE_ACT = 5, SITE_FINAL = 6,
-  SITE_FULL = 7, SITE_EMPTY = 8, SITE_DRAIN = 9,
+  SITE_FULL = 7, SITE_EMPTY = 8, SITE_DRAIN = 9, SITE_VATT = 10,
 };
 
 struct Control {  // each word on its own 128-byte line
@@ -77,15 +79,28 @@ struct DecodeArgs {
   int grid_part;      // CTAs the work is split over (== gridDim.x except in fault tests)
   uint64_t wait_ns;   // bound on every wait
   float eps;
+  uint64_t* trace;    // optional per-CTA phase stamps (global timer, ns), or null
+  int trace_stride;   // stamps per CTA
+  uint32_t poll_ns;   // back-off between failed polls (0 = spin)
+  int max_inflight;   // bulk copies in flight per CTA (<= kStages)
 };
+
+// Phase-stamp slots (per CTA): 0 = start, then per layer kTracePerLayer
+// stamps, then final gather / logits / end.
+constexpr int kTracePerLayer = 13;
+__device__ __forceinline__ void trace_stamp(const DecodeArgs& A, int slot) {
+  if (A.trace != nullptr && threadIdx.x == 0 && slot < A.trace_stride)
+    A.trace[static_cast<size_t>(blockIdx.x) * A.trace_stride + slot] = globaltimer_ns();
+}
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
 constexpr int kStageBytes = 16896;  // 8 rows x 2 KB or 3 rows x 5.5 KB (306M shapes)
-constexpr int kStages = 12;
+constexpr int kStages = 10;
 constexpr int kAttWords = 66;       // per attention unit: o[64], m, l
-constexpr int kMaxSplits = 8;       // attention units per head
+constexpr int kMaxSplits = 4;       // attention units per head
+constexpr int kMinGrid = 128;       // fewest CTAs the phase register budgets assume
 
 template <int D_, int DFF_, int NH_, int NKV_>
 struct Shape {
@@ -100,6 +115,12 @@ struct Shape {
   static constexpr int PPS = kStageBytes / (2 * ROWB_D);    // gate/up pairs per stage
   static constexpr int RPS_F = kStageBytes / ROWB_F;        // down rows per stage
   static constexpr int XMAX = DFF > D ? DFF : D;
+  // Units per warp per phase, for grids of at least kMinGrid CTAs.
+  static constexpr int units_per_warp(int n) {
+    return ((n + kMinGrid - 1) / kMinGrid + kConsumerWarps - 1) / kConsumerWarps;
+  }
+  static constexpr int J_QKV = units_per_warp(QKV), J_O = units_per_warp(D);
+  static constexpr int J_GU = units_per_warp(DFF), J_DOWN = units_per_warp(D);
   static_assert(D % 256 == 0 && DFF % 256 == 0, "row length must be a multiple of 256");
   static_assert(RPS_D >= 1 && PPS >= 1 && RPS_F >= 1, "stage too small");
   static_assert(NH % NKV == 0, "GQA");
@@ -114,9 +135,13 @@ struct Smem {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   float h[S::D];          // residual stream (f32)
-  float x[S::XMAX];       // GEMV input (bf16-rounded values)
+  alignas(16) __nv_bfloat16 xb[S::XMAX];  // GEMV input vector (bf16)
+  alignas(128) __nv_bfloat16 katt[128][64];  // K rows of the attention unit's pass
+  alignas(128) __nv_bfloat16 vatt[128][64];  // V rows of the attention unit's pass
+  uint64_t att_bar;       // completes the K/V staging copies
   float qkv[3 * 64];      // attention unit inputs
-  float rq[64], rk[64];   // post-RoPE q (pre-scaled), k
+  alignas(16) float rq[64];  // post-RoPE q (pre-scaled); read as float4
+  alignas(16) float rk[64];  // post-RoPE k
   float wm[kConsumerWarps], wl[kConsumerWarps];
   float wo[kConsumerWarps][64];
   float red[kConsumerWarps];
@@ -124,6 +149,19 @@ struct Smem {
   float am_v[kConsumerWarps];
   int am_i[kConsumerWarps];
   int abort;
+};
+
+// Fields read with 16-byte vector loads or written by bulk copies.
+template <class S>
+struct SmemChecks {
+  static_assert(offsetof(Smem<S>, stage) % 128 == 0, "stage alignment");
+  static_assert(kStageBytes % 16 == 0, "stage size");
+  static_assert(offsetof(Smem<S>, xb) % 16 == 0, "xb alignment");
+  static_assert(offsetof(Smem<S>, vatt) % 128 == 0 && offsetof(Smem<S>, katt) % 128 == 0, "K/V staging alignment");
+  static_assert(offsetof(Smem<S>, rq) % 16 == 0, "rq alignment");
+  static_assert(offsetof(Smem<S>, full) % 8 == 0 && offsetof(Smem<S>, att_bar) % 8 == 0, "mbarrier alignment");
+  static_assert(sizeof(Smem<S>) <= 232448, "shared memory per CTA");
+  static constexpr bool ok = true;
 };
 
 __device__ __forceinline__ int split_begin(int c, int n, int g) {
@@ -147,6 +185,21 @@ __device__ __forceinline__ bool wait_expired(const DecodeArgs& A, uint32_t flag,
   return false;
 }
 
+// Bounded-wait bookkeeping that stays off the critical path: the clock is
+// read every 128 polls and the abort marker (a global load) only once a wait
+// has already lasted 20 us, which normal waits never reach.
+struct Waiter {
+  uint64_t start = 0;
+  uint32_t spins = 0;
+  __device__ __forceinline__ bool expired(const DecodeArgs& A, uint32_t flag, uint64_t t0, uint32_t site) {
+    if ((++spins & 127u) != 0) return false;
+    const uint64_t now = globaltimer_ns();
+    if (start == 0) { start = now; return false; }
+    if (now - start < 20000u) return false;
+    return wait_expired(A, flag, t0, site);
+  }
+};
+
 // Gather up to N word pairs per thread.  addr(i) -> pointer to pair i (16-B
 // aligned); valid(i) says whether this thread owns item i; store(i, a, b)
 // receives the payloads.  All owned loads are issued together, then the
@@ -160,7 +213,7 @@ __device__ __forceinline__ bool gather_pairs(const DecodeArgs& A, uint32_t flag,
 #pragma unroll
   for (int i = 0; i < N; ++i)
     if (valid(i)) pending |= 1u << i;
-  uint32_t spins = 0;
+  Waiter wt;
   while (pending) {
 #pragma unroll
     for (int g = 0; g < N; g += GRP) {
@@ -188,7 +241,8 @@ __device__ __forceinline__ bool gather_pairs(const DecodeArgs& A, uint32_t flag,
       uint64_t x, y;
       ld_words2(p0, x, y);
       if (word_flag(x) == flag && word_flag(y) == flag) break;
-      if ((++spins & 31u) == 0 && wait_expired(A, flag, t0, site)) return false;
+      if (A.poll_ns) __nanosleep(A.poll_ns);
+      if (wt.expired(A, flag, t0, site)) return false;
     }
   }
   return true;
@@ -206,27 +260,87 @@ struct Ring {
 __device__ __forceinline__ bool wait_full(const DecodeArgs& A, Ring& r, uint32_t flag, uint64_t t0) {
   const uint32_t slot = r.seq % kStages, par = (r.seq / kStages) & 1u;
   const int lane = threadIdx.x & 31;
-  uint32_t spins = 0;
+  Waiter wt;
   while (true) {
     const bool done = mbar_test(&r.full[slot], par);
     if (__all_sync(0xffffffffu, done)) return true;
-    if ((++spins & 63u) == 0) {
-      const bool exp = lane == 0 ? wait_expired(A, flag, t0, SITE_FULL) : false;
-      if (__shfl_sync(0xffffffffu, exp ? 1 : 0, 0)) return false;
-    }
+    const bool exp = lane == 0 ? wt.expired(A, flag, t0, SITE_FULL) : false;
+    if (__shfl_sync(0xffffffffu, exp ? 1 : 0, 0)) return false;
   }
 }
 
 // One GEMV phase over this CTA's units [u_begin, u_end) (a unit is one row, or
 // a gate/up row pair when PAIR), streamed in stages of `per_stage` units.
-// Warp w takes units u with (u - u_begin) % 8 == w.  out(u, dot0, dot1) is
-// called on every lane with the warp-reduced dot products.
-template <int KI, int ROWB, bool PAIR, class Out>
+// Warp w owns units u_begin + w + 8j (j < MAXJ).  Each lane accumulates its
+// partial dot products for all of its units across the phase's stages (two
+// accumulators per row to shorten the FMA chain); the cross-lane reductions
+// of all units run together once, after the last stage, so their shuffle
+// latencies overlap.  out(u, dot0, dot1) is then called on every lane.
+template <int KI, int ROWB, bool PAIR, int MAXJ, class Out>
 __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
                                            int u_begin, int u_end, int per_stage,
-                                           const uint4 (&x)[KI], Out out) {
+                                           const __nv_bfloat16* xsm, Out out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int UNIT_BYTES = PAIR ? 2 * ROWB : ROWB;
+  constexpr int NR = PAIR ? 2 : 1;
+  const uint4* xp = reinterpret_cast<const uint4*>(xsm);
+  float acc[MAXJ][NR][2];
+#pragma unroll
+  for (int j = 0; j < MAXJ; ++j)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[j][r][0] = acc[j][r][1] = 0.f;
+  bool ok = true;
+  for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
+    const int u1 = min(u0 + per_stage, u_end);
+    if (ok) ok = wait_full(A, ring, flag, t0);
+    const uint32_t slot = ring.seq % kStages;
+    if (ok) {
+      const uint8_t* sb = ring.stage[slot];
+#pragma unroll
+      for (int j = 0; j < MAXJ; ++j) {
+        const int u = u_begin + warp + kConsumerWarps * j;
+        if (u >= u0 && u < u1) {
+          const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * UNIT_BYTES);
+#pragma unroll
+          for (int k = 0; k < KI; ++k) {
+            const uint4 xv = xp[k * 32 + lane];
+#pragma unroll
+            for (int r = 0; r < NR; ++r) acc[j][r][k & 1] = dot8(rp[r * (ROWB / 16) + k * 32 + lane], xv, acc[j][r][k & 1]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[slot]);
+    ring.seq++;
+    if (!ok) return false;
+  }
+  float v[MAXJ][NR];
+#pragma unroll
+  for (int j = 0; j < MAXJ; ++j)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) v[j][r] = acc[j][r][0] + acc[j][r][1];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < MAXJ; ++j)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) v[j][r] += __shfl_xor_sync(0xffffffffu, v[j][r], o);
+#pragma unroll
+  for (int j = 0; j < MAXJ; ++j) {
+    const int u = u_begin + warp + kConsumerWarps * j;
+    if (u < u_end) out(u, v[j][0], v[j][NR - 1]);
+  }
+  return true;
+}
+
+// Same streaming for many units per warp (the logits): reduce per stage.
+template <int KI, int ROWB, class Out>
+__device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
+                                                int u_begin, int u_end, int per_stage,
+                                                const __nv_bfloat16* xsm, Out out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* xp = reinterpret_cast<const uint4*>(xsm);
   bool ok = true;
   for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
     const int u1 = min(u0 + per_stage, u_end);
@@ -236,18 +350,14 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
       const uint8_t* sb = ring.stage[slot];
       const int first = u0 + ((warp - (u0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
       for (int u = first; u < u1; u += kConsumerWarps) {
-        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * UNIT_BYTES);
-        float acc0 = 0.f, acc1 = 0.f;
+        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * ROWB);
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-        for (int k = 0; k < KI; ++k) acc0 = dot8(rp[k * 32 + lane], x[k], acc0);
-        if (PAIR) {
-          const uint4* rq = rp + ROWB / 16;
-#pragma unroll
-          for (int k = 0; k < KI; ++k) acc1 = dot8(rq[k * 32 + lane], x[k], acc1);
+        for (int k = 0; k < KI; k += 2) {
+          a0 = dot8(rp[k * 32 + lane], xp[k * 32 + lane], a0);
+          if (k + 1 < KI) a1 = dot8(rp[(k + 1) * 32 + lane], xp[(k + 1) * 32 + lane], a1);
         }
-        acc0 = warp_sum(acc0);
-        if (PAIR) acc1 = warp_sum(acc1);
-        out(u, acc0, acc1);
+        out(u, warp_sum(a0 + a1), 0.f);
       }
     }
     __syncwarp();
@@ -258,23 +368,18 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
   return true;
 }
 
-// Lane l holds x[k*256 + l*8 .. +8) as packed bf16 pairs (matches the
-// weight chunk it reads from the stage).
-template <class S, int KI>
-__device__ __forceinline__ void load_x(const float* xs, uint4 (&x)[KI]) {
-  const int lane = threadIdx.x & 31;
+// Norm gains for this thread's elements (t + k*256), loaded ahead of the
+// wait that precedes the norm so their latency is hidden.
+template <class S>
+__device__ __forceinline__ void load_gain(const float* g, float (&gr)[S::D / kConsumers]) {
 #pragma unroll
-  for (int k = 0; k < KI; ++k) {
-    const float4* p = reinterpret_cast<const float4*>(xs + k * 256 + lane * 8);
-    const float4 a = p[0], b = p[1];
-    x[k] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
-                      pack_bf16x2(b.z, b.w));
-  }
+  for (int k = 0; k < S::D / kConsumers; ++k) gr[k] = __ldg(g + threadIdx.x + k * kConsumers);
 }
 
 // x = bf16(h * rsqrt(mean(h^2) + eps) * g)  (RMSNorm, reference :121-126)
 template <class S>
-__device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float* g, float eps) {
+__device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float (&gr)[S::D / kConsumers], float eps) {
+  static_assert(S::D % kConsumers == 0, "D must be a multiple of the consumer count");
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   float ss = 0.f;
 #pragma unroll
@@ -286,7 +391,11 @@ __device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float* g, float 
 #pragma unroll
   for (int w = 0; w < kConsumerWarps; ++w) tot += sm.red[w];
   const float r = rsqrtf(tot / static_cast<float>(S::D) + eps);
-  for (int i = t; i < S::D; i += kConsumers) sm.x[i] = round_bf16(sm.h[i] * r * __ldg(g + i));
+#pragma unroll
+  for (int k = 0; k < S::D / kConsumers; ++k) {
+    const int i = t + k * kConsumers;
+    sm.xb[i] = __float2bfloat16_rn(sm.h[i] * r * gr[k]);
+  }
   consumer_sync<kConsumers>();
 }
 
@@ -297,14 +406,28 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
   const int G = A.grid_part;
   uint32_t seq = 0;
   bool ok = true;
+  // Copies are capped at max_inflight per CTA: enough to keep HBM busy, few
+  // enough that the memory queues stay short for the latency-critical
+  // exchange words.  Landed stages still accumulate in the ring.
+  uint32_t landed = 0;
+  const uint32_t cap = static_cast<uint32_t>(A.max_inflight);
   auto issue = [&](const uint8_t* src, uint32_t bytes) {
     const uint32_t slot = seq % kStages;
+    while (seq - landed >= cap) {
+      Waiter wt;
+      while (!mbar_test(&sm.full[landed % kStages], (landed / kStages) & 1u)) {
+        if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_FULL))) {
+          ok = false;
+          return;
+        }
+      }
+      ++landed;
+    }
     if (seq >= kStages) {
       const uint32_t par = ((seq / kStages) - 1) & 1u;
-      uint32_t spins = 0;
+      Waiter wt;
       while (!mbar_test(&sm.empty[slot], par)) {
-        if (((++spins & 63u) == 0) &&
-            (*reinterpret_cast<volatile int*>(&sm.abort) || wait_expired(A, flag, t0, SITE_EMPTY))) {
+        if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_EMPTY))) {
           ok = false;
           return;
         }
@@ -344,29 +467,90 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
 
 // One attention unit: head h, KV positions [p0, p1) (reference :182-221).
 // Writes o (unnormalised), m, l as exchange words.
+//
+// Layout for latency: a warp owns 16 positions per pass, two lanes per
+// position (each lane holds half of the 64 dims), so QK needs one shuffle per
+// position instead of a full warp reduction; PV is lane-per-dim over
+// probabilities staged in shared memory.  The K/V of the unit's first pass
+// are requested at the start of the layer (att_prefetch), so their latency
+// hides behind the QKV phase.
+struct AttPre {
+  uint32_t vbytes;  // bytes of each of the pass's K and V copies in flight (0 = none)
+  float rc, rs;     // RoPE cos/sin (threads < 64)
+  int unit;         // unit the prefetch belongs to (-1 = none)
+};
+
+// Issue one pass (up to 128 positions from `base`) of unit (h, j): the cached
+// K and V rows into shared memory by two bulk copies (each contiguous in the
+// cache).  Position `pos` is new: it comes from q/k/v.
+template <class S>
+__device__ __forceinline__ void att_load_pass(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
+                                              int h, int j, int base) {
+  const int t = threadIdx.x;
+  const int g = h / S::GQA;
+  const int p1 = min(j * A.att_T + A.att_T, pos + 1);
+  const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
+  const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
+  const __nv_bfloat16* Vc = Kc + half;
+  const int ncached = max(0, min(min(base + 128, p1), pos) - base);
+  pre.vbytes = static_cast<uint32_t>(ncached) * S::DH * 2;
+  if (t == 0 && pre.vbytes) {
+    const uint64_t pol = l2_policy_evict_last();
+    mbar_arrive_expect_tx(&sm.att_bar, 2 * pre.vbytes);
+    bulk_g2s(sm.katt, Kc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
+    bulk_g2s(sm.vatt, Vc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
+  }
+}
+
+template <class S>
+__device__ __forceinline__ void att_prefetch(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
+                                             int u, int nsplit) {
+  const int t = threadIdx.x;
+  pre.unit = u;
+  att_load_pass<S>(A, sm, pre, l, pos, u / nsplit, u % nsplit, (u % nsplit) * A.att_T);
+  pre.rc = pre.rs = 0.f;
+  if (t < 64) {
+    pre.rc = __ldg(A.rcos + static_cast<size_t>(pos) * 32 + (t & 31));
+    pre.rs = __ldg(A.rsin + static_cast<size_t>(pos) * 32 + (t & 31));
+  }
+}
+
 template <class S>
 __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm, uint32_t flag,
-                                               uint64_t t0, int l, int pos, int h, int j, int nsplit) {
+                                               uint64_t t0, int l, int pos, int u, int nsplit,
+                                               int trace_slot, uint32_t& att_phase, AttPre& pre) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int h = u / nsplit, j = u % nsplit;
   const int g = h / S::GQA;
   const int p0 = j * A.att_T, p1 = min(p0 + A.att_T, pos + 1);
   const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
   const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
   const __nv_bfloat16* Vc = Kc + half;
   uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
+  const int qi = lane & 15, hf = lane >> 4;  // position within the warp's 16, dim half
 
-  // Prefetch the first 64 positions' K/V (lane holds dims 2*lane, 2*lane+1)
-  // while the q/k/v words are still in flight.
-  uint32_t kr[8], vr[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int p = p0 + warp + 8 * i;
-    kr[i] = vr[i] = 0u;
-    if (p < p1 && p < pos) {
-      kr[i] = __ldg(reinterpret_cast<const unsigned int*>(Kc + static_cast<size_t>(p) * S::DH) + lane);
-      vr[i] = __ldg(reinterpret_cast<const unsigned int*>(Vc + static_cast<size_t>(p) * S::DH) + lane);
+  if (pre.unit != u) att_prefetch<S>(A, sm, pre, l, pos, u, nsplit);
+  pre.unit = -1;
+  uint32_t& vbytes = pre.vbytes;
+  const float rc = pre.rc, rs = pre.rs;
+  auto load_pass = [&](int base) { att_load_pass<S>(A, sm, pre, l, pos, h, j, base); };
+  // Wait (bounded, ignoring the abort marker) for this pass's V copy; used on
+  // every path so the CTA never leaves with the copy in flight.
+  auto wait_v = [&]() -> bool {
+    if (!vbytes) return true;
+    const uint64_t ts0 = globaltimer_ns();
+    bool landed = false;
+    uint32_t n = 0;
+    while (!(landed = mbar_test(&sm.att_bar, att_phase & 1u))) {
+      if ((++n & 63u) == 0 && globaltimer_ns() - ts0 > 10000000ull) {
+        raise_error(A.ctl, ST_TIMEOUT | SITE_VATT, flag);
+        break;
+      }
     }
-  }
+    ++att_phase;
+    vbytes = 0;
+    return landed;
+  };
   // q head h, k/v of kv head g: 3 x 32 word pairs.
   bool ok = gather_pairs<1>(
       A, flag, t0, SITE_QKV,
@@ -378,59 +562,93 @@ __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm,
       [&](int) { return t < 96; },
       [&](int, float a, float b) { sm.qkv[2 * t] = a; sm.qkv[2 * t + 1] = b; });
   ok = consumer_sync_and<kConsumers>(ok);
-  if (!ok) return false;
+  if (!ok) {
+    wait_v();
+    return false;
+  }
+  trace_stamp(A, trace_slot);
   // RoPE (rotate-half, reference :154-173; f32 tables as model.py:101-107).
   if (t < 64) {
     const int i = t & 31;
     const float* src = sm.qkv + (t < 32 ? 0 : 64);
-    const float c = __ldg(A.rcos + static_cast<size_t>(pos) * 32 + i);
-    const float s = __ldg(A.rsin + static_cast<size_t>(pos) * 32 + i);
     const float lo = src[i], hi = src[i + 32];
     float* dst = t < 32 ? sm.rq : sm.rk;
     const float sc = t < 32 ? 0.125f : 1.0f;  // 1/sqrt(64) folded into q (exact)
-    dst[i] = (lo * c - hi * s) * sc;
-    dst[i + 32] = (lo * s + hi * c) * sc;
+    dst[i] = (lo * rc - hi * rs) * sc;
+    dst[i + 32] = (lo * rs + hi * rc) * sc;
   }
   consumer_sync<kConsumers>();
-  const float q0 = sm.rq[2 * lane], q1 = sm.rq[2 * lane + 1];
-  const float kn0 = sm.rk[2 * lane], kn1 = sm.rk[2 * lane + 1];
+  const float4* q4 = reinterpret_cast<const float4*>(sm.rq + hf * 32);
   const float vn0 = sm.qkv[128 + 2 * lane], vn1 = sm.qkv[128 + 2 * lane + 1];
 
   float m = -INFINITY, lsum = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int base = p0; base < p1; base += 64) {
-    if (base != p0) {
+  for (int base = p0; base < p1; base += 16 * kConsumerWarps) {
+    if (base != p0) load_pass(base);
+    if (!__all_sync(0xffffffffu, wait_v())) ok = false;  // K/V rows of this pass landed
+    const int pk = base + warp * 16 + qi;
+    float sdot = 0.f;
+    if (pk == pos) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int p = base + warp + 8 * i;
-        kr[i] = vr[i] = 0u;
-        if (p < p1 && p < pos) {
-          kr[i] = __ldg(reinterpret_cast<const unsigned int*>(Kc + static_cast<size_t>(p) * S::DH) + lane);
-          vr[i] = __ldg(reinterpret_cast<const unsigned int*>(Vc + static_cast<size_t>(p) * S::DH) + lane);
-        }
+      for (int d = 0; d < 32; ++d) sdot = fmaf(sm.rq[hf * 32 + d], sm.rk[hf * 32 + d], sdot);
+    } else if (ok && pk < p1) {
+      // lane qi starts at chunk qi & 3 so a quarter-warp's 8 rows spread over banks
+      const uint4* kr = reinterpret_cast<const uint4*>(sm.katt[pk - base]) + hf * 4;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int cc = (c + qi) & 3;
+        const uint4 kw = kr[cc];
+        const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+        sdot = fmaf(qa.x, bf16_lo(kw.x), sdot);
+        sdot = fmaf(qa.y, bf16_hi(kw.x), sdot);
+        sdot = fmaf(qa.z, bf16_lo(kw.y), sdot);
+        sdot = fmaf(qa.w, bf16_hi(kw.y), sdot);
+        sdot = fmaf(qb.x, bf16_lo(kw.z), sdot);
+        sdot = fmaf(qb.y, bf16_hi(kw.z), sdot);
+        sdot = fmaf(qb.z, bf16_lo(kw.w), sdot);
+        sdot = fmaf(qb.w, bf16_hi(kw.w), sdot);
       }
     }
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+    const bool valid = pk < p1;
+    float s = valid ? sdot : -INFINITY;
+    float mx = s;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int p = base + warp + 8 * i;
-      if (p < p1) {
-        float k0, k1, v0, v1;
-        if (p == pos) {
-          k0 = kn0; k1 = kn1; v0 = vn0; v1 = vn1;
-        } else {
-          k0 = bf16_lo(kr[i]); k1 = bf16_hi(kr[i]);
-          v0 = bf16_lo(vr[i]); v1 = bf16_hi(vr[i]);
+    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mn = fmaxf(m, mx);
+    const float pe = valid ? __expf(s - mn) : 0.f;
+    float ps = pe;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
+    if (hf == 0) sm.wo[warp][qi] = pe;   // stage probabilities for PV
+    __syncwarp();
+    float a0 = 0.f, a1 = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int pv = base + warp * 16 + i;
+        const float pi = sm.wo[warp][i];
+        float v0 = 0.f, v1 = 0.f;
+        if (pv == pos) {
+          v0 = vn0; v1 = vn1;
+        } else if (pv < p1) {
+          const uint32_t vw = reinterpret_cast<const uint32_t*>(sm.vatt[pv - base])[lane];
+          v0 = bf16_lo(vw); v1 = bf16_hi(vw);
         }
-        const float s = warp_sum(fmaf(q0, k0, q1 * k1));
-        const float mn = fmaxf(m, s);
-        const float alpha = __expf(m - mn);
-        const float pe = __expf(s - mn);
-        lsum = fmaf(lsum, alpha, pe);
-        o0 = fmaf(o0, alpha, pe * v0);
-        o1 = fmaf(o1, alpha, pe * v1);
-        m = mn;
+        a0 = fmaf(pi, v0, a0);
+        a1 = fmaf(pi, v1, a1);
       }
     }
+    __syncwarp();
+    lsum = fmaf(lsum, alpha, ps);
+    o0 = fmaf(o0, alpha, a0);
+    o1 = fmaf(o1, alpha, a1);
+    m = mn;
+    // every warp is done reading the staged V before the next pass reuses it
+    ok = consumer_sync_and<kConsumers>(ok);
+    if (!ok) return false;
   }
+  // per-warp state -> shared, then warp 0 merges in fixed order
   sm.wo[warp][2 * lane] = o0;
   sm.wo[warp][2 * lane + 1] = o1;
   if (lane == 0) { sm.wm[warp] = m; sm.wl[warp] = lsum; }
@@ -439,17 +657,17 @@ __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm,
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.wm[w]);
-    float L = 0.f, a0 = 0.f, a1 = 0.f;
+    float L = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) {
       const float e = sm.wl[w] > 0.f ? __expf(sm.wm[w] - M) : 0.f;
       L = fmaf(sm.wl[w], e, L);
-      a0 = fmaf(sm.wo[w][2 * lane], e, a0);
-      a1 = fmaf(sm.wo[w][2 * lane + 1], e, a1);
+      b0 = fmaf(sm.wo[w][2 * lane], e, b0);
+      b1 = fmaf(sm.wo[w][2 * lane + 1], e, b1);
     }
     uint64_t* out = lw + A.w_att + static_cast<size_t>(h * nsplit + j) * kAttWords;
-    st_word(out + 2 * lane, a0, flag);
-    st_word(out + 2 * lane + 1, a1, flag);
+    st_word(out + 2 * lane, b0, flag);
+    st_word(out + 2 * lane + 1, b1, flag);
     if (lane == 0) {
       st_word(out + 64, M, flag);
       st_word(out + 65, L, flag);
@@ -458,7 +676,7 @@ __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm,
   // The first head of the group, owning the split that holds `pos`, appends
   // this position's K (post-RoPE) and V to the cache in bf16.
   if (warp == 1 && (h % S::GQA) == 0 && pos >= p0 && pos < p1) {
-    __nv_bfloat162 kk = __floats2bfloat162_rn(kn0, kn1);
+    __nv_bfloat162 kk = __floats2bfloat162_rn(sm.rk[2 * lane], sm.rk[2 * lane + 1]);
     __nv_bfloat162 vv = __floats2bfloat162_rn(vn0, vn1);
     __nv_bfloat16* kd = const_cast<__nv_bfloat16*>(Kc) + static_cast<size_t>(pos) * S::DH;
     __nv_bfloat16* vd = const_cast<__nv_bfloat16*>(Vc) + static_cast<size_t>(pos) * S::DH;
@@ -472,6 +690,7 @@ __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm,
 template <class S>
 __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs A) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
+  static_assert(SmemChecks<S>::ok, "");
   Smem<S>& sm = *reinterpret_cast<Smem<S>*>(smem_raw);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int cta = blockIdx.x;
@@ -492,6 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
+    mbar_init(&sm.att_bar, 1);
     sm.abort = 0;
     fence_mbar_init();
   }
@@ -504,6 +724,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
 
   Ring ring{sm.stage, sm.full, sm.empty, 0u};
   bool ok = true;
+  uint32_t att_phase = 0;  // completed uses of sm.att_bar
+  AttPre pre;
+  pre.unit = -1;
+  pre.vbytes = 0;
+  trace_stamp(A, 0);
   const int nsplit = (pos + A.att_T) / A.att_T;  // ceil((pos+1)/T)
   const int n_units = S::NH * nsplit;
 
@@ -515,9 +740,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
   }
   consumer_sync<kConsumers>();
 
-  uint4 xr[S::KD];
+  float gr[S::D / kConsumers];
   for (int l = 0; l < A.n_layers; ++l) {
     uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
+    load_gain<S>(A.ln1 + static_cast<size_t>(l) * S::D, gr);
+    if (cta < n_units) att_prefetch<S>(A, sm, pre, l, pos, cta, nsplit);  // K/V of this layer's unit
     // ---- residual in: H_l (written by layer l-1's down phase) ----
     if (l > 0) {
       ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
@@ -527,23 +754,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
     }
-    rmsnorm_to_x<S>(sm, A.ln1 + static_cast<size_t>(l) * S::D, A.eps);
-    load_x<S, S::KD>(sm.x, xr);
+    const int ts = 1 + l * kTracePerLayer;
+    trace_stamp(A, ts + 0);
+    rmsnorm_to_x<S>(sm, gr, A.eps);
+    trace_stamp(A, ts + 1);
     // ---- QKV rows -> exchange words ----
     {
       const int a = split_begin(cta, S::QKV, G), b = split_begin(cta + 1, S::QKV, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false>(A, ring, flag, t0, a, b, S::RPS_D, xr,
+      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(lw + S::D + u, v, flag);
                                                });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
     }
+    trace_stamp(A, ts + 2);
+    trace_stamp(A, ts + 3);  // rewritten by a CTA that runs an attention unit
     // ---- attention units ----
     for (int u = cta; u < n_units && ok; u += G) {
-      ok = attention_unit<S>(A, sm, flag, t0, l, pos, u / nsplit, u % nsplit, nsplit);
+      ok = attention_unit<S>(A, sm, flag, t0, l, pos, u, nsplit, ts + 3, att_phase, pre);
     }
     if (!ok) break;
+    trace_stamp(A, ts + 4);
     // ---- gather attention partials, merge splits -> x (bf16) ----
     // Item 0 (threads < NH*nsplit): the (m, l) pair of unit t -> shared memory.
     // Items 1..2*nsplit: this thread's 4 output dims of head t/16 per split.
@@ -564,6 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
           });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
+      trace_stamp(A, ts + 5);
       if (hh < S::NH) {
         const float* ml = sm.ml + 2 * hh * nsplit;
         float M = -INFINITY;
@@ -582,21 +815,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
         }
         const float inv = 1.0f / fmaxf(L, 1e-10f);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) sm.x[hh * 64 + d0 + k] = round_bf16(o[k] * inv);
+        for (int k = 0; k < 4; ++k) sm.xb[hh * 64 + d0 + k] = __float2bfloat16_rn(o[k] * inv);
       }
       consumer_sync<kConsumers>();
-      load_x<S, S::KD>(sm.x, xr);
     }
+    trace_stamp(A, ts + 6);
     // ---- O rows: HM = H + attn @ Wo^T ----
     {
       const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false>(A, ring, flag, t0, a, b, S::RPS_D, xr,
+      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
                                                });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
     }
+    trace_stamp(A, ts + 7);
+    load_gain<S>(A.ln2 + static_cast<size_t>(l) * S::D, gr);
     // ---- gather HM (the residual after attention) ----
     ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
         A, flag, t0, SITE_HM, [&](int i) { return lw + A.w_hm + 2 * (t + i * kConsumers); },
@@ -604,12 +839,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
         [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
     ok = consumer_sync_and<kConsumers>(ok);
     if (!ok) break;
-    rmsnorm_to_x<S>(sm, A.ln2 + static_cast<size_t>(l) * S::D, A.eps);
-    load_x<S, S::KD>(sm.x, xr);
+    trace_stamp(A, ts + 8);
+    rmsnorm_to_x<S>(sm, gr, A.eps);
+    trace_stamp(A, ts + 9);
     // ---- gate/up pairs -> act = silu(g) * u ----
     {
       const int a = split_begin(cta, S::DFF, G), b = split_begin(cta + 1, S::DFF, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, true>(A, ring, flag, t0, a, b, S::PPS, xr,
+      ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xb,
                                               [&](int u, float gt, float up) {
                                                 if (lane == 0) {
                                                   const float act = gt * (1.0f / (1.0f + __expf(-gt))) * up;
@@ -619,6 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
     }
+    trace_stamp(A, ts + 10);
     // ---- gather act -> x (bf16), down rows: H_{l+1} = HM + act @ Wd^T ----
     {
       ok = gather_pairs<(S::DFF / 2 + kConsumers - 1) / kConsumers>(
@@ -626,23 +863,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
           [&](int i) { return t + i * kConsumers < S::DFF / 2; },
           [&](int i, float a, float b) {
             const int k = t + i * kConsumers;
-            sm.x[2 * k] = round_bf16(a);
-            sm.x[2 * k + 1] = round_bf16(b);
+            sm.xb[2 * k] = __float2bfloat16_rn(a);
+            sm.xb[2 * k + 1] = __float2bfloat16_rn(b);
           });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
-      uint4 xf[S::KF];
-      load_x<S, S::KF>(sm.x, xf);
+      trace_stamp(A, ts + 11);
       uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
       const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KF, S::ROWB_F, false>(A, ring, flag, t0, a, b, S::RPS_F, xf,
+      ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xb,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
                                                });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
     }
+    trace_stamp(A, ts + 12);
   }
+  const int tf = 1 + A.n_layers * kTracePerLayer;
 
   if (ok) {
     // ---- final norm + tied logits + argmax (reference :314-357) ----
@@ -653,18 +891,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
         [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
     ok = consumer_sync_and<kConsumers>(ok);
   }
+  trace_stamp(A, tf + 0);
   if (ok) {
-    rmsnorm_to_x<S>(sm, A.lnf, A.eps);
-    load_x<S, S::KD>(sm.x, xr);
+    load_gain<S>(A.lnf, gr);
+    rmsnorm_to_x<S>(sm, gr, A.eps);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     const int a = split_begin(cta, A.vocab, G), b = split_begin(cta + 1, A.vocab, G);
-    ok = gemv_phase<S::KD, S::ROWB_D, false>(A, ring, flag, t0, a, b, S::RPS_D, xr,
+    ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
                                              [&](int u, float v, float) {
                                                if (lane == 0 && A.logits) A.logits[u] = v;
                                                if (v > best_v) { best_v = v; best_i = u; }
                                              });
     ok = consumer_sync_and<kConsumers>(ok);
+    trace_stamp(A, tf + 1);
     if (ok) {
       if (lane == 0) { sm.am_v[warp] = best_v; sm.am_i[warp] = best_i; }
       consumer_sync<kConsumers>();
@@ -695,7 +935,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
       }
     }
   }
+  trace_stamp(A, tf + 2);
   if (!ok) {
+    // a K/V staging copy requested for an attention unit that never ran
+    if (pre.vbytes) {
+      const uint64_t ts0 = globaltimer_ns();
+      while (!mbar_test(&sm.att_bar, att_phase & 1u) && globaltimer_ns() - ts0 < 10000000ull) {
+      }
+    }
     *reinterpret_cast<volatile int*>(&sm.abort) = 1;
   }
 }

@@ -125,6 +125,28 @@ class DecodeEngine:
     def debug_set(self, wait_ns: int, extra_ctas: int = 0):
         _lib.check(self.lib.b2d_debug_set(self.ws, int(wait_ns), int(extra_ctas)), "b2d_debug_set")
 
+    def trace_slots(self) -> int:
+        return 1 + 13 * self.cfg.n_layers + 3
+
+    def debug_trace(self, enable: bool = True) -> torch.Tensor | None:
+        """Turn per-CTA phase stamps on (returns the int64 [grid, slots]
+        device buffer the kernel fills) or off (returns None)."""
+        if enable:
+            self._trace = torch.zeros(self.grid, self.trace_slots(), dtype=torch.int64, device=self.device)
+            _lib.check(self.lib.b2d_debug_trace(self.ws, _ptr(self._trace), self.trace_slots()), "b2d_debug_trace")
+            return self._trace
+        _lib.check(self.lib.b2d_debug_trace(self.ws, None, 0), "b2d_debug_trace")
+        self._trace = None
+        return None
+
+    def debug_tune(self, poll_ns: int | None = None, max_inflight: int | None = None):
+        """Diagnostic knobs: back-off between failed polls (ns) and weight
+        copies in flight per CTA."""
+        if poll_ns is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 1, int(poll_ns)), "b2d_debug_tune")
+        if max_inflight is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 2, int(max_inflight)), "b2d_debug_tune")
+
     # ---- prompt ingestion ----------------------------------------------
     def prefill(self, prompt, kv: torch.Tensor, start: int = 0, stream=None) -> torch.Tensor:
         """Feed prompt tokens one step at a time (teacher forcing), writing the
