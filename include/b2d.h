@@ -51,7 +51,8 @@ typedef enum {
   B2D_ERR_LAUNCH = 5,         /* cooperative launch refused (grid not co-resident) */
   B2D_ERR_DEVICE_TIMEOUT = 6, /* a bounded in-kernel wait ran out (status word) */
   B2D_ERR_DEVICE_INPUT = 7,   /* kernel saw a token/pos out of range (status word) */
-  B2D_ERR_DEVICE_HALTED = 8   /* workspace holds an earlier device error; reset it */
+  B2D_ERR_DEVICE_HALTED = 8,  /* workspace holds an earlier device error; reset it */
+  B2D_ERR_SCRATCH_LIMIT = 9   /* needs more than b2d_decode_step_static's fixed scratch */
 } b2d_status;
 
 /* Model shape.  Same keys as the reference config dict (model.py:37-47). */
@@ -158,6 +159,27 @@ B2D_API b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, in
                       const int32_t* history_dev, int hist_cap,
                       const int32_t* hist_len_dev, const float* uniforms_dev,
                       const b2d_sampling* params, int32_t* out_tok_dev, void* stream);
+
+/*
+ * b2d_decode_step_static: one decode step (batch 1) that allocates nothing.
+ * No counterpart in the reference (its wrapper allocates a fresh workspace
+ * with every call).  It exists for callers that cannot allocate device
+ * memory themselves or through this library: hosts that own every device
+ * buffer (a serving process with its own memory pool, a plugin host) or code
+ * running where cudaMalloc is not permitted.  Instead of a workspace it uses
+ * one fixed 4 MiB array of device memory inside the library (held by every
+ * GPU that loads it, until exit); a model whose exchange area does not fit
+ * gets B2D_ERR_SCRATCH_LIMIT.  The caller passes the packed weights, the
+ * inputs and the outputs exactly as for b2d_decode_step on the current
+ * device.  The first call on a device looks up the array's device address,
+ * so make it before any stream capture.  Each call clears the array on
+ * `stream` before launching; calls that overlap on the GPU race on it.  No
+ * model or workspace handle, no cudaMalloc/cudaFree, no host heap use.
+ */
+B2D_API b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* weights_dev,
+                                          uint64_t weights_bytes, const int32_t* tok_dev,
+                                          const int32_t* pos_dev, void* kv_dev, float* logits_dev,
+                                          int32_t* next_tok_dev, void* stream);
 
 /*
  * Test hook, not part of the reference surface: bound every in-kernel wait by

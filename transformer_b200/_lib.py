@@ -23,6 +23,7 @@ B2D_ERR_LAUNCH = 5
 B2D_ERR_DEVICE_TIMEOUT = 6
 B2D_ERR_DEVICE_INPUT = 7
 B2D_ERR_DEVICE_HALTED = 8
+B2D_ERR_SCRATCH_LIMIT = 9
 
 
 class B2DError(RuntimeError):
@@ -76,6 +77,8 @@ _SIGS = {
     "b2d_decode_step": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, _P, _P]),
     "b2d_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P,
                                   ctypes.POINTER(Sampling), _P, _P]),
+    "b2d_decode_step_static": (ctypes.c_int, [ctypes.POINTER(Config), _P, ctypes.c_uint64, _P, _P, _P, _P,
+                                              _P, _P]),
     "b2d_debug_set": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int]),
     "b2d_debug_trace": (ctypes.c_int, [_P, _P, ctypes.c_int]),
     "b2d_debug_tune": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),

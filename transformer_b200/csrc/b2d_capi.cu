@@ -7,6 +7,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "../../include/b2d.h"
@@ -123,6 +124,7 @@ const char* b2d_status_str(b2d_status s) {
     case B2D_ERR_DEVICE_TIMEOUT: return "device wait timed out";
     case B2D_ERR_DEVICE_INPUT: return "device saw token/pos out of range";
     case B2D_ERR_DEVICE_HALTED: return "workspace halted by an earlier device error";
+    case B2D_ERR_SCRATCH_LIMIT: return "model needs more scratch than the no-allocation entry point's fixed 4 MiB array";
   }
   return "unknown status";
 }
@@ -370,3 +372,153 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode step without any allocation (b2d_decode_step_static).
+//
+// Some callers cannot allocate device memory at all: a host that hands this
+// library only the buffers it owns (an inference server or plugin host with
+// its own device-memory pool), or code running where cudaMalloc is not
+// allowed.  For them the exchange words, control words and argmax partials
+// that b2d_workspace_create would allocate live in one fixed array in device
+// memory, defined here at file scope.  The array is b2d::kStaticScratchBytes
+// (4 MiB) long, and every GPU that loads this library holds it until the
+// process exits.
+//
+// Host code must not hand `g_static_scratch` itself to a kernel: in host code
+// that name is a host-side stand-in, not a device address.  The device address
+// is looked up once per device with cudaGetSymbolAddress (with that device
+// current) on the first call made on that device, so make that first call
+// before any stream capture.  Every call reuses the same array and finds in it
+// whatever the previous call left: each call therefore clears the area it uses
+// (a stream-ordered memset) before its launch.  Calls that overlap on the GPU
+// (other streams, other threads) race on the array; keep them ordered.
+// ---------------------------------------------------------------------------
+namespace b2d {
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;
+constexpr size_t kStaticCtlOffset = 0;          // Control (512 B)
+constexpr size_t kStaticArgmaxOffset = 1024;    // am_val[kStaticMaxGrid], am_idx[kStaticMaxGrid]
+constexpr int kStaticMaxGrid = 1024;
+constexpr size_t kStaticWordsOffset = 16384;    // exchange words
+static_assert(sizeof(Control) <= kStaticArgmaxOffset - kStaticCtlOffset, "control block");
+static_assert(kStaticArgmaxOffset + 8 * kStaticMaxGrid <= kStaticWordsOffset, "argmax partials");
+}  // namespace b2d
+
+static __device__ __align__(256) unsigned char g_static_scratch[b2d::kStaticScratchBytes];
+
+namespace {
+
+struct StaticDeviceState {
+  bool ready;
+  unsigned char* scratch;  // device address of g_static_scratch on this device
+  int sms;
+  int smem_set;            // bitmask of shape ops whose smem attribute is set
+};
+constexpr int kMaxDevices = 64;
+StaticDeviceState g_static_dev[kMaxDevices];
+std::mutex g_static_mu;
+
+b2d_status static_setup(int device, const ShapeOps* ops, int ops_index, StaticDeviceState** out) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  StaticDeviceState& st = g_static_dev[device];
+  if (!st.ready) {
+    void* p = nullptr;
+    B2D_CUDA(cudaGetSymbolAddress(&p, g_static_scratch), "cudaGetSymbolAddress(g_static_scratch)");
+    if (p == nullptr) return cuda_fail(cudaErrorInvalidSymbol, "cudaGetSymbolAddress(g_static_scratch)");
+    int sms = 0, coop = 0;
+    B2D_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+    B2D_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device), "coop attr");
+    if (!coop) return B2D_ERR_LAUNCH;
+    if (sms < b2d::kMinGrid || sms > b2d::kStaticMaxGrid) return B2D_ERR_UNSUPPORTED;
+    st.scratch = static_cast<unsigned char*>(p);
+    st.sms = sms;
+    st.ready = true;
+  }
+  if (!(st.smem_set & (1 << ops_index))) {
+    B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(ops->smem)),
+             "cudaFuncSetAttribute(smem)");
+    st.smem_set |= 1 << ops_index;
+  }
+  *out = &st;
+  return B2D_OK;
+}
+
+}  // namespace
+
+extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* weights_dev,
+                                             uint64_t weights_bytes, const int32_t* tok_dev,
+                                             const int32_t* pos_dev, void* kv_dev, float* logits_dev,
+                                             int32_t* next_tok_dev, void* stream) {
+  if (!config_valid(cfg) || !weights_dev || (reinterpret_cast<uintptr_t>(weights_dev) & 255u) || !tok_dev ||
+      !pos_dev || !kv_dev || !next_tok_dev)
+    return B2D_ERR_INVALID_ARG;
+  const ShapeOps* ops = find_ops(cfg);
+  if (!ops) return B2D_ERR_UNSUPPORTED;
+  b2d_weights_layout_t lay;
+  compute_layout(cfg, &lay);
+  if (weights_bytes < lay.total_bytes) return B2D_ERR_INVALID_ARG;
+  // Exchange-word layout, as b2d_workspace_create lays it out.
+  const uint32_t qkv = uint32_t(cfg->n_heads + 2 * cfg->n_kv_heads) * 64;
+  const uint32_t w_att = uint32_t(cfg->d_model) + qkv;
+  const uint32_t w_hm = w_att + uint32_t(cfg->n_heads) * b2d::kMaxSplits * b2d::kAttWords;
+  const uint32_t w_act = w_hm + uint32_t(cfg->d_model);
+  const uint32_t layer_words = (w_act + uint32_t(cfg->d_ff) + 1) & ~1u;
+  const size_t n_words = size_t(cfg->n_layers) * layer_words + cfg->d_model;
+  if (b2d::kStaticWordsOffset + n_words * sizeof(uint64_t) > b2d::kStaticScratchBytes)
+    return B2D_ERR_SCRATCH_LIMIT;
+  int device = 0;
+  B2D_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  if (device < 0 || device >= kMaxDevices) return B2D_ERR_UNSUPPORTED;
+  cudaPointerAttributes pa;
+  B2D_CUDA(cudaPointerGetAttributes(&pa, weights_dev), "cudaPointerGetAttributes");
+  if (pa.type != cudaMemoryTypeDevice || pa.device != device) return B2D_ERR_INVALID_ARG;
+  StaticDeviceState* st = nullptr;
+  const int ops_index = ops->d == 1024 ? 0 : 1;
+  b2d_status s = static_setup(device, ops, ops_index, &st);
+  if (s != B2D_OK) return s;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  // Everything this call reads before writing starts from zero.
+  B2D_CUDA(cudaMemsetAsync(st->scratch, 0, b2d::kStaticWordsOffset + n_words * sizeof(uint64_t), cs),
+           "clear static scratch");
+  const uint8_t* w = static_cast<const uint8_t*>(weights_dev);
+  b2d::DecodeArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.wbase = w;
+  A.layer_stride = lay.layer_stride;
+  A.off_qkv = lay.off_qkv;
+  A.off_o = lay.off_o;
+  A.off_gu = lay.off_gu;
+  A.off_down = lay.off_down;
+  A.off_emb = lay.off_emb;
+  A.ln1 = reinterpret_cast<const float*>(w + lay.off_ln1);
+  A.ln2 = reinterpret_cast<const float*>(w + lay.off_ln2);
+  A.lnf = reinterpret_cast<const float*>(w + lay.off_lnf);
+  A.rcos = reinterpret_cast<const float*>(w + lay.off_cos);
+  A.rsin = reinterpret_cast<const float*>(w + lay.off_sin);
+  A.tok = tok_dev;
+  A.pos = pos_dev;
+  A.kv = static_cast<__nv_bfloat16*>(kv_dev);
+  A.logits = logits_dev;
+  A.next_tok = next_tok_dev;
+  A.words = reinterpret_cast<uint64_t*>(st->scratch + b2d::kStaticWordsOffset);
+  A.ctl = reinterpret_cast<b2d::Control*>(st->scratch + b2d::kStaticCtlOffset);
+  A.am_val = reinterpret_cast<float*>(st->scratch + b2d::kStaticArgmaxOffset);
+  A.am_idx = reinterpret_cast<int32_t*>(st->scratch + b2d::kStaticArgmaxOffset + 4 * b2d::kStaticMaxGrid);
+  A.layer_words = layer_words;
+  A.w_att = w_att;
+  A.w_hm = w_hm;
+  A.w_act = w_act;
+  A.vocab = cfg->vocab_size;
+  A.n_layers = cfg->n_layers;
+  A.ctx = cfg->context_len;
+  A.att_T = 128 * ((cfg->context_len + 511) / 512);
+  A.grid_part = st->sms;
+  A.wait_ns = 2000000000ull;
+  A.eps = cfg->rms_eps;
+  A.max_inflight = 4;
+  void* args[] = {&A};
+  B2D_CUDA(cudaLaunchCooperativeKernel(ops->kernel, dim3(st->sms), dim3(b2d::kThreads), args, ops->smem, cs),
+           "static decode launch");
+  return B2D_OK;
+}
