@@ -132,6 +132,39 @@ __device__ __forceinline__ float dot8(const uint4 w, const uint4 x, float acc) {
   acc = fmaf(bf16_hi(w.w), bf16_hi(x.w), acc);
   return acc;
 }
+// ---- packed f32x2 arithmetic (sm_100: fma.rn.f32x2) ----------------------
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+// bf16x2 word -> (lo, hi) as f32x2 (exact)
+__device__ __forceinline__ uint64_t bf2pack(uint32_t w) {
+  uint64_t r;
+  asm("{\n\t.reg .b32 l, h;\n\tshl.b32 l, %1, 16;\n\tand.b32 h, %1, 0xffff0000;\n\tmov.b64 %0, {l, h};\n\t}"
+      : "=l"(r) : "r"(w));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float f2sum(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  return lo + hi;
+}
+// 8 bf16 weights (w) times 8 f32 activations (xa: elements 0-3, xb: 4-7),
+// accumulated into two f32x2 accumulators.
+__device__ __forceinline__ void dot8x2(const uint4 w, const float4 xa, const float4 xb, uint64_t& a0,
+                                       uint64_t& a1) {
+  a0 = ffma2(bf2pack(w.x), f2pack(xa.x, xa.y), a0);
+  a1 = ffma2(bf2pack(w.y), f2pack(xa.z, xa.w), a1);
+  a0 = ffma2(bf2pack(w.z), f2pack(xb.x, xb.y), a0);
+  a1 = ffma2(bf2pack(w.w), f2pack(xb.z, xb.w), a1);
+}
+
 // Pack two f32 (already bf16-representable) into a bf16x2 word.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);

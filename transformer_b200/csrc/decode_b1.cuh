@@ -135,7 +135,7 @@ struct Smem {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   float h[S::D];          // residual stream (f32)
-  alignas(16) __nv_bfloat16 xb[S::XMAX];  // GEMV input vector (bf16)
+  alignas(16) float xf[S::XMAX];  // GEMV input vector (bf16 values as f32), see xidx
   alignas(128) __nv_bfloat16 katt[128][64];  // K rows of the attention unit's pass
   alignas(128) __nv_bfloat16 vatt[128][64];  // V rows of the attention unit's pass
   uint64_t att_bar;       // completes the K/V staging copies
@@ -156,13 +156,21 @@ template <class S>
 struct SmemChecks {
   static_assert(offsetof(Smem<S>, stage) % 128 == 0, "stage alignment");
   static_assert(kStageBytes % 16 == 0, "stage size");
-  static_assert(offsetof(Smem<S>, xb) % 16 == 0, "xb alignment");
+  static_assert(offsetof(Smem<S>, xf) % 16 == 0, "xf alignment");
   static_assert(offsetof(Smem<S>, vatt) % 128 == 0 && offsetof(Smem<S>, katt) % 128 == 0, "K/V staging alignment");
   static_assert(offsetof(Smem<S>, rq) % 16 == 0, "rq alignment");
   static_assert(offsetof(Smem<S>, full) % 8 == 0 && offsetof(Smem<S>, att_bar) % 8 == 0, "mbarrier alignment");
   static_assert(sizeof(Smem<S>) <= 232448, "shared memory per CTA");
   static constexpr bool ok = true;
 };
+
+// Position of GEMV input element e in Smem::xf.  Lane l of a warp multiplies
+// weights e = k*256 + l*8 + j (j < 8); the layout puts j < 4 of all lanes
+// first, then j >= 4, so both of a lane's 16-byte reads are conflict-free.
+__device__ __forceinline__ int xidx(int e) {
+  const int k = e >> 8, r = e & 255, ln = r >> 3, j = r & 7;
+  return (k << 8) + ((j >> 2) << 7) + (ln << 2) + (j & 3);
+}
 
 __device__ __forceinline__ int split_begin(int c, int n, int g) {
   return static_cast<int>((static_cast<long long>(c) * n) / g);
@@ -279,16 +287,16 @@ __device__ __forceinline__ bool wait_full(const DecodeArgs& A, Ring& r, uint32_t
 template <int KI, int ROWB, bool PAIR, int MAXJ, class Out>
 __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
                                            int u_begin, int u_end, int per_stage,
-                                           const __nv_bfloat16* xsm, Out out) {
+                                           const float* xsm, Out out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int UNIT_BYTES = PAIR ? 2 * ROWB : ROWB;
   constexpr int NR = PAIR ? 2 : 1;
-  const uint4* xp = reinterpret_cast<const uint4*>(xsm);
-  float acc[MAXJ][NR][2];
+  const float4* xp = reinterpret_cast<const float4*>(xsm);
+  uint64_t acc[MAXJ][NR][2];
 #pragma unroll
   for (int j = 0; j < MAXJ; ++j)
 #pragma unroll
-    for (int r = 0; r < NR; ++r) acc[j][r][0] = acc[j][r][1] = 0.f;
+    for (int r = 0; r < NR; ++r) acc[j][r][0] = acc[j][r][1] = 0ull;
   bool ok = true;
   for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
     const int u1 = min(u0 + per_stage, u_end);
@@ -303,9 +311,10 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
           const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * UNIT_BYTES);
 #pragma unroll
           for (int k = 0; k < KI; ++k) {
-            const uint4 xv = xp[k * 32 + lane];
+            const float4 xa = xp[k * 64 + lane], xb = xp[k * 64 + 32 + lane];
 #pragma unroll
-            for (int r = 0; r < NR; ++r) acc[j][r][k & 1] = dot8(rp[r * (ROWB / 16) + k * 32 + lane], xv, acc[j][r][k & 1]);
+            for (int r = 0; r < NR; ++r)
+              dot8x2(rp[r * (ROWB / 16) + k * 32 + lane], xa, xb, acc[j][r][0], acc[j][r][1]);
           }
         }
       }
@@ -319,7 +328,7 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
 #pragma unroll
   for (int j = 0; j < MAXJ; ++j)
 #pragma unroll
-    for (int r = 0; r < NR; ++r) v[j][r] = acc[j][r][0] + acc[j][r][1];
+    for (int r = 0; r < NR; ++r) v[j][r] = f2sum(acc[j][r][0]) + f2sum(acc[j][r][1]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
@@ -338,9 +347,9 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
 template <int KI, int ROWB, class Out>
 __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
                                                 int u_begin, int u_end, int per_stage,
-                                                const __nv_bfloat16* xsm, Out out) {
+                                                const float* xsm, Out out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint4* xp = reinterpret_cast<const uint4*>(xsm);
+  const float4* xp = reinterpret_cast<const float4*>(xsm);
   bool ok = true;
   for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
     const int u1 = min(u0 + per_stage, u_end);
@@ -351,13 +360,10 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring,
       const int first = u0 + ((warp - (u0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
       for (int u = first; u < u1; u += kConsumerWarps) {
         const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * ROWB);
-        float a0 = 0.f, a1 = 0.f;
+        uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll
-        for (int k = 0; k < KI; k += 2) {
-          a0 = dot8(rp[k * 32 + lane], xp[k * 32 + lane], a0);
-          if (k + 1 < KI) a1 = dot8(rp[(k + 1) * 32 + lane], xp[(k + 1) * 32 + lane], a1);
-        }
-        out(u, warp_sum(a0 + a1), 0.f);
+        for (int k = 0; k < KI; ++k) dot8x2(rp[k * 32 + lane], xp[k * 64 + lane], xp[k * 64 + 32 + lane], a0, a1);
+        out(u, warp_sum(f2sum(a0) + f2sum(a1)), 0.f);
       }
     }
     __syncwarp();
@@ -394,7 +400,7 @@ __device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float (&gr)[S::D
 #pragma unroll
   for (int k = 0; k < S::D / kConsumers; ++k) {
     const int i = t + k * kConsumers;
-    sm.xb[i] = __float2bfloat16_rn(sm.h[i] * r * gr[k]);
+    sm.xf[xidx(i)] = round_bf16(sm.h[i] * r * gr[k]);
   }
   consumer_sync<kConsumers>();
 }
@@ -761,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
     // ---- QKV rows -> exchange words ----
     {
       const int a = split_begin(cta, S::QKV, G), b = split_begin(cta + 1, S::QKV, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
+      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(lw + S::D + u, v, flag);
                                                });
@@ -815,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
         }
         const float inv = 1.0f / fmaxf(L, 1e-10f);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) sm.xb[hh * 64 + d0 + k] = __float2bfloat16_rn(o[k] * inv);
+        for (int k = 0; k < 4; ++k) sm.xf[xidx(hh * 64 + d0 + k)] = round_bf16(o[k] * inv);
       }
       consumer_sync<kConsumers>();
     }
@@ -823,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
     // ---- O rows: HM = H + attn @ Wo^T ----
     {
       const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
+      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
                                                });
@@ -845,7 +851,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
     // ---- gate/up pairs -> act = silu(g) * u ----
     {
       const int a = split_begin(cta, S::DFF, G), b = split_begin(cta + 1, S::DFF, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xb,
+      ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xf,
                                               [&](int u, float gt, float up) {
                                                 if (lane == 0) {
                                                   const float act = gt * (1.0f / (1.0f + __expf(-gt))) * up;
@@ -863,15 +869,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
           [&](int i) { return t + i * kConsumers < S::DFF / 2; },
           [&](int i, float a, float b) {
             const int k = t + i * kConsumers;
-            sm.xb[2 * k] = __float2bfloat16_rn(a);
-            sm.xb[2 * k + 1] = __float2bfloat16_rn(b);
+            sm.xf[xidx(2 * k)] = round_bf16(a);
+            sm.xf[xidx(2 * k + 1)] = round_bf16(b);
           });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
       trace_stamp(A, ts + 11);
       uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
       const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xb,
+      ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xf,
                                                [&](int u, float v, float) {
                                                  if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
                                                });
@@ -898,7 +904,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     const int a = split_begin(cta, A.vocab, G), b = split_begin(cta + 1, A.vocab, G);
-    ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xb,
+    ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
                                              [&](int u, float v, float) {
                                                if (lane == 0 && A.logits) A.logits[u] = v;
                                                if (v > best_v) { best_v = v; best_i = u; }
