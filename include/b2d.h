@@ -152,12 +152,13 @@ B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_
  *   logits_dev   f32[batch][vocab]     (read only)
  *   history_dev  int32[batch][hist_cap] tokens generated so far (prompt excluded)
  *   hist_len_dev int32[batch]          valid entries in history
- *   uniforms_dev f32[batch]            one uniform in [0,1) per sequence
+ *   uniforms_dev f64[batch]            one uniform in [0,1) per sequence (the
+ *                                      value np.random.choice would draw)
  *   out_tok_dev  int32[batch]
  */
 B2D_API b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
                       const int32_t* history_dev, int hist_cap,
-                      const int32_t* hist_len_dev, const float* uniforms_dev,
+                      const int32_t* hist_len_dev, const double* uniforms_dev,
                       const b2d_sampling* params, int32_t* out_tok_dev, void* stream);
 
 /*

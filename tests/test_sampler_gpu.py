@@ -1,0 +1,156 @@
+"""GPU: the device sampler (b2d_sample) against the reference's sample_token
+fixtures and the CPU restatement, and the config-4 sampled streams."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import sampler as OS
+from transformer_b200.generate import Sampler
+
+pytestmark = pytest.mark.gpu
+
+
+def _device_sample(smp, logits, temp, top_p, rp, hist, u):
+    dev = smp.eng.device
+    lg = torch.from_numpy(np.ascontiguousarray(logits, np.float32)).to(dev).reshape(1, -1)
+    n = len(hist)
+    if n:
+        smp.history[0, :n].copy_(torch.as_tensor(np.asarray(hist, np.int32)))
+    smp.hist_len[0] = n
+    smp.uniforms[0] = float(u)
+    return int(smp.sample(lg, temp, top_p, rp, 1).item())
+
+
+def _boundary(logits, temp, top_p, rp, hist, u, tol=1e-9):
+    """True when u lies within tol of a CDF boundary of the oracle's choice
+    (the only place a float64 prefix-sum order could change the token)."""
+    lg = OS.apply_rep_penalty(logits, rp, hist)
+    if temp == 0.0:
+        return False
+    if temp != 1.0:
+        lg = lg / np.float32(temp)
+    lg -= lg.max()
+    p = OS.exp_f32(lg)
+    p /= OS.pairwise_sum_f32(p)
+    if top_p < 1.0:
+        order = np.lexsort((np.arange(p.size), -p))
+        cut = int(np.searchsorted(np.cumsum(p[order]), top_p)) + 1
+        q = p[order][:cut]
+        q = q / OS.pairwise_sum_f32(q)
+    else:
+        q = p
+    cdf = np.cumsum(q.astype(np.float64))
+    cdf /= cdf[-1]
+    return bool(np.min(np.abs(cdf - u)) < tol)
+
+
+def test_sampler_matches_reference_fixture(engine306):
+    """The 48 recorded cases of the reference's own sample_token (seeded
+    np.random, host-independent exp): the device returns the same tokens."""
+    g = golden("sampling.npz")
+    cols = list(g["columns"])
+    rng = np.random.default_rng(int(g["logits_seed"]))
+    smp = Sampler(engine306, 1, 64)
+    for row in g["cases"]:
+        r = dict(zip(cols, row))
+        case = int(r["case"])
+        logits = (rng.standard_normal(32000) * 0.64 * (1 + case % 3)).astype(np.float32)
+        hist = rng.integers(0, 32000, case % 40).astype(np.int32)
+        tok = _device_sample(smp, logits, r["temp"], r["top_p"], r["rp"], hist, r["u"])
+        assert tok == int(r["ref_tok"]), f"case {case}"
+
+
+@pytest.mark.parametrize("temp,top_p,rp,scale", [(0.7, 0.95, 1.2, 0.64), (1.0, 0.95, 1.0, 2.0),
+                                                 (0.7, 1.0, 1.2, 0.64), (0.3, 0.5, 1.5, 1.5),
+                                                 (0.0, 1.0, 1.2, 1.0), (1.5, 0.99, 1.1, 4.0)])
+def test_sampler_bit_exact_vs_oracle(engine306, temp, top_p, rp, scale):
+    """Same logits and uniform -> the same token as the CPU restatement
+    (except u within 1e-9 of a CDF boundary, counted and bounded)."""
+    rng = np.random.default_rng(int(1000 * temp + 10 * top_p + scale))
+    smp = Sampler(engine306, 1, 256)
+    boundary = 0
+    for case in range(60):
+        logits = (rng.standard_normal(32000) * scale).astype(np.float32)
+        if case % 5 == 0:  # exact ties in the logits
+            logits[rng.integers(0, 32000, 500)] = logits[7]
+        hist = rng.integers(0, 32000, int(rng.integers(0, 200))).astype(np.int32)
+        u = float(rng.random())
+        want = OS.sample_token(logits, temp, top_p, rp, list(hist), u)
+        got = _device_sample(smp, logits, temp, top_p, rp, hist, u)
+        if got != want:
+            assert _boundary(logits, temp, top_p, rp, list(hist), u), (case, got, want)
+            boundary += 1
+    assert boundary <= 1
+
+
+def test_sampler_batched_rows_independent(engine306):
+    """Rows of a batch are sampled independently (one CTA per sequence)."""
+    rng = np.random.default_rng(9)
+    B = 8
+    smp = Sampler(engine306, B, 128)
+    dev = engine306.device
+    logits = (rng.standard_normal((B, 32000)) * 0.64).astype(np.float32)
+    hists = [rng.integers(0, 32000, 10 + 3 * b).astype(np.int32) for b in range(B)]
+    us = rng.random(B)
+    for b in range(B):
+        smp.history[b, :len(hists[b])].copy_(torch.as_tensor(hists[b]))
+        smp.hist_len[b] = len(hists[b])
+    smp.uniforms.copy_(torch.as_tensor(us))
+    got = smp.sample(torch.from_numpy(logits).to(dev), 0.7, 0.95, 1.2, B).cpu().numpy()
+    want = [OS.sample_token(logits[b], 0.7, 0.95, 1.2, list(hists[b]), us[b]) for b in range(B)]
+    assert list(got) == want
+
+
+def test_cfg4_sampled_streams_teacher_forced(engine306, params306_f32):
+    """Config 4 (B=8, T=0.7, top-p 0.95, rp 1.2, uniforms [128,8] from seed 4),
+    teacher-forced on the oracle's sampled streams:
+
+    * every step, the device sampler on the device logits returns exactly the
+      token the CPU restatement returns on those same logits;
+    * for sequence 0 the device logits stay within the parity tolerance of the
+      float32 oracle at every step.
+
+    Agreement with the float32 oracle's own stream is reported, not required:
+    with random weights the sampling distribution is nearly flat (max p about
+    1e-3 over ~25k kept tokens), so bf16-level logit differences move the CDF
+    enough to change most draws."""
+    from conftest import assert_logits_close
+    from oracle.ref_forward import CachedDecoder
+    from transformer_b200.config import CONFIG_306M
+    g = golden("cfg4_sampled.npz")
+    prompts, u, toks = g["prompts"], g["uniforms"], g["tokens"]
+    eng = engine306
+    smp = Sampler(eng, 1, 256)
+    dev = eng.device
+    steps = 48  # of 128: keeps the test short; every step is checked
+    same_as_stream = 0
+    for b in range(prompts.shape[0]):
+        kv = eng.new_kv()
+        lg = eng.prefill(prompts[b], kv).clone()
+        dec = None
+        if b == 0:
+            dec = CachedDecoder(params306_f32, CONFIG_306M, 1)
+            for p_, t_ in enumerate(prompts[b]):
+                ref = dec.step([t_], [p_])[0]
+        hist = []
+        for i in range(steps):
+            lg_np = lg.cpu().numpy()
+            if dec is not None:
+                assert_logits_close(lg_np, ref, f"cfg4 seq 0 step {i}")
+            got = _device_sample(smp, lg_np, 0.7, 0.95, 1.2, hist, u[i, b])
+            want = OS.sample_token(lg_np, 0.7, 0.95, 1.2, hist, u[i, b])
+            assert got == want or _boundary(lg_np, 0.7, 0.95, 1.2, hist, u[i, b]), (b, i)
+            same_as_stream += int(got == toks[b, i])
+            hist.append(int(toks[b, i]))
+            t = torch.tensor([int(toks[b, i])], dtype=torch.int32, device=dev)
+            p = torch.tensor([prompts.shape[1] + i], dtype=torch.int32, device=dev)
+            eng.step(t, p, kv, eng.logits, eng.next_tok)
+            lg = eng.logits[0].clone()
+            if dec is not None:
+                ref = dec.step([int(toks[b, i])], [prompts.shape[1] + i])[0]
+    total = steps * prompts.shape[0]
+    print(f"cfg4: device draw equals the float32 oracle's stream at {same_as_stream}/{total} steps")

@@ -356,7 +356,7 @@ b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, con
 }
 
 b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab, const int32_t* history_dev,
-                      int hist_cap, const int32_t* hist_len_dev, const float* uniforms_dev,
+                      int hist_cap, const int32_t* hist_len_dev, const double* uniforms_dev,
                       const b2d_sampling* params, int32_t* out_tok_dev, void* stream) {
   if (!ws || !logits_dev || batch < 1 || vocab < 1 || vocab > b2d::kSamplerMaxVocab || !params ||
       !out_tok_dev || hist_cap < 0 || (hist_cap > 0 && (!history_dev || !hist_len_dev)) ||

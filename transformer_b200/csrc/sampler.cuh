@@ -1,14 +1,346 @@
-// sampler.cuh — device sampler (generate.py:28-65 semantics).  Placeholder:
-// the launcher reports "not supported" until the kernel lands.
+// sampler.cuh — device sampler, one CTA per sequence (sm_100a).
+//
+// Replaces the reference's host numpy sampler, generate.py:28-65 sample_token:
+// repetition penalty over the set of generated tokens, temperature, softmax,
+// top-p (nucleus) filtering, and numpy's legacy RandomState.choice, which
+// draws one uniform u and returns keep[searchsorted(cumsum(p64)/last, u,
+// 'right')].  The caller supplies u (float64), so a token is a function of
+// (logits, u) alone.  The arithmetic follows the reference's order so the token
+// equals the CPU restatement's:
+//   * penalty / temperature: float32 IEEE division or product by the
+//     float32-rounded parameter (numpy's weak Python-float scalars);
+//   * exp: the float64 exponential rounded to float32 (host independent; the
+//     reference's own np.exp is host dependent, up to 2 ulp on AVX-512);
+//   * normalisers: numpy's pairwise float32 summation (blocks of <= 128 with 8
+//     accumulators, halving at multiples of 8), evaluated as a tree;
+//   * top-p: order by descending probability, ties by ascending token id; the
+//     cutoff from a sequential float32 cumsum compared in float64 (numpy's
+//     searchsorted promotes the Python float);
+//   * choice: float64 prefix sums, divided by the total, first value > u.  The
+//     prefix sums are computed in parallel, so their last bits can differ from
+//     numpy's sequential cumsum; a token differs only if u falls within about
+//     1e-12 of a CDF boundary.
+// Everything for one sequence lives in shared memory (vocabularies up to
+// kSamplerMaxVocab); nothing is allocated.
 #pragma once
+
 #include <cuda_runtime.h>
+
 #include <cstdint>
 
 namespace b2d {
-constexpr int kSamplerMaxVocab = 65536;
 
-inline cudaError_t launch_sampler(const float*, int, int, const int32_t*, int, const int32_t*, const float*,
-                                  double, double, double, int32_t*, cudaStream_t) {
-  return cudaErrorNotSupported;
+constexpr int kSamplerMaxVocab = 32768;
+constexpr int kSamplerThreads = 1024;
+constexpr int kTreeNodes = 1024;  // heap-indexed pairwise-sum tree (depth <= 9)
+
+struct SampleArgs {
+  const float* logits;     // [batch][vocab]
+  const int32_t* history;  // [batch][hist_cap] or null
+  const int32_t* hist_len; // [batch] or null
+  const double* uniforms;  // [batch] or null (temperature == 0)
+  int32_t* out;            // [batch]
+  int vocab, hist_cap;
+  float temperature, rep_penalty;
+  double top_p;
+};
+
+struct SamplerSmem {
+  uint32_t key[kSamplerMaxVocab];   // float bits of p, then ~bits for the sort
+  uint16_t idx[kSamplerMaxVocab];   // token id travelling with the key
+  uint32_t seen[kSamplerMaxVocab / 32];
+  int node_start[kTreeNodes];
+  int node_len[kTreeNodes];
+  float node_val[kTreeNodes];
+  double red_d[kSamplerThreads / 32];
+  float red_f[kSamplerThreads / 32];
+  int red_i[kSamplerThreads / 32];
+  int cutoff;
+  int token;
+};
+
+__device__ __forceinline__ float key_to_p(uint32_t k) { return __uint_as_float(~k); }
+
+// numpy's pairwise float32 sum of get(0..n-1), evaluated level by level over
+// a heap-indexed tree of its recursion; returns 0 + sum like np.sum.  All
+// threads of the block must call it.
+template <class Get>
+__device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
+  const int t = threadIdx.x;
+  if (t == 0) {
+    for (int i = 0; i < kTreeNodes; ++i) sm.node_len[i] = -1;
+    sm.node_start[1] = 0;
+    sm.node_len[1] = n;
+  }
+  __syncthreads();
+  // top-down: split every node longer than 128 (n2 = n/2 rounded down to 8)
+  for (int d = 0; d < 9; ++d) {
+    const int first = 1 << d, count = 1 << d;
+    for (int i = t; i < count; i += blockDim.x) {
+      const int nd = first + i;
+      const int len = sm.node_len[nd];
+      if (len > 128 && 2 * nd + 1 < kTreeNodes) {
+        int n2 = len / 2;
+        n2 -= n2 % 8;
+        sm.node_start[2 * nd] = sm.node_start[nd];
+        sm.node_len[2 * nd] = n2;
+        sm.node_start[2 * nd + 1] = sm.node_start[nd] + n2;
+        sm.node_len[2 * nd + 1] = len - n2;
+      }
+    }
+    __syncthreads();
+  }
+  // leaves (len <= 128): numpy's 8-accumulator block sum
+  for (int nd = 1 + t; nd < kTreeNodes; nd += blockDim.x) {
+    const int len = sm.node_len[nd];
+    if (len < 0 || len > 128) continue;
+    const int s0 = sm.node_start[nd];
+    float res;
+    if (len < 8) {
+      res = 0.f;
+      for (int i = 0; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+    } else {
+      float r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = get(s0 + j);
+      int i = 8;
+      for (; i < len - (len % 8); i += 8) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], get(s0 + i + j));
+      }
+      res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                      __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+      for (; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+    }
+    sm.node_val[nd] = res;
+  }
+  __syncthreads();
+  // bottom-up: internal node = left + right
+  for (int d = 8; d >= 0; --d) {
+    const int first = 1 << d, count = 1 << d;
+    for (int i = t; i < count; i += blockDim.x) {
+      const int nd = first + i;
+      if (sm.node_len[nd] > 128 && 2 * nd + 1 < kTreeNodes)
+        sm.node_val[nd] = __fadd_rn(sm.node_val[2 * nd], sm.node_val[2 * nd + 1]);
+    }
+    __syncthreads();
+  }
+  const float total = __fadd_rn(0.f, sm.node_val[1]);
+  __syncthreads();
+  return total;
 }
+
+// Block-wide float64 prefix sums of get(0..n-1) (thread-contiguous chunks);
+// returns the first k with prefix_k / total > u (numpy's searchsorted 'right'
+// after cdf /= cdf[-1]).
+template <class Get>
+__device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int per = (n + kSamplerThreads - 1) / kSamplerThreads;
+  const int i0 = min(t * per, n), i1 = min(i0 + per, n);
+  double local = 0.0;
+  for (int i = i0; i < i1; ++i) local += static_cast<double>(get(i));
+  // exclusive scan of the thread sums
+  double incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sm.red_d[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    double w = sm.red_d[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += v;
+    }
+    sm.red_d[lane] = w;  // inclusive warp-total prefix
+  }
+  __syncthreads();
+  const double total = sm.red_d[31];
+  double run = (warp > 0 ? sm.red_d[warp - 1] : 0.0) + (incl - local);
+  int found = 0x7fffffff;
+  for (int i = i0; i < i1; ++i) {
+    run += static_cast<double>(get(i));
+    if (run / total > u) { found = i; break; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) found = min(found, __shfl_xor_sync(0xffffffffu, found, o));
+  __syncthreads();
+  if (lane == 0) sm.red_i[warp] = found;
+  __syncthreads();
+  int k = 0x7fffffff;
+  for (int w = 0; w < kSamplerThreads / 32; ++w) k = min(k, sm.red_i[w]);
+  __syncthreads();
+  return k == 0x7fffffff ? n - 1 : k;
+}
+
+__global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const SampleArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(smem_raw);
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int V = a.vocab;
+  const float* lg = a.logits + static_cast<size_t>(b) * V;
+  constexpr int PER = kSamplerMaxVocab / kSamplerThreads;
+
+  // ---- repetition penalty over the set of generated tokens (ref :32-39) ----
+  const int hl = (a.history && a.hist_len) ? min(max(a.hist_len[b], 0), a.hist_cap) : 0;
+  const bool penalize = a.rep_penalty != 1.0f && hl > 0;
+  if (penalize) {
+    for (int i = t; i < kSamplerMaxVocab / 32; i += kSamplerThreads) sm.seen[i] = 0u;
+    __syncthreads();
+    for (int i = t; i < hl; i += kSamplerThreads) {
+      const int tok = a.history[static_cast<size_t>(b) * a.hist_cap + i];
+      if (tok >= 0 && tok < V) atomicOr(&sm.seen[tok >> 5], 1u << (tok & 31));
+    }
+    __syncthreads();
+  }
+  float v[PER];
+#pragma unroll
+  for (int r = 0; r < PER; ++r) {
+    const int i = t + r * kSamplerThreads;
+    float x = -INFINITY;
+    if (i < V) {
+      x = lg[i];
+      if (penalize && (sm.seen[i >> 5] >> (i & 31)) & 1u)
+        x = x > 0.f ? __fdiv_rn(x, a.rep_penalty) : __fmul_rn(x, a.rep_penalty);
+    }
+    v[r] = x;
+  }
+
+  // ---- greedy: first index of the maximum (ref :41-42, np.argmax) ----
+  if (a.temperature == 0.0f) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int r = 0; r < PER; ++r) {
+      const int i = t + r * kSamplerThreads;
+      if (i < V && (v[r] > bv || (v[r] == bv && i < bi))) { bv = v[r]; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { sm.red_f[warp] = bv; sm.red_i[warp] = bi; }
+    __syncthreads();
+    if (t == 0) {
+      float gv = sm.red_f[0];
+      int gi = sm.red_i[0];
+      for (int w = 1; w < kSamplerThreads / 32; ++w)
+        if (sm.red_f[w] > gv || (sm.red_f[w] == gv && sm.red_i[w] < gi)) { gv = sm.red_f[w]; gi = sm.red_i[w]; }
+      a.out[b] = gi == 0x7fffffff ? 0 : gi;
+    }
+    return;
+  }
+
+  // ---- temperature, max shift, exp (ref :44-50) ----
+  float mx = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < PER; ++r) {
+    if (a.temperature != 1.0f && t + r * kSamplerThreads < V) v[r] = __fdiv_rn(v[r], a.temperature);
+    mx = fmaxf(mx, v[r]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) sm.red_f[warp] = mx;
+  __syncthreads();
+  mx = sm.red_f[0];
+  for (int w = 1; w < kSamplerThreads / 32; ++w) mx = fmaxf(mx, sm.red_f[w]);
+#pragma unroll
+  for (int r = 0; r < PER; ++r) {
+    const int i = t + r * kSamplerThreads;
+    if (i < V) {
+      const float sh = __fsub_rn(v[r], mx);
+      sm.key[i] = __float_as_uint(__double2float_rn(exp(static_cast<double>(sh))));
+    }
+  }
+  __syncthreads();
+  // ---- normalise: p /= p.sum() (ref :51) ----
+  const float S = pairwise_sum(sm, V, [&](int i) { return __uint_as_float(sm.key[i]); });
+  const bool top = a.top_p < 1.0;
+  for (int i = t; i < kSamplerMaxVocab; i += kSamplerThreads) {
+    if (i < V) {
+      const float p = __fdiv_rn(__uint_as_float(sm.key[i]), S);
+      sm.key[i] = top ? ~__float_as_uint(p) : __float_as_uint(p);
+    } else {
+      sm.key[i] = 0xffffffffu;  // sorts after every real key
+    }
+    sm.idx[i] = static_cast<uint16_t>(i < V ? i : 0xffff);
+  }
+  __syncthreads();
+
+  if (!top) {  // choice over all tokens in id order (ref :65)
+    const int k = cdf_search(sm, V, a.uniforms[b], [&](int i) { return __uint_as_float(sm.key[i]); });
+    if (t == 0) a.out[b] = k;
+    return;
+  }
+
+  // ---- top-p (ref :53-63): sort by (descending p, ascending id) ----
+  for (int kk = 2; kk <= kSamplerMaxVocab; kk <<= 1) {
+    for (int j = kk >> 1; j > 0; j >>= 1) {
+      for (int i = t; i < kSamplerMaxVocab / 2; i += kSamplerThreads) {
+        const int lo = 2 * j * (i / j) + (i % j), hi = lo + j;
+        const bool asc = (lo & kk) == 0;
+        const uint32_t klo = sm.key[lo], khi = sm.key[hi];
+        const uint16_t ilo = sm.idx[lo], ihi = sm.idx[hi];
+        const bool gt = klo > khi || (klo == khi && ilo > ihi);
+        if (gt == asc) {
+          sm.key[lo] = khi; sm.key[hi] = klo;
+          sm.idx[lo] = ihi; sm.idx[hi] = ilo;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one
+  if (t == 0) {
+    float c = 0.f;
+    int cut = V;
+    for (int i = 0; i < V; ++i) {
+      c = __fadd_rn(c, key_to_p(sm.key[i]));
+      if (static_cast<double>(c) >= a.top_p) { cut = i + 1; break; }
+    }
+    sm.cutoff = cut;
+  }
+  __syncthreads();
+  const int cut = sm.cutoff;
+  const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
+  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
+  if (t == 0) a.out[b] = sm.idx[k];
+}
+
+inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, const int32_t* history,
+                                  int hist_cap, const int32_t* hist_len, const double* uniforms,
+                                  double temperature, double top_p, double rep_penalty, int32_t* out,
+                                  cudaStream_t st) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(SamplerSmem)));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  SampleArgs a;
+  a.logits = logits;
+  a.history = history;
+  a.hist_len = hist_len;
+  a.uniforms = uniforms;
+  a.out = out;
+  a.vocab = vocab;
+  a.hist_cap = hist_cap;
+  a.temperature = static_cast<float>(temperature);
+  a.rep_penalty = static_cast<float>(rep_penalty);
+  a.top_p = top_p;
+  sample_kernel<<<batch, kSamplerThreads, sizeof(SamplerSmem), st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace b2d
