@@ -203,6 +203,16 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
 B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);
 
+/*
+ * Test hook (no reference counterpart): one tensor-core projection
+ * Y[n][m] = sum_k X[n][k] W[m][k] (bf16 inputs, f32 accumulation) with the
+ * batched path's epilogue `epi`: 0 = store f32 to y, 1 = y = resid + result,
+ * 2 = SwiGLU of row pairs (2j gate, 2j+1 up) stored as bf16 column j of ybf.
+ * M % 128 == 0, K % 64 == 0.  Synchronises `stream`.
+ */
+B2D_API b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int N, int epi,
+                                 float* y_dev, const float* resid_dev, void* ybf_dev, int ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -82,6 +82,8 @@ _SIGS = {
     "b2d_debug_set": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int]),
     "b2d_debug_trace": (ctypes.c_int, [_P, _P, ctypes.c_int]),
     "b2d_debug_tune": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
+    "b2d_test_gemm": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P,
+                                     ctypes.c_int, _P]),
 }
 
 _lib = None

@@ -12,6 +12,7 @@
 
 #include "../../include/b2d.h"
 #include "decode_b1.cuh"
+#include "gemm_tc.cuh"
 #include "sampler.cuh"
 
 namespace {
@@ -369,6 +370,31 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
                                params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st),
            "sampler launch");
   return B2D_OK;
+}
+
+// Test hook: Y = X . W^T on the tensor-core GEMM with the chosen epilogue.
+b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int N, int epi, float* y_dev,
+                         const float* resid_dev, void* ybf_dev, int ldy, void* stream) {
+  if (!w_dev || !x_dev || M <= 0 || K <= 0 || N <= 0 || M % b2d::kGemmBM || K % b2d::kGemmBK || epi < 0 ||
+      epi > 2 || ldy <= 0 || (epi != b2d::EPI_SWIGLU_BF16 && !y_dev) || (epi == b2d::EPI_RESID_F32 && !resid_dev) ||
+      (epi == b2d::EPI_SWIGLU_BF16 && !ybf_dev))
+    return B2D_ERR_INVALID_ARG;
+  static uint32_t* err = nullptr;
+  if (!err) B2D_CUDA(cudaMalloc(&err, sizeof(uint32_t)), "err word");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  B2D_CUDA(cudaMemsetAsync(err, 0, sizeof(uint32_t), st), "clear err");
+  CUtensorMap wm, xm;
+  if (!b2d::make_kmajor_map(&wm, w_dev, K, M, b2d::kGemmBM) ||
+      !b2d::make_kmajor_map(&xm, x_dev, K, N, b2d::gemm_bn_for(N)))
+    return B2D_ERR_INVALID_ARG;
+  b2d::GemmArgs g;
+  g.M = M; g.N = N; g.K = K;
+  g.y = y_dev; g.resid = resid_dev; g.ybf = static_cast<__nv_bfloat16*>(ybf_dev); g.ldy = ldy; g.err = err;
+  B2D_CUDA(b2d::launch_gemm(wm, xm, g, epi, st), "gemm launch");
+  uint32_t h = 0;
+  B2D_CUDA(cudaMemcpyAsync(&h, err, sizeof(h), cudaMemcpyDeviceToHost, st), "read err");
+  B2D_CUDA(cudaStreamSynchronize(st), "sync");
+  return h ? B2D_ERR_DEVICE_TIMEOUT : B2D_OK;
 }
 
 }  // extern "C"
