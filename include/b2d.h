@@ -148,6 +148,26 @@ B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_
                            float* logits_dev, int32_t* next_tok_dev, void* stream);
 
 /*
+ * Batched decode step over a paged KV pool (no
+ * reference counterpart: the reference's batched kernels were deleted).
+ *   tok_dev / pos_dev int32[batch]; pos < 0 marks a sequence inactive for this
+ *                     step (no cache write; its outputs are not meaningful)
+ *   kv_pool_dev       bf16 [n_layers][num_blocks][K|V][kv_heads][16][d_head]
+ *   block_table_dev   int32[batch][blocks_per_seq]: physical block of
+ *                     positions 16i..16i+15 of each sequence
+ *   logits_dev        f32[batch][vocab] or NULL (workspace buffer used)
+ *   next_tok_dev      int32[batch] argmax
+ * Needs a workspace created with max_batch >= 2.  Projections run on the
+ * tensor cores (tcgen05); out-of-range tokens / table entries set the status
+ * word read by b2d_last_error.
+ */
+B2D_API b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev,
+                                         const int32_t* pos_dev, int batch, void* kv_pool_dev,
+                                         const int32_t* block_table_dev, int blocks_per_seq,
+                                         int num_blocks, float* logits_dev, int32_t* next_tok_dev,
+                                         void* stream);
+
+/*
  * Device sampler, one sequence per CTA (generate.py:28-65 semantics).
  *   logits_dev   f32[batch][vocab]     (read only)
  *   history_dev  int32[batch][hist_cap] tokens generated so far (prompt excluded)

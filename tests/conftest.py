@@ -96,3 +96,20 @@ def assert_logits_close(got, ref, what=""):
     assert not bad.any(), (f"{what}: {bad.sum()} logits outside atol={ATOL} rtol={RTOL}; "
                            f"max abs err {err.max():.4g}")
     return float(err.max())
+
+
+@pytest.fixture(scope="session")
+def engine306_batched(engine306):
+    """The 306M weights bound a second time with a batched workspace."""
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    eng = DecodeEngine(engine306.w, max_batch=256)
+    yield eng
+    eng.close()
+
+
+@pytest.fixture(scope="session")
+def engine_tiny_batched(engine_tiny):
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    eng = DecodeEngine(engine_tiny.w, max_batch=64)
+    yield eng
+    eng.close()

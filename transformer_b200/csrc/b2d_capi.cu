@@ -11,6 +11,7 @@
 #include <new>
 
 #include "../../include/b2d.h"
+#include "batched.cuh"
 #include "decode_b1.cuh"
 #include "gemm_tc.cuh"
 #include "sampler.cuh"
@@ -92,6 +93,9 @@ struct b2d_model {
   b2d_weights_layout_t lay;
   const ShapeOps* ops;
   int grid;
+  // batched path: TMA descriptors of every projection (created on first use)
+  bool maps_ready;
+  CUtensorMap* wmaps;  // [4 * n_layers + 1]: per layer qkv, o, gu, down; then the embedding
 };
 
 struct b2d_ws {
@@ -110,6 +114,11 @@ struct b2d_ws {
   int trace_stride;
   uint32_t poll_ns;
   int max_inflight;
+  // batched path (max_batch > 1)
+  int rows;                        // activation rows allocated (max_batch rounded up to 64)
+  float *H, *Hm, *qkv, *logits;
+  __nv_bfloat16 *X, *A, *ACT;
+  CUtensorMap xmap[3], amap[3], actmap[3];  // box rows 16 / 32 / 64
 };
 
 extern "C" {
@@ -184,11 +193,14 @@ b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint
   m->lay = lay;
   m->ops = ops;
   m->grid = sms;
+  m->maps_ready = false;
+  m->wmaps = nullptr;
   *out = m;
   return B2D_OK;
 }
 
 b2d_status b2d_model_destroy(b2d_model* m) {
+  if (m) delete[] m->wmaps;
   delete m;
   return B2D_OK;
 }
@@ -221,6 +233,27 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ws->ctl, sizeof(b2d::Control));
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_val, sizeof(float) * m->grid);
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
+  if (e == cudaSuccess && max_batch > 1) {
+    const size_t D = c.d_model, F = c.d_ff, Q = qkv, V = c.vocab_size;
+    ws->rows = (max_batch + 63) / 64 * 64;
+    e = cudaMalloc(&ws->H, sizeof(float) * D * max_batch);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * max_batch);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->qkv, sizeof(float) * Q * max_batch);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->logits, sizeof(float) * V * max_batch);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->X, 2 * D * ws->rows);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->A, 2 * D * ws->rows);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->ACT, 2 * F * ws->rows);
+    if (e == cudaSuccess) e = cudaMemset(ws->X, 0, 2 * D * ws->rows);
+    if (e == cudaSuccess) e = cudaMemset(ws->A, 0, 2 * D * ws->rows);
+    if (e == cudaSuccess) e = cudaMemset(ws->ACT, 0, 2 * F * ws->rows);
+    for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+      const uint32_t box = 16u << i;
+      if (!b2d::make_kmajor_map(&ws->xmap[i], ws->X, D, ws->rows, box) ||
+          !b2d::make_kmajor_map(&ws->amap[i], ws->A, D, ws->rows, box) ||
+          !b2d::make_kmajor_map(&ws->actmap[i], ws->ACT, F, ws->rows, box))
+        e = cudaErrorInvalidValue;
+    }
+  }
   if (e == cudaSuccess) e = cudaMemset(ws->words, 0, ws->n_words * sizeof(uint64_t));
   if (e == cudaSuccess) e = cudaMemset(ws->ctl, 0, sizeof(b2d::Control));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -235,6 +268,13 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
 b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   if (!ws) return B2D_OK;
   if (ws->m) cudaSetDevice(ws->m->device);
+  cudaFree(ws->H);
+  cudaFree(ws->Hm);
+  cudaFree(ws->qkv);
+  cudaFree(ws->logits);
+  cudaFree(ws->X);
+  cudaFree(ws->A);
+  cudaFree(ws->ACT);
   cudaFree(ws->words);
   cudaFree(ws->ctl);
   cudaFree(ws->am_val);
@@ -369,6 +409,94 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
   B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
                                params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st),
            "sampler launch");
+  return B2D_OK;
+}
+
+namespace {
+
+b2d_status ensure_weight_maps(b2d_model* m) {
+  if (m->maps_ready) return B2D_OK;
+  const b2d_config& c = m->cfg;
+  const uint64_t D = c.d_model, F = c.d_ff, Q = uint64_t(c.n_heads + 2 * c.n_kv_heads) * 64;
+  if (Q % b2d::kGemmBM || D % b2d::kGemmBM || (2 * F) % b2d::kGemmBM || c.vocab_size % b2d::kGemmBM ||
+      D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4)
+    return B2D_ERR_UNSUPPORTED;
+  CUtensorMap* maps = new (std::nothrow) CUtensorMap[4 * c.n_layers + 1];
+  if (!maps) return B2D_ERR_NO_MEMORY;
+  bool ok = true;
+  for (int l = 0; l < c.n_layers && ok; ++l) {
+    const uint8_t* base = m->w + uint64_t(l) * m->lay.layer_stride;
+    ok = b2d::make_kmajor_map(&maps[4 * l + 0], base + m->lay.off_qkv, D, Q, b2d::kGemmBM) &&
+         b2d::make_kmajor_map(&maps[4 * l + 1], base + m->lay.off_o, D, D, b2d::kGemmBM) &&
+         b2d::make_kmajor_map(&maps[4 * l + 2], base + m->lay.off_gu, D, 2 * F, b2d::kGemmBM) &&
+         b2d::make_kmajor_map(&maps[4 * l + 3], base + m->lay.off_down, F, D, b2d::kGemmBM);
+  }
+  ok = ok && b2d::make_kmajor_map(&maps[4 * c.n_layers], m->w + m->lay.off_emb, D, c.vocab_size, b2d::kGemmBM);
+  if (!ok) {
+    delete[] maps;
+    return B2D_ERR_CUDA;
+  }
+  m->wmaps = maps;
+  m->maps_ready = true;
+  return B2D_OK;
+}
+
+}  // namespace
+
+b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                                 int batch, void* kv_pool_dev, const int32_t* block_table_dev,
+                                 int blocks_per_seq, int num_blocks, float* logits_dev, int32_t* next_tok_dev,
+                                 void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_pool_dev || !block_table_dev || !next_tok_dev ||
+      batch < 1 || batch > ws->max_batch || ws->max_batch < 2 || blocks_per_seq < 1 || num_blocks < 1)
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  b2d_status s = ensure_weight_maps(m);
+  if (s != B2D_OK) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const b2d_config& c = m->cfg;
+  const int D = c.d_model, F = c.d_ff, Q = (c.n_heads + 2 * c.n_kv_heads) * 64, V = c.vocab_size;
+  const int bn = b2d::gemm_bn_for(batch), mi = bn == 16 ? 0 : (bn == 32 ? 1 : 2);
+  uint32_t* status = &ws->ctl->status;
+  float* logits = logits_dev ? logits_dev : ws->logits;
+  const float* ln1 = reinterpret_cast<const float*>(m->w + m->lay.off_ln1);
+  const float* ln2 = reinterpret_cast<const float*>(m->w + m->lay.off_ln2);
+  const float* lnf = reinterpret_cast<const float*>(m->w + m->lay.off_lnf);
+  const __nv_bfloat16* emb = reinterpret_cast<const __nv_bfloat16*>(m->w + m->lay.off_emb);
+
+  b2d::embed_rows_kernel<<<batch, 256, 0, st>>>(emb, tok_dev, V, D, ws->H, status);
+  B2D_CUDA(cudaGetLastError(), "embed");
+  b2d::GemmArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.N = batch;
+  g.err = status;
+  b2d::PagedAttnArgs pa;
+  pa.qkv = ws->qkv; pa.pos = pos_dev; pa.pool = static_cast<__nv_bfloat16*>(kv_pool_dev);
+  pa.table = block_table_dev; pa.bps = blocks_per_seq; pa.num_blocks = num_blocks;
+  pa.n_heads = c.n_heads; pa.n_kv = c.n_kv_heads; pa.ctx = c.context_len;
+  pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
+  pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
+  pa.out = ws->A; pa.ldo = D; pa.status = status;
+  for (int l = 0; l < c.n_layers; ++l) {
+    b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->H, ln1 + size_t(l) * D, D, c.rms_eps, ws->X, D);
+    g.M = Q; g.K = D; g.y = ws->qkv; g.ldy = Q;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 0], ws->xmap[mi], g, b2d::EPI_F32, st), "qkv");
+    pa.layer = l;
+    b2d::paged_attn_kernel<<<dim3(batch, c.n_kv_heads), 32 * (c.n_heads / c.n_kv_heads), 0, st>>>(pa);
+    B2D_CUDA(cudaGetLastError(), "attention");
+    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 1], ws->amap[mi], g, b2d::EPI_RESID_F32, st), "o");
+    b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->Hm, ln2 + size_t(l) * D, D, c.rms_eps, ws->X, D);
+    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 2], ws->xmap[mi], g, b2d::EPI_SWIGLU_BF16, st), "gate/up");
+    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 3], ws->actmap[mi], g, b2d::EPI_RESID_F32, st), "down");
+  }
+  b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->H, lnf, D, c.rms_eps, ws->X, D);
+  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V;
+  B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * c.n_layers], ws->xmap[mi], g, b2d::EPI_F32, st), "logits");
+  b2d::argmax_rows_kernel<<<batch, 1024, 0, st>>>(logits, V, V, next_tok_dev);
+  B2D_CUDA(cudaGetLastError(), "argmax");
   return B2D_OK;
 }
 

@@ -34,7 +34,7 @@ struct GemmArgs {
   const float* resid;       // EPI_RESID_F32: [N][ldy] (may equal y)
   __nv_bfloat16* ybf;       // EPI_SWIGLU_BF16: [N][ldy] bf16, column m/2
   int ldy;
-  uint32_t* err;            // set to 1 if a wait ran out
+  uint32_t* err;            // status word: set (if still 0) when a wait runs out
 };
 
 template <int BN>
@@ -55,7 +55,7 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
   uint32_t n = 0;
   while (!mbar_test(bar, parity)) {
     if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kGemmWaitNs) {
-      atomicExch(err, 1u);
+      atomicCAS(err, 0u, 0x10Bu);  // timeout | site 11 (projection)
       return false;
     }
   }

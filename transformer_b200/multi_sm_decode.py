@@ -24,6 +24,8 @@ from . import _lib
 from .config import ModelConfig
 from .packing import kv_elems, new_kv_cache
 
+PAGE_TOKENS = 16  # positions per KV block of the paged pool
+
 
 def _ptr(t: torch.Tensor | None):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
@@ -107,6 +109,45 @@ class DecodeEngine:
         st = self.lib.b2d_decode_step(self.model, self.ws, _ptr(tok), _ptr(pos), batch, _ptr(kv),
                                       _ptr(logits), _ptr(next_tok), _stream_ptr(stream))
         _lib.check(st, "b2d_decode_step")
+
+    def new_kv_pool(self, num_blocks: int) -> torch.Tensor:
+        """Zeroed paged KV pool: bf16 [n_layers, num_blocks, 2 (K|V), kv_heads,
+        16, d_head]; block i of a sequence holds its positions 16i..16i+15."""
+        c = self.cfg
+        return torch.zeros(c.n_layers, num_blocks, 2, c.n_kv_heads, PAGE_TOKENS, c.d_head,
+                           dtype=torch.bfloat16, device=self.device)
+
+    def step_paged(self, tok: torch.Tensor, pos: torch.Tensor, pool: torch.Tensor,
+                   block_table: torch.Tensor, logits: torch.Tensor | None = None,
+                   next_tok: torch.Tensor | None = None, stream=None, batch: int | None = None) -> None:
+        """One batched decode step over a paged KV pool (async, stream-ordered).
+
+        ``tok`` / ``pos``: int32 [batch] (``pos < 0``: sequence idle this step);
+        ``block_table``: int32 [batch, blocks_per_seq]; ``logits``: float32
+        [batch, vocab] or None; ``next_tok``: int32 [batch] (argmax)."""
+        if self.max_batch < 2:
+            raise ValueError("step_paged needs an engine created with max_batch >= 2")
+        batch = batch or tok.numel()
+        if next_tok is None:
+            next_tok = self.next_tok
+        for t, name in ((tok, "tok"), (pos, "pos"), (next_tok, "next_tok")):
+            if t.dtype != torch.int32 or t.device != self.device or t.numel() < batch or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous int32 tensor on {self.device} with >= {batch} items")
+        c = self.cfg
+        if (pool.dtype != torch.bfloat16 or pool.device != self.device or not pool.is_contiguous() or pool.dim() != 6
+                or tuple(pool.shape[i] for i in (0, 2, 3, 4, 5)) != (c.n_layers, 2, c.n_kv_heads, PAGE_TOKENS,
+                                                                     c.d_head)):
+            raise ValueError("pool must be a paged KV pool of this model (see new_kv_pool)")
+        if (block_table.dtype != torch.int32 or block_table.device != self.device or block_table.dim() != 2
+                or block_table.shape[0] < batch or not block_table.is_contiguous()):
+            raise ValueError("block_table must be a contiguous int32 [batch, blocks_per_seq] device tensor")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() < batch * c.vocab_size
+                                   or not logits.is_contiguous()):
+            raise ValueError("logits must be contiguous float32 [batch, vocab]")
+        st = self.lib.b2d_decode_step_paged(self.model, self.ws, _ptr(tok), _ptr(pos), batch, _ptr(pool),
+                                            _ptr(block_table), block_table.shape[1], pool.shape[1],
+                                            _ptr(logits), _ptr(next_tok), _stream_ptr(stream))
+        _lib.check(st, "b2d_decode_step_paged")
 
     def last_error(self, stream=None):
         """(status, raw device word); synchronises the stream."""
