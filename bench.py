@@ -2,22 +2,31 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload ("b1"): the 306M decoder (seeded synthetic bf16
-weights, N(0,0.02), seed 0), batch 1, the seeded 16-token prompt prefilled,
-then greedy decode.  A step = one decode step (one token).  Timed steps run at
-positions 16..143 (config 1's 128 greedy positions), wrapping around, with the
-device's own argmax fed back as the next token (no host round trip).  With N
-GPUs every rank decodes its own replica (weak scaling, no collective on the
-data path); `value` is the tokens all ranks produced / max-over-ranks time.
+Headline workload ("serve"): the 306M decoder (seeded
+synthetic bf16 weights N(0,0.02), seed 0), 2048 sequences with seeded 64-token
+prompts, partitioned evenly over the N ranks (one GPU each, a full weight
+replica per GPU, no collective on the data path).  Each rank keeps its
+2048/N sequences resident in a paged KV pool and decodes them in waves of at
+most 256 (the batched tensor-core step, one CUDA graph per wave).  A step =
+one greedy token for every sequence of the job; `value` = 2048 * K tokens /
+max-over-ranks device time of the K timed steps (total work fixed as N grows:
+"strong" scaling).  Positions run 64.. upward (config 5's 256 decode steps
+fit; a longer run wraps back to 64).
 
-`e2e` runs the same decode through the public call with host buffers: every
-step copies the token and position from pinned host memory, launches, and
-reads the next token back (as the reference's generate loop does with
-``int(tok_out)``, generate.py:115-116), all inside the timed region.
+At N=1, rank 0 also measures the B=1 latency path (configs 1 and 2: the
+single-launch decode megakernel, us/token and its HBM roofline), config 3
+(B=64 ragged prompts U[32,448], random block table, 64 greedy steps) and
+config 4 (B=8, temperature 0.7 / top-p 0.95 / repetition penalty 1.2 with the
+seeded uniforms); they appear as sub-objects of the line.
 
-`--impl reference` times the reference algorithm's CPU implementation on the
-host cores: the reference needs JAX, which this image lacks, so the oracle's
-numpy restatement of model.py (KV-cached, float32) stands in for it.
+`e2e` runs the serve step through the public call with host buffers: every
+step copies each wave's tokens and positions from pinned host memory, runs the
+step, and reads the next tokens back, all inside the timed region.
+
+`--impl reference` times the reference algorithm on the host cores: the
+reference needs JAX, which this image lacks, so the oracle's numpy
+restatement of model.py (KV-cached, float32) stands in for it, on a bounded
+sample of the same workload.
 """
 
 from __future__ import annotations
@@ -37,18 +46,21 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 FALLBACK_HBM_GBS = 6650.0
+TOTAL_SEQS = 2048
+PROMPT_LEN = 64
+WAVE = 256
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1024)
-    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["b1"], default="b1")
-    ap.add_argument("--cpu-sample-steps", type=int, default=48)
+    ap.add_argument("--cpu-sample-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=256)
+    ap.add_argument("--no-configs", action="store_true", help="skip the N=1 sub-measurements (configs 1-4)")
+    ap.add_argument("--e2e-steps", type=int, default=8)
     return ap.parse_args()
 
 
@@ -133,12 +145,50 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+_PARAMS = []
+
+
+def oracle_params():
+    if not _PARAMS:
+        from transformer_b200.config import CONFIG_306M
+        from transformer_b200.synth import params_f32, synth_params
+        _PARAMS.append(params_f32(synth_params(CONFIG_306M, 0)))
+    return _PARAMS[0]
+
+
+def cpu_baseline_serve(steps, batch=32):
+    """Oracle (numpy restatement of model.py, KV-cached float32) on the host
+    cores: `batch` sequences of the serve workload decoding at positions 64..
+    (their caches hold seeded values in place of an ingested prompt: the step's
+    work does not depend on them)."""
+    from oracle.ref_forward import CachedDecoder
+    from transformer_b200.config import CONFIG_306M as cfg
+    from transformer_b200.synth import batch_cfg5
+    P = oracle_params()
+    dec = CachedDecoder(P, cfg, batch)
+    rng = np.random.default_rng(0)
+    dec.K[:, :, :, :PROMPT_LEN] = rng.standard_normal(dec.K[:, :, :, :PROMPT_LEN].shape, dtype=np.float32)
+    dec.V[:, :, :, :PROMPT_LEN] = rng.standard_normal(dec.V[:, :, :, :PROMPT_LEN].shape, dtype=np.float32)
+    tok = batch_cfg5(cfg)[:batch, -1]
+    dec.step(tok, [PROMPT_LEN] * batch)  # warm-up
+    t0 = time.perf_counter()
+    for i in range(steps):
+        lg = dec.step(tok, [PROMPT_LEN + 1 + i] * batch)
+        tok = np.argmax(lg, axis=1)
+    dt = time.perf_counter() - t0
+    cores = os.cpu_count()
+    return {"value": steps * batch / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} greedy decode steps of {batch} serve-workload sequences at positions "
+                      f"{PROMPT_LEN + 1}..{PROMPT_LEN + steps}, numpy float32 KV-cached restatement of "
+                      f"model.py, BLAS threads={cores}"}
+
+
 def cpu_baseline_b1(steps):
-    """Oracle (numpy restatement of model.py, KV-cached float32) on host cores."""
+    """Oracle on the host cores, config 1 (B=1, 16-token prompt)."""
     from oracle.ref_forward import CachedDecoder
     from transformer_b200.config import CONFIG_306M
-    from transformer_b200.synth import params_f32, prompt_cfg1, synth_params
-    P = params_f32(synth_params(CONFIG_306M, 0))
+    from transformer_b200.synth import prompt_cfg1
+    P = oracle_params()
     prompt = prompt_cfg1()
     dec = CachedDecoder(P, CONFIG_306M, 1)
     lg = None
@@ -150,64 +200,211 @@ def cpu_baseline_b1(steps):
         lg = dec.step([tok], [len(prompt) + i])[0]
         tok = int(np.argmax(lg))
     dt = time.perf_counter() - t0
-    cores = os.cpu_count()
-    return {"value": steps / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} greedy decode steps of config 1 (positions 16..{15 + steps}), "
-                      f"numpy float32 KV-cached restatement of model.py, BLAS threads={cores}"}
+    return {"value": steps / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} greedy decode steps of config 1 (positions 16..{15 + steps})"}
+
+
+METRIC = "batched decode tok/s (config 5: 2048 seqs, 64-token prompts, greedy, replicas over N GPUs)"
+
+
+def serve_config(world):
+    return {"workload": f"serve (config 5): 306M decoder (d=1024, 16 heads, 4 kv heads, 24 layers, d_ff 2816, "
+                        f"vocab 32000, ctx 512); {TOTAL_SEQS} sequences, seeded {PROMPT_LEN}-token prompts, "
+                        f"{TOTAL_SEQS // world} per GPU decoded in waves of <= {WAVE} on a paged KV pool "
+                        f"(16-token blocks, random block tables), greedy",
+            "model": "306M", "global_batch": TOTAL_SEQS, "seq_len": 512, "parallelism": f"replicas{world}",
+            "l2": "inputs larger than L2: 607 MB of weights per wave-step plus the KV pages"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    cb = cpu_baseline_b1(max(4, min(args.steps, args.cpu_sample_steps)))
-    line = {"metric": "decode tok/s (B=1 greedy, 306M, config 1)", "value": cb["value"], "unit": "tok/s",
+    cb = cpu_baseline_serve(max(1, min(args.steps, args.cpu_sample_steps)))
+    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "b1: 306M, batch 1, 16-token seeded prompt, greedy decode positions 16..143",
-                       "global_batch": 1, "seq_len": 512, "parallelism": "cpu"},
+            "ms_per_step": 1000.0 * TOTAL_SEQS / cb["value"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": serve_config(1),
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference needs JAX (absent); its numpy restatement (oracle) is timed instead"}
+            "note": "reference needs JAX (absent); its numpy restatement (oracle) is timed instead, "
+                    "on a bounded sample of the workload"}
     print(json.dumps(line))
     return 0
+
+
+def events_ms(fn, stream, torch):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
+    """B=1 megakernel: prefill `prompt`, time n_steps greedy steps (device
+    argmax fed back), return us/token and the HBM roofline of the kernel."""
+    P0 = len(prompt)
+    kv = eng.new_kv()
+    eng.prefill(prompt, kv)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    tok.copy_(torch.argmax(eng.logits[0]).to(torch.int32).reshape(1))
+    span = cfg.context_len - P0
+    posarr = torch.tensor([P0 + (i % span) for i in range(n_steps + 3)], dtype=torch.int32, device=dev)
+    for i in range(3):
+        eng.step(tok, posarr[i:i + 1], kv, eng.logits, tok, stream)
+    torch.cuda.synchronize(dev)
+
+    def run():
+        for i in range(3, 3 + n_steps):
+            eng.step(tok, posarr[i:i + 1], kv, eng.logits, tok, stream)
+    ms = events_ms(run, stream, torch)
+    eng.check_device()
+    us = ms * 1000.0 / n_steps
+    positions = [P0 + (i % span) for i in range(3, 3 + n_steps)]
+    alg = float(np.mean([cfg.step_bytes([p]) for p in positions]))
+    peak, kind = measured_peaks()
+    ach = alg / (us * 1e-6) / 1e9
+    return {"workload": label, "us_per_token": us, "tok_s": 1e6 / us, "steps": n_steps,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
+                         "traffic": profile_traffic()},
+            "gpu_launches": n_steps}
+
+
+def measure_b1_e2e(eng, dev, stream, torch, prompt, n_steps):
+    """Config 1 through the public call with host buffers (pinned H2D of the
+    token and position, launch, D2H of the next token, sync per step)."""
+    P0 = len(prompt)
+    kv = eng.new_kv()
+    eng.prefill(prompt, kv)
+    tok = int(torch.argmax(eng.logits[0]).item())
+    h_in = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+    h_out = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+    d_in = torch.zeros(2, dtype=torch.int32, device=dev)
+    d_out = torch.zeros(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        h_in[0] = tok
+        h_in[1] = P0 + (i % 128)
+        d_in.copy_(h_in, non_blocking=True)
+        eng.step(d_in[0:1], d_in[1:2], kv, eng.logits, d_out, stream)
+        h_out.copy_(d_out, non_blocking=True)
+        stream.synchronize()
+        tok = int(h_out[0])
+    dt = time.perf_counter() - t0
+    return {"value": n_steps / dt, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+            "steps": n_steps}
+
+
+def measure_cfg3(eng, cfg, torch):
+    """Config 3: B=64, prompts U[32,448] (seed 2) ingested raggedly into the
+    paged pool (random block table), then 64 greedy steps (graph replay)."""
+    from transformer_b200.batched import BatchedDecoder
+    from transformer_b200.synth import batch_cfg3
+    lens, prompts, table = batch_cfg3(cfg)
+    dec = BatchedDecoder(eng, len(prompts), table=table, num_blocks=int(table.size))
+    dec.ingest(prompts)
+    dec.capture()
+    pos0 = dec.pos.cpu().numpy().copy()
+    n = 64
+    ms = events_ms(lambda: [dec.replay() for _ in range(n)], torch.cuda.current_stream(), torch)
+    eng.check_device()
+    alg = float(np.mean([cfg.step_bytes(pos0 + i) for i in range(n)]))
+    peak, kind = measured_peaks()
+    ach = alg / (ms / n * 1e-3) / 1e9
+    dec.release()
+    return {"workload": "config 3: B=64 paged, prompt lengths U[32,448] seed 2, random block table, "
+                        "64 greedy steps", "tok_s": 64 * n / (ms / 1000), "ms_per_step": ms / n,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "scope": "whole step (123 kernels)", "peak_source": f"{kind} hbm_gbs"},
+            "gpu_launches": 123 * n}
+
+
+def measure_cfg4(eng, cfg, torch):
+    """Config 4: B=8 64-token prompts (seed 3), 128 sampled steps with
+    temperature 0.7, top-p 0.95, repetition penalty 1.2 and the seeded
+    uniforms [128, 8] (seed 4); one batched step + one sampler launch each."""
+    from transformer_b200.batched import BatchedDecoder
+    from transformer_b200.generate import Sampler
+    from transformer_b200.synth import batch_cfg4
+    prompts, u = batch_cfg4(cfg)
+    B, steps = prompts.shape[0], u.shape[0]
+    dev = eng.device
+    dec = BatchedDecoder(eng, B, seed=4)
+    last = dec.ingest(list(prompts))
+    smp = Sampler(eng, B, steps + 1)
+    uni = torch.from_numpy(u.astype(np.float64)).to(dev)
+    nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+    logits = last.contiguous()
+    smp.hist_len.zero_()
+    tok = smp.sample(logits, 0.7, 0.95, 1.2, B, uniforms=uni[0]).clone()
+
+    def run():
+        nonlocal tok
+        for i in range(1, steps):
+            smp.history[:, i - 1].copy_(tok)
+            smp.hist_len.fill_(i)
+            dec.tok.copy_(tok)
+            eng.step_paged(dec.tok, dec.pos, dec.pool, dec.table, dec.logits, nxt)
+            dec.pos.add_(1)
+            tok = smp.sample(dec.logits, 0.7, 0.95, 1.2, B, uniforms=uni[i]).clone()
+    ms = events_ms(run, torch.cuda.current_stream(), torch)
+    eng.check_device()
+    return {"workload": "config 4: B=8 sampling (T 0.7, top-p 0.95, rep 1.2, seeded uniforms), 64-token "
+                        "prompts, 127 sampled steps after the first", "tok_s": B * (steps - 1) / (ms / 1000),
+            "ms_per_step": ms / (steps - 1), "gpu_launches": (123 + 1) * (steps - 1)}
 
 
 def run_ours(args, rank, local_rank, world):
     import torch
     import torch.distributed as dist
 
+    from transformer_b200.batched import BatchedDecoder
     from transformer_b200.config import CONFIG_306M
     from transformer_b200.multi_sm_decode import DecodeEngine
     from transformer_b200.packing import prepare_decode_weights_nlayer
-    from transformer_b200.synth import prompt_cfg1, synth_params
+    from transformer_b200.synth import batch_cfg5, prompt_cfg1, prompt_cfg2, synth_params
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    if TOTAL_SEQS % world:
+        raise SystemExit("world size must divide 2048")
     cfg = CONFIG_306M
     w = prepare_decode_weights_nlayer(synth_params(cfg, 0), cfg, device=dev)
-    eng = DecodeEngine(w)
+    n_seq = TOTAL_SEQS // world
+    n_waves = (n_seq + WAVE - 1) // WAVE
+    wave_b = n_seq // n_waves
+    eng = DecodeEngine(w, max_batch=max(2, wave_b))
     stream = torch.cuda.current_stream(dev)
-    prompt = prompt_cfg1()
-    P0, NPOS = len(prompt), 128
-    kv = eng.new_kv()
-    eng.prefill(prompt, kv)
-    tokbuf = torch.zeros(1, dtype=torch.int32, device=dev)
-    tokbuf.copy_(torch.argmax(eng.logits[0]).to(torch.int32).reshape(1))
-    total = args.warmup + args.steps
-    posarr = torch.tensor([P0 + (i % NPOS) for i in range(total)], dtype=torch.int32, device=dev)
-    logits = eng.logits
+    prompts = batch_cfg5(cfg)[rank * n_seq:(rank + 1) * n_seq]
+    waves = []
+    for i in range(n_waves):
+        d = BatchedDecoder(eng, wave_b, seed=1000 * rank + i)
+        d.ingest(list(prompts[i * wave_b:(i + 1) * wave_b]))
+        d.capture()
+        waves.append(d)
+    pos = PROMPT_LEN
 
-    def run(i0, n):
-        for i in range(i0, i0 + n):
-            eng.step(tokbuf, posarr[i:i + 1], kv, logits, tokbuf, stream)
+    def one_step():
+        nonlocal pos
+        if pos >= cfg.context_len:  # wrap (only for runs longer than 448 steps)
+            for d in waves:
+                d.pos.fill_(PROMPT_LEN)
+            pos = PROMPT_LEN
+        for d in waves:
+            d.replay()
+        pos += 1
 
-    run(0, args.warmup)
+    for _ in range(args.warmup):
+        one_step()
     torch.cuda.synchronize(dev)
     eng.check_device()
+    pos_t0 = pos
 
     # ---- device-timed region ----
     clocks = ClockSampler(local_rank) if rank == 0 else None
@@ -216,14 +413,10 @@ def run_ours(args, rank, local_rank, world):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    run(args.warmup, args.steps)
-    e1.record(stream)
+    ms = events_ms(lambda: [one_step() for _ in range(args.steps)], stream, torch)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    ms = e0.elapsed_time(e1)
     clk = clocks.stop() if clocks else None
     eng.check_device()
     if world > 1:
@@ -231,72 +424,88 @@ def run_ours(args, rank, local_rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / args.steps
-    value = world * args.steps / (ms / 1000.0)
+    value = TOTAL_SEQS * args.steps / (ms / 1000.0)
+    positions = [pos_t0 + i if pos_t0 + i < cfg.context_len else PROMPT_LEN for i in range(args.steps)]
+    alg_step = float(np.mean([n_waves * cfg.step_bytes([p] * wave_b) for p in positions]))
+    peak, peak_kind = measured_peaks()
+    achieved = alg_step / (ms_per_step / 1000.0) / 1e9
 
     # ---- end to end through the public call, host buffers ----
-    h_in = torch.zeros(2, dtype=torch.int32, pin_memory=True)
-    h_out = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-    d_in = torch.zeros(2, dtype=torch.int32, device=dev)
-    d_out = torch.zeros(1, dtype=torch.int32, device=dev)
-    kv2 = eng.new_kv()
-    eng.prefill(prompt, kv2)
-    tok = int(torch.argmax(eng.logits[0]).item())
-    ne = args.e2e_steps
+    ne = max(1, args.e2e_steps)
+    h_in = [torch.zeros(2, wave_b, dtype=torch.int32, pin_memory=True) for _ in waves]
+    h_out = [torch.zeros(wave_b, dtype=torch.int32, pin_memory=True) for _ in waves]
+    d_in = [torch.zeros(2, wave_b, dtype=torch.int32, device=dev) for _ in waves]
+    for i, d in enumerate(waves):
+        h_out[i].copy_(d.tok)
+    p_e2e = pos
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    for i in range(ne):
-        h_in[0] = tok
-        h_in[1] = P0 + (i % NPOS)
-        d_in.copy_(h_in, non_blocking=True)
-        eng.step(d_in[0:1], d_in[1:2], kv2, logits, d_out, stream)
-        h_out.copy_(d_out, non_blocking=True)
+    for s in range(ne):
+        if p_e2e >= cfg.context_len:
+            p_e2e = PROMPT_LEN
+        for i, d in enumerate(waves):
+            h_in[i][0].copy_(h_out[i])
+            h_in[i][1].fill_(p_e2e)
+            d_in[i].copy_(h_in[i], non_blocking=True)
+            eng.step_paged(d_in[i][0], d_in[i][1], d.pool, d.table, d.logits, d.tok, stream)
+            h_out[i].copy_(d.tok, non_blocking=True)
         stream.synchronize()
-        tok = int(h_out[0])
+        p_e2e += 1
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * ne / e2e_s
+    e2e_value = TOTAL_SEQS * ne / e2e_s
+    for d in waves:
+        d.release()
 
-    # ---- roofline of the decode kernel ----
-    positions = [P0 + ((args.warmup + i) % NPOS) for i in range(args.steps)]
-    alg_bytes = float(np.mean([cfg.step_bytes([p]) for p in positions]))
-    peak, peak_kind = measured_peaks()
-    achieved = alg_bytes / (ms_per_step / 1000.0) / 1e9
-    traffic = profile_traffic()
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_configs:
+        eng1 = DecodeEngine(w)
+        extra["config1_b1"] = measure_b1(eng1, cfg, dev, stream, torch, prompt_cfg1(), 128,
+                                         "config 1: B=1, 16-token prompt, greedy positions 16..143")
+        extra["config1_b1"]["e2e"] = measure_b1_e2e(eng1, dev, stream, torch, prompt_cfg1(), 128)
+        extra["config2_b1_long"] = measure_b1(eng1, cfg, dev, stream, torch, prompt_cfg2(), 128,
+                                              "config 2: B=1, 384-token prompt, greedy positions 384..511")
+        eng1.close()
+        eng3 = DecodeEngine(w, max_batch=64)
+        extra["config3_paged_b64"] = measure_cfg3(eng3, cfg, torch)
+        extra["config4_sampled_b8"] = measure_cfg4(eng3, cfg, torch)
+        eng3.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_b1(args.cpu_sample_steps)
+        cpu = cpu_baseline_serve(args.cpu_sample_steps)
+        if "config1_b1" in extra:
+            extra["config1_b1"]["cpu_baseline"] = cpu_baseline_b1(16)
 
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    launches = 123 * n_waves * args.steps
     line = {
-        "metric": "decode tok/s (B=1 greedy, 306M, config 1)",
-        "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "us_per_token": ms_per_step * 1000.0,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded prompt; no checkpoint on the box)",
-        "config": {"workload": "b1: 306M decoder (d=1024, 16 heads, 4 kv heads, 24 layers, d_ff 2816, "
-                               "vocab 32000, ctx 512), batch 1, 16-token seeded prompt, greedy decode at "
-                               "positions 16..143, one replica per GPU",
-                   "model": "306M", "global_batch": world, "seq_len": 512,
-                   "parallelism": f"replicas{world}",
-                   "l2": "inputs larger than L2: 607 MB of weights streamed every step"},
-        "gpu_launches": args.steps,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                     "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes},
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
-                "steps": ne, "note": "host loop: pinned H2D tok+pos, launch, D2H next token, sync per step"},
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded prompts; no checkpoint on the box)",
+        "config": serve_config(world),
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} hbm_gbs", "scope": "whole batched step per GPU (123 kernels "
+                     "per wave: projections on tcgen05, paged attention, embedding, argmax)",
+                     "traffic": None, "algorithmic_bytes_per_step": alg_step},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
+                "d2h_bytes_per_step": 4 * n_seq, "steps": ne,
+                "note": "per wave: pinned H2D of tokens+positions, b2d_decode_step_paged, D2H next tokens; "
+                        "one sync per step"},
         "clocks": clk,
     }
+    line.update(extra)
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line))

@@ -218,7 +218,9 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * [grid][stamps_per_cta] (slot 0 = start, 13 per layer, 3 final; NULL/0 turns
  * it off).  b2d_debug_tune: knob 1 = sleep (ns) between failed polls of the
  * exchange words (0 = spin); knob 2 = weight-stream copies in flight per CTA
- * (1..12, default 4).
+ * (1..12, default 4); knob 3 = batched step with (1, default) or without (0)
+ * programmatic dependent launch; knob 4 = batched step K split forced to
+ * 1..8 (0 = automatic).
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
 B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);
@@ -228,7 +230,8 @@ B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);
  * Y[n][m] = sum_k X[n][k] W[m][k] (bf16 inputs, f32 accumulation) with the
  * batched path's epilogue `epi`: 0 = store f32 to y, 1 = y = resid + result,
  * 2 = SwiGLU of row pairs (2j gate, 2j+1 up) stored as bf16 column j of ybf.
- * M % 128 == 0, K % 64 == 0.  Synchronises `stream`.
+ * Bits 8.. of `epi` force the K split (1..8 cluster CTAs; 0 = the split the
+ * decode step would pick).  M % 128 == 0, K % 64 == 0.  Synchronises `stream`.
  */
 B2D_API b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int N, int epi,
                                  float* y_dev, const float* resid_dev, void* ybf_dev, int ldy, void* stream);

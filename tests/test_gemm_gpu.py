@@ -17,28 +17,54 @@ def _p(t):
     return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
 
-def _gemm(W, X, epi, resid=None, ldy=None):
+def _gemm(W, X, epi, resid=None, ldy=None, ksplit=0):
     lib = _lib.load()
     M, K = W.shape
     N = X.shape[0]
     ldy = ldy or M
     y = torch.full((N, ldy), float("nan"), dtype=torch.float32, device=W.device) if epi != 2 else None
     ybf = torch.zeros((N, ldy), dtype=torch.bfloat16, device=W.device) if epi == 2 else None
-    st = lib.b2d_test_gemm(_p(W), M, K, _p(X), N, epi, _p(y), _p(resid), _p(ybf), ldy,
+    st = lib.b2d_test_gemm(_p(W), M, K, _p(X), N, epi | (ksplit << 8), _p(y), _p(resid), _p(ybf), ldy,
                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == _lib.B2D_OK, _lib.status_str(st)
     return y if epi != 2 else ybf
 
 
 @pytest.mark.parametrize("M,K,N", [(128, 64, 16), (256, 1024, 8), (1536, 1024, 64), (1024, 2816, 37),
-                                   (384, 256, 130)])
+                                   (384, 256, 130), (1024, 1024, 100), (5632, 1024, 256), (1024, 2816, 300)])
 def test_gemm_f32_matches_torch(cuda, M, K, N):
+    """Every tile width (16..256 batch rows) with the decode step's K split."""
     g = torch.Generator(device="cpu").manual_seed(M + K + N)
     W = (torch.randn(M, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
     X = torch.randn(N, K, generator=g).to(torch.bfloat16).to(cuda)
     y = _gemm(W, X, 0)
     ref = X.float() @ W.float().T
     torch.testing.assert_close(y, ref, atol=1e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("ks", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_cluster_split_k(cuda, ks, epi):
+    """K split over 1..8 cluster CTAs (uneven slices at ks=3, 5) for each
+    epilogue; the split result equals the unsplit one up to f32 reassociation
+    and is bitwise reproducible."""
+    g = torch.Generator(device="cpu").manual_seed(40 + ks)
+    M, K, N = 1024, 1344, 48
+    W = (torch.randn(M, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    X = torch.randn(N, K, generator=g).to(torch.bfloat16).to(cuda)
+    R = torch.randn(N, M, generator=g).to(cuda) if epi == 1 else None
+    ldy = M // 2 if epi == 2 else None
+    out = _gemm(W, X, epi, resid=R, ldy=ldy, ksplit=ks)
+    again = _gemm(W, X, epi, resid=R, ldy=ldy, ksplit=ks)
+    assert torch.equal(out, again)
+    full = X.float() @ W.float().T
+    if epi == 0:
+        torch.testing.assert_close(out, full, atol=1e-3, rtol=1e-3)
+    elif epi == 1:
+        torch.testing.assert_close(out, R + full, atol=1e-3, rtol=1e-3)
+    else:
+        ref = torch.nn.functional.silu(full[:, 0::2]) * full[:, 1::2]
+        torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
 
 
 def test_gemm_residual_epilogue(cuda):

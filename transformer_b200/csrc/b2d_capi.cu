@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <utility>
 
 #include "../../include/b2d.h"
 #include "batched.cuh"
@@ -115,11 +116,36 @@ struct b2d_ws {
   uint32_t poll_ns;
   int max_inflight;
   // batched path (max_batch > 1)
-  int rows;                        // activation rows allocated (max_batch rounded up to 64)
-  float *H, *Hm, *qkv, *logits;
+  int rows;                        // activation rows allocated (max_batch rounded up to the widest tile)
+  float *H, *Hm, *qkv, *logits, *att_part;
+  uint32_t* att_tickets;
+  uint32_t* norm_tickets;  // fused-RMSNorm tickets of the residual projections
+  bool no_pdl;             // diagnostics: launch without programmatic dependencies
+  int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
+  int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
-  CUtensorMap xmap[3], amap[3], actmap[3];  // box rows 16 / 32 / 64
+  CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
 };
+
+namespace {
+inline int bn_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4; }
+
+// Launch with an optional programmatic dependency on the previous kernel of
+// the stream (the kernels call griddepcontrol.wait before reading its output).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+}  // namespace
 
 extern "C" {
 
@@ -235,7 +261,9 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
   if (e == cudaSuccess && max_batch > 1) {
     const size_t D = c.d_model, F = c.d_ff, Q = qkv, V = c.vocab_size;
-    ws->rows = (max_batch + 63) / 64 * 64;
+    const int bn_max = b2d::gemm_bn_for(max_batch);
+    ws->rows = (max_batch + bn_max - 1) / bn_max * bn_max;
+    ws->att_chunks = (c.context_len + b2d::kAttChunk - 1) / b2d::kAttChunk;
     e = cudaMalloc(&ws->H, sizeof(float) * D * max_batch);
     if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * max_batch);
     if (e == cudaSuccess) e = cudaMalloc(&ws->qkv, sizeof(float) * Q * max_batch);
@@ -246,7 +274,14 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     if (e == cudaSuccess) e = cudaMemset(ws->X, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->A, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->ACT, 0, 2 * F * ws->rows);
-    for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+    if (e == cudaSuccess)
+      e = cudaMalloc(&ws->att_part, sizeof(float) * size_t(max_batch) * c.n_heads * ws->att_chunks * b2d::kAttPart);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->att_tickets, sizeof(uint32_t) * size_t(max_batch) * c.n_kv_heads);
+    if (e == cudaSuccess) e = cudaMemset(ws->att_tickets, 0, sizeof(uint32_t) * size_t(max_batch) * c.n_kv_heads);
+    const size_t nt = size_t((max_batch + 15) / 16) * b2d::kGemmMaxSplit;  // >= ceil(N/BN) * ksplit
+    if (e == cudaSuccess) e = cudaMalloc(&ws->norm_tickets, sizeof(uint32_t) * nt);
+    if (e == cudaSuccess) e = cudaMemset(ws->norm_tickets, 0, sizeof(uint32_t) * nt);
+    for (int i = 0; i < 5 && e == cudaSuccess && (16 << i) <= bn_max; ++i) {
       const uint32_t box = 16u << i;
       if (!b2d::make_kmajor_map(&ws->xmap[i], ws->X, D, ws->rows, box) ||
           !b2d::make_kmajor_map(&ws->amap[i], ws->A, D, ws->rows, box) ||
@@ -275,6 +310,9 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   cudaFree(ws->X);
   cudaFree(ws->A);
   cudaFree(ws->ACT);
+  cudaFree(ws->att_part);
+  cudaFree(ws->att_tickets);
+  cudaFree(ws->norm_tickets);
   cudaFree(ws->words);
   cudaFree(ws->ctl);
   cudaFree(ws->am_val);
@@ -336,6 +374,14 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 2:  // bulk copies in flight per CTA
       if (value < 1 || value > b2d::kStages) return B2D_ERR_INVALID_ARG;
       ws->max_inflight = static_cast<int>(value);
+      return B2D_OK;
+    case 3:  // batched step: programmatic dependent launch on (1) / off (0)
+      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
+      ws->no_pdl = value == 0;
+      return B2D_OK;
+    case 4:  // batched step: force the projections' K split (0 = automatic)
+      if (value < 0 || value > b2d::kGemmMaxSplit) return B2D_ERR_INVALID_ARG;
+      ws->force_ksplit = static_cast<int>(value);
       return B2D_OK;
   }
   return B2D_ERR_INVALID_ARG;
@@ -419,7 +465,8 @@ b2d_status ensure_weight_maps(b2d_model* m) {
   const b2d_config& c = m->cfg;
   const uint64_t D = c.d_model, F = c.d_ff, Q = uint64_t(c.n_heads + 2 * c.n_kv_heads) * 64;
   if (Q % b2d::kGemmBM || D % b2d::kGemmBM || (2 * F) % b2d::kGemmBM || c.vocab_size % b2d::kGemmBM ||
-      D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4)
+      D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4 ||
+      c.context_len > 32 * b2d::kAttChunk)  // the attention merge holds one chunk per lane
     return B2D_ERR_UNSUPPORTED;
   CUtensorMap* maps = new (std::nothrow) CUtensorMap[4 * c.n_layers + 1];
   if (!maps) return B2D_ERR_NO_MEMORY;
@@ -456,7 +503,7 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const b2d_config& c = m->cfg;
   const int D = c.d_model, F = c.d_ff, Q = (c.n_heads + 2 * c.n_kv_heads) * 64, V = c.vocab_size;
-  const int bn = b2d::gemm_bn_for(batch), mi = bn == 16 ? 0 : (bn == 32 ? 1 : 2);
+  const int mi = bn_index(b2d::gemm_bn_for(batch));
   uint32_t* status = &ws->ctl->status;
   float* logits = logits_dev ? logits_dev : ws->logits;
   const float* ln1 = reinterpret_cast<const float*>(m->w + m->lay.off_ln1);
@@ -464,47 +511,58 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
   const float* lnf = reinterpret_cast<const float*>(m->w + m->lay.off_lnf);
   const __nv_bfloat16* emb = reinterpret_cast<const __nv_bfloat16*>(m->w + m->lay.off_emb);
 
-  b2d::embed_rows_kernel<<<batch, 256, 0, st>>>(emb, tok_dev, V, D, ws->H, status);
-  B2D_CUDA(cudaGetLastError(), "embed");
-  b2d::GemmArgs g;
-  std::memset(&g, 0, sizeof(g));
+  const int sms = m->grid;
+  const bool pdl = !ws->no_pdl;
+  B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok_dev, V, D, ln1, c.rms_eps,
+                    ws->H, ws->X, status), "embed");
+  b2d::GemmArgs g{};
   g.N = batch;
   g.err = status;
-  b2d::PagedAttnArgs pa;
+  g.tickets = ws->norm_tickets;
+  g.norm_eps = c.rms_eps;
+  b2d::PagedAttnArgs pa{};
   pa.qkv = ws->qkv; pa.pos = pos_dev; pa.pool = static_cast<__nv_bfloat16*>(kv_pool_dev);
   pa.table = block_table_dev; pa.bps = blocks_per_seq; pa.num_blocks = num_blocks;
   pa.n_heads = c.n_heads; pa.n_kv = c.n_kv_heads; pa.ctx = c.context_len;
   pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
+  pa.part = ws->att_part; pa.tickets = ws->att_tickets; pa.max_chunks = ws->att_chunks;
+  int ks_qkv = b2d::gemm_ksplit_for(Q, batch, D, sms), ks_o = b2d::gemm_ksplit_for(D, batch, D, sms);
+  int ks_gu = b2d::gemm_ksplit_for(2 * F, batch, D, sms), ks_dn = b2d::gemm_ksplit_for(D, batch, F, sms);
+  int ks_lg = b2d::gemm_ksplit_for(V, batch, D, sms);
+  if (ws->force_ksplit) ks_qkv = ks_o = ks_gu = ks_dn = ks_lg = ws->force_ksplit;
   for (int l = 0; l < c.n_layers; ++l) {
-    b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->H, ln1 + size_t(l) * D, D, c.rms_eps, ws->X, D);
-    g.M = Q; g.K = D; g.y = ws->qkv; g.ldy = Q;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 0], ws->xmap[mi], g, b2d::EPI_F32, st), "qkv");
+    // X = RMSNorm(H, ln1[l]) was written by the embedding (l = 0) or the previous down projection
+    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.ksplit = ks_qkv; g.norm_g = nullptr;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 0], ws->xmap[mi], g, b2d::EPI_F32, st, pdl), "qkv");
     pa.layer = l;
-    b2d::paged_attn_kernel<<<dim3(batch, c.n_kv_heads), 32 * (c.n_heads / c.n_kv_heads), 0, st>>>(pa);
-    B2D_CUDA(cudaGetLastError(), "attention");
-    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 1], ws->amap[mi], g, b2d::EPI_RESID_F32, st), "o");
-    b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->Hm, ln2 + size_t(l) * D, D, c.rms_eps, ws->X, D);
-    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 2], ws->xmap[mi], g, b2d::EPI_SWIGLU_BF16, st), "gate/up");
-    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 3], ws->actmap[mi], g, b2d::EPI_RESID_F32, st), "down");
+    B2D_CUDA(launch_k(b2d::paged_attn_kernel, dim3(ws->att_chunks, c.n_kv_heads, batch), dim3(128), st, pdl, pa),
+             "attention");
+    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D; g.ksplit = ks_o;
+    g.norm_g = ln2 + size_t(l) * D; g.norm_out = ws->X;  // X = RMSNorm(Hm, ln2[l])
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 1], ws->amap[mi], g, b2d::EPI_RESID_F32, st, pdl), "o");
+    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F; g.ksplit = ks_gu; g.norm_g = nullptr;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 2], ws->xmap[mi], g, b2d::EPI_SWIGLU_BF16, st, pdl), "gate/up");
+    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D; g.ksplit = ks_dn;
+    g.norm_g = l + 1 < c.n_layers ? ln1 + size_t(l + 1) * D : lnf;  // next layer's ln1, or the final norm
+    g.norm_out = ws->X;
+    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 3], ws->actmap[mi], g, b2d::EPI_RESID_F32, st, pdl), "down");
   }
-  b2d::rmsnorm_rows_kernel<<<batch, 256, 0, st>>>(ws->H, lnf, D, c.rms_eps, ws->X, D);
-  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V;
-  B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * c.n_layers], ws->xmap[mi], g, b2d::EPI_F32, st), "logits");
-  b2d::argmax_rows_kernel<<<batch, 1024, 0, st>>>(logits, V, V, next_tok_dev);
-  B2D_CUDA(cudaGetLastError(), "argmax");
+  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V; g.ksplit = ks_lg; g.norm_g = nullptr;
+  B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * c.n_layers], ws->xmap[mi], g, b2d::EPI_F32, st, pdl), "logits");
+  B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
+                    next_tok_dev), "argmax");
   return B2D_OK;
 }
 
 // Test hook: Y = X . W^T on the tensor-core GEMM with the chosen epilogue.
 b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int N, int epi, float* y_dev,
                          const float* resid_dev, void* ybf_dev, int ldy, void* stream) {
+  int ks = epi >> 8;
+  epi &= 0xff;
   if (!w_dev || !x_dev || M <= 0 || K <= 0 || N <= 0 || M % b2d::kGemmBM || K % b2d::kGemmBK || epi < 0 ||
-      epi > 2 || ldy <= 0 || (epi != b2d::EPI_SWIGLU_BF16 && !y_dev) || (epi == b2d::EPI_RESID_F32 && !resid_dev) ||
+      epi > 2 || ldy <= 0 || ks < 0 || ks > b2d::kGemmMaxSplit || ks > K / b2d::kGemmBK || (epi != b2d::EPI_SWIGLU_BF16 && !y_dev) || (epi == b2d::EPI_RESID_F32 && !resid_dev) ||
       (epi == b2d::EPI_SWIGLU_BF16 && !ybf_dev))
     return B2D_ERR_INVALID_ARG;
   static uint32_t* err = nullptr;
@@ -515,9 +573,12 @@ b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int
   if (!b2d::make_kmajor_map(&wm, w_dev, K, M, b2d::kGemmBM) ||
       !b2d::make_kmajor_map(&xm, x_dev, K, N, b2d::gemm_bn_for(N)))
     return B2D_ERR_INVALID_ARG;
-  b2d::GemmArgs g;
+  b2d::GemmArgs g{};
   g.M = M; g.N = N; g.K = K;
   g.y = y_dev; g.resid = resid_dev; g.ybf = static_cast<__nv_bfloat16*>(ybf_dev); g.ldy = ldy; g.err = err;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  g.ksplit = ks ? ks : b2d::gemm_ksplit_for(M, N, K, sms);
   B2D_CUDA(b2d::launch_gemm(wm, xm, g, epi, st), "gemm launch");
   uint32_t h = 0;
   B2D_CUDA(cudaMemcpyAsync(&h, err, sizeof(h), cudaMemcpyDeviceToHost, st), "read err");

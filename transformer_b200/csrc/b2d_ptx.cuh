@@ -170,4 +170,10 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xffff0000u);
 }
 
+// Programmatic dependent launch: wait for the preceding kernel's results /
+// allow the next kernel's CTAs to start their prologue.  No-ops when the
+// launch carries no programmatic dependency.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace b2d

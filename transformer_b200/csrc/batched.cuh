@@ -24,28 +24,28 @@ namespace b2d {
 
 constexpr int kPageTokens = 16;
 
-// H[b][:] = f32(emb[tok[b]])
+// H[b][:] = f32(emb[tok[b]]);  X[b][:] = bf16(RMSNorm(H[b]) * g)  (model.py:94-98,
+// layer 0's ln1).  One CTA (256 threads) per row; fixed-order reduction.
 __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ emb, const int32_t* __restrict__ tok,
-                                  int vocab, int D, float* __restrict__ H, uint32_t* status) {
-  const int b = blockIdx.x;
-  int t = tok[b];
-  if (t < 0 || t >= vocab) {
-    if (threadIdx.x == 0) atomicCAS(status, 0u, 0x201u);
-    t = 0;
-  }
-  const __nv_bfloat16* e = emb + static_cast<size_t>(t) * D;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) H[static_cast<size_t>(b) * D + i] = __bfloat162float(e[i]);
-}
-
-// X[b][:] = bf16(H[b] * rsqrt(mean(H[b]^2) + eps) * g)   (model.py:94-98)
-// One CTA (256 threads) per row; fixed-order reduction.
-__global__ void rmsnorm_rows_kernel(const float* __restrict__ H, const float* __restrict__ g, int D, float eps,
-                                    __nv_bfloat16* __restrict__ X, int ldx) {
+                                  int vocab, int D, const float* __restrict__ g, float eps, float* __restrict__ H,
+                                  __nv_bfloat16* __restrict__ X, uint32_t* status) {
   __shared__ float red[8];
+  pdl_wait();
+  pdl_launch();
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const float* h = H + static_cast<size_t>(b) * D;
+  int tk = tok[b];
+  if (tk < 0 || tk >= vocab) {
+    if (t == 0) atomicCAS(status, 0u, 0x201u);
+    tk = 0;
+  }
+  const __nv_bfloat16* e = emb + static_cast<size_t>(tk) * D;
+  float* h = H + static_cast<size_t>(b) * D;
   float ss = 0.f;
-  for (int i = t; i < D; i += 256) ss = fmaf(h[i], h[i], ss);
+  for (int i = t; i < D; i += 256) {
+    const float v = __bfloat162float(e[i]);
+    h[i] = v;
+    ss = fmaf(v, v, ss);
+  }
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
   __syncthreads();
@@ -54,7 +54,7 @@ __global__ void rmsnorm_rows_kernel(const float* __restrict__ H, const float* __
   for (int w = 0; w < 8; ++w) tot += red[w];
   const float r = rsqrtf(tot / static_cast<float>(D) + eps);
   for (int i = t; i < D; i += 256)
-    X[static_cast<size_t>(b) * ldx + i] = __float2bfloat16_rn(h[i] * r * __ldg(g + i));
+    X[static_cast<size_t>(b) * D + i] = __float2bfloat16_rn(__bfloat162float(e[i]) * r * __ldg(g + i));
 }
 
 struct PagedAttnArgs {
@@ -68,124 +68,197 @@ struct PagedAttnArgs {
   __nv_bfloat16* out;          // [B][ldo] bf16: head h at columns h*64..
   int ldo;
   uint32_t* status;            // set when a block-table entry is out of range
+  float* part;                 // [B][n_heads][max_chunks][kAttPart] chunk partials
+  uint32_t* tickets;           // [B][n_kv]; zero between launches (the combining CTA resets it)
+  int max_chunks;              // >= ceil(ctx / kAttChunk)
 };
+
+constexpr int kAttChunk = 64;  // cached positions per CTA
+constexpr int kAttPart = 68;   // m, l, 2 pad, o[64]
+constexpr int kAttRow = 72;    // smem row pitch (bf16): 144 B keeps 16-byte row reads conflict-free
 
 __device__ __forceinline__ size_t page_row(const PagedAttnArgs& a, int blk, int kv, int g, int slot) {
   return ((((static_cast<size_t>(a.layer) * a.num_blocks + blk) * 2 + kv) * a.n_kv + g) * kPageTokens + slot) * 64;
 }
 
-// grid (B, n_kv), block 32 * (n_heads / n_kv): warp w serves query head
-// g * GQA + w; the K/V pages of kv head g are read once per CTA (L1 shared).
-// GQA <= 4 (the shared buffers hold four query heads).
+// Split ("flash-decoding") paged attention.  grid (max_chunks, n_kv, B),
+// block 128: CTA (c, g, b) handles cached positions 64c..64c+63 of sequence b
+// for the GQA query heads of kv head g (warp w = query head g*GQA + w,
+// GQA <= 4).  The chunk holding the new position appends its K (post-RoPE) /
+// V to the pool.  K/V rows are staged in padded shared memory; scores are
+// lane-per-position, P.V lane-per-dimension.  Each CTA writes (m, l, o) for
+// its chunk; the last CTA of (b, g) to finish (ticket) merges the chunks in
+// chunk order and writes the bf16 attention output.  Math: model.py:100-131
+// (rotate-half RoPE, causal softmax over positions 0..p, GQA head sharing).
 __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__ PagedAttnArgs a) {
-  __shared__ float sq[4][64];
-  __shared__ float skn[64], svn[64];
-  __shared__ float sprob[4][32];
-  const int b = blockIdx.x, g = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ __align__(16) __nv_bfloat16 sk[kAttChunk][kAttRow];
+  __shared__ __align__(16) __nv_bfloat16 sv[kAttChunk][kAttRow];
+  __shared__ __align__(16) float sq[4][64];
+  __shared__ float sp[4][kAttChunk];
+  __shared__ uint32_t s_last;
+  const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int GQA = a.n_heads / a.n_kv;
-  const int h = g * GQA + warp;
+  pdl_wait();
+  pdl_launch();
   const int p = a.pos[b];
-  const int qkvd = (a.n_heads + 2 * a.n_kv) * 64;
-  __nv_bfloat16* o = a.out + static_cast<size_t>(b) * a.ldo + h * 64;
-  if (p < 0 || p >= a.ctx) {  // inactive (or invalid) sequence: no cache write
-    reinterpret_cast<__nv_bfloat162*>(o)[lane] = __floats2bfloat162_rn(0.f, 0.f);
+  if (p < 0 || p >= a.ctx) {  // idle sequence: no cache write, zero output
+    if (c == 0 && warp < GQA)
+      reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + warp) * 64)[lane] =
+          __floats2bfloat162_rn(0.f, 0.f);
     return;
   }
-  const float* row = a.qkv + static_cast<size_t>(b) * qkvd;
-  const float c = a.rcos[static_cast<size_t>(p) * 32 + lane], s = a.rsin[static_cast<size_t>(p) * 32 + lane];
-  {  // RoPE (rotate-half, model.py:110-117); q pre-scaled by 1/sqrt(64) (exact)
-    const float* q = row + h * 64;
-    const float lo = q[lane], hi = q[lane + 32];
-    sq[warp][lane] = (lo * c - hi * s) * 0.125f;
-    sq[warp][lane + 32] = (lo * s + hi * c) * 0.125f;
-    if (warp == 0) {
+  const int nch = p / kAttChunk + 1;
+  if (c >= nch) return;
+  const int base = c * kAttChunk;
+  const int npos = min(kAttChunk, p + 1 - base);  // rows 0..npos-1 = positions base..
+  const int32_t* tb = a.table + static_cast<size_t>(b) * a.bps;
+  // every page this CTA touches must exist
+  bool bad = (p / kPageTokens) >= a.bps;
+  if (!bad && t < kAttChunk / kPageTokens && t * kPageTokens < npos) {
+    const int e = tb[base / kPageTokens + t];
+    bad = e < 0 || e >= a.num_blocks;
+  }
+  bad = __syncthreads_or(bad);
+  if (bad && t == 0) atomicCAS(a.status, 0u, 0x203u);
+
+  const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
+  const bool owner = c == nch - 1;  // this chunk holds position p
+  if (t < 32) {
+    const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
+    for (int w = 0; w < GQA; ++w) {  // RoPE (rotate-half); q pre-scaled by 1/sqrt(64) (exact)
+      const float* q = row + (g * GQA + w) * 64;
+      const float lo = q[lane], hi = q[lane + 32];
+      sq[w][lane] = (lo * cs - hi * sn) * 0.125f;
+      sq[w][lane + 32] = (lo * sn + hi * cs) * 0.125f;
+    }
+    if (owner) {  // the new position's K (post-RoPE) / V, bf16 as cached
       const float* k = row + a.n_heads * 64 + g * 64;
-      const float klo = k[lane], khi = k[lane + 32];
-      skn[lane] = klo * c - khi * s;
-      skn[lane + 32] = klo * s + khi * c;
       const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
-      svn[lane] = v[lane];
-      svn[lane + 32] = v[lane + 32];
+      const float klo = k[lane], khi = k[lane + 32];
+      const int r = p - base;
+      const __nv_bfloat16 k0 = __float2bfloat16_rn(klo * cs - khi * sn);
+      const __nv_bfloat16 k1 = __float2bfloat16_rn(klo * sn + khi * cs);
+      sk[r][lane] = k0;
+      sk[r][lane + 32] = k1;
+      sv[r][lane] = __float2bfloat16_rn(v[lane]);
+      sv[r][lane + 32] = __float2bfloat16_rn(v[lane + 32]);
+      if (!bad) {
+        const int blk = tb[p / kPageTokens], slot = p % kPageTokens;
+        __nv_bfloat16* kd = a.pool + page_row(a, blk, 0, g, slot);
+        __nv_bfloat16* vd = a.pool + page_row(a, blk, 1, g, slot);
+        kd[lane] = k0;
+        kd[lane + 32] = k1;
+        vd[lane] = sv[r][lane];
+        vd[lane + 32] = sv[r][lane + 32];
+      }
+    }
+  }
+  if (!bad) {  // stage the chunk's cached rows (all but p): 8 x 16 B per row
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = t + 128 * i, r = idx >> 3, cc = idx & 7, pp = base + r;
+      if (r < npos && pp != p) {
+        const int blk = tb[pp / kPageTokens], slot = pp % kPageTokens;
+        *reinterpret_cast<uint4*>(&sk[r][cc * 8]) =
+            __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 0, g, slot)) + cc);
+        *reinterpret_cast<uint4*>(&sv[r][cc * 8]) =
+            __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 1, g, slot)) + cc);
+      }
     }
   }
   __syncthreads();
-  const int* tb = a.table + static_cast<size_t>(b) * a.bps;
-  // every block this step touches must exist (checked by every warp: uniform)
-  bool bad = p / kPageTokens >= a.bps;
-  for (int i = lane; !bad && i <= p / kPageTokens; i += 32) bad = tb[i] < 0 || tb[i] >= a.num_blocks;
-  if (__any_sync(0xffffffffu, bad)) {
-    if (threadIdx.x == 0) atomicCAS(a.status, 0u, 0x203u);
-    reinterpret_cast<__nv_bfloat162*>(o)[lane] = __floats2bfloat162_rn(0.f, 0.f);
-    return;
-  }
-  if (warp == 0) {  // append this position's K (post-RoPE) / V, bf16
-    const int blk = tb[p / kPageTokens], slot = p % kPageTokens;
-    reinterpret_cast<__nv_bfloat162*>(a.pool + page_row(a, blk, 0, g, slot))[lane] =
-        __floats2bfloat162_rn(skn[2 * lane], skn[2 * lane + 1]);
-    reinterpret_cast<__nv_bfloat162*>(a.pool + page_row(a, blk, 1, g, slot))[lane] =
-        __floats2bfloat162_rn(svn[2 * lane], svn[2 * lane + 1]);
-  }
-  // attention over positions 0..p: lane-per-position QK, lane-per-dim PV
-  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int base = 0; base <= p; base += 32) {
-    const int pp = base + lane;
-    float sc = -INFINITY;
-    if (pp < p) {
-      const uint4* kr = reinterpret_cast<const uint4*>(a.pool + page_row(a, tb[pp / kPageTokens], 0, g, pp % kPageTokens));
-      float d = 0.f;
+
+  const int h = g * GQA + warp;
+  float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks + c) * kAttPart;
+  if (warp < GQA) {
+    float sc[2];
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const uint4 w = __ldg(kr + cc);
-        const float* qq = sq[warp] + cc * 8;
-        d = fmaf(qq[0], bf16_lo(w.x), d); d = fmaf(qq[1], bf16_hi(w.x), d);
-        d = fmaf(qq[2], bf16_lo(w.y), d); d = fmaf(qq[3], bf16_hi(w.y), d);
-        d = fmaf(qq[4], bf16_lo(w.z), d); d = fmaf(qq[5], bf16_hi(w.z), d);
-        d = fmaf(qq[6], bf16_lo(w.w), d); d = fmaf(qq[7], bf16_hi(w.w), d);
+    for (int half = 0; half < 2; ++half) {
+      const int r = lane + 32 * half;
+      float d = -INFINITY;
+      if (r < npos && !bad) {
+        d = 0.f;
+        const float4* q4 = reinterpret_cast<const float4*>(sq[warp]);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const uint4 w = *reinterpret_cast<const uint4*>(&sk[r][cc * 8]);
+          const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+          d = fmaf(qa.x, bf16_lo(w.x), d); d = fmaf(qa.y, bf16_hi(w.x), d);
+          d = fmaf(qa.z, bf16_lo(w.y), d); d = fmaf(qa.w, bf16_hi(w.y), d);
+          d = fmaf(qb.x, bf16_lo(w.z), d); d = fmaf(qb.y, bf16_hi(w.z), d);
+          d = fmaf(qb.z, bf16_lo(w.w), d); d = fmaf(qb.w, bf16_hi(w.w), d);
+        }
       }
-      sc = d;
-    } else if (pp == p) {
-      float d = 0.f;
+      sc[half] = d;
+    }
+    float m = fmaxf(sc[0], sc[1]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float e0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - m);
+    const float e1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - m);
+    sp[warp][lane] = e0;
+    sp[warp][lane + 32] = e1;
+    float l = e0 + e1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    __syncwarp();
+    float o0 = 0.f, o1 = 0.f;
+    for (int r = 0; r < (bad ? 0 : npos); ++r) {
+      const float pr = sp[warp][r];
+      const uint32_t vw = *reinterpret_cast<const uint32_t*>(&sv[r][2 * lane]);
+      o0 = fmaf(pr, bf16_lo(vw), o0);
+      o1 = fmaf(pr, bf16_hi(vw), o1);
+    }
+    if (nch == 1) {  // single chunk: final output directly
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
+          __floats2bfloat162_rn(o0 * inv, o1 * inv);
+    } else {
+      reinterpret_cast<float2*>(part + 4)[lane] = make_float2(o0, o1);
+      if (lane == 0) {
+        part[0] = bad ? -INFINITY : m;
+        part[1] = l;
+      }
+    }
+  }
+  if (nch == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    const uint32_t prev = atomicAdd(&a.tickets[b * a.n_kv + g], 1u);
+    s_last = prev == static_cast<uint32_t>(nch - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (t == 0) a.tickets[b * a.n_kv + g] = 0u;
+  if (warp < GQA) {  // merge the chunks of head h in chunk order (lane c holds chunk c's m, l)
+    const float* ph = a.part + (static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks * kAttPart;
+    float mc = -INFINITY, lc = 0.f;
+    if (lane < nch) {
+      mc = __ldcg(ph + lane * kAttPart);
+      lc = __ldcg(ph + lane * kAttPart + 1);
+    }
+    float M = mc;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float wl = mc == -INFINITY ? 0.f : __expf(mc - M);
+    float L = wl * lc;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    float o0 = 0.f, o1 = 0.f;
 #pragma unroll 8
-      for (int k = 0; k < 64; ++k) d = fmaf(sq[warp][k], skn[k], d);
-      sc = d;
+    for (int cc = 0; cc < nch; ++cc) {
+      const float wgt = __shfl_sync(0xffffffffu, wl, cc);
+      const float2 oc = __ldcg(reinterpret_cast<const float2*>(ph + cc * kAttPart + 4) + lane);
+      o0 = fmaf(wgt, oc.x, o0);
+      o1 = fmaf(wgt, oc.y, o1);
     }
-    float mx = sc;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    const float mn = fmaxf(m, mx);
-    const float pe = pp <= p ? __expf(sc - mn) : 0.f;
-    float ps = pe;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-    const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-    sprob[warp][lane] = pe;
-    __syncwarp();
-    float a0 = 0.f, a1 = 0.f;
-    const int n = min(32, p + 1 - base);
-    for (int i = 0; i < n; ++i) {
-      const int pv = base + i;
-      const float pi = sprob[warp][i];
-      float v0, v1;
-      if (pv == p) {
-        v0 = svn[2 * lane];
-        v1 = svn[2 * lane + 1];
-      } else {
-        const uint32_t vw = __ldg(reinterpret_cast<const unsigned int*>(
-                                      a.pool + page_row(a, tb[pv / kPageTokens], 1, g, pv % kPageTokens)) + lane);
-        v0 = bf16_lo(vw);
-        v1 = bf16_hi(vw);
-      }
-      a0 = fmaf(pi, v0, a0);
-      a1 = fmaf(pi, v1, a1);
-    }
-    __syncwarp();
-    l = fmaf(l, alpha, ps);
-    o0 = fmaf(o0, alpha, a0);
-    o1 = fmaf(o1, alpha, a1);
-    m = mn;
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
+        __floats2bfloat162_rn(o0 * inv, o1 * inv);
   }
-  const float inv = 1.0f / fmaxf(l, 1e-10f);
-  reinterpret_cast<__nv_bfloat162*>(o)[lane] = __floats2bfloat162_rn(o0 * inv, o1 * inv);
 }
 
 // next[b] = first index of the maximum of logits[b][0..V)  (one CTA per row)
@@ -193,6 +266,8 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int 
   __shared__ float rv[32];
   __shared__ int ri[32];
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  pdl_wait();
+  pdl_launch();
   const float* r = logits + static_cast<size_t>(b) * ldl;
   float bv = -INFINITY;
   int bi = 0x7fffffff;

@@ -695,9 +695,9 @@ __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm,
 
 template <class S>
 __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs A) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+  extern __shared__ __align__(128) uint8_t decode_smem_raw[];
   static_assert(SmemChecks<S>::ok, "");
-  Smem<S>& sm = *reinterpret_cast<Smem<S>*>(smem_raw);
+  Smem<S>& sm = *reinterpret_cast<Smem<S>*>(decode_smem_raw);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int cta = blockIdx.x;
   const int G = A.grid_part;

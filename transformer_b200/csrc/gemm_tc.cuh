@@ -8,10 +8,20 @@
 // tcgen05.ld and fuses the store: plain f32, f32 + residual, or SwiGLU of the
 // interleaved gate/up rows to bf16 (the next projection's K-major input).
 //
+// Decode projections are short and wide (N = batch), so a weight tile alone
+// would keep too few SMs busy: the K range is split over the CTAs of a
+// (1, 1, ksplit) thread-block cluster.  Each CTA accumulates its K slice, the
+// partial tiles meet in shared memory, and CTA r of the cluster reduces
+// columns [r*BN/ks, (r+1)*BN/ks) by reading every partial through distributed
+// shared memory in rank order (deterministic), then applies the epilogue.
+//
 // CTA = 4 warps: warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
 // allocator, all four the epilogue (warp w owns TMEM lanes 32w..32w+31).
-// Grid = (M/128, ceil(N/BN)).  Every wait is bounded; on expiry the kernel
-// records an error word and leaves through the normal exit (TMEM freed).
+// Grid = (M/128, ceil(N/BN), ksplit).  Launched with programmatic dependent
+// launch: the weight tiles of the first stages are requested before waiting
+// for the previous kernel (they do not depend on it).  Every wait is bounded;
+// on expiry the kernel records an error word, waits (bounded) for its own
+// copies in flight and leaves through the normal exit (TMEM freed).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -22,30 +32,65 @@ namespace b2d {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kGemmStages = 6;
 constexpr int kGemmThreads = 128;
+constexpr int kGemmMaxSplit = 8;  // portable cluster size
 constexpr uint64_t kGemmWaitNs = 200000000ull;  // 200 ms
 
 enum : int { EPI_F32 = 0, EPI_RESID_F32 = 1, EPI_SWIGLU_BF16 = 2 };
 
 struct GemmArgs {
-  int M, N, K;
-  float* y;                 // EPI_F32 / EPI_RESID_F32: [N][ldy] f32
-  const float* resid;       // EPI_RESID_F32: [N][ldy] (may equal y)
-  __nv_bfloat16* ybf;       // EPI_SWIGLU_BF16: [N][ldy] bf16, column m/2
-  int ldy;
-  uint32_t* err;            // status word: set (if still 0) when a wait runs out
+  int M = 0, N = 0, K = 0;
+  float* y = nullptr;                 // EPI_F32 / EPI_RESID_F32: [N][ldy] f32
+  const float* resid = nullptr;       // EPI_RESID_F32: [N][ldy] (may equal y)
+  __nv_bfloat16* ybf = nullptr;       // EPI_SWIGLU_BF16: [N][ldy] bf16, column m/2
+  int ldy = 0;
+  uint32_t* err = nullptr;            // status word: set (if still 0) when a wait runs out
+  int ksplit = 1;                     // 1..kGemmMaxSplit, <= K/64; > 1 needs a (1,1,ksplit) cluster launch
+  // EPI_RESID_F32 only, optional fused RMSNorm of the finished rows:
+  // norm_out[n][:] = bf16(y[n] * rsqrt(mean(y[n]^2) + eps) * norm_g), written
+  // by the last M tile to finish each column slice (ticket per slice).
+  const float* norm_g = nullptr;      // [M] gain, or nullptr (no norm)
+  __nv_bfloat16* norm_out = nullptr;  // [N][M]
+  uint32_t* tickets = nullptr;        // [ceil(N/BN) * ksplit], zero between launches
+  float norm_eps = 0.f;
 };
+
+// RMSNorm of rows [n_lo, n_hi) of y (row length M) by the whole CTA, one
+// warp per row; fixed summation order (model.py:94-98).
+__device__ __forceinline__ void gemm_norm_rows(const GemmArgs& g, int n_lo, int n_hi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int n = n_lo + warp; n < n_hi; n += kGemmThreads / 32) {
+    const float4* h = reinterpret_cast<const float4*>(g.y + static_cast<size_t>(n) * g.ldy);
+    float ss = 0.f;
+    for (int i = lane; i < g.M / 4; i += 32) {
+      const float4 v = __ldcg(h + i);
+      ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / static_cast<float>(g.M) + g.norm_eps);
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(g.norm_out + static_cast<size_t>(n) * g.M);
+    const float4* gg = reinterpret_cast<const float4*>(g.norm_g);
+    for (int i = lane; i < g.M / 4; i += 32) {
+      const float4 v = __ldcg(h + i), w = __ldg(gg + i);
+      o[2 * i] = __floats2bfloat162_rn(v.x * rs * w.x, v.y * rs * w.y);
+      o[2 * i + 1] = __floats2bfloat162_rn(v.z * rs * w.z, v.w * rs * w.w);
+    }
+  }
+}
 
 template <int BN>
 struct GemmSmem {
   static constexpr int A_BYTES = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int B_BYTES = BN * kGemmBK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int BARS = kGemmStages * STAGE;
-  static constexpr int BYTES = BARS + (2 * kGemmStages + 1) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int STAGES = (196608 / STAGE) < 6 ? (196608 / STAGE) : 6;
+  static constexpr int BARS = STAGES * STAGE;
+  static constexpr int RED_BYTES = BN * kGemmBM * 4;  // partial tile [BN][128] f32 (reuses the stages)
+  static constexpr int BYTES = BARS + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
   static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment for the swizzle atoms");
+  static_assert(RED_BYTES <= BARS, "the partial tile must fit in the stage buffers");
+  static_assert(BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 // Bounded wait: gives up after kGemmWaitNs of global time, records the error.
@@ -62,24 +107,63 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
   return true;
 }
 
+template <int EPI>
+__device__ __forceinline__ void gemm_store(const GemmArgs& g, float v, int row, int n, bool valid) {
+  if (EPI == EPI_SWIGLU_BF16) {
+    const float up = __shfl_xor_sync(0xffffffffu, v, 1);  // rows 2j / 2j+1 sit in adjacent lanes
+    if (valid && (row & 1) == 0) {
+      const float act = v * (1.0f / (1.0f + __expf(-v))) * up;
+      g.ybf[static_cast<size_t>(n) * g.ldy + (row >> 1)] = __float2bfloat16_rn(act);
+    }
+  } else if (valid) {
+    float out = v;
+    if (EPI == EPI_RESID_F32) out += g.resid[static_cast<size_t>(n) * g.ldy + row];
+    g.y[static_cast<size_t>(n) * g.ldy + row] = out;
+  }
+}
+
+// Rows row..row+3 of output column n (row % 4 == 0): SwiGLU pairs (2j, 2j+1)
+// lie inside the group.
+template <int EPI>
+__device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row, int n) {
+  if (EPI == EPI_SWIGLU_BF16) {
+    const float a0 = v.x * (1.0f / (1.0f + __expf(-v.x))) * v.y;
+    const float a1 = v.z * (1.0f / (1.0f + __expf(-v.z))) * v.w;
+    *reinterpret_cast<__nv_bfloat162*>(g.ybf + static_cast<size_t>(n) * g.ldy + (row >> 1)) =
+        __floats2bfloat162_rn(a0, a1);
+  } else {
+    float4* y = reinterpret_cast<float4*>(g.y + static_cast<size_t>(n) * g.ldy + row);
+    if (EPI == EPI_RESID_F32) {
+      const float4 r = *reinterpret_cast<const float4*>(g.resid + static_cast<size_t>(n) * g.ldy + row);
+      v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
+    }
+    *y = v;
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                const GemmArgs g) {
   using L = GemmSmem<BN>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int S = L::STAGES;
+  extern __shared__ uint8_t gemm_smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::BARS);
-  uint64_t* empty = full + kGemmStages;
-  uint64_t* done = empty + kGemmStages;
+  uint64_t* empty = full + S;
+  uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  __shared__ uint32_t s_norm_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * BN;
-  const int nk = g.K / kGemmBK;
+  const int ks = g.ksplit;
+  const int nk_all = g.K / kGemmBK;
+  const int kb0 = static_cast<int>(blockIdx.z) * nk_all / ks;
+  const int nk = (static_cast<int>(blockIdx.z) + 1) * nk_all / ks - kb0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -93,33 +177,43 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch();
 
+  int issued = 0;  // producer thread: loads requested
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     const uint64_t pol_w = l2_policy_evict_first();
     const uint64_t pol_x = l2_policy_evict_last();
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kGemmStages;
-      if (kb >= kGemmStages && !gemm_wait(&empty[s], ((kb / kGemmStages) - 1) & 1u, g.err)) break;
+    const int pre = nk < S ? nk : S;
+    for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
+      mbar_arrive_expect_tx(&full[i], L::STAGE);
+      tma_load_2d(sm + i * L::STAGE, &wmap, (kb0 + i) * kGemmBK, m0, &full[i], pol_w);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(sm + i * L::STAGE + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, n0, &full[i], pol_x);
+    issued = pre;
+    for (int i = pre; i < nk; ++i) {
+      const int s = i % S;
+      if (!gemm_wait(&empty[s], ((i / S) - 1) & 1u, g.err)) break;
       uint8_t* a = sm + s * L::STAGE;
       mbar_arrive_expect_tx(&full[s], L::STAGE);
-      tma_load_2d(a, &wmap, kb * kGemmBK, m0, &full[s], pol_w);
-      tma_load_2d(a + L::A_BYTES, &xmap, kb * kGemmBK, n0, &full[s], pol_x);
+      tma_load_2d(a, &wmap, (kb0 + i) * kGemmBK, m0, &full[s], pol_w);
+      tma_load_2d(a + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, n0, &full[s], pol_x);
+      issued = i + 1;
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     const uint32_t idesc = idesc_bf16_f32(kGemmBM, BN);
-    bool ok = true;
-    for (int kb = 0; kb < nk && ok; ++kb) {
-      const int s = kb % kGemmStages;
-      ok = gemm_wait(&full[s], (kb / kGemmStages) & 1u, g.err);
-      if (!ok) break;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % S;
+      if (!gemm_wait(&full[s], (i / S) & 1u, g.err)) break;
       tc_fence_after();
       const uint32_t a = smem_addr(sm + s * L::STAGE);
       const uint32_t b = a + L::A_BYTES;
 #pragma unroll
       for (int k = 0; k < kGemmBK / 16; ++k)
-        tc_mma_bf16(tmem, sdesc_kmajor_sw128(a + 32 * k), sdesc_kmajor_sw128(b + 32 * k), idesc, kb > 0 || k > 0);
+        tc_mma_bf16(tmem, sdesc_kmajor_sw128(a + 32 * k), sdesc_kmajor_sw128(b + 32 * k), idesc, i > 0 || k > 0);
       tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
     }
     tc_commit(done);  // accumulator complete (or the issued part of it)
@@ -127,29 +221,76 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
 
   // ---- epilogue: all four warps ----
   __syncwarp();
+  pdl_wait();  // the residual comes from earlier kernels
   const bool got = __all_sync(0xffffffffu, gemm_wait(done, 0, g.err));
   tc_fence_after();
-  const int row = m0 + warp * 32 + lane;  // weight row = output column m
+  const int r = warp * 32 + lane;  // accumulator row = weight row m0 + r
+  const int row = m0 + r;
+  int slice = blockIdx.y, j0 = 0, j1 = BN;  // output columns this CTA stores
+  if (ks == 1) {
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    float v[32];
-    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-    if (!got) continue;
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+      if (!got) continue;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int n = n0 + c0 + j;
-      if (EPI == EPI_SWIGLU_BF16) {
-        const float up = __shfl_xor_sync(0xffffffffu, v[j], 1);
-        if (c0 + j < BN && n < g.N && (lane & 1) == 0 && row < g.M) {
-          const float act = v[j] * (1.0f / (1.0f + __expf(-v[j]))) * up;
-          g.ybf[static_cast<size_t>(n) * g.ldy + (row >> 1)] = __float2bfloat16_rn(act);
-        }
-      } else if (c0 + j < BN && n < g.N && row < g.M) {
-        float out = v[j];
-        if (EPI == EPI_RESID_F32) out += g.resid[static_cast<size_t>(n) * g.ldy + row];
-        g.y[static_cast<size_t>(n) * g.ldy + row] = out;
+      for (int j = 0; j < 32; ++j) {
+        const int n = n0 + c0 + j;
+        gemm_store<EPI>(g, v[j], row, n, c0 + j < BN && n < g.N && row < g.M);
       }
     }
+  } else {
+    float* red = reinterpret_cast<float*>(sm);  // [BN][128]; every MMA has read its stage by now
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < BN) red[(c0 + j) * kGemmBM + r] = got ? v[j] : 0.f;
+    }
+    cluster_sync_all();
+    // CTA `rank` reduces columns [j0, j1): items of 4 consecutive rows, the
+    // partials summed in cluster-rank order (deterministic).
+    const int rank = static_cast<int>(cluster_ctarank());
+    slice = blockIdx.y * ks + rank;
+    j0 = rank * BN / ks;
+    j1 = (rank + 1) * BN / ks;
+    const int items = (j1 - j0) * (kGemmBM / 4);
+    const uint32_t red_base = smem_addr(red);
+#pragma unroll 1
+    for (int it = threadIdx.x; it < items; it += kGemmThreads) {
+      const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
+      const uint32_t off = red_base + 4u * (kGemmBM * j + r4);
+      float4 part[kGemmMaxSplit];  // all loads issued before the first add
+#pragma unroll
+      for (int z = 0; z < kGemmMaxSplit; ++z)
+        if (z < ks) part[z] = ld_dsmem_f32x4(mapa_shared(off, z));
+      float4 acc = part[0];
+#pragma unroll
+      for (int z = 1; z < kGemmMaxSplit; ++z)
+        if (z < ks) {
+          acc.x += part[z].x; acc.y += part[z].y; acc.z += part[z].z; acc.w += part[z].w;
+        }
+      const int n = n0 + j, rw = m0 + r4;
+      if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, acc, rw, n);
+    }
+    cluster_sync_all();  // no CTA leaves while another still reads its partial
+  }
+  if (EPI == EPI_RESID_F32 && g.norm_g != nullptr) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      s_norm_last = atomicAdd(&g.tickets[slice], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_norm_last) {  // every M tile of these columns is stored: normalise the rows
+      __threadfence();
+      if (threadIdx.x == 0) g.tickets[slice] = 0u;
+      gemm_norm_rows(g, n0 + j0, min(n0 + j1, g.N));
+    }
+  }
+  if (warp == 0 && lane == 0) {  // timeout paths: wait (bounded) for copies never consumed
+    for (int i = issued > S ? issued - S : 0; i < issued; ++i) gemm_wait(&full[i % S], (i / S) & 1u, g.err);
   }
   tc_fence_before();
   __syncthreads();
@@ -189,10 +330,21 @@ inline bool make_kmajor_map(CUtensorMap* map, const void* base, uint64_t inner, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-inline int gemm_bn_for(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 64); }
+inline int gemm_bn_for(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256))); }
+
+// K split so that the grid covers the SMs about once: tiles x ksplit <= sms.
+inline int gemm_ksplit_for(int M, int N, int K, int sms) {
+  const int bn = gemm_bn_for(N);
+  const int tiles = (M / kGemmBM) * ((N + bn - 1) / bn);
+  int ks = tiles > 0 ? sms / tiles : 1;
+  if (ks > kGemmMaxSplit) ks = kGemmMaxSplit;
+  if (ks > K / kGemmBK) ks = K / kGemmBK;
+  return ks < 1 ? 1 : ks;
+}
 
 template <int BN, int EPI>
-inline cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArgs& g, cudaStream_t st) {
+inline cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArgs& g, cudaStream_t st,
+                                 bool pdl) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -202,25 +354,49 @@ inline cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, c
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  dim3 grid(g.M / kGemmBM, (g.N + BN - 1) / BN);
-  gemm_tc_kernel<BN, EPI><<<grid, kGemmThreads, GemmSmem<BN>::BYTES, st>>>(wm, xm, g);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g.M / kGemmBM, (g.N + BN - 1) / BN, g.ksplit);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = GemmSmem<BN>::BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  unsigned na = 0;
+  if (g.ksplit > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = 1;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = static_cast<unsigned>(g.ksplit);
+    ++na;
+  }
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, EPI>, wm, xm, g);
 }
 
-// Requires M % 128 == 0 and K % 64 == 0; xmap's box rows must equal
-// gemm_bn_for(N).
+// Requires M % 128 == 0, K % 64 == 0, 1 <= ksplit <= min(8, K/64); xmap's box
+// rows must equal gemm_bn_for(N).
 inline cudaError_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArgs& g, int epi,
-                               cudaStream_t st) {
+                               cudaStream_t st, bool pdl = false) {
+  if (g.M % kGemmBM || g.K % kGemmBK || g.ksplit < 1 || g.ksplit > kGemmMaxSplit || g.ksplit > g.K / kGemmBK ||
+      epi < EPI_F32 || epi > EPI_SWIGLU_BF16)
+    return cudaErrorInvalidValue;
   const int bn = gemm_bn_for(g.N);
-#define B2D_GEMM_CASE(BNV)                                                       \
-  if (bn == BNV) {                                                               \
-    if (epi == EPI_F32) return launch_gemm_t<BNV, EPI_F32>(wm, xm, g, st);       \
-    if (epi == EPI_RESID_F32) return launch_gemm_t<BNV, EPI_RESID_F32>(wm, xm, g, st); \
-    return launch_gemm_t<BNV, EPI_SWIGLU_BF16>(wm, xm, g, st);                   \
+#define B2D_GEMM_CASE(BNV)                                                            \
+  if (bn == BNV) {                                                                    \
+    if (epi == EPI_F32) return launch_gemm_t<BNV, EPI_F32>(wm, xm, g, st, pdl);       \
+    if (epi == EPI_RESID_F32) return launch_gemm_t<BNV, EPI_RESID_F32>(wm, xm, g, st, pdl); \
+    return launch_gemm_t<BNV, EPI_SWIGLU_BF16>(wm, xm, g, st, pdl);                   \
   }
   B2D_GEMM_CASE(16)
   B2D_GEMM_CASE(32)
   B2D_GEMM_CASE(64)
+  B2D_GEMM_CASE(128)
+  B2D_GEMM_CASE(256)
 #undef B2D_GEMM_CASE
   return cudaErrorInvalidValue;
 }

@@ -178,8 +178,8 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
 }
 
 __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const SampleArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(smem_raw);
+  extern __shared__ __align__(16) uint8_t sampler_smem_raw[];
+  SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(sampler_smem_raw);
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int V = a.vocab;
   const float* lg = a.logits + static_cast<size_t>(b) * V;

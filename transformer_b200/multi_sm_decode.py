@@ -180,9 +180,15 @@ class DecodeEngine:
         self._trace = None
         return None
 
-    def debug_tune(self, poll_ns: int | None = None, max_inflight: int | None = None):
-        """Diagnostic knobs: back-off between failed polls (ns) and weight
-        copies in flight per CTA."""
+    def debug_tune(self, poll_ns: int | None = None, max_inflight: int | None = None,
+                   pdl: bool | None = None, ksplit: int | None = None):
+        """Diagnostic knobs: back-off between failed polls (ns), weight copies
+        in flight per CTA; batched step: programmatic dependent launch on/off,
+        forced K split (0 = automatic)."""
+        if pdl is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 3, int(bool(pdl))), "b2d_debug_tune")
+        if ksplit is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 4, int(ksplit)), "b2d_debug_tune")
         if poll_ns is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 1, int(poll_ns)), "b2d_debug_tune")
         if max_inflight is not None:
