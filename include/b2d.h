@@ -220,7 +220,10 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * exchange words (0 = spin); knob 2 = weight-stream copies in flight per CTA
  * (1..12, default 4); knob 3 = batched step with (1, default) or without (0)
  * programmatic dependent launch; knob 4 = batched step K split forced to
- * 1..8 (0 = automatic).
+ * 1..8 (0 = automatic); knob 5 = batched attention chunks (64 positions) per
+ * CTA forced to 1..32 (0 = automatic); knob 6 = device address of a uint64
+ * buffer [257 launches][256 CTAs][8] that the batched step's projections fill
+ * with global-timer stamps (0 = off).
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
 B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);

@@ -83,6 +83,23 @@ def test_paged_tiny_ragged_all_positions(engine_tiny_batched, params_tiny):
     _run_ragged(engine_tiny_batched, params_f32(params_tiny), CONFIG_TINY, prompts, rng, check_kv=True)
 
 
+@pytest.mark.parametrize("cpc,ks", [(1, 1), (3, 2), (32, 8)])
+def test_paged_tiny_work_splits(engine_tiny_batched, params_tiny, cpc, ks):
+    """Forced attention chunks per CTA (one chunk per CTA with multi-CTA
+    merges, uneven groups, the whole sequence in one CTA) and K splits of the
+    projections give the same parity."""
+    from transformer_b200.config import CONFIG_TINY
+    from transformer_b200.synth import params_f32
+    eng = engine_tiny_batched
+    rng = np.random.default_rng(200 + cpc)
+    prompts = [rng.integers(0, CONFIG_TINY.vocab_size, n).astype(np.int32) for n in (128, 70, 9)]
+    eng.debug_tune(att_cpc=cpc, ksplit=ks)
+    try:
+        _run_ragged(eng, params_f32(params_tiny), CONFIG_TINY, prompts, rng, check_every=7)
+    finally:
+        eng.debug_tune(att_cpc=0, ksplit=0)
+
+
 @pytest.mark.parametrize("B", [2, 17, 33, 64])
 def test_paged_tiny_batch_sizes(engine_tiny_batched, params_tiny, B):
     """Each projection tile width (16 / 32 / 64 rows) and a batch spanning

@@ -5,6 +5,7 @@
 // Nothing here allocates per step; workspaces are allocated once.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -122,12 +123,17 @@ struct b2d_ws {
   uint32_t* norm_tickets;  // fused-RMSNorm tickets of the residual projections
   bool no_pdl;             // diagnostics: launch without programmatic dependencies
   int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
+  int force_att_cpc;       // diagnostics: fixed attention chunks per CTA (0 = automatic)
+  uint64_t* gemm_trace;    // diagnostics: [launch][kTraceCtas][kGemmStamps] projection stamps, or null
   int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
 };
 
 namespace {
+constexpr int kTraceCtas = 256;        // projection CTAs stamped per launch (diagnostics)
+constexpr int kTraceLaunches = 4 * 64 + 1;  // stamped projection launches per step (n_layers <= 64)
+constexpr int kFusedNormRows = 2;           // see b2d_decode_step_paged
 inline int bn_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4; }
 
 // Launch with an optional programmatic dependency on the previous kernel of
@@ -261,8 +267,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
   if (e == cudaSuccess && max_batch > 1) {
     const size_t D = c.d_model, F = c.d_ff, Q = qkv, V = c.vocab_size;
-    const int bn_max = b2d::gemm_bn_for(max_batch);
-    ws->rows = (max_batch + bn_max - 1) / bn_max * bn_max;
+    ws->rows = (max_batch + 255) / 256 * 256;  // any tile width may be chosen (see gemm_plan)
     ws->att_chunks = (c.context_len + b2d::kAttChunk - 1) / b2d::kAttChunk;
     e = cudaMalloc(&ws->H, sizeof(float) * D * max_batch);
     if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * max_batch);
@@ -281,7 +286,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     const size_t nt = size_t((max_batch + 15) / 16) * b2d::kGemmMaxSplit;  // >= ceil(N/BN) * ksplit
     if (e == cudaSuccess) e = cudaMalloc(&ws->norm_tickets, sizeof(uint32_t) * nt);
     if (e == cudaSuccess) e = cudaMemset(ws->norm_tickets, 0, sizeof(uint32_t) * nt);
-    for (int i = 0; i < 5 && e == cudaSuccess && (16 << i) <= bn_max; ++i) {
+    for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
       const uint32_t box = 16u << i;
       if (!b2d::make_kmajor_map(&ws->xmap[i], ws->X, D, ws->rows, box) ||
           !b2d::make_kmajor_map(&ws->amap[i], ws->A, D, ws->rows, box) ||
@@ -383,6 +388,13 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
       if (value < 0 || value > b2d::kGemmMaxSplit) return B2D_ERR_INVALID_ARG;
       ws->force_ksplit = static_cast<int>(value);
       return B2D_OK;
+    case 5:  // batched step: force the attention's chunks per CTA (0 = automatic)
+      if (value < 0 || value > 32) return B2D_ERR_INVALID_ARG;
+      ws->force_att_cpc = static_cast<int>(value);
+      return B2D_OK;
+    case 6:  // batched step: projection stamp buffer (device address; 0 = off)
+      ws->gemm_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
+      return B2D_OK;
   }
   return B2D_ERR_INVALID_ARG;
 }
@@ -466,7 +478,8 @@ b2d_status ensure_weight_maps(b2d_model* m) {
   const uint64_t D = c.d_model, F = c.d_ff, Q = uint64_t(c.n_heads + 2 * c.n_kv_heads) * 64;
   if (Q % b2d::kGemmBM || D % b2d::kGemmBM || (2 * F) % b2d::kGemmBM || c.vocab_size % b2d::kGemmBM ||
       D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4 ||
-      c.context_len > 32 * b2d::kAttChunk)  // the attention merge holds one chunk per lane
+      c.context_len > 32 * b2d::kAttChunk ||  // the attention merge holds one chunk per lane
+      D > 2048)                               // the row RMSNorm holds a row in registers
     return B2D_ERR_UNSUPPORTED;
   CUtensorMap* maps = new (std::nothrow) CUtensorMap[4 * c.n_layers + 1];
   if (!maps) return B2D_ERR_NO_MEMORY;
@@ -503,7 +516,6 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const b2d_config& c = m->cfg;
   const int D = c.d_model, F = c.d_ff, Q = (c.n_heads + 2 * c.n_kv_heads) * 64, V = c.vocab_size;
-  const int mi = bn_index(b2d::gemm_bn_for(batch));
   uint32_t* status = &ws->ctl->status;
   float* logits = logits_dev ? logits_dev : ws->logits;
   const float* ln1 = reinterpret_cast<const float*>(m->w + m->lay.off_ln1);
@@ -511,11 +523,33 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
   const float* lnf = reinterpret_cast<const float*>(m->w + m->lay.off_lnf);
   const __nv_bfloat16* emb = reinterpret_cast<const __nv_bfloat16*>(m->w + m->lay.off_emb);
 
-  const int sms = m->grid;
   const bool pdl = !ws->no_pdl;
+  int gl = 0;  // projection launches so far (diagnostic stamps)
+  b2d::GemmArgs g{};
+  auto gemm = [&](const CUtensorMap& wm, const CUtensorMap* xmaps, int epi, const b2d::GemmPlan& pl) {
+    g.ksplit = pl.ksplit;
+    g.trace = ws->gemm_trace && gl < kTraceLaunches ? ws->gemm_trace + size_t(gl) * kTraceCtas * b2d::kGemmStamps
+                                                     : nullptr;
+    g.trace_ctas = kTraceCtas;
+    ++gl;
+    return b2d::launch_gemm(wm, xmaps[bn_index(pl.bn)], g, epi, st, pdl, pl.bn);
+  };
+  // Layer projections prefer tiles of at most 64 batch rows (more CTAs, a
+  // shorter epilogue each); the logits projection up to 256 (fewer re-reads
+  // of the 65 MB embedding).
+  b2d::GemmPlan p_qkv = b2d::gemm_plan(Q, batch, D, 64), p_o = b2d::gemm_plan(D, batch, D, 64);
+  b2d::GemmPlan p_gu = b2d::gemm_plan(2 * F, batch, D, 64), p_dn = b2d::gemm_plan(D, batch, F, 64);
+  b2d::GemmPlan p_lg = b2d::gemm_plan(V, batch, D, 256);
+  if (ws->force_ksplit) {  // clamped to each projection's K / 64
+    const int f = ws->force_ksplit;
+    p_qkv.ksplit = std::min(f, D / b2d::kGemmBK);
+    p_o.ksplit = std::min(f, D / b2d::kGemmBK);
+    p_gu.ksplit = std::min(f, D / b2d::kGemmBK);
+    p_dn.ksplit = std::min(f, F / b2d::kGemmBK);
+    p_lg.ksplit = std::min(f, D / b2d::kGemmBK);
+  }
   B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok_dev, V, D, ln1, c.rms_eps,
                     ws->H, ws->X, status), "embed");
-  b2d::GemmArgs g{};
   g.N = batch;
   g.err = status;
   g.tickets = ws->norm_tickets;
@@ -528,29 +562,45 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
   pa.part = ws->att_part; pa.tickets = ws->att_tickets; pa.max_chunks = ws->att_chunks;
-  int ks_qkv = b2d::gemm_ksplit_for(Q, batch, D, sms), ks_o = b2d::gemm_ksplit_for(D, batch, D, sms);
-  int ks_gu = b2d::gemm_ksplit_for(2 * F, batch, D, sms), ks_dn = b2d::gemm_ksplit_for(D, batch, F, sms);
-  int ks_lg = b2d::gemm_ksplit_for(V, batch, D, sms);
-  if (ws->force_ksplit) ks_qkv = ks_o = ks_gu = ks_dn = ks_lg = ws->force_ksplit;
-  for (int l = 0; l < c.n_layers; ++l) {
-    // X = RMSNorm(H, ln1[l]) was written by the embedding (l = 0) or the previous down projection
-    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.ksplit = ks_qkv; g.norm_g = nullptr;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 0], ws->xmap[mi], g, b2d::EPI_F32, st, pdl), "qkv");
-    pa.layer = l;
-    B2D_CUDA(launch_k(b2d::paged_attn_kernel, dim3(ws->att_chunks, c.n_kv_heads, batch), dim3(128), st, pdl, pa),
-             "attention");
-    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D; g.ksplit = ks_o;
-    g.norm_g = ln2 + size_t(l) * D; g.norm_out = ws->X;  // X = RMSNorm(Hm, ln2[l])
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 1], ws->amap[mi], g, b2d::EPI_RESID_F32, st, pdl), "o");
-    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F; g.ksplit = ks_gu; g.norm_g = nullptr;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 2], ws->xmap[mi], g, b2d::EPI_SWIGLU_BF16, st, pdl), "gate/up");
-    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D; g.ksplit = ks_dn;
-    g.norm_g = l + 1 < c.n_layers ? ln1 + size_t(l + 1) * D : lnf;  // next layer's ln1, or the final norm
-    g.norm_out = ws->X;
-    B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * l + 3], ws->actmap[mi], g, b2d::EPI_RESID_F32, st, pdl), "down");
+  {  // chunks per CTA: about 8 resident attention CTAs per SM over the whole (b, kv head, chunk) space
+    const int items = batch * c.n_kv_heads * ws->att_chunks, target = 8 * m->grid;
+    pa.cpc = (items + target - 1) / target;
+    if (pa.cpc < 1) pa.cpc = 1;
+    if (pa.cpc > ws->att_chunks) pa.cpc = ws->att_chunks;
+    if (ws->force_att_cpc) pa.cpc = ws->force_att_cpc;
   }
-  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V; g.ksplit = ks_lg; g.norm_g = nullptr;
-  B2D_CUDA(b2d::launch_gemm(m->wmaps[4 * c.n_layers], ws->xmap[mi], g, b2d::EPI_F32, st, pdl), "logits");
+  // RMSNorm of the residual stream: fused into the residual projection's
+  // epilogue (last M tile per column slice) when a slice has at most
+  // kFusedNormRows rows, else a separate one-CTA-per-row kernel.
+  auto norm_fused = [&](const b2d::GemmPlan& pl) { return (pl.bn + pl.ksplit - 1) / pl.ksplit <= kFusedNormRows; };
+  auto norm = [&](const float* h, const float* gain) {
+    return launch_k(b2d::rmsnorm_rows_kernel, dim3(batch), dim3(128), st, pdl, h, gain, D, c.rms_eps, ws->X);
+  };
+  for (int l = 0; l < c.n_layers; ++l) {
+    // X = RMSNorm(H, ln1[l]) was written by the embedding (l = 0) or after the previous down projection
+    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.norm_g = nullptr;
+    B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
+    pa.layer = l;
+    B2D_CUDA(launch_k(b2d::paged_attn_kernel, dim3((ws->att_chunks + pa.cpc - 1) / pa.cpc, c.n_kv_heads, batch),
+                      dim3(128), st, pdl, pa),
+             "attention");
+    const float* ln2_l = ln2 + size_t(l) * D;
+    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D; 
+    g.norm_g = norm_fused(p_o) ? ln2_l : nullptr;
+    g.norm_out = ws->X;
+    B2D_CUDA(gemm(m->wmaps[4 * l + 1], ws->amap, b2d::EPI_RESID_F32, p_o), "o");
+    if (!g.norm_g) B2D_CUDA(norm(ws->Hm, ln2_l), "rmsnorm");
+    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F; g.norm_g = nullptr;
+    B2D_CUDA(gemm(m->wmaps[4 * l + 2], ws->xmap, b2d::EPI_SWIGLU_BF16, p_gu), "gate/up");
+    const float* next_g = l + 1 < c.n_layers ? ln1 + size_t(l + 1) * D : lnf;  // next ln1, or the final norm
+    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D; 
+    g.norm_g = norm_fused(p_dn) ? next_g : nullptr;
+    g.norm_out = ws->X;
+    B2D_CUDA(gemm(m->wmaps[4 * l + 3], ws->actmap, b2d::EPI_RESID_F32, p_dn), "down");
+    if (!g.norm_g) B2D_CUDA(norm(ws->H, next_g), "rmsnorm");
+  }
+  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V; g.norm_g = nullptr;
+  B2D_CUDA(gemm(m->wmaps[4 * c.n_layers], ws->xmap, b2d::EPI_F32, p_lg), "logits");
   B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
                     next_tok_dev), "argmax");
   return B2D_OK;
@@ -579,7 +629,7 @@ b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
   g.ksplit = ks ? ks : b2d::gemm_ksplit_for(M, N, K, sms);
-  B2D_CUDA(b2d::launch_gemm(wm, xm, g, epi, st), "gemm launch");
+  B2D_CUDA(b2d::launch_gemm(wm, xm, g, epi, st, false, b2d::gemm_bn_for(N)), "gemm launch");
   uint32_t h = 0;
   B2D_CUDA(cudaMemcpyAsync(&h, err, sizeof(h), cudaMemcpyDeviceToHost, st), "read err");
   B2D_CUDA(cudaStreamSynchronize(st), "sync");

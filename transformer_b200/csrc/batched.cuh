@@ -57,6 +57,41 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ emb, const i
     X[static_cast<size_t>(b) * D + i] = __float2bfloat16_rn(__bfloat162float(e[i]) * r * __ldg(g + i));
 }
 
+// X[b][:] = bf16(H[b] * rsqrt(mean(H[b]^2) + eps) * g)   (model.py:94-98)
+// One CTA (128 threads) per row, the row held in registers (D <= 2048,
+// D % 4 == 0); fixed-order reduction.
+__global__ void __launch_bounds__(128) rmsnorm_rows_kernel(const float* __restrict__ H, const float* __restrict__ g,
+                                                           int D, float eps, __nv_bfloat16* __restrict__ X) {
+  __shared__ float red[4];
+  pdl_wait();
+  pdl_launch();
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float4* h = reinterpret_cast<const float4*>(H + static_cast<size_t>(b) * D);
+  const int q4 = D / 4;  // float4s per row, <= 4 per thread
+  float4 v[4] = {};
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (t + 128 * i < q4) {
+      v[i] = h[t + 128 * i];
+      ss = fmaf(v[i].x, v[i].x, ss); ss = fmaf(v[i].y, v[i].y, ss);
+      ss = fmaf(v[i].z, v[i].z, ss); ss = fmaf(v[i].w, v[i].w, ss);
+    }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  const float r = rsqrtf((red[0] + red[1] + red[2] + red[3]) / static_cast<float>(D) + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  __nv_bfloat162* x = reinterpret_cast<__nv_bfloat162*>(X + static_cast<size_t>(b) * D);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (t + 128 * i < q4) {
+      const float4 w = __ldg(g4 + t + 128 * i);
+      x[2 * (t + 128 * i)] = __floats2bfloat162_rn(v[i].x * r * w.x, v[i].y * r * w.y);
+      x[2 * (t + 128 * i) + 1] = __floats2bfloat162_rn(v[i].z * r * w.z, v[i].w * r * w.w);
+    }
+}
+
 struct PagedAttnArgs {
   const float* qkv;            // [B][(H+2KVH)*64] f32 (pre-RoPE q, k; v)
   const int32_t* pos;          // [B]
@@ -68,9 +103,10 @@ struct PagedAttnArgs {
   __nv_bfloat16* out;          // [B][ldo] bf16: head h at columns h*64..
   int ldo;
   uint32_t* status;            // set when a block-table entry is out of range
-  float* part;                 // [B][n_heads][max_chunks][kAttPart] chunk partials
+  float* part;                 // [B][n_heads][max_chunks][kAttPart] per-CTA partials
   uint32_t* tickets;           // [B][n_kv]; zero between launches (the combining CTA resets it)
   int max_chunks;              // >= ceil(ctx / kAttChunk)
+  int cpc;                     // chunks per CTA (>= 1)
 };
 
 constexpr int kAttChunk = 64;  // cached positions per CTA
@@ -81,49 +117,54 @@ __device__ __forceinline__ size_t page_row(const PagedAttnArgs& a, int blk, int 
   return ((((static_cast<size_t>(a.layer) * a.num_blocks + blk) * 2 + kv) * a.n_kv + g) * kPageTokens + slot) * 64;
 }
 
-// Split ("flash-decoding") paged attention.  grid (max_chunks, n_kv, B),
-// block 128: CTA (c, g, b) handles cached positions 64c..64c+63 of sequence b
-// for the GQA query heads of kv head g (warp w = query head g*GQA + w,
-// GQA <= 4).  The chunk holding the new position appends its K (post-RoPE) /
-// V to the pool.  K/V rows are staged in padded shared memory; scores are
-// lane-per-position, P.V lane-per-dimension.  Each CTA writes (m, l, o) for
-// its chunk; the last CTA of (b, g) to finish (ticket) merges the chunks in
-// chunk order and writes the bf16 attention output.  Math: model.py:100-131
-// (rotate-half RoPE, causal softmax over positions 0..p, GQA head sharing).
+// Split ("flash-decoding") paged attention.  grid (ceil(max_chunks / cpc),
+// n_kv, B), block 128: CTA (x, g, b) handles the cached positions of chunks
+// x*cpc .. x*cpc+cpc-1 (64 positions each) of sequence b for the GQA query
+// heads of kv head g (warp w = query head g*GQA + w, GQA <= 4), merging its
+// chunks with an online softmax; the next chunk's K/V loads are in flight
+// while the current chunk is computed.  The CTA holding the new position
+// appends its K (post-RoPE) / V to the pool.  K/V rows are staged in padded
+// shared memory; scores are lane-per-position, P.V lane-per-dimension.  When
+// a sequence spans several CTAs each writes (m, l, o) and the last to finish
+// (ticket) merges them in CTA order and writes the bf16 output.  Math:
+// model.py:100-131 (rotate-half RoPE, causal softmax over 0..p, GQA sharing).
 __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__ PagedAttnArgs a) {
   __shared__ __align__(16) __nv_bfloat16 sk[kAttChunk][kAttRow];
   __shared__ __align__(16) __nv_bfloat16 sv[kAttChunk][kAttRow];
   __shared__ __align__(16) float sq[4][64];
-  __shared__ float sp[4][kAttChunk];
+  __shared__ __align__(16) float sp[4][kAttChunk];
+  __shared__ __align__(16) __nv_bfloat16 skn[64], svn[64];  // the new position's K / V
   __shared__ uint32_t s_last;
-  const int c = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int x = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int GQA = a.n_heads / a.n_kv;
   pdl_wait();
   pdl_launch();
   const int p = a.pos[b];
   if (p < 0 || p >= a.ctx) {  // idle sequence: no cache write, zero output
-    if (c == 0 && warp < GQA)
+    if (x == 0 && warp < GQA)
       reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + warp) * 64)[lane] =
           __floats2bfloat162_rn(0.f, 0.f);
     return;
   }
   const int nch = p / kAttChunk + 1;
-  if (c >= nch) return;
-  const int base = c * kAttChunk;
-  const int npos = min(kAttChunk, p + 1 - base);  // rows 0..npos-1 = positions base..
+  const int c_lo = x * a.cpc;
+  if (c_lo >= nch) return;
+  const int c_hi = min(c_lo + a.cpc, nch);
+  const int ncta = (nch + a.cpc - 1) / a.cpc;  // CTAs sharing this (b, g)
   const int32_t* tb = a.table + static_cast<size_t>(b) * a.bps;
   // every page this CTA touches must exist
   bool bad = (p / kPageTokens) >= a.bps;
-  if (!bad && t < kAttChunk / kPageTokens && t * kPageTokens < npos) {
-    const int e = tb[base / kPageTokens + t];
+  const int pg_hi = (min(c_hi * kAttChunk, p + 1) - 1) / kPageTokens;
+  for (int i = c_lo * (kAttChunk / kPageTokens) + t; !bad && i <= pg_hi; i += 128) {
+    const int e = tb[i];
     bad = e < 0 || e >= a.num_blocks;
   }
   bad = __syncthreads_or(bad);
   if (bad && t == 0) atomicCAS(a.status, 0u, 0x203u);
 
   const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
-  const bool owner = c == nch - 1;  // this chunk holds position p
+  const bool owner = c_hi == nch;  // this CTA's last chunk holds position p
   if (t < 32) {
     const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
     for (int w = 0; w < GQA; ++w) {  // RoPE (rotate-half); q pre-scaled by 1/sqrt(64) (exact)
@@ -136,107 +177,142 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
       const float* k = row + a.n_heads * 64 + g * 64;
       const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
       const float klo = k[lane], khi = k[lane + 32];
-      const int r = p - base;
-      const __nv_bfloat16 k0 = __float2bfloat16_rn(klo * cs - khi * sn);
-      const __nv_bfloat16 k1 = __float2bfloat16_rn(klo * sn + khi * cs);
-      sk[r][lane] = k0;
-      sk[r][lane + 32] = k1;
-      sv[r][lane] = __float2bfloat16_rn(v[lane]);
-      sv[r][lane + 32] = __float2bfloat16_rn(v[lane + 32]);
+      skn[lane] = __float2bfloat16_rn(klo * cs - khi * sn);
+      skn[lane + 32] = __float2bfloat16_rn(klo * sn + khi * cs);
+      svn[lane] = __float2bfloat16_rn(v[lane]);
+      svn[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
       if (!bad) {
         const int blk = tb[p / kPageTokens], slot = p % kPageTokens;
         __nv_bfloat16* kd = a.pool + page_row(a, blk, 0, g, slot);
         __nv_bfloat16* vd = a.pool + page_row(a, blk, 1, g, slot);
-        kd[lane] = k0;
-        kd[lane + 32] = k1;
-        vd[lane] = sv[r][lane];
-        vd[lane + 32] = sv[r][lane + 32];
+        kd[lane] = skn[lane];
+        kd[lane + 32] = skn[lane + 32];
+        vd[lane] = svn[lane];
+        vd[lane + 32] = svn[lane + 32];
       }
     }
   }
-  if (!bad) {  // stage the chunk's cached rows (all but p): 8 x 16 B per row
+
+  // thread t stages rows (t + 128 i) >> 3, 16-byte column (t + 128 i) & 7, i < 4
+  uint4 kr[4] = {}, vr[4] = {};
+  auto fetch = [&](int c) {
+    const int base = c * kAttChunk;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = t + 128 * i, r = idx >> 3, cc = idx & 7, pp = base + r;
-      if (r < npos && pp != p) {
+      if (!bad && pp < p) {
         const int blk = tb[pp / kPageTokens], slot = pp % kPageTokens;
-        *reinterpret_cast<uint4*>(&sk[r][cc * 8]) =
-            __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 0, g, slot)) + cc);
-        *reinterpret_cast<uint4*>(&sv[r][cc * 8]) =
-            __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 1, g, slot)) + cc);
+        kr[i] = __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 0, g, slot)) + cc);
+        vr[i] = __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 1, g, slot)) + cc);
       }
+    }
+  };
+  fetch(c_lo);
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  const int h = g * GQA + warp;
+  for (int c = c_lo; c < c_hi; ++c) {
+    const int base = c * kAttChunk;
+    const int npos = min(kAttChunk, p + 1 - base);  // rows 0..npos-1 = positions base..
+    __syncthreads();  // the previous chunk's reads of sk / sv / sp are done
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = t + 128 * i, r = idx >> 3, cc = idx & 7, pp = base + r;
+      if (pp < p) {
+        *reinterpret_cast<uint4*>(&sk[r][cc * 8]) = kr[i];
+        *reinterpret_cast<uint4*>(&sv[r][cc * 8]) = vr[i];
+      } else if (pp == p) {
+        *reinterpret_cast<uint4*>(&sk[r][cc * 8]) = reinterpret_cast<const uint4*>(skn)[cc];
+        *reinterpret_cast<uint4*>(&sv[r][cc * 8]) = reinterpret_cast<const uint4*>(svn)[cc];
+      } else {  // past p: zero V so the 4-row P.V steps below read finite values
+        *reinterpret_cast<uint4*>(&sv[r][cc * 8]) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    __syncthreads();
+    if (c + 1 < c_hi) fetch(c + 1);  // in flight during this chunk's math
+    if (warp < GQA && !bad) {
+      float sc[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = lane + 32 * half;
+        float d = -INFINITY;
+        if (r < npos) {
+          d = 0.f;
+          const float4* q4 = reinterpret_cast<const float4*>(sq[warp]);
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            const uint4 w = *reinterpret_cast<const uint4*>(&sk[r][cc * 8]);
+            const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+            d = fmaf(qa.x, bf16_lo(w.x), d); d = fmaf(qa.y, bf16_hi(w.x), d);
+            d = fmaf(qa.z, bf16_lo(w.y), d); d = fmaf(qa.w, bf16_hi(w.y), d);
+            d = fmaf(qb.x, bf16_lo(w.z), d); d = fmaf(qb.y, bf16_hi(w.z), d);
+            d = fmaf(qb.z, bf16_lo(w.w), d); d = fmaf(qb.w, bf16_hi(w.w), d);
+          }
+        }
+        sc[half] = d;
+      }
+      float mc = fmaxf(sc[0], sc[1]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
+      const float mn = fmaxf(m, mc);  // finite: every chunk has >= 1 position
+      const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
+      const float e0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn);
+      const float e1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn);
+      sp[warp][lane] = e0;
+      sp[warp][lane + 32] = e1;
+      float ls = e0 + e1;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      __syncwarp();
+      float a0 = 0.f, a1 = 0.f;  // rows npos.. have p = 0 and V = 0
+#pragma unroll 2
+      for (int r = 0; r < npos; r += 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&sp[warp][r]);
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(&sv[r][2 * lane]);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(&sv[r + 1][2 * lane]);
+        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(&sv[r + 2][2 * lane]);
+        const uint32_t v3 = *reinterpret_cast<const uint32_t*>(&sv[r + 3][2 * lane]);
+        a0 = fmaf(p4.x, bf16_lo(v0), a0); a1 = fmaf(p4.x, bf16_hi(v0), a1);
+        a0 = fmaf(p4.y, bf16_lo(v1), a0); a1 = fmaf(p4.y, bf16_hi(v1), a1);
+        a0 = fmaf(p4.z, bf16_lo(v2), a0); a1 = fmaf(p4.z, bf16_hi(v2), a1);
+        a0 = fmaf(p4.w, bf16_lo(v3), a0); a1 = fmaf(p4.w, bf16_hi(v3), a1);
+      }
+      l = fmaf(l, alpha, ls);
+      o0 = fmaf(o0, alpha, a0);
+      o1 = fmaf(o1, alpha, a1);
+      m = mn;
     }
   }
-  __syncthreads();
 
-  const int h = g * GQA + warp;
-  float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks + c) * kAttPart;
-  if (warp < GQA) {
-    float sc[2];
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = lane + 32 * half;
-      float d = -INFINITY;
-      if (r < npos && !bad) {
-        d = 0.f;
-        const float4* q4 = reinterpret_cast<const float4*>(sq[warp]);
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          const uint4 w = *reinterpret_cast<const uint4*>(&sk[r][cc * 8]);
-          const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
-          d = fmaf(qa.x, bf16_lo(w.x), d); d = fmaf(qa.y, bf16_hi(w.x), d);
-          d = fmaf(qa.z, bf16_lo(w.y), d); d = fmaf(qa.w, bf16_hi(w.y), d);
-          d = fmaf(qb.x, bf16_lo(w.z), d); d = fmaf(qb.y, bf16_hi(w.z), d);
-          d = fmaf(qb.z, bf16_lo(w.w), d); d = fmaf(qb.w, bf16_hi(w.w), d);
-        }
-      }
-      sc[half] = d;
-    }
-    float m = fmaxf(sc[0], sc[1]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float e0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - m);
-    const float e1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - m);
-    sp[warp][lane] = e0;
-    sp[warp][lane + 32] = e1;
-    float l = e0 + e1;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    __syncwarp();
-    float o0 = 0.f, o1 = 0.f;
-    for (int r = 0; r < (bad ? 0 : npos); ++r) {
-      const float pr = sp[warp][r];
-      const uint32_t vw = *reinterpret_cast<const uint32_t*>(&sv[r][2 * lane]);
-      o0 = fmaf(pr, bf16_lo(vw), o0);
-      o1 = fmaf(pr, bf16_hi(vw), o1);
-    }
-    if (nch == 1) {  // single chunk: final output directly
+  if (ncta == 1) {  // the whole sequence in this CTA: final output directly
+    if (warp < GQA) {
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
           __floats2bfloat162_rn(o0 * inv, o1 * inv);
-    } else {
-      reinterpret_cast<float2*>(part + 4)[lane] = make_float2(o0, o1);
-      if (lane == 0) {
-        part[0] = bad ? -INFINITY : m;
-        part[1] = l;
-      }
+    }
+    return;
+  }
+  if (warp < GQA) {
+    float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks + x) * kAttPart;
+    reinterpret_cast<float2*>(part + 4)[lane] = make_float2(o0, o1);
+    if (lane == 0) {
+      part[0] = bad ? -INFINITY : m;
+      part[1] = l;
     }
   }
-  if (nch == 1) return;
   __threadfence();
   __syncthreads();
   if (t == 0) {
     const uint32_t prev = atomicAdd(&a.tickets[b * a.n_kv + g], 1u);
-    s_last = prev == static_cast<uint32_t>(nch - 1);
+    s_last = prev == static_cast<uint32_t>(ncta - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   if (t == 0) a.tickets[b * a.n_kv + g] = 0u;
-  if (warp < GQA) {  // merge the chunks of head h in chunk order (lane c holds chunk c's m, l)
+  if (warp < GQA) {  // merge the CTAs' partials of head h in CTA order (lane j holds CTA j's m, l)
     const float* ph = a.part + (static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks * kAttPart;
     float mc = -INFINITY, lc = 0.f;
-    if (lane < nch) {
+    if (lane < ncta) {
       mc = __ldcg(ph + lane * kAttPart);
       lc = __ldcg(ph + lane * kAttPart + 1);
     }
@@ -247,17 +323,17 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
     float L = wl * lc;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    float o0 = 0.f, o1 = 0.f;
+    float r0 = 0.f, r1 = 0.f;
 #pragma unroll 8
-    for (int cc = 0; cc < nch; ++cc) {
-      const float wgt = __shfl_sync(0xffffffffu, wl, cc);
-      const float2 oc = __ldcg(reinterpret_cast<const float2*>(ph + cc * kAttPart + 4) + lane);
-      o0 = fmaf(wgt, oc.x, o0);
-      o1 = fmaf(wgt, oc.y, o1);
+    for (int j = 0; j < ncta; ++j) {
+      const float wgt = __shfl_sync(0xffffffffu, wl, j);
+      const float2 oc = __ldcg(reinterpret_cast<const float2*>(ph + j * kAttPart + 4) + lane);
+      r0 = fmaf(wgt, oc.x, r0);
+      r1 = fmaf(wgt, oc.y, r1);
     }
     const float inv = L > 0.f ? 1.0f / L : 0.f;
     reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
-        __floats2bfloat162_rn(o0 * inv, o1 * inv);
+        __floats2bfloat162_rn(r0 * inv, r1 * inv);
   }
 }
 

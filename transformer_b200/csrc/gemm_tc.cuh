@@ -53,7 +53,20 @@ struct GemmArgs {
   __nv_bfloat16* norm_out = nullptr;  // [N][M]
   uint32_t* tickets = nullptr;        // [ceil(N/BN) * ksplit], zero between launches
   float norm_eps = 0.f;
+  // diagnostics: global-timer stamps [cta][kGemmStamps] (CTAs >= trace_ctas skipped), or nullptr
+  uint64_t* trace = nullptr;
+  int trace_ctas = 0;
 };
+
+// Stamp slots: 0 entry, 1 prologue done, 2 producer past the programmatic
+// wait, 3 first stage landed (MMA thread), 4 accumulator complete, 5 partial
+// tiles exchanged (cluster barrier), 6 outputs stored, 7 exit.
+constexpr int kGemmStamps = 8;
+__device__ __forceinline__ void gemm_stamp(const GemmArgs& g, int slot) {
+  if (g.trace == nullptr) return;
+  const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (cta < g.trace_ctas) g.trace[static_cast<size_t>(cta) * kGemmStamps + slot] = globaltimer_ns();
+}
 
 // RMSNorm of rows [n_lo, n_hi) of y (row length M) by the whole CTA, one
 // warp per row; fixed summation order (model.py:94-98).
@@ -107,21 +120,6 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
   return true;
 }
 
-template <int EPI>
-__device__ __forceinline__ void gemm_store(const GemmArgs& g, float v, int row, int n, bool valid) {
-  if (EPI == EPI_SWIGLU_BF16) {
-    const float up = __shfl_xor_sync(0xffffffffu, v, 1);  // rows 2j / 2j+1 sit in adjacent lanes
-    if (valid && (row & 1) == 0) {
-      const float act = v * (1.0f / (1.0f + __expf(-v))) * up;
-      g.ybf[static_cast<size_t>(n) * g.ldy + (row >> 1)] = __float2bfloat16_rn(act);
-    }
-  } else if (valid) {
-    float out = v;
-    if (EPI == EPI_RESID_F32) out += g.resid[static_cast<size_t>(n) * g.ldy + row];
-    g.y[static_cast<size_t>(n) * g.ldy + row] = out;
-  }
-}
-
 // Rows row..row+3 of output column n (row % 4 == 0): SwiGLU pairs (2j, 2j+1)
 // lie inside the group.
 template <int EPI>
@@ -163,6 +161,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   const int nk = (static_cast<int>(blockIdx.z) + 1) * nk_all / ks - kb0;
 
   if (threadIdx.x == 0) {
+    gemm_stamp(g, 0);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -178,6 +177,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch();
+  if (threadIdx.x == 0) gemm_stamp(g, 1);
 
   int issued = 0;  // producer thread: loads requested
   if (warp == 0 && lane == 0) {
@@ -190,6 +190,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
       tma_load_2d(sm + i * L::STAGE, &wmap, (kb0 + i) * kGemmBK, m0, &full[i], pol_w);
     }
     pdl_wait();
+    gemm_stamp(g, 2);
     for (int i = 0; i < pre; ++i)
       tma_load_2d(sm + i * L::STAGE + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, n0, &full[i], pol_x);
     issued = pre;
@@ -208,6 +209,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
     for (int i = 0; i < nk; ++i) {
       const int s = i % S;
       if (!gemm_wait(&full[s], (i / S) & 1u, g.err)) break;
+      if (i == 0) gemm_stamp(g, 3);
       tc_fence_after();
       const uint32_t a = smem_addr(sm + s * L::STAGE);
       const uint32_t b = a + L::A_BYTES;
@@ -224,59 +226,71 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   pdl_wait();  // the residual comes from earlier kernels
   const bool got = __all_sync(0xffffffffu, gemm_wait(done, 0, g.err));
   tc_fence_after();
+  if (threadIdx.x == 0) gemm_stamp(g, 4);
   const int r = warp * 32 + lane;  // accumulator row = weight row m0 + r
-  const int row = m0 + r;
   int slice = blockIdx.y, j0 = 0, j1 = BN;  // output columns this CTA stores
-  if (ks == 1) {
+  // The accumulator goes to shared memory as [BN][128] f32; the outputs are
+  // then written as items of 4 consecutive rows (float4 / bf16x2 stores).
+  // With a K split, the cluster's partial tiles are summed in rank order
+  // through distributed shared memory and CTA `rank` stores columns
+  // [rank*BN/ks, (rank+1)*BN/ks).
+  float* red = reinterpret_cast<float*>(sm);  // every MMA has read its stage by now
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-      if (!got) continue;
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    float v[32];
+    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = n0 + c0 + j;
-        gemm_store<EPI>(g, v[j], row, n, c0 + j < BN && n < g.N && row < g.M);
-      }
-    }
-  } else {
-    float* red = reinterpret_cast<float*>(sm);  // [BN][128]; every MMA has read its stage by now
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      float v[32];
-      tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < BN) red[(c0 + j) * kGemmBM + r] = got ? v[j] : 0.f;
-    }
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j < BN) red[(c0 + j) * kGemmBM + r] = got ? v[j] : 0.f;
+  }
+  if (ks > 1) {
     cluster_sync_all();
-    // CTA `rank` reduces columns [j0, j1): items of 4 consecutive rows, the
-    // partials summed in cluster-rank order (deterministic).
     const int rank = static_cast<int>(cluster_ctarank());
     slice = blockIdx.y * ks + rank;
     j0 = rank * BN / ks;
     j1 = (rank + 1) * BN / ks;
-    const int items = (j1 - j0) * (kGemmBM / 4);
-    const uint32_t red_base = smem_addr(red);
-#pragma unroll 1
-    for (int it = threadIdx.x; it < items; it += kGemmThreads) {
-      const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
-      const uint32_t off = red_base + 4u * (kGemmBM * j + r4);
-      float4 part[kGemmMaxSplit];  // all loads issued before the first add
-#pragma unroll
-      for (int z = 0; z < kGemmMaxSplit; ++z)
-        if (z < ks) part[z] = ld_dsmem_f32x4(mapa_shared(off, z));
-      float4 acc = part[0];
-#pragma unroll
-      for (int z = 1; z < kGemmMaxSplit; ++z)
-        if (z < ks) {
-          acc.x += part[z].x; acc.y += part[z].y; acc.z += part[z].z; acc.w += part[z].w;
-        }
-      const int n = n0 + j, rw = m0 + r4;
-      if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, acc, rw, n);
-    }
-    cluster_sync_all();  // no CTA leaves while another still reads its partial
+  } else {
+    __syncthreads();
   }
+  if (threadIdx.x == 0) gemm_stamp(g, 5);
+  const int items = (j1 - j0) * (kGemmBM / 4);
+  const uint32_t red_base = smem_addr(red);
+#pragma unroll 1
+  for (int it0 = threadIdx.x; it0 < items; it0 += 2 * kGemmThreads) {
+    float4 part[2][kGemmMaxSplit];  // both items' loads issued before the first add
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int it = it0 + u * kGemmThreads;
+      if (it < items) {
+        const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
+        if (ks == 1) {
+          part[u][0] = *reinterpret_cast<const float4*>(red + kGemmBM * j + r4);
+        } else {
+          const uint32_t off = red_base + 4u * (kGemmBM * j + r4);
+#pragma unroll
+          for (int z = 0; z < kGemmMaxSplit; ++z)
+            if (z < ks) part[u][z] = ld_dsmem_f32x4(mapa_shared(off, z));
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int it = it0 + u * kGemmThreads;
+      if (it < items) {
+        float4 acc = part[u][0];
+#pragma unroll
+        for (int z = 1; z < kGemmMaxSplit; ++z)
+          if (z < ks) {
+            acc.x += part[u][z].x; acc.y += part[u][z].y; acc.z += part[u][z].z; acc.w += part[u][z].w;
+          }
+        const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
+        const int n = n0 + j, rw = m0 + r4;
+        if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, acc, rw, n);
+      }
+    }
+  }
+  if (ks > 1) cluster_sync_all();  // no CTA leaves while another still reads its partial
+  if (threadIdx.x == 0) gemm_stamp(g, 6);
   if (EPI == EPI_RESID_F32 && g.norm_g != nullptr) {
     __threadfence();
     __syncthreads();
@@ -294,6 +308,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) gemm_stamp(g, 7);
   if (warp == 2) tmem_dealloc(tmem, L::TMEM_COLS);
 }
 
@@ -330,11 +345,88 @@ inline bool make_kmajor_map(CUtensorMap* map, const void* base, uint64_t inner, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-inline int gemm_bn_for(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256))); }
+// Batch rows per tile: the smallest width covering N, at most `cap`.
+inline int gemm_bn_for(int n, int cap = 256) {
+  const int bn = n <= 16 ? 16 : (n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256)));
+  return bn < cap ? bn : cap;
+}
 
-// K split so that the grid covers the SMs about once: tiles x ksplit <= sms.
-inline int gemm_ksplit_for(int M, int N, int K, int sms) {
-  const int bn = gemm_bn_for(N);
+template <int BN>
+inline cudaError_t gemm_set_smem_attr() {
+  static bool done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || done[dev]) return cudaSuccess;
+  const int bytes = GemmSmem<BN>::BYTES;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_RESID_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI_SWIGLU_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
+}
+
+// Clusters of `ks` CTAs of the BN-wide kernel that the device runs at once
+// (occupancy query, cached per device).
+template <int BN>
+inline int gemm_max_clusters_t(int ks) {
+  static int cache[64][kGemmMaxSplit + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || ks < 1 || ks > kGemmMaxSplit) return 0;
+  if (cache[dev][ks] == 0) {
+    if (gemm_set_smem_attr<BN>() != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, ks);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmSmem<BN>::BYTES;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = static_cast<unsigned>(ks);
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_kernel<BN, EPI_F32>, &cfg) != cudaSuccess || n < 1) n = 1;
+    cache[dev][ks] = n;
+  }
+  return cache[dev][ks];
+}
+
+inline int gemm_max_clusters(int bn, int ks) {
+  switch (bn) {
+    case 16: return gemm_max_clusters_t<16>(ks);
+    case 32: return gemm_max_clusters_t<32>(ks);
+    case 64: return gemm_max_clusters_t<64>(ks);
+    case 128: return gemm_max_clusters_t<128>(ks);
+    default: return gemm_max_clusters_t<256>(ks);
+  }
+}
+
+struct GemmPlan {
+  int bn, ksplit;
+};
+
+// Tile width and K split of one projection: the narrowest tile (>= the
+// batch's width, <= bn_cap unless the grid would need a second wave) whose
+// tiles fit in one wave, then the largest K split whose clusters all fit at
+// once.
+inline GemmPlan gemm_plan(int M, int N, int K, int bn_cap) {
+  const int mt = M / kGemmBM;
+  int bn = gemm_bn_for(N, bn_cap);
+  while (bn < 256 && mt * ((N + bn - 1) / bn) > gemm_max_clusters(bn, 1)) bn *= 2;
+  const int tiles = mt * ((N + bn - 1) / bn);
+  int ks = 1;
+  for (int k = 2; k <= kGemmMaxSplit && k <= K / kGemmBK; ++k)
+    if (tiles <= gemm_max_clusters(bn, k)) ks = k;
+  return {bn, ks};
+}
+
+// K split so that the grid covers the SMs about once (test hook default).
+inline int gemm_ksplit_for(int M, int N, int K, int sms, int bn_cap = 256) {
+  const int bn = gemm_bn_for(N, bn_cap);
   const int tiles = (M / kGemmBM) * ((N + bn - 1) / bn);
   int ks = tiles > 0 ? sms / tiles : 1;
   if (ks > kGemmMaxSplit) ks = kGemmMaxSplit;
@@ -345,15 +437,8 @@ inline int gemm_ksplit_for(int M, int N, int K, int sms) {
 template <int BN, int EPI>
 inline cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArgs& g, cudaStream_t st,
                                  bool pdl) {
-  static bool attr[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GemmSmem<BN>::BYTES);
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
+  cudaError_t e = gemm_set_smem_attr<BN>();
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g.M / kGemmBM, (g.N + BN - 1) / BN, g.ksplit);
   cfg.blockDim = dim3(kGemmThreads);
@@ -379,19 +464,19 @@ inline cudaError_t launch_gemm_t(const CUtensorMap& wm, const CUtensorMap& xm, c
 }
 
 // Requires M % 128 == 0, K % 64 == 0, 1 <= ksplit <= min(8, K/64); xmap's box
-// rows must equal gemm_bn_for(N).
+// rows must equal `bn` (a supported tile width).
 inline cudaError_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, const GemmArgs& g, int epi,
-                               cudaStream_t st, bool pdl = false) {
+                               cudaStream_t st, bool pdl, int bn) {
   if (g.M % kGemmBM || g.K % kGemmBK || g.ksplit < 1 || g.ksplit > kGemmMaxSplit || g.ksplit > g.K / kGemmBK ||
       epi < EPI_F32 || epi > EPI_SWIGLU_BF16)
     return cudaErrorInvalidValue;
-  const int bn = gemm_bn_for(g.N);
 #define B2D_GEMM_CASE(BNV)                                                            \
   if (bn == BNV) {                                                                    \
     if (epi == EPI_F32) return launch_gemm_t<BNV, EPI_F32>(wm, xm, g, st, pdl);       \
     if (epi == EPI_RESID_F32) return launch_gemm_t<BNV, EPI_RESID_F32>(wm, xm, g, st, pdl); \
     return launch_gemm_t<BNV, EPI_SWIGLU_BF16>(wm, xm, g, st, pdl);                   \
   }
+  if (bn != 16 && bn != 32 && bn != 64 && bn != 128 && bn != 256) return cudaErrorInvalidValue;
   B2D_GEMM_CASE(16)
   B2D_GEMM_CASE(32)
   B2D_GEMM_CASE(64)
