@@ -1,0 +1,168 @@
+"""Profile the decode kernels (the reference's ``profile_kernels.py`` for this
+engine).
+
+    python profile_kernels.py                         # B=1 megakernel, config 1
+    python profile_kernels.py --mode paged --batch 256 --pos 64
+    python profile_kernels.py --weights weights.pkl   # a trained checkpoint
+
+``measure_decode`` and ``compute_memory_stats`` keep the reference's names,
+arguments and results (``profile_kernels.py:44-87``): a host loop of
+``multi_sm_decode_nlayer`` calls with an ``int()`` read per token, median of
+``n_runs``, and the reference's theoretical memory figures.  The roofline line
+uses this engine's algorithmic bytes (weights once, the KV rows actually read,
+one row written) and the measured HBM copy bandwidth.
+
+``--mode paged`` runs the batched step over a paged KV pool with every
+sequence at ``--pos`` (the pool holds zeros: the step's work does not depend
+on the cached values), launched eagerly ``--warmup`` + ``--steps`` times; it is
+the small, self-contained case the ncu captures use.
+
+Without ``--weights`` the model is the seeded synthetic 306M decoder
+(N(0,0.02) bf16 weights, seed 0); with it, a reference checkpoint
+(``{"params": ..., "config": ...}`` as written by the reference's trainer,
+``generate.py:161-164``) is packed instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pickle
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+
+def load_params(path):
+    """``profile_kernels.py:21-25``: a pickled checkpoint's params and config."""
+    with open(path, "rb") as f:
+        saved = pickle.load(f)
+    params = {k: np.asarray(v) for k, v in saved["params"].items()}
+    return params, saved["config"]
+
+
+def measure_decode(w, config, tok, start_pos, kv_packed, n_tokens=128, n_runs=10):
+    """``profile_kernels.py:44-64``: median wall time (ms) of ``n_tokens``
+    greedy steps through ``multi_sm_decode_nlayer`` with a host read of every
+    token, after 5 warm-up steps; returns (ms, tokens of the last run)."""
+    from transformer_b200.multi_sm_decode import multi_sm_decode_nlayer
+    kv_tmp = kv_packed.clone()
+    t = tok
+    for i in range(5):
+        t, _, kv_tmp = multi_sm_decode_nlayer(w, config, t, start_pos + i, kv_tmp)
+        _ = int(t)
+    times, all_tokens = [], []
+    for _ in range(n_runs):
+        kv_tmp.copy_(kv_packed)
+        t = tok
+        tokens = []
+        t0 = time.perf_counter()
+        for i in range(n_tokens):
+            t, _, kv_tmp = multi_sm_decode_nlayer(w, config, t, start_pos + i, kv_tmp)
+            tokens.append(int(t))
+        times.append(time.perf_counter() - t0)
+        all_tokens = tokens
+    return float(np.median(times)) * 1000, all_tokens
+
+
+def compute_memory_stats(config):
+    """``profile_kernels.py:67-87``: theoretical weight and KV sizes (MB)."""
+    c = config if isinstance(config, dict) else config.as_dict()
+    d, n_layers, d_head, ctx = c["d_model"], c["n_layers"], c["d_head"], c["context_len"]
+    n_kv_heads = c.get("n_kv_heads", c["n_heads"])
+    d_kv = n_kv_heads * d_head
+    d_ff = c.get("d_ff", 4 * d)
+    per_layer = d + d * d + d * d_kv + d * d_kv + d * d + d + d * d_ff + d * d_ff + d_ff * d
+    weight_bytes = (c["vocab_size"] * d + n_layers * per_layer + d) * 2
+    kv_total = n_layers * 2 * n_kv_heads * ctx * d_head * 2
+    return {"weight_buffer_mb": weight_bytes / 1e6, "kv_cache_mb": kv_total / 1e6,
+            "total_inference_mb": (weight_bytes + kv_total) / 1e6}
+
+
+def hbm_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_b1(w, cfg, args, torch):
+    from transformer_b200.multi_sm_decode import engine_for
+    from transformer_b200.synth import prompt_cfg1
+    eng = engine_for(w)
+    prompt = prompt_cfg1(cfg)
+    kv = eng.new_kv()
+    first = eng.prefill(prompt, kv)
+    tok = int(torch.argmax(first).item())
+    ms, tokens = measure_decode(w, cfg, tok, len(prompt), kv, args.gen_len, args.n_runs)
+    us = ms * 1000 / args.gen_len
+    alg = float(np.mean([cfg.step_bytes([len(prompt) + i]) for i in range(args.gen_len)]))
+    peak, kind = hbm_peak()
+    return {"mode": "b1", "gen_len": args.gen_len, "host_loop_us_per_token": us,
+            "tok_s": 1e6 / us, "hbm_frac_host_loop": alg / (us * 1e-6) / 1e9 / peak,
+            "peak_gbs": peak, "peak_source": kind, "first_tokens": tokens[:8]}
+
+
+def profile_paged(w, cfg, args, torch):
+    from transformer_b200.batched import BatchedDecoder
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    dec = BatchedDecoder(eng, args.batch, seed=args.batch)
+    dec.pos.fill_(args.pos)
+    dec.tok.copy_(torch.randint(0, cfg.vocab_size, (args.batch,), dtype=torch.int32))
+    for _ in range(args.warmup):
+        dec.step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec.step()
+    e1.record()
+    torch.cuda.synchronize()
+    eng.check_device()
+    us = e0.elapsed_time(e1) * 1000 / args.steps
+    alg = cfg.step_bytes([args.pos] * args.batch)
+    peak, kind = hbm_peak()
+    return {"mode": "paged", "batch": args.batch, "pos": args.pos, "steps": args.steps,
+            "us_per_step": us, "tok_s": args.batch * 1e6 / us, "algorithmic_bytes_per_step": alg,
+            "hbm_frac": alg / (us * 1e-6) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["b1", "paged"], default="b1")
+    ap.add_argument("--gen-len", type=int, default=128)
+    ap.add_argument("--n-runs", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--pos", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--weights", default=None, help="reference checkpoint (pickle with params and config)")
+    args = ap.parse_args()
+
+    import torch
+
+    from transformer_b200.config import CONFIG_306M, ModelConfig
+    from transformer_b200.packing import prepare_decode_weights_nlayer
+    from transformer_b200.synth import synth_params
+    if args.weights:
+        params, config = load_params(args.weights)
+        cfg = ModelConfig.from_dict(config)
+    else:
+        cfg = CONFIG_306M
+        params = synth_params(cfg, 0)
+    w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
+    out = {"memory": compute_memory_stats(cfg)}
+    out.update(profile_b1(w, cfg, args, torch) if args.mode == "b1" else profile_paged(w, cfg, args, torch))
+    print(json.dumps(out))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
