@@ -120,19 +120,23 @@ __device__ __forceinline__ size_t page_row(const PagedAttnArgs& a, int blk, int 
 // Split ("flash-decoding") paged attention.  grid (ceil(max_chunks / cpc),
 // n_kv, B), block 128: CTA (x, g, b) handles the cached positions of chunks
 // x*cpc .. x*cpc+cpc-1 (64 positions each) of sequence b for the GQA query
-// heads of kv head g (warp w = query head g*GQA + w, GQA <= 4), merging its
-// chunks with an online softmax; the next chunk's K/V loads are in flight
-// while the current chunk is computed.  The CTA holding the new position
-// appends its K (post-RoPE) / V to the pool.  K/V rows are staged in padded
-// shared memory; scores are lane-per-position, P.V lane-per-dimension.  When
-// a sequence spans several CTAs each writes (m, l, o) and the last to finish
-// (ticket) merges them in CTA order and writes the bf16 output.  Math:
-// model.py:100-131 (rotate-half RoPE, causal softmax over 0..p, GQA sharing).
+// heads of kv head g (GQA <= 4), merging its chunks with an online softmax;
+// the next chunk's K/V loads are in flight while the current chunk is
+// computed.  The CTA holding the new position appends its K (post-RoPE) / V
+// to the pool.  K/V rows are staged in padded shared memory and every
+// element is read and converted once for all the GQA heads: scores by
+// (position, half of the dimensions), P.V by (dimension pair, group of 16
+// positions), packed f32x2 FMAs.  When a sequence spans several CTAs each
+// writes (m, l, o) and the last to finish (ticket) merges them in CTA order
+// and writes the bf16 output.  Math: model.py:100-131 (rotate-half RoPE,
+// causal softmax over 0..p, GQA sharing).
 __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__ PagedAttnArgs a) {
   __shared__ __align__(16) __nv_bfloat16 sk[kAttChunk][kAttRow];
   __shared__ __align__(16) __nv_bfloat16 sv[kAttChunk][kAttRow];
-  __shared__ __align__(16) float sq[4][64];
-  __shared__ __align__(16) float sp[4][kAttChunk];
+  __shared__ __align__(16) float sq[4][2][36];      // q by head and half of the dims (padded: no bank clash)
+  __shared__ __align__(16) float ss[kAttChunk][4];  // probabilities by position and head
+  __shared__ float smax[4][4], ssum[4][4];          // per warp, per head
+  __shared__ __align__(16) float sacc[4][4][64];    // P.V partials by position group, head, dim
   __shared__ __align__(16) __nv_bfloat16 skn[64], svn[64];  // the new position's K / V
   __shared__ uint32_t s_last;
   const int x = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
@@ -167,11 +171,16 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
   const bool owner = c_hi == nch;  // this CTA's last chunk holds position p
   if (t < 32) {
     const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
-    for (int w = 0; w < GQA; ++w) {  // RoPE (rotate-half); q pre-scaled by 1/sqrt(64) (exact)
-      const float* q = row + (g * GQA + w) * 64;
-      const float lo = q[lane], hi = q[lane + 32];
-      sq[w][lane] = (lo * cs - hi * sn) * 0.125f;
-      sq[w][lane + 32] = (lo * sn + hi * cs) * 0.125f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {  // RoPE (rotate-half); q pre-scaled by 1/sqrt(64) (exact); unused heads 0
+      float lo = 0.f, hi = 0.f;
+      if (w < GQA) {
+        const float* q = row + (g * GQA + w) * 64;
+        lo = q[lane];
+        hi = q[lane + 32];
+      }
+      sq[w][0][lane] = (lo * cs - hi * sn) * 0.125f;
+      sq[w][1][lane] = (lo * sn + hi * cs) * 0.125f;
     }
     if (owner) {  // the new position's K (post-RoPE) / V, bf16 as cached
       const float* k = row + a.n_heads * 64 + g * 64;
@@ -208,12 +217,14 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
     }
   };
   fetch(c_lo);
-  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-  const int h = g * GQA + warp;
+  // online-softmax state per head, the same in every thread
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, l[4] = {0.f, 0.f, 0.f, 0.f};
+  uint64_t acc[4] = {0, 0, 0, 0};          // f32x2: dims 2*lane, 2*lane+1 of each head, this warp's 16 rows
+  const int rs = t >> 1, half = t & 1;     // score mapping: row rs, dims 32*half .. 32*half+31
   for (int c = c_lo; c < c_hi; ++c) {
     const int base = c * kAttChunk;
     const int npos = min(kAttChunk, p + 1 - base);  // rows 0..npos-1 = positions base..
-    __syncthreads();  // the previous chunk's reads of sk / sv / sp are done
+    __syncthreads();  // the previous chunk's reads of sk / sv / ss are done
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int idx = t + 128 * i, r = idx >> 3, cc = idx & 7, pp = base + r;
@@ -223,69 +234,99 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
       } else if (pp == p) {
         *reinterpret_cast<uint4*>(&sk[r][cc * 8]) = reinterpret_cast<const uint4*>(skn)[cc];
         *reinterpret_cast<uint4*>(&sv[r][cc * 8]) = reinterpret_cast<const uint4*>(svn)[cc];
-      } else {  // past p: zero V so the 4-row P.V steps below read finite values
+      } else {  // past p: zero V so the P.V rows below read finite values
         *reinterpret_cast<uint4*>(&sv[r][cc * 8]) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
     __syncthreads();
     if (c + 1 < c_hi) fetch(c + 1);  // in flight during this chunk's math
-    if (warp < GQA && !bad) {
-      float sc[2];
+
+    // scores: row rs, half the dimensions, all four heads; the halves meet by shuffle
+    const bool valid = !bad && rs < npos;
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+      uint64_t a2[4] = {0, 0, 0, 0};
+      const uint4* kr4 = reinterpret_cast<const uint4*>(&sk[rs][32 * half]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int r = lane + 32 * half;
-        float d = -INFINITY;
-        if (r < npos) {
-          d = 0.f;
-          const float4* q4 = reinterpret_cast<const float4*>(sq[warp]);
+      for (int i = 0; i < 4; ++i) {
+        const uint4 kw = kr4[i];
+        const uint64_t k0 = bf2pack(kw.x), k1 = bf2pack(kw.y), k2 = bf2pack(kw.z), k3 = bf2pack(kw.w);
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const uint4 w = *reinterpret_cast<const uint4*>(&sk[r][cc * 8]);
-            const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
-            d = fmaf(qa.x, bf16_lo(w.x), d); d = fmaf(qa.y, bf16_hi(w.x), d);
-            d = fmaf(qa.z, bf16_lo(w.y), d); d = fmaf(qa.w, bf16_hi(w.y), d);
-            d = fmaf(qb.x, bf16_lo(w.z), d); d = fmaf(qb.y, bf16_hi(w.z), d);
-            d = fmaf(qb.z, bf16_lo(w.w), d); d = fmaf(qb.w, bf16_hi(w.w), d);
-          }
+        for (int h = 0; h < 4; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[h][half][8 * i]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sq[h][half][8 * i + 4]);
+          a2[h] = ffma2(k0, f2pack(qa.x, qa.y), a2[h]);
+          a2[h] = ffma2(k1, f2pack(qa.z, qa.w), a2[h]);
+          a2[h] = ffma2(k2, f2pack(qb.x, qb.y), a2[h]);
+          a2[h] = ffma2(k3, f2pack(qb.z, qb.w), a2[h]);
         }
-        sc[half] = d;
       }
-      float mc = fmaxf(sc[0], sc[1]);
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, off));
-      const float mn = fmaxf(m, mc);  // finite: every chunk has >= 1 position
-      const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-      const float e0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mn);
-      const float e1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mn);
-      sp[warp][lane] = e0;
-      sp[warp][lane + 32] = e1;
-      float ls = e0 + e1;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-      __syncwarp();
-      float a0 = 0.f, a1 = 0.f;  // rows npos.. have p = 0 and V = 0
-#pragma unroll 2
-      for (int r = 0; r < npos; r += 4) {
-        const float4 p4 = *reinterpret_cast<const float4*>(&sp[warp][r]);
-        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(&sv[r][2 * lane]);
-        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(&sv[r + 1][2 * lane]);
-        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(&sv[r + 2][2 * lane]);
-        const uint32_t v3 = *reinterpret_cast<const uint32_t*>(&sv[r + 3][2 * lane]);
-        a0 = fmaf(p4.x, bf16_lo(v0), a0); a1 = fmaf(p4.x, bf16_hi(v0), a1);
-        a0 = fmaf(p4.y, bf16_lo(v1), a0); a1 = fmaf(p4.y, bf16_hi(v1), a1);
-        a0 = fmaf(p4.z, bf16_lo(v2), a0); a1 = fmaf(p4.z, bf16_hi(v2), a1);
-        a0 = fmaf(p4.w, bf16_lo(v3), a0); a1 = fmaf(p4.w, bf16_hi(v3), a1);
-      }
-      l = fmaf(l, alpha, ls);
-      o0 = fmaf(o0, alpha, a0);
-      o1 = fmaf(o1, alpha, a1);
-      m = mn;
+      for (int h = 0; h < 4; ++h) sc[h] = f2sum(a2[h]);
     }
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], 1);
+      if (!valid) sc[h] = -INFINITY;
+      float mx = sc[h];
+#pragma unroll
+      for (int off = 16; off > 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (lane == 0) smax[warp][h] = mx;
+    }
+    __syncthreads();
+    float alpha[4], pr[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float mc = fmaxf(fmaxf(smax[0][h], smax[1][h]), fmaxf(smax[2][h], smax[3][h]));
+      const float mn = fmaxf(m[h], mc);
+      alpha[h] = m[h] == -INFINITY ? 0.f : __expf(m[h] - mn);
+      pr[h] = valid ? __expf(sc[h] - mn) : 0.f;
+      m[h] = mn;
+      float sm = half == 0 ? pr[h] : 0.f;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+      if (lane == 0) ssum[warp][h] = sm;
+    }
+    if (half == 0) *reinterpret_cast<float4*>(ss[rs]) = make_float4(pr[0], pr[1], pr[2], pr[3]);
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      l[h] = fmaf(l[h], alpha[h], (ssum[0][h] + ssum[1][h]) + (ssum[2][h] + ssum[3][h]));
+      acc[h] = ffma2(acc[h], f2pack(alpha[h], alpha[h]), 0ull);
+    }
+    if (!bad) {  // P.V: dims 2*lane, 2*lane+1, rows 16*warp .. 16*warp+15, all heads
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int r = warp * 16 + i;
+        const uint64_t v = bf2pack(*reinterpret_cast<const uint32_t*>(&sv[r][2 * lane]));
+        const float4 p4 = *reinterpret_cast<const float4*>(ss[r]);
+        acc[0] = ffma2(f2pack(p4.x, p4.x), v, acc[0]);
+        acc[1] = ffma2(f2pack(p4.y, p4.y), v, acc[1]);
+        acc[2] = ffma2(f2pack(p4.z, p4.z), v, acc[2]);
+        acc[3] = ffma2(f2pack(p4.w, p4.w), v, acc[3]);
+      }
+    }
+  }
+  // sum the four row groups in group order; warp h < GQA then owns head g*GQA + h
+#pragma unroll
+  for (int h = 0; h < 4; ++h) *reinterpret_cast<uint64_t*>(&sacc[warp][h][2 * lane]) = acc[h];
+  __syncthreads();
+  const int h = g * GQA + warp;
+  float o0 = 0.f, o1 = 0.f, mw = -INFINITY, lw = 0.f;
+  if (warp < GQA) {
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      const float2 v = *reinterpret_cast<const float2*>(&sacc[grp][warp][2 * lane]);
+      o0 += v.x;
+      o1 += v.y;
+    }
+    mw = warp == 0 ? m[0] : warp == 1 ? m[1] : warp == 2 ? m[2] : m[3];
+    lw = warp == 0 ? l[0] : warp == 1 ? l[1] : warp == 2 ? l[2] : l[3];
   }
 
   if (ncta == 1) {  // the whole sequence in this CTA: final output directly
     if (warp < GQA) {
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const float inv = lw > 0.f ? 1.0f / lw : 0.f;
       reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
           __floats2bfloat162_rn(o0 * inv, o1 * inv);
     }
@@ -295,8 +336,8 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
     float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks + x) * kAttPart;
     reinterpret_cast<float2*>(part + 4)[lane] = make_float2(o0, o1);
     if (lane == 0) {
-      part[0] = bad ? -INFINITY : m;
-      part[1] = l;
+      part[0] = bad ? -INFINITY : mw;
+      part[1] = lw;
     }
   }
   __threadfence();
