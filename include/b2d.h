@@ -168,6 +168,22 @@ B2D_API b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t
                                          void* stream);
 
 /*
+ * Device prefill (replaces the JAX prefill of generate.py:68-89 /
+ * model.py:194-231 for the decode cache): feeds n_tokens prompt tokens
+ * (tok_dev, int32) at positions start_pos.. of ONE sequence through the
+ * batched tensor-core step, 128 positions per chunk, writing their K/V into
+ * kv_dev (one sequence's cache in the reference layout, b2d_kv_layout).
+ * Outputs the logits of the last position (f32 [vocab], or NULL) and its
+ * argmax (or NULL).  Each position's math is the decode step's at that
+ * position.  start_pos + n_tokens <= context_len.
+ */
+B2D_API b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos,
+                               void* kv_dev, float* logits_dev, int32_t* next_tok_dev, void* stream);
+
+/* Kernels launched by the last b2d_decode_step_paged (or prefill chunk). */
+B2D_API int b2d_batched_launches(const b2d_ws* ws);
+
+/*
  * Device sampler, one sequence per CTA (generate.py:28-65 semantics).
  *   logits_dev   f32[batch][vocab]     (read only)
  *   history_dev  int32[batch][hist_cap] tokens generated so far (prompt excluded)

@@ -77,6 +77,8 @@ _SIGS = {
     "b2d_decode_step": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, _P, _P]),
     "b2d_decode_step_paged": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int,
                                              _P, _P, _P]),
+    "b2d_prefill": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P]),
+    "b2d_batched_launches": (ctypes.c_int, [_P]),
     "b2d_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P,
                                   ctypes.POINTER(Sampling), _P, _P]),
     "b2d_decode_step_static": (ctypes.c_int, [ctypes.POINTER(Config), _P, ctypes.c_uint64, _P, _P, _P, _P,

@@ -116,7 +116,10 @@ struct b2d_ws {
   int trace_stride;
   uint32_t poll_ns;
   int max_inflight;
-  // batched path (max_batch > 1)
+  // batched path and prefill: buffers for brows = max(max_batch, kPrefillRows) rows
+  int brows;
+  int32_t* prefill_pos;            // [kPrefillRows] positions of a prefill chunk
+  int last_launches;               // kernels launched by the last batched step / prefill chunk
   int rows;                        // activation rows allocated (max_batch rounded up to the widest tile)
   float *H, *Hm, *qkv, *logits, *att_part;
   uint32_t* att_tickets;
@@ -133,7 +136,15 @@ struct b2d_ws {
 namespace {
 constexpr int kTraceCtas = 256;        // projection CTAs stamped per launch (diagnostics)
 constexpr int kTraceLaunches = 4 * 64 + 1;  // stamped projection launches per step (n_layers <= 64)
-constexpr int kFusedNormRows = 2;           // see b2d_decode_step_paged
+constexpr int kFusedNormRows = 2;           // see run_rows
+constexpr int kPrefillRows = 128;           // prompt positions per prefill chunk
+
+__global__ void iota_kernel(int32_t* out, int start, int n) {
+  b2d::pdl_wait();
+  b2d::pdl_launch();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = start + i;
+}
 inline int bn_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4; }
 
 // Launch with an optional programmatic dependency on the previous kernel of
@@ -265,14 +276,16 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   if (e == cudaSuccess) e = cudaMalloc(&ws->ctl, sizeof(b2d::Control));
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_val, sizeof(float) * m->grid);
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
-  if (e == cudaSuccess && max_batch > 1) {
+  if (e == cudaSuccess) {  // batched step and prefill buffers
+    ws->brows = std::max(max_batch, kPrefillRows);
     const size_t D = c.d_model, F = c.d_ff, Q = qkv, V = c.vocab_size;
-    ws->rows = (max_batch + 255) / 256 * 256;  // any tile width may be chosen (see gemm_plan)
+    ws->rows = (ws->brows + 255) / 256 * 256;  // any tile width may be chosen (see gemm_plan)
+    e = cudaMalloc(&ws->prefill_pos, sizeof(int32_t) * kPrefillRows);
     ws->att_chunks = (c.context_len + b2d::kAttChunk - 1) / b2d::kAttChunk;
-    e = cudaMalloc(&ws->H, sizeof(float) * D * max_batch);
-    if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * max_batch);
-    if (e == cudaSuccess) e = cudaMalloc(&ws->qkv, sizeof(float) * Q * max_batch);
-    if (e == cudaSuccess) e = cudaMalloc(&ws->logits, sizeof(float) * V * max_batch);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->H, sizeof(float) * D * ws->brows);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * ws->brows);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->qkv, sizeof(float) * Q * ws->brows);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->logits, sizeof(float) * V * ws->brows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->X, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->A, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->ACT, 2 * F * ws->rows);
@@ -280,10 +293,10 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     if (e == cudaSuccess) e = cudaMemset(ws->A, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->ACT, 0, 2 * F * ws->rows);
     if (e == cudaSuccess)
-      e = cudaMalloc(&ws->att_part, sizeof(float) * size_t(max_batch) * c.n_heads * ws->att_chunks * b2d::kAttPart);
-    if (e == cudaSuccess) e = cudaMalloc(&ws->att_tickets, sizeof(uint32_t) * size_t(max_batch) * c.n_kv_heads);
-    if (e == cudaSuccess) e = cudaMemset(ws->att_tickets, 0, sizeof(uint32_t) * size_t(max_batch) * c.n_kv_heads);
-    const size_t nt = size_t((max_batch + 15) / 16) * b2d::kGemmMaxSplit;  // >= ceil(N/BN) * ksplit
+      e = cudaMalloc(&ws->att_part, sizeof(float) * size_t(ws->brows) * c.n_heads * ws->att_chunks * b2d::kAttPart);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->att_tickets, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
+    if (e == cudaSuccess) e = cudaMemset(ws->att_tickets, 0, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
+    const size_t nt = size_t((ws->brows + 15) / 16) * b2d::kGemmMaxSplit;  // >= ceil(N/BN) * ksplit
     if (e == cudaSuccess) e = cudaMalloc(&ws->norm_tickets, sizeof(uint32_t) * nt);
     if (e == cudaSuccess) e = cudaMemset(ws->norm_tickets, 0, sizeof(uint32_t) * nt);
     for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
@@ -318,6 +331,7 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   cudaFree(ws->att_part);
   cudaFree(ws->att_tickets);
   cudaFree(ws->norm_tickets);
+  cudaFree(ws->prefill_pos);
   cudaFree(ws->words);
   cudaFree(ws->ctl);
   cudaFree(ws->am_val);
@@ -503,21 +517,24 @@ b2d_status ensure_weight_maps(b2d_model* m) {
 
 }  // namespace
 
-b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
-                                 int batch, void* kv_pool_dev, const int32_t* block_table_dev,
-                                 int blocks_per_seq, int num_blocks, float* logits_dev, int32_t* next_tok_dev,
-                                 void* stream) {
-  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_pool_dev || !block_table_dev || !next_tok_dev ||
-      batch < 1 || batch > ws->max_batch || ws->max_batch < 2 || blocks_per_seq < 1 || num_blocks < 1)
-    return B2D_ERR_INVALID_ARG;
-  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+namespace {
+
+// The batched step's kernel sequence over `batch` rows (tokens `tok`, positions
+// `pos`, device arrays).  prefill = false: decode rows of independent
+// sequences over a paged pool (`table` [batch][bps]); each row's new K/V is
+// appended by the attention kernel.  prefill = true: rows are positions of
+// ONE sequence whose cache `cache` is contiguous in the reference layout
+// (table = nullptr); the K/V of all rows are appended first, per layer.
+// logits == nullptr skips the output projection (earlier prefill chunks);
+// next_tok == nullptr skips the argmax.
+b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t* pos, int batch, void* cache,
+                    const int32_t* table, int bps, int num_blocks, bool prefill, float* logits, int32_t* next_tok,
+                    cudaStream_t st) {
   b2d_status s = ensure_weight_maps(m);
   if (s != B2D_OK) return s;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const b2d_config& c = m->cfg;
   const int D = c.d_model, F = c.d_ff, Q = (c.n_heads + 2 * c.n_kv_heads) * 64, V = c.vocab_size;
   uint32_t* status = &ws->ctl->status;
-  float* logits = logits_dev ? logits_dev : ws->logits;
   const float* ln1 = reinterpret_cast<const float*>(m->w + m->lay.off_ln1);
   const float* ln2 = reinterpret_cast<const float*>(m->w + m->lay.off_ln2);
   const float* lnf = reinterpret_cast<const float*>(m->w + m->lay.off_lnf);
@@ -525,6 +542,7 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
 
   const bool pdl = !ws->no_pdl;
   int gl = 0;  // projection launches so far (diagnostic stamps)
+  int launches_other = 0;  // embedding, attention, RMSNorm, argmax launches
   b2d::GemmArgs g{};
   auto gemm = [&](const CUtensorMap& wm, const CUtensorMap* xmaps, int epi, const b2d::GemmPlan& pl) {
     g.ksplit = pl.ksplit;
@@ -548,15 +566,16 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
     p_dn.ksplit = std::min(f, F / b2d::kGemmBK);
     p_lg.ksplit = std::min(f, D / b2d::kGemmBK);
   }
-  B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok_dev, V, D, ln1, c.rms_eps,
+  B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok, V, D, ln1, c.rms_eps,
                     ws->H, ws->X, status), "embed");
+  ++launches_other;
   g.N = batch;
   g.err = status;
   g.tickets = ws->norm_tickets;
   g.norm_eps = c.rms_eps;
   b2d::PagedAttnArgs pa{};
-  pa.qkv = ws->qkv; pa.pos = pos_dev; pa.pool = static_cast<__nv_bfloat16*>(kv_pool_dev);
-  pa.table = block_table_dev; pa.bps = blocks_per_seq; pa.num_blocks = num_blocks;
+  pa.qkv = ws->qkv; pa.pos = pos; pa.pool = static_cast<__nv_bfloat16*>(cache);
+  pa.table = table; pa.bps = bps; pa.num_blocks = num_blocks; pa.append = !prefill;
   pa.n_heads = c.n_heads; pa.n_kv = c.n_kv_heads; pa.ctx = c.context_len;
   pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
@@ -581,15 +600,21 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
     g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.norm_g = nullptr;
     B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
     pa.layer = l;
+    if (prefill)  // every row's K/V in the cache before any row attends
+      B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
     B2D_CUDA(launch_k(b2d::paged_attn_kernel, dim3((ws->att_chunks + pa.cpc - 1) / pa.cpc, c.n_kv_heads, batch),
                       dim3(128), st, pdl, pa),
              "attention");
+    launches_other += prefill ? 2 : 1;
     const float* ln2_l = ln2 + size_t(l) * D;
     g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D; 
     g.norm_g = norm_fused(p_o) ? ln2_l : nullptr;
     g.norm_out = ws->X;
     B2D_CUDA(gemm(m->wmaps[4 * l + 1], ws->amap, b2d::EPI_RESID_F32, p_o), "o");
-    if (!g.norm_g) B2D_CUDA(norm(ws->Hm, ln2_l), "rmsnorm");
+    if (!g.norm_g) {
+      B2D_CUDA(norm(ws->Hm, ln2_l), "rmsnorm");
+      ++launches_other;
+    }
     g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F; g.norm_g = nullptr;
     B2D_CUDA(gemm(m->wmaps[4 * l + 2], ws->xmap, b2d::EPI_SWIGLU_BF16, p_gu), "gate/up");
     const float* next_g = l + 1 < c.n_layers ? ln1 + size_t(l + 1) * D : lnf;  // next ln1, or the final norm
@@ -597,14 +622,69 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
     g.norm_g = norm_fused(p_dn) ? next_g : nullptr;
     g.norm_out = ws->X;
     B2D_CUDA(gemm(m->wmaps[4 * l + 3], ws->actmap, b2d::EPI_RESID_F32, p_dn), "down");
-    if (!g.norm_g) B2D_CUDA(norm(ws->H, next_g), "rmsnorm");
+    if (!g.norm_g) {
+      B2D_CUDA(norm(ws->H, next_g), "rmsnorm");
+      ++launches_other;
+    }
+  }
+  if (logits == nullptr) {  // an earlier prefill chunk: only its cache rows are needed
+    ws->last_launches = gl + launches_other;
+    return B2D_OK;
   }
   g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V; g.norm_g = nullptr;
   B2D_CUDA(gemm(m->wmaps[4 * c.n_layers], ws->xmap, b2d::EPI_F32, p_lg), "logits");
-  B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
-                    next_tok_dev), "argmax");
+  if (next_tok) {
+    B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
+                      next_tok), "argmax");
+    ++launches_other;
+  }
+  ws->last_launches = gl + launches_other;
   return B2D_OK;
 }
+
+}  // namespace
+
+b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                                 int batch, void* kv_pool_dev, const int32_t* block_table_dev,
+                                 int blocks_per_seq, int num_blocks, float* logits_dev, int32_t* next_tok_dev,
+                                 void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_pool_dev || !block_table_dev || !next_tok_dev ||
+      batch < 1 || batch > ws->max_batch || ws->max_batch < 2 || blocks_per_seq < 1 || num_blocks < 1)
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  return run_rows(m, ws, tok_dev, pos_dev, batch, kv_pool_dev, block_table_dev, blocks_per_seq, num_blocks, false,
+                  logits_dev ? logits_dev : ws->logits, next_tok_dev, static_cast<cudaStream_t>(stream));
+}
+
+b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos, void* kv_dev,
+                       float* logits_dev, int32_t* next_tok_dev, void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !kv_dev || n_tokens < 1 || start_pos < 0 ||
+      start_pos + n_tokens > m->cfg.context_len)
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int V = m->cfg.vocab_size;
+  for (int c0 = 0; c0 < n_tokens; c0 += kPrefillRows) {
+    const int rows = std::min(kPrefillRows, n_tokens - c0);
+    const bool last = c0 + rows == n_tokens;
+    B2D_CUDA(launch_k(iota_kernel, dim3((rows + 127) / 128), dim3(128), st, !ws->no_pdl, ws->prefill_pos,
+                      start_pos + c0, rows), "positions");
+    b2d_status s = run_rows(m, ws, tok_dev + c0, ws->prefill_pos, rows, kv_dev, nullptr, 0, 0, true,
+                            last && (logits_dev || next_tok_dev) ? ws->logits : nullptr, nullptr, st);
+    if (s != B2D_OK) return s;
+    if (last) {
+      const float* lrow = ws->logits + size_t(rows - 1) * V;
+      if (logits_dev)
+        B2D_CUDA(cudaMemcpyAsync(logits_dev, lrow, sizeof(float) * V, cudaMemcpyDeviceToDevice, st), "logits row");
+      if (next_tok_dev)
+        B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(1), dim3(1024), st, false, lrow, V, V, next_tok_dev),
+                 "argmax");
+    }
+  }
+  return B2D_OK;
+}
+
+int b2d_batched_launches(const b2d_ws* ws) { return ws ? ws->last_launches : 0; }
 
 // Test hook: Y = X . W^T on the tensor-core GEMM with the chosen epilogue.
 b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int N, int epi, float* y_dev,

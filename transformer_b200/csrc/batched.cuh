@@ -107,15 +107,57 @@ struct PagedAttnArgs {
   uint32_t* tickets;           // [B][n_kv]; zero between launches (the combining CTA resets it)
   int max_chunks;              // >= ceil(ctx / kAttChunk)
   int cpc;                     // chunks per CTA (>= 1)
+  // Cache addressing: table != nullptr -> the paged pool above; table ==
+  // nullptr -> one sequence's contiguous cache in the reference layout
+  // [layer][K|V][kv_head][ctx][64] (every row of the launch is a position of
+  // that sequence, as in a prefill).
+  bool append;                 // the CTA holding a row's position writes its K/V (else done before)
 };
+
+// K (kv = 0) or V (kv = 1) row of position `pos` of the launch row's sequence.
+__device__ __forceinline__ __nv_bfloat16* kv_row(const PagedAttnArgs& a, const int32_t* tb, int pos, int kv, int g) {
+  if (a.table == nullptr)
+    return a.pool + ((((static_cast<size_t>(a.layer) * 2 + kv) * a.n_kv + g) * a.ctx) + pos) * 64;
+  return a.pool + ((((static_cast<size_t>(a.layer) * a.num_blocks + tb[pos / kPageTokens]) * 2 + kv) * a.n_kv + g) *
+                       kPageTokens + pos % kPageTokens) * 64;
+}
+
+// Writes row b's K (post-RoPE) / V for kv head blockIdx.y at position pos[b]
+// (bf16, as cached).  grid (rows, n_kv), 32 threads.  Used before a prefill
+// launch of the attention (append = false) so that every row's K/V is in the
+// cache before any row attends.  Positions out of range / idle rows: skipped.
+__global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ PagedAttnArgs a) {
+  pdl_wait();
+  pdl_launch();
+  const int b = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
+  const int p = a.pos[b];
+  if (p < 0 || p >= a.ctx) return;
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
+  if (tb != nullptr) {
+    if (p / kPageTokens >= a.bps) return;
+    const int e = tb[p / kPageTokens];
+    if (e < 0 || e >= a.num_blocks) {
+      if (lane == 0) atomicCAS(a.status, 0u, 0x203u);
+      return;
+    }
+  }
+  const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
+  const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
+  const float* k = row + a.n_heads * 64 + g * 64;
+  const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
+  const float klo = k[lane], khi = k[lane + 32];
+  __nv_bfloat16* kd = kv_row(a, tb, p, 0, g);
+  __nv_bfloat16* vd = kv_row(a, tb, p, 1, g);
+  kd[lane] = __float2bfloat16_rn(klo * cs - khi * sn);
+  kd[lane + 32] = __float2bfloat16_rn(klo * sn + khi * cs);
+  vd[lane] = __float2bfloat16_rn(v[lane]);
+  vd[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
+}
 
 constexpr int kAttChunk = 64;  // cached positions per CTA
 constexpr int kAttPart = 68;   // m, l, 2 pad, o[64]
 constexpr int kAttRow = 72;    // smem row pitch (bf16): 144 B keeps 16-byte row reads conflict-free
 
-__device__ __forceinline__ size_t page_row(const PagedAttnArgs& a, int blk, int kv, int g, int slot) {
-  return ((((static_cast<size_t>(a.layer) * a.num_blocks + blk) * 2 + kv) * a.n_kv + g) * kPageTokens + slot) * 64;
-}
 
 // Split ("flash-decoding") paged attention.  grid (ceil(max_chunks / cpc),
 // n_kv, B), block 128: CTA (x, g, b) handles the cached positions of chunks
@@ -156,11 +198,11 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
   if (c_lo >= nch) return;
   const int c_hi = min(c_lo + a.cpc, nch);
   const int ncta = (nch + a.cpc - 1) / a.cpc;  // CTAs sharing this (b, g)
-  const int32_t* tb = a.table + static_cast<size_t>(b) * a.bps;
-  // every page this CTA touches must exist
-  bool bad = (p / kPageTokens) >= a.bps;
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
+  // every page this CTA touches must exist (paged cache)
+  bool bad = tb != nullptr && (p / kPageTokens) >= a.bps;
   const int pg_hi = (min(c_hi * kAttChunk, p + 1) - 1) / kPageTokens;
-  for (int i = c_lo * (kAttChunk / kPageTokens) + t; !bad && i <= pg_hi; i += 128) {
+  for (int i = c_lo * (kAttChunk / kPageTokens) + t; tb != nullptr && !bad && i <= pg_hi; i += 128) {
     const int e = tb[i];
     bad = e < 0 || e >= a.num_blocks;
   }
@@ -190,10 +232,9 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
       skn[lane + 32] = __float2bfloat16_rn(klo * sn + khi * cs);
       svn[lane] = __float2bfloat16_rn(v[lane]);
       svn[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
-      if (!bad) {
-        const int blk = tb[p / kPageTokens], slot = p % kPageTokens;
-        __nv_bfloat16* kd = a.pool + page_row(a, blk, 0, g, slot);
-        __nv_bfloat16* vd = a.pool + page_row(a, blk, 1, g, slot);
+      if (!bad && a.append) {
+        __nv_bfloat16* kd = kv_row(a, tb, p, 0, g);
+        __nv_bfloat16* vd = kv_row(a, tb, p, 1, g);
         kd[lane] = skn[lane];
         kd[lane + 32] = skn[lane + 32];
         vd[lane] = svn[lane];
@@ -210,9 +251,8 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(const __grid_constant__
     for (int i = 0; i < 4; ++i) {
       const int idx = t + 128 * i, r = idx >> 3, cc = idx & 7, pp = base + r;
       if (!bad && pp < p) {
-        const int blk = tb[pp / kPageTokens], slot = pp % kPageTokens;
-        kr[i] = __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 0, g, slot)) + cc);
-        vr[i] = __ldg(reinterpret_cast<const uint4*>(a.pool + page_row(a, blk, 1, g, slot)) + cc);
+        kr[i] = __ldg(reinterpret_cast<const uint4*>(kv_row(a, tb, pp, 0, g)) + cc);
+        vr[i] = __ldg(reinterpret_cast<const uint4*>(kv_row(a, tb, pp, 1, g)) + cc);
       }
     }
   };

@@ -202,8 +202,26 @@ class DecodeEngine:
 
     # ---- prompt ingestion ----------------------------------------------
     def prefill(self, prompt, kv: torch.Tensor, start: int = 0, stream=None) -> torch.Tensor:
-        """Feed prompt tokens one step at a time (teacher forcing), writing the
-        KV cache; returns the logits of the last prompt position (device)."""
+        """Device prefill (``b2d_prefill``): the prompt's positions run through
+        the batched tensor-core step, writing the KV cache ``kv`` (one
+        sequence, reference layout); returns the logits of the last prompt
+        position (device [vocab]) and leaves its argmax in ``next_tok[0]``."""
+        prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
+        if prompt.size == 0:
+            raise ValueError("empty prompt")
+        if start + prompt.size > self.cfg.context_len:
+            raise ValueError("prompt longer than the context")
+        if kv.dtype != torch.bfloat16 or kv.device != self.device or kv.numel() < self.kv_elems:
+            raise ValueError("kv must be a bf16 cache on the model device (see new_kv)")
+        toks = torch.from_numpy(prompt).to(self.device)
+        st = self.lib.b2d_prefill(self.model, self.ws, _ptr(toks), int(prompt.size), int(start), _ptr(kv),
+                                  _ptr(self.logits), _ptr(self.next_tok), _stream_ptr(stream))
+        _lib.check(st, "b2d_prefill")
+        return self.logits[0]
+
+    def prefill_stepwise(self, prompt, kv: torch.Tensor, start: int = 0, stream=None) -> torch.Tensor:
+        """Feed prompt tokens one decode step at a time (teacher forcing),
+        writing the KV cache; returns the logits of the last prompt position."""
         prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
         if prompt.size == 0:
             raise ValueError("empty prompt")
