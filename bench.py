@@ -307,6 +307,7 @@ def measure_cfg3(eng, cfg, torch):
     dec = BatchedDecoder(eng, len(prompts), table=table, num_blocks=int(table.size))
     dec.ingest(prompts)
     dec.capture()
+    per_step = eng.lib.b2d_batched_launches(eng.ws)
     pos0 = dec.pos.cpu().numpy().copy()
     n = 64
     ms = events_ms(lambda: [dec.replay() for _ in range(n)], torch.cuda.current_stream(), torch)
@@ -318,8 +319,8 @@ def measure_cfg3(eng, cfg, torch):
     return {"workload": "config 3: B=64 paged, prompt lengths U[32,448] seed 2, random block table, "
                         "64 greedy steps", "tok_s": 64 * n / (ms / 1000), "ms_per_step": ms / n,
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                         "scope": "whole step (123 kernels)", "peak_source": f"{kind} hbm_gbs"},
-            "gpu_launches": 123 * n}
+                         "scope": f"whole step ({per_step} kernels)", "peak_source": f"{kind} hbm_gbs"},
+            "gpu_launches": per_step * n}
 
 
 def measure_cfg4(eng, cfg, torch):
@@ -352,9 +353,10 @@ def measure_cfg4(eng, cfg, torch):
             tok = smp.sample(dec.logits, 0.7, 0.95, 1.2, B, uniforms=uni[i]).clone()
     ms = events_ms(run, torch.cuda.current_stream(), torch)
     eng.check_device()
+    per_step = eng.lib.b2d_batched_launches(eng.ws) + 1  # + the sampler
     return {"workload": "config 4: B=8 sampling (T 0.7, top-p 0.95, rep 1.2, seeded uniforms), 64-token "
                         "prompts, 127 sampled steps after the first", "tok_s": B * (steps - 1) / (ms / 1000),
-            "ms_per_step": ms / (steps - 1), "gpu_launches": (123 + 1) * (steps - 1)}
+            "ms_per_step": ms / (steps - 1), "gpu_launches": per_step * (steps - 1)}
 
 
 def run_ours(args, rank, local_rank, world):
@@ -405,6 +407,7 @@ def run_ours(args, rank, local_rank, world):
     torch.cuda.synchronize(dev)
     eng.check_device()
     pos_t0 = pos
+    per_wave = eng.lib.b2d_batched_launches(eng.ws)  # kernels of one wave-step (the captured step's)
 
     # ---- device-timed region ----
     clocks = ClockSampler(local_rank) if rank == 0 else None
@@ -470,6 +473,12 @@ def run_ours(args, rank, local_rank, world):
         extra["config1_b1"]["e2e"] = measure_b1_e2e(eng1, dev, stream, torch, prompt_cfg1(), 128)
         extra["config2_b1_long"] = measure_b1(eng1, cfg, dev, stream, torch, prompt_cfg2(), 128,
                                               "config 2: B=1, 384-token prompt, greedy positions 384..511")
+        kvp = eng1.new_kv()
+        for _ in range(3):
+            eng1.prefill(prompt_cfg2(), kvp)
+        pf_ms = events_ms(lambda: [eng1.prefill(prompt_cfg2(), kvp) for _ in range(10)], stream, torch) / 10
+        extra["config2_b1_long"]["prefill_384"] = {"ms": pf_ms, "tok_s": 384 / (pf_ms / 1000),
+                                                   "how": "b2d_prefill, 3 chunks of 128 positions, CUDA events"}
         eng1.close()
         eng3 = DecodeEngine(w, max_batch=64)
         extra["config3_paged_b64"] = measure_cfg3(eng3, cfg, torch)
@@ -487,7 +496,7 @@ def run_ours(args, rank, local_rank, world):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    launches = 123 * n_waves * args.steps
+    launches = per_wave * n_waves * args.steps
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -496,8 +505,8 @@ def run_ours(args, rank, local_rank, world):
         "config": serve_config(world),
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_kind} hbm_gbs", "scope": "whole batched step per GPU (123 kernels "
-                     "per wave: projections on tcgen05, paged attention, embedding, argmax)",
+                     "peak_source": f"{peak_kind} hbm_gbs", "scope": f"whole batched step per GPU ({per_wave} "
+                     "kernels per wave: projections on tcgen05, paged attention, RMSNorm, embedding, argmax)",
                      "traffic": None, "algorithmic_bytes_per_step": alg_step},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                 "d2h_bytes_per_step": 4 * n_seq, "steps": ne,

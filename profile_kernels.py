@@ -46,6 +46,27 @@ def load_params(path):
     return params, saved["config"]
 
 
+def measure_prefill(w, config, prompt, n_runs=20):
+    """``profile_kernels.py:28-41``: median latency (ms) of a prefill of
+    ``prompt`` (the device prefill, ``b2d_prefill``) after 3 warm-ups;
+    returns (ms, last-position logits, kv cache)."""
+    import torch
+
+    from transformer_b200.multi_sm_decode import engine_for
+    eng = engine_for(w)
+    kv = eng.new_kv()
+    for _ in range(3):
+        logits = eng.prefill(prompt, kv)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(n_runs):
+        t0 = time.perf_counter()
+        logits = eng.prefill(prompt, kv)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    return float(np.median(times)) * 1000, logits, kv
+
+
 def measure_decode(w, config, tok, start_pos, kv_packed, n_tokens=128, n_runs=10):
     """``profile_kernels.py:44-64``: median wall time (ms) of ``n_tokens``
     greedy steps through ``multi_sm_decode_nlayer`` with a host read of every
@@ -94,8 +115,9 @@ def hbm_peak():
 
 def profile_b1(w, cfg, args, torch):
     from transformer_b200.multi_sm_decode import engine_for
-    from transformer_b200.synth import prompt_cfg1
+    from transformer_b200.synth import prompt_cfg1, prompt_cfg2
     eng = engine_for(w)
+    prefill_ms, _, _ = measure_prefill(w, cfg, prompt_cfg2(cfg)[:min(384, cfg.context_len - 1)], args.n_runs)
     prompt = prompt_cfg1(cfg)
     kv = eng.new_kv()
     first = eng.prefill(prompt, kv)
@@ -104,7 +126,7 @@ def profile_b1(w, cfg, args, torch):
     us = ms * 1000 / args.gen_len
     alg = float(np.mean([cfg.step_bytes([len(prompt) + i]) for i in range(args.gen_len)]))
     peak, kind = hbm_peak()
-    return {"mode": "b1", "gen_len": args.gen_len, "host_loop_us_per_token": us,
+    return {"mode": "b1", "gen_len": args.gen_len, "prefill_384_ms": prefill_ms, "host_loop_us_per_token": us,
             "tok_s": 1e6 / us, "hbm_frac_host_loop": alg / (us * 1e-6) / 1e9 / peak,
             "peak_gbs": peak, "peak_source": kind, "first_tokens": tokens[:8]}
 
