@@ -128,6 +128,8 @@ struct b2d_ws {
   int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
   int force_att_cpc;       // diagnostics: fixed attention chunks per CTA (0 = automatic)
   uint64_t* gemm_trace;    // diagnostics: [launch][kTraceCtas][kGemmStamps] projection stamps, or null
+  uint64_t* stage_trace;   // diagnostics: B=1 stage stamps [grid][3][stage_stride], or null
+  int stage_stride;
   int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
@@ -409,6 +411,13 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 6:  // batched step: projection stamp buffer (device address; 0 = off)
       ws->gemm_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
       return B2D_OK;
+    case 7:  // B=1 step: stage stamp buffer (device address; 0 = off)
+      ws->stage_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
+      return B2D_OK;
+    case 8:  // B=1 step: stage stamps per CTA and kind
+      if (value < 0 || value > 4096) return B2D_ERR_INVALID_ARG;
+      ws->stage_stride = static_cast<int>(value);
+      return B2D_OK;
   }
   return B2D_ERR_INVALID_ARG;
 }
@@ -459,6 +468,8 @@ b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, con
   A.eps = c.rms_eps;
   A.trace = ws->trace;
   A.trace_stride = ws->trace_stride;
+  A.stage_trace = ws->stage_trace;
+  A.stage_stride = ws->stage_stride;
   A.poll_ns = ws->poll_ns;
   A.max_inflight = ws->max_inflight;
   void* args[] = {&A};

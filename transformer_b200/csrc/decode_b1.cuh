@@ -83,6 +83,10 @@ struct DecodeArgs {
   int trace_stride;   // stamps per CTA
   uint32_t poll_ns;   // back-off between failed polls (0 = spin)
   int max_inflight;   // bulk copies in flight per CTA (<= kStages)
+  // diagnostics: per-CTA stage stamps [3][stage_stride] (copy issued by the
+  // producer; stage seen full by consumer warp 0; warp 0 done with it), or null
+  uint64_t* stage_trace;
+  int stage_stride;
 };
 
 // Phase-stamp slots (per CTA): 0 = start, then per layer kTracePerLayer
@@ -277,6 +281,36 @@ __device__ __forceinline__ bool wait_full(const DecodeArgs& A, Ring& r, uint32_t
   }
 }
 
+// Warp-uniform: waits until the n stages ring.seq .. ring.seq+n-1 (n <=
+// kStages / 2) have landed.  Lane i tests stage seq+i, so a phase whose
+// stages are already resident (the usual case: the producer runs ~20 us
+// ahead) costs one barrier round trip instead of one per stage; __syncwarp
+// then orders every lane after the acquiring lanes.
+__device__ __forceinline__ bool wait_full_n(const DecodeArgs& A, Ring& r, int n, uint32_t flag, uint64_t t0) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t sq = r.seq + static_cast<uint32_t>(lane);
+  Waiter wt;
+  while (true) {
+    const bool done = lane >= n || mbar_test(&r.full[sq % kStages], (sq / kStages) & 1u);
+    if (__all_sync(0xffffffffu, done)) break;
+    const bool exp = lane == 0 ? wt.expired(A, flag, t0, SITE_FULL) : false;
+    if (__shfl_sync(0xffffffffu, exp ? 1 : 0, 0)) return false;
+  }
+  __syncwarp();
+  return true;
+}
+
+// Warp-uniform: this warp is done with stages seq .. seq+n-1 (lane i arrives
+// on stage seq+i's empty barrier).
+__device__ __forceinline__ void release_n(Ring& r, int n) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  if (lane < n) mbar_arrive(&r.empty[(r.seq + static_cast<uint32_t>(lane)) % kStages]);
+  r.seq += static_cast<uint32_t>(n);
+}
+
+constexpr int kGroupStages = kStages / 2;  // stages waited for together
+
 // One GEMV phase over this CTA's units [u_begin, u_end) (a unit is one row, or
 // a gate/up row pair when PAIR), streamed in stages of `per_stage` units.
 // Warp w owns units u_begin + w + 8j (j < MAXJ).  Each lane accumulates its
@@ -298,17 +332,20 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
 #pragma unroll
     for (int r = 0; r < NR; ++r) acc[j][r][0] = acc[j][r][1] = 0ull;
   bool ok = true;
-  for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
-    const int u1 = min(u0 + per_stage, u_end);
-    if (ok) ok = wait_full(A, ring, flag, t0);
-    const uint32_t slot = ring.seq % kStages;
+  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * per_stage) {
+    const int ns = min(kGroupStages, (u_end - g0 + per_stage - 1) / per_stage);
+    ok = wait_full_n(A, ring, ns, flag, t0);
+    if (A.stage_trace != nullptr && threadIdx.x == 0 && ring.seq < static_cast<uint32_t>(A.stage_stride))
+      A.stage_trace[(static_cast<size_t>(blockIdx.x) * 3 + 1) * A.stage_stride + ring.seq] = globaltimer_ns();
     if (ok) {
-      const uint8_t* sb = ring.stage[slot];
 #pragma unroll
       for (int j = 0; j < MAXJ; ++j) {
         const int u = u_begin + warp + kConsumerWarps * j;
-        if (u >= u0 && u < u1) {
-          const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * UNIT_BYTES);
+        const int st = (u - g0) / per_stage;  // stage of the group holding unit u
+        if (u >= g0 && st < ns && u < u_end) {
+          const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
+          const uint4* rp = reinterpret_cast<const uint4*>(
+              sb + static_cast<size_t>(u - g0 - st * per_stage) * UNIT_BYTES);
 #pragma unroll
           for (int k = 0; k < KI; ++k) {
             const float4 xa = xp[k * 64 + lane], xb = xp[k * 64 + 32 + lane];
@@ -319,11 +356,11 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ring.empty[slot]);
-    ring.seq++;
-    if (!ok) return false;
+    if (A.stage_trace != nullptr && threadIdx.x == 0 && ring.seq < static_cast<uint32_t>(A.stage_stride))
+      A.stage_trace[(static_cast<size_t>(blockIdx.x) * 3 + 2) * A.stage_stride + ring.seq] = globaltimer_ns();
+    release_n(ring, ns);
   }
+  if (!ok) return false;
   float v[MAXJ][NR];
 #pragma unroll
   for (int j = 0; j < MAXJ; ++j)
@@ -351,27 +388,25 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float4* xp = reinterpret_cast<const float4*>(xsm);
   bool ok = true;
-  for (int u0 = u_begin; u0 < u_end; u0 += per_stage) {
-    const int u1 = min(u0 + per_stage, u_end);
-    if (ok) ok = wait_full(A, ring, flag, t0);
-    const uint32_t slot = ring.seq % kStages;
+  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * per_stage) {
+    const int g1 = min(g0 + kGroupStages * per_stage, u_end);
+    const int ns = (g1 - g0 + per_stage - 1) / per_stage;
+    ok = wait_full_n(A, ring, ns, flag, t0);
     if (ok) {
-      const uint8_t* sb = ring.stage[slot];
-      const int first = u0 + ((warp - (u0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
-      for (int u = first; u < u1; u += kConsumerWarps) {
-        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - u0) * ROWB);
+      const int first = g0 + ((warp - (g0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
+      for (int u = first; u < g1; u += kConsumerWarps) {
+        const int st = (u - g0) / per_stage;
+        const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
+        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * per_stage) * ROWB);
         uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll
         for (int k = 0; k < KI; ++k) dot8x2(rp[k * 32 + lane], xp[k * 64 + lane], xp[k * 64 + 32 + lane], a0, a1);
         out(u, warp_sum(f2sum(a0) + f2sum(a1)), 0.f);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&ring.empty[slot]);
-    ring.seq++;
-    if (!ok) return false;
+    release_n(ring, ns);
   }
-  return true;
+  return ok;
 }
 
 // Norm gains for this thread's elements (t + k*256), loaded ahead of the
@@ -441,6 +476,8 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     }
     mbar_arrive_expect_tx(&sm.full[slot], bytes);
     bulk_g2s(sm.stage[slot], src, bytes, &sm.full[slot], pol);
+    if (A.stage_trace != nullptr && seq < static_cast<uint32_t>(A.stage_stride))
+      A.stage_trace[static_cast<size_t>(cta) * 3 * A.stage_stride + seq] = globaltimer_ns();
     ++seq;
   };
   auto stream = [&](const uint8_t* base, int n, int unit_bytes, int per_stage) {
