@@ -367,6 +367,7 @@ def run_ours(args, rank, local_rank, world):
     from transformer_b200.config import CONFIG_306M
     from transformer_b200.multi_sm_decode import DecodeEngine
     from transformer_b200.packing import prepare_decode_weights_nlayer
+    from transformer_b200.replicas import max_over_ranks, shard
     from transformer_b200.synth import batch_cfg5, prompt_cfg1, prompt_cfg2, synth_params
 
     torch.cuda.set_device(local_rank)
@@ -374,20 +375,18 @@ def run_ours(args, rank, local_rank, world):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    if TOTAL_SEQS % world:
-        raise SystemExit("world size must divide 2048")
     cfg = CONFIG_306M
     w = prepare_decode_weights_nlayer(synth_params(cfg, 0), cfg, device=dev)
-    n_seq = TOTAL_SEQS // world
-    n_waves = (n_seq + WAVE - 1) // WAVE
-    wave_b = n_seq // n_waves
+    part = shard(TOTAL_SEQS, world, rank, WAVE)
+    n_seq, n_waves, wave_b = part.n, part.n_waves, part.wave
     eng = DecodeEngine(w, max_batch=max(2, wave_b))
     stream = torch.cuda.current_stream(dev)
-    prompts = batch_cfg5(cfg)[rank * n_seq:(rank + 1) * n_seq]
+    all_prompts = batch_cfg5(cfg)
     waves = []
     for i in range(n_waves):
+        b0, b1 = part.wave_slice(i)
         d = BatchedDecoder(eng, wave_b, seed=1000 * rank + i)
-        d.ingest(list(prompts[i * wave_b:(i + 1) * wave_b]))
+        d.ingest(list(all_prompts[b0:b1]))
         d.capture()
         waves.append(d)
     pos = PROMPT_LEN
@@ -422,10 +421,7 @@ def run_ours(args, rank, local_rank, world):
         dist.barrier()
     clk = clocks.stop() if clocks else None
     eng.check_device()
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, dev)
     ms_per_step = ms / args.steps
     value = TOTAL_SEQS * args.steps / (ms / 1000.0)
     positions = [pos_t0 + i if pos_t0 + i < cfg.context_len else PROMPT_LEN for i in range(args.steps)]
@@ -456,11 +452,7 @@ def run_ours(args, rank, local_rank, world):
             h_out[i].copy_(d.tok, non_blocking=True)
         stream.synchronize()
         p_e2e += 1
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dev)
     e2e_value = TOTAL_SEQS * ne / e2e_s
     for d in waves:
         d.release()

@@ -1,0 +1,69 @@
+"""CPU: the multi-GPU host logic of config 5 (partition of the job's
+sequences over ranks, waves per rank, max-over-ranks timing) on world-size-2
+``gloo`` process groups — no GPU involved."""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch.multiprocessing as mp
+
+from transformer_b200.replicas import max_over_ranks, shard
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_shards_partition_the_job(world):
+    seen = []
+    for r in range(world):
+        s = shard(2048, world, r, 256)
+        assert s.n == 2048 // world and s.n_waves * s.wave == s.n and s.wave <= 256
+        for i in range(s.n_waves):
+            b0, b1 = s.wave_slice(i)
+            assert s.begin <= b0 < b1 <= s.end
+            seen.extend(range(b0, b1))
+    assert sorted(seen) == list(range(2048))  # every sequence exactly once
+
+
+def test_shard_rejects_uneven_splits():
+    with pytest.raises(ValueError):
+        shard(2048, 3, 0)
+    with pytest.raises(ValueError):
+        shard(2048, 2, 2)
+    with pytest.raises(ValueError):
+        shard(257, 1, 0, 256)  # 257 does not split into 2 equal waves
+
+
+def _worker(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        s = shard(2048, world, rank, 256)
+        # per-rank "elapsed" values; every rank must see the slowest
+        got = max_over_ranks(10.0 + rank * 5.0)
+        tokens = max_over_ranks(float(s.n))  # equal shares: the max equals any rank's share
+        out.put((rank, got, tokens, s.begin, s.end))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_max_over_ranks_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 300
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(2))
+    assert [r[1] for r in res] == [15.0, 15.0]
+    assert [r[2] for r in res] == [1024.0, 1024.0]
+    assert res[0][3:] == (0, 1024) and res[1][3:] == (1024, 2048)
+
+
+def test_max_over_ranks_without_group():
+    assert max_over_ranks(3.5) == 3.5
