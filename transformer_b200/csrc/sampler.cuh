@@ -281,9 +281,9 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
 
   // ---- top-p (ref :53-63): sort by (descending p, ascending id) ----
   for (int kk = 2; kk <= kSamplerMaxVocab; kk <<= 1) {
-    for (int j = kk >> 1; j > 0; j >>= 1) {
+    for (int j = kk >> 1, lj = __ffs(kk) - 2; j > 0; j >>= 1, --lj) {  // lj = log2(j)
       for (int i = t; i < kSamplerMaxVocab / 2; i += kSamplerThreads) {
-        const int lo = 2 * j * (i / j) + (i % j), hi = lo + j;
+        const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
         const bool asc = (lo & kk) == 0;
         const uint32_t klo = sm.key[lo], khi = sm.key[hi];
         const uint16_t ilo = sm.idx[lo], ihi = sm.idx[hi];
@@ -296,15 +296,35 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
       __syncthreads();
     }
   }
-  // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one
-  if (t == 0) {
+  // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one.  The
+  // running sum is a float, so float64(c) >= top_p  <=>  c >= thr with thr =
+  // top_p rounded up to a float: the chain stays in float32 (the cumulative
+  // sum itself is sequential, as numpy's).
+  if (warp == 0) {  // warp 0 loads 128 keys per round; lane 0 runs the float32 chain over them in order
+    const float thr = __double2float_ru(a.top_p);
+    const uint4* k4 = reinterpret_cast<const uint4*>(sm.key);
+    const int n4 = (V + 3) / 4;  // keys past V decode to p = 0
     float c = 0.f;
     int cut = V;
-    for (int i = 0; i < V; ++i) {
-      c = __fadd_rn(c, key_to_p(sm.key[i]));
-      if (static_cast<double>(c) >= a.top_p) { cut = i + 1; break; }
+    for (int base = 0; base < n4 && cut == V; base += 32) {
+      const uint4 kk = base + lane < n4 ? k4[base + lane] : make_uint4(~0u, ~0u, ~0u, ~0u);
+#pragma unroll 8
+      for (int src = 0; src < 32; ++src) {
+        const uint32_t kx = __shfl_sync(0xffffffffu, kk.x, src), ky = __shfl_sync(0xffffffffu, kk.y, src);
+        const uint32_t kz = __shfl_sync(0xffffffffu, kk.z, src), kw = __shfl_sync(0xffffffffu, kk.w, src);
+        const int i0 = 4 * (base + src);
+        c = __fadd_rn(c, key_to_p(kx));
+        if (cut == V && c >= thr) cut = i0 + 1;
+        c = __fadd_rn(c, key_to_p(ky));
+        if (cut == V && c >= thr) cut = i0 + 2;
+        c = __fadd_rn(c, key_to_p(kz));
+        if (cut == V && c >= thr) cut = i0 + 3;
+        c = __fadd_rn(c, key_to_p(kw));
+        if (cut == V && c >= thr) cut = i0 + 4;
+      }
+      cut = __shfl_sync(0xffffffffu, cut, 0);  // every lane ran the same chain; keep them in step
     }
-    sm.cutoff = cut;
+    if (lane == 0) sm.cutoff = min(cut, V);
   }
   __syncthreads();
   const int cut = sm.cutoff;
