@@ -175,6 +175,32 @@ def test_paged_matches_single_sequence_kernel(engine306_batched, engine306):
     assert_logits_close(logits[0].cpu().numpy(), ref, "batched vs B=1 kernel")
 
 
+def test_paged_step_bitwise_reproducible(engine306_batched):
+    """Every reduction of the batched step has a fixed order (cluster split-K
+    partials in rank order, attention partials in CTA order): the same step
+    repeated gives bit-identical logits and cache rows."""
+    from transformer_b200.config import CONFIG_306M as cfg
+    eng = engine306_batched
+    dev = eng.device
+    rng = np.random.default_rng(21)
+    B = 64
+    table, nb = _table(rng, B, cfg.context_len // PAGE_TOKENS)
+    table_d = torch.from_numpy(table).to(dev)
+    pool = eng.new_kv_pool(nb)
+    pool.copy_((torch.randn(pool.shape, generator=torch.Generator().manual_seed(3)) * 0.5).to(torch.bfloat16))
+    tok = torch.from_numpy(rng.integers(0, cfg.vocab_size, B).astype(np.int32)).to(dev)
+    pos = torch.from_numpy(rng.integers(0, 400, B).astype(np.int32)).to(dev)
+    outs = []
+    for _ in range(3):
+        logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+        nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+        eng.step_paged(tok, pos, pool, table_d, logits, nxt)
+        outs.append((logits.clone(), nxt.clone(), pool.clone()))
+    eng.check_device()
+    for lg, nx, pl in outs[1:]:
+        assert torch.equal(lg, outs[0][0]) and torch.equal(nx, outs[0][1]) and torch.equal(pl, outs[0][2])
+
+
 def test_paged_bad_inputs_set_status(engine_tiny_batched):
     """An out-of-range token or block-table entry is reported through the
     workspace status word (B2D_ERR_DEVICE_INPUT), not a fault."""

@@ -67,3 +67,40 @@ def test_max_over_ranks_gloo_world2():
 
 def test_max_over_ranks_without_group():
     assert max_over_ranks(3.5) == 3.5
+
+
+def _dying_worker(rank, world, port, out):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # a worker that dies between steps (host fault), without joining the collective
+    try:
+        max_over_ranks(1.0)
+        out.put((rank, "completed"))
+    except Exception as e:  # the survivor learns of it through the collective's error
+        out.put((rank, type(e).__name__))
+
+
+def test_dead_rank_is_reported_not_hung():
+    """A rank that exits between steps: the surviving rank's next timing
+    reduction fails with an error within the process-group timeout instead of
+    waiting for ever."""
+    import time
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29900 + os.getpid() % 90
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode is not None for p in procs), "a rank hung"
+    assert procs[1].exitcode == 3
+    rank, what = q.get(timeout=10)
+    assert rank == 0 and what != "completed"
+    assert time.time() - t0 < 120
