@@ -78,13 +78,13 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
-    p = os.path.join(REPO, "profiles", "decode_b1_cfg1.md")
+def profile_traffic(name="decode_b1_cfg1.md", key="traffic_bytes_per_launch"):
+    """DRAM bytes (per launch / per step) from a committed ncu summary."""
+    p = os.path.join(REPO, "profiles", name)
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith(key + ":"):
             try:
                 return int(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
@@ -428,6 +428,7 @@ def run_ours(args, rank, local_rank, world):
     alg_step = float(np.mean([n_waves * cfg.step_bytes([p] * wave_b) for p in positions]))
     peak, peak_kind = measured_peaks()
     achieved = alg_step / (ms_per_step / 1000.0) / 1e9
+    serve_traffic = profile_traffic("paged_step_b256_pos80.md", "traffic_bytes_per_step") if wave_b == 256 else None
 
     # ---- end to end through the public call, host buffers ----
     ne = max(1, args.e2e_steps)
@@ -499,7 +500,10 @@ def run_ours(args, rank, local_rank, world):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "scope": f"whole batched step per GPU ({per_wave} "
                      "kernels per wave: projections on tcgen05, paged attention, RMSNorm, embedding, argmax)",
-                     "traffic": None, "algorithmic_bytes_per_step": alg_step},
+                     "traffic": serve_traffic * n_waves if serve_traffic else None,
+                     "traffic_source": "profiles/paged_step_b256_pos80.md (one wave-step of 256 at position 80, "
+                                       "x waves)",
+                     "algorithmic_bytes_per_step": alg_step},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                 "d2h_bytes_per_step": 4 * n_seq, "steps": ne,
                 "note": "per wave: pinned H2D of tokens+positions, b2d_decode_step_paged, D2H next tokens; "
