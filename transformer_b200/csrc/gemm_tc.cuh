@@ -15,8 +15,9 @@
 // columns [r*BN/ks, (r+1)*BN/ks) by reading every partial through distributed
 // shared memory in rank order (deterministic), then applies the epilogue.
 //
-// CTA = 4 warps: warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
-// allocator, all four the epilogue (warp w owns TMEM lanes 32w..32w+31).
+// CTA = 8 warps: warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
+// allocator, all eight the epilogue (warps w and w+4 read TMEM lanes
+// 32(w%4).. in alternate 32-column chunks; all 256 threads store).
 // Grid = (M/128, ceil(N/BN), ksplit).  Launched with programmatic dependent
 // launch: the weight tiles of the first stages are requested before waiting
 // for the previous kernel (they do not depend on it).  Every wait is bounded;
@@ -32,7 +33,7 @@ namespace b2d {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle atom of bf16
-constexpr int kGemmThreads = 128;
+constexpr int kGemmThreads = 256;
 constexpr int kGemmMaxSplit = 8;  // portable cluster size
 constexpr uint64_t kGemmWaitNs = 200000000ull;  // 200 ms
 
@@ -125,8 +126,8 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
 template <int EPI>
 __device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row, int n) {
   if (EPI == EPI_SWIGLU_BF16) {
-    const float a0 = v.x * (1.0f / (1.0f + __expf(-v.x))) * v.y;
-    const float a1 = v.z * (1.0f / (1.0f + __expf(-v.z))) * v.w;
+    const float a0 = v.x * __frcp_rn(1.0f + __expf(-v.x)) * v.y;  // 1/(1+e): the same rounding as a division
+    const float a1 = v.z * __frcp_rn(1.0f + __expf(-v.z)) * v.w;
     *reinterpret_cast<__nv_bfloat162*>(g.ybf + static_cast<size_t>(n) * g.ldy + (row >> 1)) =
         __floats2bfloat162_rn(a0, a1);
   } else {
@@ -221,13 +222,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
     tc_commit(done);  // accumulator complete (or the issued part of it)
   }
 
-  // ---- epilogue: all four warps ----
+  // ---- epilogue: all eight warps ----
   __syncwarp();
   pdl_wait();  // the residual comes from earlier kernels
   const bool got = __all_sync(0xffffffffu, gemm_wait(done, 0, g.err));
   tc_fence_after();
   if (threadIdx.x == 0) gemm_stamp(g, 4);
-  const int r = warp * 32 + lane;  // accumulator row = weight row m0 + r
+  const int r = (warp & 3) * 32 + lane;  // accumulator row = weight row m0 + r (this warp's TMEM lanes)
   int slice = blockIdx.y, j0 = 0, j1 = BN;  // output columns this CTA stores
   // The accumulator goes to shared memory as [BN][128] f32; the outputs are
   // then written as items of 4 consecutive rows (float4 / bf16x2 stores).
@@ -236,9 +237,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   // [rank*BN/ks, (rank+1)*BN/ks).
   float* red = reinterpret_cast<float*>(sm);  // every MMA has read its stage by now
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
+  for (int c0 = (warp >> 2) * 32; c0 < BN; c0 += 64) {  // the two warp groups take alternate chunks
     float v[32];
-    tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c0, v);
+    tmem_ld32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c0, v);
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (c0 + j < BN) red[(c0 + j) * kGemmBM + r] = got ? v[j] : 0.f;
@@ -255,8 +256,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   if (threadIdx.x == 0) gemm_stamp(g, 5);
   const int items = (j1 - j0) * (kGemmBM / 4);
   const uint32_t red_base = smem_addr(red);
+  if (ks == 1) {  // the tile is local: 8 items' loads in flight per round
+    constexpr int U = 8;
 #pragma unroll 1
-  for (int it0 = threadIdx.x; it0 < items; it0 += 2 * kGemmThreads) {
+    for (int it0 = threadIdx.x; it0 < items; it0 += U * kGemmThreads) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int it = it0 + u * kGemmThreads;
+        if (it < items) {
+          const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
+          v[u] = *reinterpret_cast<const float4*>(red + kGemmBM * j + r4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int it = it0 + u * kGemmThreads;
+        if (it < items) {
+          const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
+          const int n = n0 + j, rw = m0 + r4;
+          if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, v[u], rw, n);
+        }
+      }
+    }
+  }
+#pragma unroll 1
+  for (int it0 = threadIdx.x; ks > 1 && it0 < items; it0 += 2 * kGemmThreads) {
     float4 part[2][kGemmMaxSplit];  // both items' loads issued before the first add
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
