@@ -13,6 +13,7 @@
 #include <utility>
 
 #include "../../include/b2d.h"
+#include "attn_paged.cuh"
 #include "batched.cuh"
 #include "decode_b1.cuh"
 #include "gemm_tc.cuh"
@@ -592,12 +593,11 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
   pa.part = ws->att_part; pa.tickets = ws->att_tickets; pa.max_chunks = ws->att_chunks;
-  {  // chunks per CTA: about 8 resident attention CTAs per SM over the whole (b, kv head, chunk) space
-    const int items = batch * c.n_kv_heads * ws->att_chunks, target = 8 * m->grid;
-    pa.cpc = (items + target - 1) / target;
-    if (pa.cpc < 1) pa.cpc = 1;
-    if (pa.cpc > ws->att_chunks) pa.cpc = ws->att_chunks;
-    if (ws->force_att_cpc) pa.cpc = ws->force_att_cpc;
+  {  // CTAs per (row, kv head): about 5 resident attention CTAs per SM over all (row, kv head) pairs
+    const int pairs = batch * c.n_kv_heads, target = 5 * m->grid;
+    const int cap = std::min(b2d::kPaMaxSplits, std::min(ws->att_chunks, (c.context_len + 15) / 16));
+    pa.cpc = std::max(1, std::min(cap, (target + pairs - 1) / pairs));
+    if (ws->force_att_cpc) pa.cpc = std::min(cap, ws->force_att_cpc);
   }
   // RMSNorm of the residual stream: fused into the residual projection's
   // epilogue (last M tile per column slice) when a slice has at most
@@ -613,8 +613,8 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     pa.layer = l;
     if (prefill)  // every row's K/V in the cache before any row attends
       B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
-    B2D_CUDA(launch_k(b2d::paged_attn_kernel, dim3((ws->att_chunks + pa.cpc - 1) / pa.cpc, c.n_kv_heads, batch),
-                      dim3(128), st, pdl, pa),
+    B2D_CUDA(launch_k(b2d::paged_attn_mma_kernel, dim3(pa.cpc, c.n_kv_heads, batch), dim3(32 * b2d::kPaWarps), st,
+                      pdl, pa),
              "attention");
     launches_other += prefill ? 2 : 1;
     const float* ln2_l = ln2 + size_t(l) * D;
