@@ -126,8 +126,8 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
 template <int EPI>
 __device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row, int n) {
   if (EPI == EPI_SWIGLU_BF16) {
-    const float a0 = v.x * __frcp_rn(1.0f + __expf(-v.x)) * v.y;  // 1/(1+e): the same rounding as a division
-    const float a1 = v.z * __frcp_rn(1.0f + __expf(-v.z)) * v.w;
+    const float a0 = v.x * __fdividef(1.0f, 1.0f + __expf(-v.x)) * v.y;  // silu(gate) * up
+    const float a1 = v.z * __fdividef(1.0f, 1.0f + __expf(-v.z)) * v.w;
     *reinterpret_cast<__nv_bfloat162*>(g.ybf + static_cast<size_t>(n) * g.ldy + (row >> 1)) =
         __floats2bfloat162_rn(a0, a1);
   } else {
