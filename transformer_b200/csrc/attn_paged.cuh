@@ -1,14 +1,15 @@
 // attn_paged.cuh — decode attention over a paged (or contiguous) KV cache on
 // warp-level tensor-core MMAs (sm_100a).
 //
-// grid (splits, n_kv, rows), 4 warps.  CTA (x, g, b) takes an even share of
-// the 16-position pages 0 .. pos[b]/16 of row b (split by the row's actual
-// length, so a launch captured once serves every position), its warps take
-// the CTA's pages round-robin, and every warp runs its own online softmax:
+// Every warp is an independent attention unit (row b, kv head g, split x):
+// it takes an even share x of the 16-position pages 0 .. pos[b]/16 of row b
+// (split by the row's actual length, so a launch captured once serves every
+// position) and runs its own online softmax over them for the GQA query heads
+// of g.  kPaWarps units per CTA, no CTA-wide synchronisation.
 //
 //   * page loads: each lane copies 4 + 4 16-byte pieces of the page's K and V
 //     rows (2 KB each, contiguous in the pool) with `cp.async` into a
-//     two-stage ring private to the warp (rows padded to 144 B, so the
+//     kPaStages-deep ring private to the warp (rows padded to 144 B, so the
 //     `ldmatrix` row reads below are conflict-free).  In decode (append) mode
 //     the first pages are requested before the programmatic wait: they only
 //     depend on earlier steps, not on the QKV projection being waited for.
@@ -21,12 +22,12 @@
 //   * P.V: `mma.m16n8k16` with P = hi + lo bf16 again (rows 0..3 / 8..11) and
 //     the V rows as B (`ldmatrix.trans`), 8 n-tiles of dimensions.
 //
-// The warps' (m, l, o) are merged in warp order in shared memory; when a row
-// spans several CTAs each writes its (m, l, o) partial and the last CTA to
-// take the (row, kv head) ticket merges them in CTA order.  Every reduction
-// has a fixed order: results are bitwise reproducible.  The CTA holding
-// position pos[b] uses the new K (post-RoPE) / V rounded to bf16 (the cached
-// values) and, in append mode, writes them to the cache.  Math: model.py:
+// A unit that covers its whole row writes the output directly; when a row is
+// split, each unit writes its (m, l, o) partial and the last unit to take the
+// (row, kv head) ticket merges them in split order.  Every reduction has a
+// fixed order: results are bitwise reproducible.  The unit holding position
+// pos[b] uses the new K (post-RoPE) / V rounded to bf16 (the cached values)
+// and, in append mode, writes them to the cache.  Math: model.py:
 // 100-131 (rotate-half RoPE, causal softmax over 0..p, GQA sharing).
 #pragma once
 
@@ -36,11 +37,13 @@
 
 namespace b2d {
 
-constexpr int kPaWarps = 4;     // warps per CTA
-constexpr int kPaStages = 2;    // pages in each warp's ring
+constexpr int kPaWarps = 2;     // units (warps) per CTA
+constexpr int kPaStages = 4;    // pages in each warp's ring (consumed two at a time)
 constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
-constexpr int kPaMaxSplits = 8; // CTAs per (row, kv head); <= the partial buffer's chunks
+constexpr int kPaMaxSplits = 8; // units per (row, kv head); <= the partial buffer's chunks
+constexpr int kPaWarpSmem = kPaStages * kPaStageElems * 2 + 256;  // ring + the new K / V row (bytes)
+constexpr int kPaSmem = kPaWarps * kPaWarpSmem;
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -80,63 +83,84 @@ __device__ __forceinline__ void split_bf2(float x0, float x1, uint32_t& hi, uint
   lo = bf2_rn(x0 - __low2float(h), x1 - __high2float(h));
 }
 
-// First element of page `pg`'s K (kv = 0) or V (kv = 1) rows: 16 rows of 64.
-__device__ __forceinline__ const __nv_bfloat16* page_rows(const PagedAttnArgs& a, const int32_t* tb, int pg,
-                                                          int kv, int g) {
+// First element of page `pg`'s K (kv = 0) or V (kv = 1) rows: 16 rows of 64
+// (paged pool: physical block `blk`; contiguous cache: blk unused).
+__device__ __forceinline__ const __nv_bfloat16* page_rows(const PagedAttnArgs& a, int blk, int pg, int kv, int g) {
   if (a.table == nullptr)
     return a.pool + ((((static_cast<size_t>(a.layer) * 2 + kv) * a.n_kv + g) * a.ctx) + pg * kPageTokens) * 64;
-  return a.pool + (((static_cast<size_t>(a.layer) * a.num_blocks + tb[pg]) * 2 + kv) * a.n_kv + g) *
+  return a.pool + (((static_cast<size_t>(a.layer) * a.num_blocks + blk) * 2 + kv) * a.n_kv + g) *
                       (kPageTokens * 64);
 }
 
-__global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const __grid_constant__ PagedAttnArgs a) {
-  __shared__ __align__(16) __nv_bfloat16 stage[kPaWarps][kPaStages][kPaStageElems];
-  __shared__ __align__(16) __nv_bfloat16 skn[64], svn[64];  // the new position's K / V (bf16, as cached)
-  __shared__ float wm[kPaWarps][4], wl[kPaWarps][4];
-  __shared__ uint32_t s_last;
-  const int x = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+// grid ceil(rows * n_kv * splits / kPaWarps), kPaWarps * 32 threads, kPaSmem
+// bytes of dynamic shared memory; a.cpc = splits.  Unit u = blockIdx.x *
+// kPaWarps + warp is (b, g, x) with u = (b * n_kv + g) * splits + x.
+__global__ void __launch_bounds__(32 * kPaWarps) paged_attn_mma_kernel(const __grid_constant__ PagedAttnArgs a,
+                                                                       int n_rows) {
+  extern __shared__ __align__(16) uint8_t pa_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
+  const int splits = a.cpc;
+  const int u = blockIdx.x * kPaWarps + warp;
+  if (u >= n_rows * a.n_kv * splits) return;
+  const int x = u % splits, g = (u / splits) % a.n_kv, b = u / (splits * a.n_kv);
+  // diagnostics: 0 entry, 1 loads issued, 2 past the programmatic wait, 3 query ready,
+  // 4 first page done, 5 pages done, 6 result / partial written, 7 merged
+  uint64_t* trace = a.trace != nullptr && u < a.trace_units ? a.trace + static_cast<size_t>(u) * 8 : nullptr;
+  auto stamp = [&](int slot) {
+    if (trace != nullptr && lane == 0) trace[slot] = globaltimer_ns();
+  };
+  stamp(0);
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * kPaWarpSmem);
+  __nv_bfloat16* skn = ring + kPaStages * kPaStageElems;  // the new position's K / V (bf16, as cached)
+  __nv_bfloat16* svn = skn + 64;
   const int GQA = a.n_heads / a.n_kv;
   const bool early = a.append;  // decode: the cache pages do not depend on the waited-for kernel
   if (!early) {
     pdl_wait();
     pdl_launch();
   }
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
+  // The row's first 32 block-table entries, read alongside the position (lane i: page i).
+  const int tbl = tb != nullptr && lane < a.bps ? __ldg(tb + lane) : 0;
   const int p = a.pos[b];
   if (p < 0 || p >= a.ctx) {  // idle row: no cache write, zero output
     if (early) {
       pdl_wait();
       pdl_launch();
     }
-    if (x == 0 && warp < GQA)
-      reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + warp) * 64)[lane] =
-          __floats2bfloat162_rn(0.f, 0.f);
+    if (x == 0)
+      for (int i = lane; i < GQA * 32; i += 32)
+        reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + g * GQA * 64)[i] =
+            __floats2bfloat162_rn(0.f, 0.f);
     return;
   }
   const int npg = p / kPageTokens + 1;
-  const int ppc = (npg + a.cpc - 1) / a.cpc;  // pages per CTA (a.cpc = splits)
-  const int pg_lo = x * ppc;
-  if (pg_lo >= npg) return;  // no pages for this CTA: no ticket either
-  const int pg_hi = min(pg_lo + ppc, npg);
-  const int ncta = (npg + ppc - 1) / ppc;  // CTAs sharing this (row, kv head)
+  const int ppu = (npg + splits - 1) / splits;  // pages per unit
+  const int pg_lo = x * ppu;
+  if (pg_lo >= npg) return;  // no pages for this unit: no ticket either
+  const int pg_hi = min(pg_lo + ppu, npg);
+  const int nunits = (npg + ppu - 1) / ppu;  // units sharing this (row, kv head)
   const bool owner = pg_hi == npg;
-  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
   bool bad = tb != nullptr && npg > a.bps;
-  for (int i = pg_lo + t; tb != nullptr && !bad && i < pg_hi; i += 32 * kPaWarps) {
-    const int e = tb[i];
-    bad = e < 0 || e >= a.num_blocks;
+  if (tb != nullptr && !bad) {  // every page of the unit must exist
+    if (lane >= pg_lo && lane < pg_hi) bad = tbl < 0 || tbl >= a.num_blocks;
+    for (int i = max(pg_lo, 32) + lane; i < pg_hi; i += 32) {
+      const int e = tb[i];
+      bad = bad || e < 0 || e >= a.num_blocks;
+    }
   }
-  bad = __syncthreads_or(bad);
+  bad = __any_sync(0xffffffffu, bad);
 
-  // ---- this warp's pages: pg_lo + warp + kPaWarps * k, k < nw ----
-  const int nw = bad ? 0 : (pg_hi - pg_lo - warp + kPaWarps - 1) / kPaWarps;
+  // ---- page ring ----
+  const int nw = bad ? 0 : pg_hi - pg_lo;
   const int rows_max = a.table == nullptr ? a.ctx : 1 << 30;  // contiguous cache: no row past the context
   auto issue = [&](int k) {
-    const int pg = pg_lo + warp + kPaWarps * k;
-    const __nv_bfloat16* ks = page_rows(a, tb, pg, 0, g);
-    const __nv_bfloat16* vs = page_rows(a, tb, pg, 1, g);
-    const uint32_t dst = smem_addr(&stage[warp][k % kPaStages][0]);
+    const int pg = pg_lo + k;  // (warp-uniform)
+    const int blk = tb == nullptr ? 0 : pg < 32 ? __shfl_sync(0xffffffffu, tbl, pg) : tb[pg];
+    const __nv_bfloat16* ks = page_rows(a, blk, pg, 0, g);
+    const __nv_bfloat16* vs = page_rows(a, blk, pg, 1, g);
+    const uint32_t dst = smem_addr(ring + (k % kPaStages) * kPaStageElems);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = lane + 32 * r, row = i >> 3, c16 = i & 7;
@@ -151,11 +175,24 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
     if (k < nw) issue(k);
     cp_async_commit();
   }
+  // RoPE factors of position p (model constants): lane (gid, tig) needs pairs
+  // 2tig, 2tig+1 and 8+2tig, 9+2tig of k-steps 0, 1; the owner's K row needs lane.
+  float2 rc[2][2], rs[2][2];
+#pragma unroll
+  for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      rc[s2][h2] = *reinterpret_cast<const float2*>(a.rcos + static_cast<size_t>(p) * 32 + 16 * s2 + 8 * h2 + 2 * tig);
+      rs[s2][h2] = *reinterpret_cast<const float2*>(a.rsin + static_cast<size_t>(p) * 32 + 16 * s2 + 8 * h2 + 2 * tig);
+    }
+  const float cs_l = a.rcos[static_cast<size_t>(p) * 32 + lane], sn_l = a.rsin[static_cast<size_t>(p) * 32 + lane];
+  stamp(1);
   if (early) {
     pdl_wait();
     pdl_launch();
   }
-  if (bad && t == 0) atomicCAS(a.status, 0u, 0x203u);
+  stamp(2);
+  if (bad && lane == 0) atomicCAS(a.status, 0u, 0x203u);
 
   // ---- query fragments (rows gid < GQA: head g*GQA + gid; hi part rows 0..7, lo part rows 8..15) ----
   const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
@@ -166,17 +203,14 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
       const float* q = row + (g * GQA + gid) * 64;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const float2 u = *reinterpret_cast<const float2*>(q + 16 * s + 2 * tig);
-        const float2 w = *reinterpret_cast<const float2*>(q + 16 * s + 8 + 2 * tig);
-        qv[s][0] = u.x; qv[s][1] = u.y; qv[s][2] = w.x; qv[s][3] = w.y;
+        const float2 v0 = *reinterpret_cast<const float2*>(q + 16 * s + 2 * tig);
+        const float2 v1 = *reinterpret_cast<const float2*>(q + 16 * s + 8 + 2 * tig);
+        qv[s][0] = v0.x; qv[s][1] = v0.y; qv[s][2] = v1.x; qv[s][3] = v1.y;
       }
 #pragma unroll
       for (int s = 0; s < 2; ++s) {  // rotate-half RoPE: dims d and d + 32 are k-steps s and s + 2
-        const float2 c0 = *reinterpret_cast<const float2*>(a.rcos + static_cast<size_t>(p) * 32 + 16 * s + 2 * tig);
-        const float2 c1 = *reinterpret_cast<const float2*>(a.rcos + static_cast<size_t>(p) * 32 + 16 * s + 8 + 2 * tig);
-        const float2 s0 = *reinterpret_cast<const float2*>(a.rsin + static_cast<size_t>(p) * 32 + 16 * s + 2 * tig);
-        const float2 s1 = *reinterpret_cast<const float2*>(a.rsin + static_cast<size_t>(p) * 32 + 16 * s + 8 + 2 * tig);
-        const float cs[4] = {c0.x, c0.y, c1.x, c1.y}, sn[4] = {s0.x, s0.y, s1.x, s1.y};
+        const float cs[4] = {rc[s][0].x, rc[s][0].y, rc[s][1].x, rc[s][1].y};
+        const float sn[4] = {rs[s][0].x, rs[s][0].y, rs[s][1].x, rs[s][1].y};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float lo = qv[s][e], hi = qv[s + 2][e];
@@ -194,8 +228,8 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
       split_bf2(qv[s][2], qv[s][3], qa[s][2], qa[s][3]);
     }
   }
-  if (owner && warp == 0) {  // the new position's K (post-RoPE) / V, bf16 as cached
-    const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
+  if (owner) {  // the new position's K (post-RoPE) / V, bf16 as cached
+    const float cs = cs_l, sn = sn_l;
     const float* k = row + a.n_heads * 64 + g * 64;
     const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
     const float klo = k[lane], khi = k[lane + 32];
@@ -211,10 +245,11 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
       vd[lane] = svn[lane];
       vd[lane + 32] = svn[lane + 32];
     }
+    __syncwarp();
   }
-  __syncthreads();  // skn / svn ready
+  stamp(3);
 
-  // ---- the warp's pages ----
+  // ---- the unit's pages ----
   float o[8][4];  // [dim n-tile][c0..c3]: rows gid (hi) and gid + 8 (lo) of head gid
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -222,14 +257,18 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
   const bool head = gid < GQA;
   // ldmatrix lane addressing: matrix mi = lane / 8, row lane % 8
   const int mi = lane >> 3, mr = lane & 7;
+  static_assert(kPaStages % 2 == 0, "pages are consumed in pairs");
 #pragma unroll 1
-  for (int k = 0; k < nw; ++k) {
-    const int pg = pg_lo + warp + kPaWarps * k;
-    __nv_bfloat16* st = &stage[warp][k % kPaStages][0];
-    cp_async_wait<kPaStages - 1>();
+  for (int k = 0; k < nw; k += 2) {  // pages k, k + 1 (when present) as one block of 32 positions
+    const int pg = pg_lo + k;
+    const bool two = k + 1 < nw;
+    __nv_bfloat16* st0 = ring + (k % kPaStages) * kPaStageElems;
+    __nv_bfloat16* st1 = ring + ((k + 1) % kPaStages) * kPaStageElems;
+    cp_async_wait<kPaStages - 2>();
     __syncwarp();
-    if (pg == npg - 1) {  // the page of position p: its row from the new K / V, V rows past p zeroed
-      const int rp = p - pg * kPageTokens;
+    if (pg == npg - 1 || (two && pg + 1 == npg - 1)) {  // the page of position p: its row from the new
+      __nv_bfloat16* st = pg == npg - 1 ? st0 : st1;   // K / V, V rows past p zeroed
+      const int rp = p - (npg - 1) * kPageTokens;
       if (lane < 8)
         *reinterpret_cast<uint4*>(st + rp * kPaPitch + lane * 8) = reinterpret_cast<const uint4*>(skn)[lane];
       else if (lane < 16)
@@ -241,142 +280,153 @@ __global__ void __launch_bounds__(32 * kPaWarps, 5) paged_attn_mma_kernel(const 
       }
       __syncwarp();
     }
-    const uint32_t sb = smem_addr(st);
-    // scores: n-tiles j (positions 8j..8j+7), k-steps s (dims 16s..16s+15)
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const uint32_t sb0 = smem_addr(st0), sb1 = smem_addr(st1);
+    // scores: n-tiles j (positions 8j..8j+7 of the block: page j / 2), k-steps s (dims 16s..16s+15)
+    float sc[4][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
-      for (int s2 = 0; s2 < 4; s2 += 2) {
+    for (int s2 = 0; s2 < 4; s2 += 2)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j >= 2 && !two) continue;
         uint32_t b0, b1, b2, b3;  // (s2: dims +0, +8), (s2 + 1: dims +0, +8)
-        ldsm_x4(sb + 2u * ((8 * j + mr) * kPaPitch + 16 * s2 + 8 * mi), b0, b1, b2, b3);
+        ldsm_x4((j < 2 ? sb0 : sb1) + 2u * ((8 * (j & 1) + mr) * kPaPitch + 16 * s2 + 8 * mi), b0, b1, b2, b3);
         mma_bf16(sc[j], qa[s2][0], qa[s2][1], qa[s2][2], qa[s2][3], b0, b1);
         mma_bf16(sc[j], qa[s2 + 1][0], qa[s2 + 1][1], qa[s2 + 1][2], qa[s2 + 1][3], b2, b3);
       }
-    // head gid's scores at positions 2tig, 2tig+1 (j = 0) and 8+2tig, 9+2tig (j = 1): hi + lo rows
-    float s4[4];
+    // head gid's scores: block positions 8j + 2tig + e (hi + lo rows)
+    float s8[8];
     const int q0 = pg * kPageTokens + 2 * tig;
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float v = sc[j][e] + sc[j][2 + e];
-        s4[2 * j + e] = head && q0 + 8 * j + e <= p ? v : -INFINITY;
+        s8[2 * j + e] = head && (j < 2 || two) && q0 + 8 * j + e <= p ? v : -INFINITY;
       }
-    float mx = fmaxf(fmaxf(s4[0], s4[1]), fmaxf(s4[2], s4[3]));
+    float mx = s8[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) mx = fmaxf(mx, s8[e]);
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float mn = fmaxf(m, mx);  // finite for heads: position pg*16 <= p is in every page
+    const float mn = fmaxf(m, mx);  // finite for heads: position pg*16 <= p is in every block
     const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-    float pr[4];
+    float pr[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) pr[e] = s4[e] == -INFINITY ? 0.f : __expf(s4[e] - mn);
+    for (int e = 0; e < 8; ++e) pr[e] = s8[e] == -INFINITY ? 0.f : __expf(s8[e] - mn);
     m = head ? mn : -INFINITY;
-    l = fmaf(l, alpha, (pr[0] + pr[1]) + (pr[2] + pr[3]));
+    l = fmaf(l, alpha, ((pr[0] + pr[1]) + (pr[2] + pr[3])) + ((pr[4] + pr[5]) + (pr[6] + pr[7])));
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       o[j][0] *= alpha; o[j][1] *= alpha; o[j][2] *= alpha; o[j][3] *= alpha;
     }
-    uint32_t pa0, pa1, pa2, pa3;  // A: rows gid = P hi, gid + 8 = P lo; k = positions 2tig.. / 8+2tig..
-    split_bf2(pr[0], pr[1], pa0, pa1);
-    split_bf2(pr[2], pr[3], pa2, pa3);
-    // P.V: n-tiles of 8 dimensions; V rows = k (ldmatrix.trans)
+    // P.V per page: A rows gid = P hi, gid + 8 = P lo; k = the page's positions; V rows (ldmatrix.trans)
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      uint32_t b0, b1, b2, b3;  // (tile j: rows 0-7, 8-15), (tile j+1: rows 0-7, 8-15)
-      ldsm_x4_t(sb + 2u * ((kPageTokens + (mi & 1) * 8 + mr) * kPaPitch + 8 * (j + (mi >> 1))), b0, b1, b2, b3);
-      mma_bf16(o[j], pa0, pa1, pa2, pa3, b0, b1);
-      mma_bf16(o[j + 1], pa0, pa1, pa2, pa3, b2, b3);
+    for (int pp = 0; pp < 2; ++pp) {
+      if (pp == 1 && !two) break;
+      uint32_t pa0, pa1, pa2, pa3;
+      split_bf2(pr[4 * pp + 0], pr[4 * pp + 1], pa0, pa1);
+      split_bf2(pr[4 * pp + 2], pr[4 * pp + 3], pa2, pa3);
+      const uint32_t sb = pp == 0 ? sb0 : sb1;
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t b0, b1, b2, b3;  // (tile j: rows 0-7, 8-15), (tile j+1: rows 0-7, 8-15)
+        ldsm_x4_t(sb + 2u * ((kPageTokens + (mi & 1) * 8 + mr) * kPaPitch + 8 * (j + (mi >> 1))), b0, b1, b2, b3);
+        mma_bf16(o[j], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16(o[j + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
     }
-    __syncwarp();  // every lane's reads of this stage are done before it is refilled
+    __syncwarp();  // every lane's reads of these stages are done before they are refilled
     if (k + kPaStages < nw) issue(k + kPaStages);
     cp_async_commit();
+    if (k + 1 + kPaStages < nw) issue(k + 1 + kPaStages);
+    cp_async_commit();
+    if (k == 0) stamp(4);
   }
   cp_async_wait<0>();
+  stamp(5);
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
 
-  // ---- merge the warps in warp order (the stages are free now) ----
-  __syncthreads();
-  float* wo = reinterpret_cast<float*>(&stage[0][0][0]);  // [warp][4 heads][64]
-  static_assert(sizeof(stage) >= kPaWarps * 4 * 64 * sizeof(float), "merge area");
-  if (head) {
+  // lane (gid < GQA, tig) holds head g*GQA + gid, dims 8j + 2tig, 8j + 2tig + 1 (j < 8)
+  if (nunits == 1) {
+    if (head) {
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      __nv_bfloat162* out = reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo +
+                                                             (g * GQA + gid) * 64);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      *reinterpret_cast<float2*>(wo + (warp * 4 + gid) * 64 + 8 * j + 2 * tig) =
-          make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
-    if (tig == 0) {
-      wm[warp][gid] = m;
-      wl[warp][gid] = l;
+      for (int j = 0; j < 8; ++j)
+        out[4 * j + tig] = __floats2bfloat162_rn((o[j][0] + o[j][2]) * inv, (o[j][1] + o[j][3]) * inv);
     }
-  }
-  __syncthreads();
-  const int h = g * GQA + warp;  // warp h < GQA merges head g*GQA + h, dims 2 lane, 2 lane + 1
-  float o0 = 0.f, o1 = 0.f, M = -INFINITY, L = 0.f;
-  if (warp < GQA) {
-#pragma unroll
-    for (int w = 0; w < kPaWarps; ++w) M = fmaxf(M, wm[w][warp]);
-#pragma unroll
-    for (int w = 0; w < kPaWarps; ++w) {
-      const float mw = wm[w][warp];
-      const float wgt = mw == -INFINITY ? 0.f : __expf(mw - M);
-      const float2 v = *reinterpret_cast<const float2*>(wo + (w * 4 + warp) * 64 + 2 * lane);
-      L = fmaf(wgt, wl[w][warp], L);
-      o0 = fmaf(wgt, v.x, o0);
-      o1 = fmaf(wgt, v.y, o1);
-    }
-  }
-  if (ncta == 1) {
-    if (warp < GQA) {
-      const float inv = L > 0.f ? 1.0f / L : 0.f;
-      reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
-          __floats2bfloat162_rn(o0 * inv, o1 * inv);
-    }
+    stamp(6);
+    stamp(7);
     return;
   }
-  if (warp < GQA) {
-    float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks + x) * kAttPart;
-    reinterpret_cast<float2*>(part + 4)[lane] = make_float2(o0, o1);
-    if (lane == 0) {
-      part[0] = M;
-      part[1] = L;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (t == 0) {
-    const uint32_t prev = atomicAdd(&a.tickets[b * a.n_kv + g], 1u);
-    s_last = prev == static_cast<uint32_t>(ncta - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (t == 0) a.tickets[b * a.n_kv + g] = 0u;
-  if (warp < GQA) {  // merge the CTAs' partials of head h in CTA order (lane j holds CTA j's m, l)
-    const float* ph = a.part + (static_cast<size_t>(b) * a.n_heads + h) * a.max_chunks * kAttPart;
-    float mc = -INFINITY, lc = 0.f;
-    if (lane < ncta) {
-      mc = __ldcg(ph + lane * kAttPart);
-      lc = __ldcg(ph + lane * kAttPart + 1);
-    }
-    float MM = mc;
+  if (head) {
+    float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + g * GQA + gid) * a.max_chunks + x) * kAttPart;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, off));
-    const float wl2 = mc == -INFINITY ? 0.f : __expf(mc - MM);
-    float LL = wl2 * lc;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) LL += __shfl_xor_sync(0xffffffffu, LL, off);
-    float r0 = 0.f, r1 = 0.f;
-    for (int j = 0; j < ncta; ++j) {
-      const float wgt = __shfl_sync(0xffffffffu, wl2, j);
-      const float2 oc = __ldcg(reinterpret_cast<const float2*>(ph + j * kAttPart + 4) + lane);
-      r0 = fmaf(wgt, oc.x, r0);
-      r1 = fmaf(wgt, oc.y, r1);
+    for (int j = 0; j < 8; ++j)
+      reinterpret_cast<float2*>(part + 4)[4 * j + tig] = make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
+    if (tig == 0) {
+      part[0] = m;
+      part[1] = l;
     }
-    const float inv = LL > 0.f ? 1.0f / LL : 0.f;
-    reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo + h * 64)[lane] =
-        __floats2bfloat162_rn(r0 * inv, r1 * inv);
   }
+  stamp(6);
+  __syncwarp();  // every lane's partial stores precede lane 0's release below
+  uint32_t last = 0;
+  if (lane == 0) {
+    uint32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(prev) : "l"(a.tickets + b * a.n_kv + g) : "memory");
+    last = prev == static_cast<uint32_t>(nunits - 1);
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  __syncwarp();  // the other lanes' reads below follow lane 0's acquire
+  if (!last) {
+    stamp(7);
+    return;
+  }
+  if (lane == 0) a.tickets[b * a.n_kv + g] = 0u;
+  // Merge the units' partials in split order.  Lane (hh = lane / 8, c = lane % 8)
+  // takes head g*GQA + hh, dims 8c .. 8c+7; every load is issued before the math.
+  const int hh = lane >> 3, c8 = lane & 7;
+  if (hh < GQA) {
+    const float* ph = a.part + (static_cast<size_t>(b) * a.n_heads + g * GQA + hh) * a.max_chunks * kAttPart;
+    float2 ml[kPaMaxSplits];
+    float4 oa[kPaMaxSplits], ob[kPaMaxSplits];
+#pragma unroll
+    for (int j = 0; j < kPaMaxSplits; ++j)
+      if (j < nunits) {
+        ml[j] = __ldcg(reinterpret_cast<const float2*>(ph + j * kAttPart));
+        oa[j] = __ldcg(reinterpret_cast<const float4*>(ph + j * kAttPart + 4 + 8 * c8));
+        ob[j] = __ldcg(reinterpret_cast<const float4*>(ph + j * kAttPart + 8 + 8 * c8));
+      }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPaMaxSplits; ++j)
+      if (j < nunits) M = fmaxf(M, ml[j].x);
+    float L = 0.f, r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kPaMaxSplits; ++j)
+      if (j < nunits) {
+        const float wgt = ml[j].x == -INFINITY ? 0.f : __expf(ml[j].x - M);
+        L = fmaf(wgt, ml[j].y, L);
+        r[0] = fmaf(wgt, oa[j].x, r[0]); r[1] = fmaf(wgt, oa[j].y, r[1]);
+        r[2] = fmaf(wgt, oa[j].z, r[2]); r[3] = fmaf(wgt, oa[j].w, r[3]);
+        r[4] = fmaf(wgt, ob[j].x, r[4]); r[5] = fmaf(wgt, ob[j].y, r[5]);
+        r[6] = fmaf(wgt, ob[j].z, r[6]); r[7] = fmaf(wgt, ob[j].w, r[7]);
+      }
+    const float inv = L > 0.f ? 1.0f / L : 0.f;
+    uint4 pk;
+    pk.x = bf2_rn(r[0] * inv, r[1] * inv);
+    pk.y = bf2_rn(r[2] * inv, r[3] * inv);
+    pk.z = bf2_rn(r[4] * inv, r[5] * inv);
+    pk.w = bf2_rn(r[6] * inv, r[7] * inv);
+    *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + hh) * 64 + 8 * c8) = pk;
+  }
+  stamp(7);
 }
 
 }  // namespace b2d

@@ -130,6 +130,7 @@ struct b2d_ws {
   int force_att_cpc;       // diagnostics: fixed attention chunks per CTA (0 = automatic)
   uint64_t* gemm_trace;    // diagnostics: [launch][kTraceCtas][kGemmStamps] projection stamps, or null
   uint64_t* stage_trace;   // diagnostics: B=1 stage stamps [grid][3][stage_stride], or null
+  uint64_t* att_trace;     // diagnostics: attention stamps [layer][kAttTraceUnits][8], or null
   int stage_stride;
   int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
@@ -139,6 +140,7 @@ struct b2d_ws {
 namespace {
 constexpr int kTraceCtas = 256;        // projection CTAs stamped per launch (diagnostics)
 constexpr int kTraceLaunches = 4 * 64 + 1;  // stamped projection launches per step (n_layers <= 64)
+constexpr int kAttTraceUnits = 8192;        // attention units stamped per launch (diagnostics)
 constexpr int kFusedNormRows = 2;           // see run_rows
 constexpr int kPrefillRows = 128;           // prompt positions per prefill chunk
 
@@ -157,6 +159,32 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+// launch_k with `smem` bytes of dynamic shared memory (the kernel's limit is
+// raised once per device).
+template <class... KArgs, class... Args>
+cudaError_t launch_k_smem(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, bool pdl,
+                          Args&&... args) {
+  static bool raised[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!raised[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    raised[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -419,6 +447,9 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
       if (value < 0 || value > 4096) return B2D_ERR_INVALID_ARG;
       ws->stage_stride = static_cast<int>(value);
       return B2D_OK;
+    case 9:  // batched step: attention stamp buffer (device address; 0 = off)
+      ws->att_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
+      return B2D_OK;
   }
   return B2D_ERR_INVALID_ARG;
 }
@@ -593,12 +624,13 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
   pa.part = ws->att_part; pa.tickets = ws->att_tickets; pa.max_chunks = ws->att_chunks;
-  {  // CTAs per (row, kv head): about 5 resident attention CTAs per SM over all (row, kv head) pairs
-    const int pairs = batch * c.n_kv_heads, target = 5 * m->grid;
+  {  // units (warps) per (row, kv head): split rows only while the pairs alone leave SMs idle
+    const int pairs = batch * c.n_kv_heads, target = 10 * m->grid;
     const int cap = std::min(b2d::kPaMaxSplits, std::min(ws->att_chunks, (c.context_len + 15) / 16));
-    pa.cpc = std::max(1, std::min(cap, (target + pairs - 1) / pairs));
+    pa.cpc = std::max(1, std::min(cap, target / pairs));
     if (ws->force_att_cpc) pa.cpc = std::min(cap, ws->force_att_cpc);
   }
+  const int att_units = batch * c.n_kv_heads * pa.cpc;
   // RMSNorm of the residual stream: fused into the residual projection's
   // epilogue (last M tile per column slice) when a slice has at most
   // kFusedNormRows rows, else a separate one-CTA-per-row kernel.
@@ -611,10 +643,12 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.norm_g = nullptr;
     B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
     pa.layer = l;
+    pa.trace = ws->att_trace ? ws->att_trace + size_t(l) * kAttTraceUnits * 8 : nullptr;
+    pa.trace_units = kAttTraceUnits;
     if (prefill)  // every row's K/V in the cache before any row attends
       B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
-    B2D_CUDA(launch_k(b2d::paged_attn_mma_kernel, dim3(pa.cpc, c.n_kv_heads, batch), dim3(32 * b2d::kPaWarps), st,
-                      pdl, pa),
+    B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel, dim3((att_units + b2d::kPaWarps - 1) / b2d::kPaWarps),
+                           dim3(32 * b2d::kPaWarps), b2d::kPaSmem, st, pdl, pa, batch),
              "attention");
     launches_other += prefill ? 2 : 1;
     const float* ln2_l = ln2 + size_t(l) * D;

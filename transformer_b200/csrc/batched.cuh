@@ -112,6 +112,9 @@ struct PagedAttnArgs {
   // [layer][K|V][kv_head][ctx][64] (every row of the launch is a position of
   // that sequence, as in a prefill).
   bool append;                 // the CTA holding a row's position writes its K/V (else done before)
+  // diagnostics: global-timer stamps [unit][8] (units >= trace_units skipped), or nullptr
+  uint64_t* trace;
+  int trace_units;
 };
 
 // K (kv = 0) or V (kv = 1) row of position `pos` of the launch row's sequence.
