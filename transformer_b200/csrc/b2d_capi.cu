@@ -124,7 +124,7 @@ struct b2d_ws {
   int rows;                        // activation rows allocated (max_batch rounded up to the widest tile)
   float *H, *Hm, *qkv, *logits, *att_part;
   uint32_t* att_tickets;
-  uint32_t* norm_tickets;  // fused-RMSNorm tickets of the residual projections
+  float* ss;               // folded RMSNorm: per-tile sums of squares [d_model / 128][rows]
   bool no_pdl;             // diagnostics: launch without programmatic dependencies
   int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
   int force_att_cpc;       // diagnostics: fixed attention chunks per CTA (0 = automatic)
@@ -141,7 +141,6 @@ namespace {
 constexpr int kTraceCtas = 256;        // projection CTAs stamped per launch (diagnostics)
 constexpr int kTraceLaunches = 4 * 64 + 1;  // stamped projection launches per step (n_layers <= 64)
 constexpr int kAttTraceUnits = 8192;        // attention units stamped per launch (diagnostics)
-constexpr int kFusedNormRows = 2;           // see run_rows
 constexpr int kPrefillRows = 128;           // prompt positions per prefill chunk
 
 __global__ void iota_kernel(int32_t* out, int start, int n) {
@@ -327,9 +326,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
       e = cudaMalloc(&ws->att_part, sizeof(float) * size_t(ws->brows) * c.n_heads * ws->att_chunks * b2d::kAttPart);
     if (e == cudaSuccess) e = cudaMalloc(&ws->att_tickets, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
     if (e == cudaSuccess) e = cudaMemset(ws->att_tickets, 0, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
-    const size_t nt = size_t((ws->brows + 15) / 16) * b2d::kGemmMaxSplit;  // >= ceil(N/BN) * ksplit
-    if (e == cudaSuccess) e = cudaMalloc(&ws->norm_tickets, sizeof(uint32_t) * nt);
-    if (e == cudaSuccess) e = cudaMemset(ws->norm_tickets, 0, sizeof(uint32_t) * nt);
+    if (e == cudaSuccess) e = cudaMalloc(&ws->ss, sizeof(float) * (D / b2d::kGemmBM) * ws->rows);
     for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
       const uint32_t box = 16u << i;
       if (!b2d::make_kmajor_map(&ws->xmap[i], ws->X, D, ws->rows, box) ||
@@ -361,7 +358,7 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   cudaFree(ws->ACT);
   cudaFree(ws->att_part);
   cudaFree(ws->att_tickets);
-  cudaFree(ws->norm_tickets);
+  cudaFree(ws->ss);
   cudaFree(ws->prefill_pos);
   cudaFree(ws->words);
   cudaFree(ws->ctl);
@@ -609,13 +606,15 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     p_dn.ksplit = std::min(f, F / b2d::kGemmBK);
     p_lg.ksplit = std::min(f, D / b2d::kGemmBK);
   }
-  B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok, V, D, ln1, c.rms_eps,
-                    ws->H, ws->X, status), "embed");
+  const int ss_tiles = D / b2d::kGemmBM;
+  B2D_CUDA(launch_k(b2d::embed_rows_kernel, dim3(batch), dim3(256), st, false, emb, tok, V, D, ln1, ws->H, ws->X,
+                    ws->ss, ws->rows, ss_tiles, status), "embed");
   ++launches_other;
   g.N = batch;
   g.err = status;
-  g.tickets = ws->norm_tickets;
   g.norm_eps = c.rms_eps;
+  g.ss_dim = D;
+  g.ss_ld = ws->rows;
   b2d::PagedAttnArgs pa{};
   pa.qkv = ws->qkv; pa.pos = pos; pa.pool = static_cast<__nv_bfloat16*>(cache);
   pa.table = table; pa.bps = bps; pa.num_blocks = num_blocks; pa.append = !prefill;
@@ -631,16 +630,13 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     if (ws->force_att_cpc) pa.cpc = std::min(cap, ws->force_att_cpc);
   }
   const int att_units = batch * c.n_kv_heads * pa.cpc;
-  // RMSNorm of the residual stream: fused into the residual projection's
-  // epilogue (last M tile per column slice) when a slice has at most
-  // kFusedNormRows rows, else a separate one-CTA-per-row kernel.
-  auto norm_fused = [&](const b2d::GemmPlan& pl) { return (pl.bn + pl.ksplit - 1) / pl.ksplit <= kFusedNormRows; };
-  auto norm = [&](const float* h, const float* gain) {
-    return launch_k(b2d::rmsnorm_rows_kernel, dim3(batch), dim3(128), st, pdl, h, gain, D, c.rms_eps, ws->X);
-  };
+  // RMSNorm of the residual stream, folded: each residual projection writes
+  // X = bf16(h * g_next) and per-tile sums of squares; the next projection
+  // (qkv, gate/up, logits) scales its result columns by rsqrt(mean + eps).
   for (int l = 0; l < c.n_layers; ++l) {
-    // X = RMSNorm(H, ln1[l]) was written by the embedding (l = 0) or after the previous down projection
-    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q; g.norm_g = nullptr;
+    // X = bf16(H * ln1[l]) and its statistics come from the embedding (l = 0) or the previous down projection
+    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q;
+    g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
     B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
     pa.layer = l;
     pa.trace = ws->att_trace ? ws->att_trace + size_t(l) * kAttTraceUnits * 8 : nullptr;
@@ -651,32 +647,23 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
                            dim3(32 * b2d::kPaWarps), b2d::kPaSmem, st, pdl, pa, batch),
              "attention");
     launches_other += prefill ? 2 : 1;
-    const float* ln2_l = ln2 + size_t(l) * D;
-    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D; 
-    g.norm_g = norm_fused(p_o) ? ln2_l : nullptr;
-    g.norm_out = ws->X;
+    g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;
+    g.ss_in = nullptr; g.xg_out = ws->X; g.xg_gain = ln2 + size_t(l) * D; g.ss_out = ws->ss;
     B2D_CUDA(gemm(m->wmaps[4 * l + 1], ws->amap, b2d::EPI_RESID_F32, p_o), "o");
-    if (!g.norm_g) {
-      B2D_CUDA(norm(ws->Hm, ln2_l), "rmsnorm");
-      ++launches_other;
-    }
-    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F; g.norm_g = nullptr;
+    g.M = 2 * F; g.K = D; g.ybf = ws->ACT; g.ldy = F;
+    g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
     B2D_CUDA(gemm(m->wmaps[4 * l + 2], ws->xmap, b2d::EPI_SWIGLU_BF16, p_gu), "gate/up");
     const float* next_g = l + 1 < c.n_layers ? ln1 + size_t(l + 1) * D : lnf;  // next ln1, or the final norm
-    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D; 
-    g.norm_g = norm_fused(p_dn) ? next_g : nullptr;
-    g.norm_out = ws->X;
+    g.M = D; g.K = F; g.y = ws->H; g.resid = ws->Hm; g.ldy = D;
+    g.ss_in = nullptr; g.xg_out = ws->X; g.xg_gain = next_g; g.ss_out = ws->ss;
     B2D_CUDA(gemm(m->wmaps[4 * l + 3], ws->actmap, b2d::EPI_RESID_F32, p_dn), "down");
-    if (!g.norm_g) {
-      B2D_CUDA(norm(ws->H, next_g), "rmsnorm");
-      ++launches_other;
-    }
   }
   if (logits == nullptr) {  // an earlier prefill chunk: only its cache rows are needed
     ws->last_launches = gl + launches_other;
     return B2D_OK;
   }
-  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V; g.norm_g = nullptr;
+  g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V;
+  g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
   B2D_CUDA(gemm(m->wmaps[4 * c.n_layers], ws->xmap, b2d::EPI_F32, p_lg), "logits");
   if (next_tok) {
     B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,

@@ -24,11 +24,14 @@ namespace b2d {
 
 constexpr int kPageTokens = 16;
 
-// H[b][:] = f32(emb[tok[b]]);  X[b][:] = bf16(RMSNorm(H[b]) * g)  (model.py:94-98,
-// layer 0's ln1).  One CTA (256 threads) per row; fixed-order reduction.
+// H[b][:] = f32(emb[tok[b]]);  layer 0's folded RMSNorm input (model.py:94-98):
+// X[b][:] = bf16(H[b] * g) and the row's sum of squares in ss[0 * ss_ld + b]
+// (the other ss_tiles - 1 partials zero; the QKV projection applies
+// rsqrt(mean + eps)).  One CTA (256 threads) per row; fixed-order reduction.
 __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ emb, const int32_t* __restrict__ tok,
-                                  int vocab, int D, const float* __restrict__ g, float eps, float* __restrict__ H,
-                                  __nv_bfloat16* __restrict__ X, uint32_t* status) {
+                                  int vocab, int D, const float* __restrict__ g, float* __restrict__ H,
+                                  __nv_bfloat16* __restrict__ X, float* __restrict__ ss, int ss_ld, int ss_tiles,
+                                  uint32_t* status) {
   __shared__ float red[8];
   pdl_wait();
   pdl_launch();
@@ -40,56 +43,23 @@ __global__ void embed_rows_kernel(const __nv_bfloat16* __restrict__ emb, const i
   }
   const __nv_bfloat16* e = emb + static_cast<size_t>(tk) * D;
   float* h = H + static_cast<size_t>(b) * D;
-  float ss = 0.f;
+  float q = 0.f;
   for (int i = t; i < D; i += 256) {
     const float v = __bfloat162float(e[i]);
     h[i] = v;
-    ss = fmaf(v, v, ss);
+    X[static_cast<size_t>(b) * D + i] = __float2bfloat16_rn(v * __ldg(g + i));
+    q = fmaf(v, v, q);
   }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
+  q = warp_sum(q);
+  if (lane == 0) red[warp] = q;
   __syncthreads();
-  float tot = 0.f;
+  if (t < ss_tiles) {
+    float tot = 0.f;
+    if (t == 0)
 #pragma unroll
-  for (int w = 0; w < 8; ++w) tot += red[w];
-  const float r = rsqrtf(tot / static_cast<float>(D) + eps);
-  for (int i = t; i < D; i += 256)
-    X[static_cast<size_t>(b) * D + i] = __float2bfloat16_rn(__bfloat162float(e[i]) * r * __ldg(g + i));
-}
-
-// X[b][:] = bf16(H[b] * rsqrt(mean(H[b]^2) + eps) * g)   (model.py:94-98)
-// One CTA (128 threads) per row, the row held in registers (D <= 2048,
-// D % 4 == 0); fixed-order reduction.
-__global__ void __launch_bounds__(128) rmsnorm_rows_kernel(const float* __restrict__ H, const float* __restrict__ g,
-                                                           int D, float eps, __nv_bfloat16* __restrict__ X) {
-  __shared__ float red[4];
-  pdl_wait();
-  pdl_launch();
-  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const float4* h = reinterpret_cast<const float4*>(H + static_cast<size_t>(b) * D);
-  const int q4 = D / 4;  // float4s per row, <= 4 per thread
-  float4 v[4] = {};
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (t + 128 * i < q4) {
-      v[i] = h[t + 128 * i];
-      ss = fmaf(v[i].x, v[i].x, ss); ss = fmaf(v[i].y, v[i].y, ss);
-      ss = fmaf(v[i].z, v[i].z, ss); ss = fmaf(v[i].w, v[i].w, ss);
-    }
-  ss = warp_sum(ss);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  const float r = rsqrtf((red[0] + red[1] + red[2] + red[3]) / static_cast<float>(D) + eps);
-  const float4* g4 = reinterpret_cast<const float4*>(g);
-  __nv_bfloat162* x = reinterpret_cast<__nv_bfloat162*>(X + static_cast<size_t>(b) * D);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    if (t + 128 * i < q4) {
-      const float4 w = __ldg(g4 + t + 128 * i);
-      x[2 * (t + 128 * i)] = __floats2bfloat162_rn(v[i].x * r * w.x, v[i].y * r * w.y);
-      x[2 * (t + 128 * i) + 1] = __floats2bfloat162_rn(v[i].z * r * w.z, v[i].w * r * w.w);
-    }
+      for (int w = 0; w < 8; ++w) tot += red[w];
+    ss[static_cast<size_t>(t) * ss_ld + b] = tot;
+  }
 }
 
 struct PagedAttnArgs {

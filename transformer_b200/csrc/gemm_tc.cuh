@@ -47,12 +47,18 @@ struct GemmArgs {
   int ldy = 0;
   uint32_t* err = nullptr;            // status word: set (if still 0) when a wait runs out
   int ksplit = 1;                     // 1..kGemmMaxSplit, <= K/64; > 1 needs a (1,1,ksplit) cluster launch
-  // EPI_RESID_F32 only, optional fused RMSNorm of the finished rows:
-  // norm_out[n][:] = bf16(y[n] * rsqrt(mean(y[n]^2) + eps) * norm_g), written
-  // by the last M tile to finish each column slice (ticket per slice).
-  const float* norm_g = nullptr;      // [M] gain, or nullptr (no norm)
-  __nv_bfloat16* norm_out = nullptr;  // [N][M]
-  uint32_t* tickets = nullptr;        // [ceil(N/BN) * ksplit], zero between launches
+  // Folded RMSNorm (model.py:94-98): the next projection's input is
+  // bf16(RMSNorm(h) * g) = r[n] * bf16(h * g) up to bf16 rounding, with
+  // r[n] = rsqrt(mean(h[n]^2) + eps) applied to that projection's result.
+  // Producer (EPI_RESID_F32 writing h): xg_out[n][m] = bf16(y * xg_gain[m])
+  // and ss_out[blockIdx.x * ss_ld + n] = sum of y^2 over this tile's 128 rows.
+  const float* xg_gain = nullptr;     // [M], or nullptr (no folded norm output)
+  __nv_bfloat16* xg_out = nullptr;    // [N][M]
+  float* ss_out = nullptr;            // [M / 128][ss_ld]
+  // Consumer: column n of the result is multiplied by
+  // rsqrt(sum_t ss_in[t * ss_ld + n] / ss_dim + norm_eps), t < ss_dim / 128.
+  const float* ss_in = nullptr;
+  int ss_dim = 0, ss_ld = 0;
   float norm_eps = 0.f;
   // diagnostics: global-timer stamps [cta][kGemmStamps] (CTAs >= trace_ctas skipped), or nullptr
   uint64_t* trace = nullptr;
@@ -67,29 +73,6 @@ __device__ __forceinline__ void gemm_stamp(const GemmArgs& g, int slot) {
   if (g.trace == nullptr) return;
   const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   if (cta < g.trace_ctas) g.trace[static_cast<size_t>(cta) * kGemmStamps + slot] = globaltimer_ns();
-}
-
-// RMSNorm of rows [n_lo, n_hi) of y (row length M) by the whole CTA, one
-// warp per row; fixed summation order (model.py:94-98).
-__device__ __forceinline__ void gemm_norm_rows(const GemmArgs& g, int n_lo, int n_hi) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int n = n_lo + warp; n < n_hi; n += kGemmThreads / 32) {
-    const float4* h = reinterpret_cast<const float4*>(g.y + static_cast<size_t>(n) * g.ldy);
-    float ss = 0.f;
-    for (int i = lane; i < g.M / 4; i += 32) {
-      const float4 v = __ldcg(h + i);
-      ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
-    }
-    ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / static_cast<float>(g.M) + g.norm_eps);
-    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(g.norm_out + static_cast<size_t>(n) * g.M);
-    const float4* gg = reinterpret_cast<const float4*>(g.norm_g);
-    for (int i = lane; i < g.M / 4; i += 32) {
-      const float4 v = __ldcg(h + i), w = __ldg(gg + i);
-      o[2 * i] = __floats2bfloat162_rn(v.x * rs * w.x, v.y * rs * w.y);
-      o[2 * i + 1] = __floats2bfloat162_rn(v.z * rs * w.z, v.w * rs * w.w);
-    }
-  }
 }
 
 template <int BN>
@@ -122,7 +105,7 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, uint32
 }
 
 // Rows row..row+3 of output column n (row % 4 == 0): SwiGLU pairs (2j, 2j+1)
-// lie inside the group.
+// lie inside the group.  `v` is final (scaled, residual added).
 template <int EPI>
 __device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row, int n) {
   if (EPI == EPI_SWIGLU_BF16) {
@@ -131,13 +114,26 @@ __device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row
     *reinterpret_cast<__nv_bfloat162*>(g.ybf + static_cast<size_t>(n) * g.ldy + (row >> 1)) =
         __floats2bfloat162_rn(a0, a1);
   } else {
-    float4* y = reinterpret_cast<float4*>(g.y + static_cast<size_t>(n) * g.ldy + row);
-    if (EPI == EPI_RESID_F32) {
-      const float4 r = *reinterpret_cast<const float4*>(g.resid + static_cast<size_t>(n) * g.ldy + row);
-      v.x += r.x; v.y += r.y; v.z += r.z; v.w += r.w;
-    }
-    *y = v;
+    *reinterpret_cast<float4*>(g.y + static_cast<size_t>(n) * g.ldy + row) = v;
   }
+}
+
+// Folded-norm producer side for one item (warp-uniform call: the 32 lanes of
+// the warp hold the 32 items of one column): bf16(y * gain) and the column's
+// sum of squares over the tile (butterfly order, fixed).
+// `w` = xg_gain[row .. row + 3].
+__device__ __forceinline__ void gemm_fold_item(const GemmArgs& g, float4 y, float4 w, int row, int n, bool live) {
+  float q = 0.f;
+  if (live) {
+    uint2 pk;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(y.x * w.x, y.y * w.y), hi = __floats2bfloat162_rn(y.z * w.z, y.w * w.w);
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(g.xg_out + static_cast<size_t>(n) * g.M + row) = pk;
+    q = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
+  }
+  q = warp_sum(q);
+  if (live && (threadIdx.x & 31) == 0) g.ss_out[static_cast<size_t>(blockIdx.x) * g.ss_ld + n] = q;
 }
 
 template <int BN, int EPI>
@@ -152,7 +148,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   uint64_t* empty = full + S;
   uint64_t* done = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  __shared__ uint32_t s_norm_last;
+  __shared__ float s_rs[256];  // folded-norm consumer: scale of each tile column
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * BN;
@@ -224,12 +220,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
 
   // ---- epilogue: all eight warps ----
   __syncwarp();
-  pdl_wait();  // the residual comes from earlier kernels
+  pdl_wait();  // the residual and the norm statistics come from earlier kernels
+  if (g.ss_in != nullptr && warp >= 2) {  // column scales (warps 2..7: idle during the main loop)
+    for (int c = threadIdx.x - 64; c < BN; c += kGemmThreads - 64) {
+      float rs = 1.f;
+      if (n0 + c < g.N) {
+        float tot = 0.f;
+        for (int t = 0; t < g.ss_dim / kGemmBM; ++t) tot += __ldcg(g.ss_in + static_cast<size_t>(t) * g.ss_ld + n0 + c);
+        rs = rsqrtf(tot / static_cast<float>(g.ss_dim) + g.norm_eps);
+      }
+      s_rs[c] = rs;
+    }
+  }
+  // Folded-norm producer: every item of this thread covers rows m0 + 4 lane .. +3.
+  const float4 gw = EPI == EPI_RESID_F32 && g.xg_out != nullptr
+                        ? __ldg(reinterpret_cast<const float4*>(g.xg_gain + m0 + 4 * lane))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
   const bool got = __all_sync(0xffffffffu, gemm_wait(done, 0, g.err));
   tc_fence_after();
   if (threadIdx.x == 0) gemm_stamp(g, 4);
   const int r = (warp & 3) * 32 + lane;  // accumulator row = weight row m0 + r (this warp's TMEM lanes)
-  int slice = blockIdx.y, j0 = 0, j1 = BN;  // output columns this CTA stores
+  int j0 = 0, j1 = BN;  // output columns this CTA stores
   // The accumulator goes to shared memory as [BN][128] f32; the outputs are
   // then written as items of 4 consecutive rows (float4 / bf16x2 stores).
   // With a K split, the cluster's partial tiles are summed in rank order
@@ -247,7 +258,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   if (ks > 1) {
     cluster_sync_all();
     const int rank = static_cast<int>(cluster_ctarank());
-    slice = blockIdx.y * ks + rank;
     j0 = rank * BN / ks;
     j1 = (rank + 1) * BN / ks;
   } else {
@@ -260,13 +270,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
     constexpr int U = 8;
 #pragma unroll 1
     for (int it0 = threadIdx.x; it0 < items; it0 += U * kGemmThreads) {
-      float4 v[U];
+      // every load of the round (tile, column scale, residual) before any store:
+      // the stores go through generic pointers the loads cannot be moved past
+      float4 v[U], rr[U];
+      float rs[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int it = it0 + u * kGemmThreads;
         if (it < items) {
           const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
           v[u] = *reinterpret_cast<const float4*>(red + kGemmBM * j + r4);
+          rs[u] = g.ss_in != nullptr ? s_rs[j] : 1.f;
+          if (EPI == EPI_RESID_F32 && n0 + j < g.N)
+            rr[u] = __ldcg(reinterpret_cast<const float4*>(g.resid + static_cast<size_t>(n0 + j) * g.ldy + m0 + r4));
         }
       }
 #pragma unroll
@@ -275,59 +291,60 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
         if (it < items) {
           const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
           const int n = n0 + j, rw = m0 + r4;
-          if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, v[u], rw, n);
+          const bool live = got && n < g.N && rw < g.M;
+          float4 y = v[u];
+          y.x *= rs[u]; y.y *= rs[u]; y.z *= rs[u]; y.w *= rs[u];
+          if (EPI == EPI_RESID_F32 && live) {
+            y.x += rr[u].x; y.y += rr[u].y; y.z += rr[u].z; y.w += rr[u].w;
+          }
+          if (live) gemm_store4<EPI>(g, y, rw, n);
+          if (EPI == EPI_RESID_F32 && g.xg_out != nullptr) gemm_fold_item(g, y, gw, rw, n, live);
         }
       }
     }
   }
 #pragma unroll 1
   for (int it0 = threadIdx.x; ks > 1 && it0 < items; it0 += 2 * kGemmThreads) {
-    float4 part[2][kGemmMaxSplit];  // both items' loads issued before the first add
+    float4 part[2][kGemmMaxSplit], rr[2];  // both items' loads issued before the first add
+    float rs[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int it = it0 + u * kGemmThreads;
       if (it < items) {
         const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
-        if (ks == 1) {
-          part[u][0] = *reinterpret_cast<const float4*>(red + kGemmBM * j + r4);
-        } else {
-          const uint32_t off = red_base + 4u * (kGemmBM * j + r4);
+        const uint32_t off = red_base + 4u * (kGemmBM * j + r4);
 #pragma unroll
-          for (int z = 0; z < kGemmMaxSplit; ++z)
-            if (z < ks) part[u][z] = ld_dsmem_f32x4(mapa_shared(off, z));
-        }
+        for (int z = 0; z < kGemmMaxSplit; ++z)
+          if (z < ks) part[u][z] = ld_dsmem_f32x4(mapa_shared(off, z));
+        rs[u] = g.ss_in != nullptr ? s_rs[j] : 1.f;
+        if (EPI == EPI_RESID_F32 && n0 + j < g.N)
+          rr[u] = __ldcg(reinterpret_cast<const float4*>(g.resid + static_cast<size_t>(n0 + j) * g.ldy + m0 + r4));
       }
     }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int it = it0 + u * kGemmThreads;
       if (it < items) {
-        float4 acc = part[u][0];
+        float4 y = part[u][0];
 #pragma unroll
         for (int z = 1; z < kGemmMaxSplit; ++z)
           if (z < ks) {
-            acc.x += part[u][z].x; acc.y += part[u][z].y; acc.z += part[u][z].z; acc.w += part[u][z].w;
+            y.x += part[u][z].x; y.y += part[u][z].y; y.z += part[u][z].z; y.w += part[u][z].w;
           }
         const int j = j0 + it / (kGemmBM / 4), r4 = (it % (kGemmBM / 4)) * 4;
         const int n = n0 + j, rw = m0 + r4;
-        if (got && n < g.N && rw < g.M) gemm_store4<EPI>(g, acc, rw, n);
+        const bool live = got && n < g.N && rw < g.M;
+        y.x *= rs[u]; y.y *= rs[u]; y.z *= rs[u]; y.w *= rs[u];
+        if (EPI == EPI_RESID_F32 && live) {
+          y.x += rr[u].x; y.y += rr[u].y; y.z += rr[u].z; y.w += rr[u].w;
+        }
+        if (live) gemm_store4<EPI>(g, y, rw, n);
+        if (EPI == EPI_RESID_F32 && g.xg_out != nullptr) gemm_fold_item(g, y, gw, rw, n, live);
       }
     }
   }
   if (ks > 1) cluster_sync_all();  // no CTA leaves while another still reads its partial
   if (threadIdx.x == 0) gemm_stamp(g, 6);
-  if (EPI == EPI_RESID_F32 && g.norm_g != nullptr) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0)
-      s_norm_last = atomicAdd(&g.tickets[slice], 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (s_norm_last) {  // every M tile of these columns is stored: normalise the rows
-      __threadfence();
-      if (threadIdx.x == 0) g.tickets[slice] = 0u;
-      gemm_norm_rows(g, n0 + j0, min(n0 + j1, g.N));
-    }
-  }
   if (warp == 0 && lane == 0) {  // timeout paths: wait (bounded) for copies never consumed
     for (int i = issued > S ? issued - S : 0; i < issued; ++i) gemm_wait(&full[i % S], (i / S) & 1u, g.err);
   }
