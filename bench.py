@@ -499,7 +499,7 @@ def run_ours(args, rank, local_rank, world):
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "scope": f"whole batched step per GPU ({per_wave} "
-                     "kernels per wave: projections on tcgen05, paged attention, RMSNorm, embedding, argmax)",
+                     "kernels per wave: projections on tcgen05 with RMSNorm folded in, paged attention, embedding, argmax)",
                      "traffic": serve_traffic * n_waves if serve_traffic else None,
                      "traffic_source": "profiles/paged_step_b256_pos80.md (one wave-step of 256 at position 80, "
                                        "x waves)",
