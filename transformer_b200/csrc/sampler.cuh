@@ -177,6 +177,60 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   return k == 0x7fffffff ? n - 1 : k;
 }
 
+// Bitonic steps with partner distance j < kSortChunk for stages kk_lo ..
+// kk_hi (powers of two) on every chunk of kSortChunk consecutive elements,
+// in registers; element e of a stage kk sorts ascending iff (e & kk) == 0.
+constexpr int kSortChunk = 16;
+__device__ __forceinline__ void sort_chunks(SamplerSmem& sm, int kk_lo, int kk_hi) {
+  for (int c = threadIdx.x; c < kSamplerMaxVocab / kSortChunk; c += kSamplerThreads) {
+    const int base = c * kSortChunk;
+    uint32_t k[kSortChunk], x[kSortChunk];
+    const uint4* k4 = reinterpret_cast<const uint4*>(sm.key + base);
+#pragma unroll
+    for (int q = 0; q < kSortChunk / 4; ++q) {
+      const uint4 v = k4[q];
+      k[4 * q] = v.x; k[4 * q + 1] = v.y; k[4 * q + 2] = v.z; k[4 * q + 3] = v.w;
+    }
+    const uint4* x4 = reinterpret_cast<const uint4*>(sm.idx + base);  // 8 ids per uint4
+#pragma unroll
+    for (int q = 0; q < kSortChunk / 8; ++q) {
+      const uint4 v = x4[q];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        x[8 * q + 2 * h] = w[h] & 0xffffu;
+        x[8 * q + 2 * h + 1] = w[h] >> 16;
+      }
+    }
+    for (int kk = kk_lo; kk <= kk_hi; kk <<= 1) {
+#pragma unroll
+      for (int j = kSortChunk / 2; j > 0; j >>= 1) {
+        if (j >= kk) continue;  // stage kk has steps j = kk/2 .. 1
+#pragma unroll
+        for (int e = 0; e < kSortChunk; ++e) {
+          if (e & j) continue;
+          const bool asc = ((base + e) & kk) == 0;
+          const bool gt = k[e] > k[e + j] || (k[e] == k[e + j] && x[e] > x[e + j]);
+          if (gt == asc) {
+            const uint32_t tk = k[e], tx = x[e];
+            k[e] = k[e + j]; x[e] = x[e + j];
+            k[e + j] = tk; x[e + j] = tx;
+          }
+        }
+      }
+    }
+    uint4* ko = reinterpret_cast<uint4*>(sm.key + base);
+#pragma unroll
+    for (int q = 0; q < kSortChunk / 4; ++q) ko[q] = make_uint4(k[4 * q], k[4 * q + 1], k[4 * q + 2], k[4 * q + 3]);
+    uint4* xo = reinterpret_cast<uint4*>(sm.idx + base);
+#pragma unroll
+    for (int q = 0; q < kSortChunk / 8; ++q)
+      xo[q] = make_uint4(x[8 * q] | (x[8 * q + 1] << 16), x[8 * q + 2] | (x[8 * q + 3] << 16),
+                         x[8 * q + 4] | (x[8 * q + 5] << 16), x[8 * q + 6] | (x[8 * q + 7] << 16));
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) uint8_t sampler_smem_raw[];
   SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(sampler_smem_raw);
@@ -280,51 +334,85 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   }
 
   // ---- top-p (ref :53-63): sort by (descending p, ascending id) ----
-  for (int kk = 2; kk <= kSamplerMaxVocab; kk <<= 1) {
-    for (int j = kk >> 1, lj = __ffs(kk) - 2; j > 0; j >>= 1, --lj) {  // lj = log2(j)
-      for (int i = t; i < kSamplerMaxVocab / 2; i += kSamplerThreads) {
-        const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
-        const bool asc = (lo & kk) == 0;
-        const uint32_t klo = sm.key[lo], khi = sm.key[hi];
-        const uint16_t ilo = sm.idx[lo], ihi = sm.idx[hi];
-        const bool gt = klo > khi || (klo == khi && ilo > ihi);
-        if (gt == asc) {
-          sm.key[lo] = khi; sm.key[hi] = klo;
-          sm.idx[lo] = ihi; sm.idx[hi] = ilo;
+  // Bitonic sort ascending by (key, id) (key = ~bits of p).  Steps whose
+  // partner distance j < kSortChunk stay inside a thread's chunk of
+  // kSortChunk consecutive elements and run in registers; wider steps are
+  // shared-memory passes with every load of a batch issued before its stores.
+  sort_chunks(sm, 2, kSortChunk);  // stages kk = 2 .. kSortChunk entirely in registers
+  for (int kk = 2 * kSortChunk; kk <= kSamplerMaxVocab; kk <<= 1) {
+    for (int j = kk >> 1, lj = __ffs(kk) - 2; j >= kSortChunk; j >>= 1, --lj) {  // lj = log2(j)
+      constexpr int PB = 8;  // pairs per batch
+#pragma unroll 1
+      for (int i0 = t; i0 < kSamplerMaxVocab / 2; i0 += PB * kSamplerThreads) {
+        uint32_t klo[PB], khi[PB], ilo[PB], ihi[PB];
+#pragma unroll
+        for (int q = 0; q < PB; ++q) {
+          const int i = i0 + q * kSamplerThreads;
+          const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
+          klo[q] = sm.key[lo]; khi[q] = sm.key[hi];
+          ilo[q] = sm.idx[lo]; ihi[q] = sm.idx[hi];
+        }
+#pragma unroll
+        for (int q = 0; q < PB; ++q) {
+          const int i = i0 + q * kSamplerThreads;
+          const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
+          const bool asc = (lo & kk) == 0;
+          const bool gt = klo[q] > khi[q] || (klo[q] == khi[q] && ilo[q] > ihi[q]);
+          if (gt == asc) {
+            sm.key[lo] = khi[q]; sm.key[hi] = klo[q];
+            sm.idx[lo] = static_cast<uint16_t>(ihi[q]); sm.idx[hi] = static_cast<uint16_t>(ilo[q]);
+          }
         }
       }
       __syncthreads();
     }
+    sort_chunks(sm, kk, kk);  // this stage's steps j < kSortChunk, in registers
   }
   // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one.  The
   // running sum is a float, so float64(c) >= top_p  <=>  c >= thr with thr =
   // top_p rounded up to a float: the chain stays in float32 (the cumulative
   // sum itself is sequential, as numpy's).
-  if (warp == 0) {  // warp 0 loads 128 keys per round; lane 0 runs the float32 chain over them in order
+  if (t == 0) {  // one thread runs the float32 chain in order, 16 keys per block
     const float thr = __double2float_ru(a.top_p);
     const uint4* k4 = reinterpret_cast<const uint4*>(sm.key);
     const int n4 = (V + 3) / 4;  // keys past V decode to p = 0
+    constexpr int Q = 4;         // uint4 per block
+    auto load_blk = [&](int base, uint4 (&dst)[Q]) {
+#pragma unroll
+      for (int q = 0; q < Q; ++q) dst[q] = base + q < n4 ? k4[base + q] : make_uint4(~0u, ~0u, ~0u, ~0u);
+    };
     float c = 0.f;
     int cut = V;
-    for (int base = 0; base < n4 && cut == V; base += 32) {
-      const uint4 kk = base + lane < n4 ? k4[base + lane] : make_uint4(~0u, ~0u, ~0u, ~0u);
-#pragma unroll 8
-      for (int src = 0; src < 32; ++src) {
-        const uint32_t kx = __shfl_sync(0xffffffffu, kk.x, src), ky = __shfl_sync(0xffffffffu, kk.y, src);
-        const uint32_t kz = __shfl_sync(0xffffffffu, kk.z, src), kw = __shfl_sync(0xffffffffu, kk.w, src);
-        const int i0 = 4 * (base + src);
-        c = __fadd_rn(c, key_to_p(kx));
-        if (cut == V && c >= thr) cut = i0 + 1;
-        c = __fadd_rn(c, key_to_p(ky));
-        if (cut == V && c >= thr) cut = i0 + 2;
-        c = __fadd_rn(c, key_to_p(kz));
-        if (cut == V && c >= thr) cut = i0 + 3;
-        c = __fadd_rn(c, key_to_p(kw));
-        if (cut == V && c >= thr) cut = i0 + 4;
+    uint4 nxt[Q];
+    load_blk(0, nxt);
+    for (int base = 0; base < n4; base += Q) {
+      uint4 cur[Q];
+#pragma unroll
+      for (int q = 0; q < Q; ++q) cur[q] = nxt[q];
+      load_blk(base + Q, nxt);  // the next block's keys are in flight during this block's chain
+      // The sum never decreases (p >= 0): the threshold is crossed inside this
+      // block iff it is crossed at its end; only then is the block rerun key by key.
+      float e = c;
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        e = __fadd_rn(e, key_to_p(cur[q].x));
+        e = __fadd_rn(e, key_to_p(cur[q].y));
+        e = __fadd_rn(e, key_to_p(cur[q].z));
+        e = __fadd_rn(e, key_to_p(cur[q].w));
       }
-      cut = __shfl_sync(0xffffffffu, cut, 0);  // every lane ran the same chain; keep them in step
+      if (e >= thr) {
+        for (int i = 0; i < 4 * Q; ++i) {
+          c = __fadd_rn(c, 4 * base + i < V ? key_to_p(sm.key[4 * base + i]) : 0.f);
+          if (c >= thr) {
+            cut = 4 * base + i + 1;
+            break;
+          }
+        }
+        break;
+      }
+      c = e;
     }
-    if (lane == 0) sm.cutoff = min(cut, V);
+    sm.cutoff = min(cut, V);
   }
   __syncthreads();
   const int cut = sm.cutoff;
