@@ -243,7 +243,9 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * buffer [grid][3][stride] for the B=1 step's weight stages (copy issued /
  * stage seen full / consumed by warp 0), knob 8 = that stride (0 = off);
  * knob 9 = device address of a uint64 buffer [n_layers][8192 units][8] that
- * the batched step's attention fills with global-timer stamps (0 = off).
+ * the batched step's attention fills with global-timer stamps (0 = off);
+ * knob 10 = device address of a uint64 buffer [batch][8] of b2d_sample phase
+ * stamps (0 = off).
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
 B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);

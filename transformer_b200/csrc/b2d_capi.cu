@@ -131,6 +131,7 @@ struct b2d_ws {
   uint64_t* gemm_trace;    // diagnostics: [launch][kTraceCtas][kGemmStamps] projection stamps, or null
   uint64_t* stage_trace;   // diagnostics: B=1 stage stamps [grid][3][stage_stride], or null
   uint64_t* att_trace;     // diagnostics: attention stamps [layer][kAttTraceUnits][8], or null
+  uint64_t* sample_trace;  // diagnostics: sampler phase stamps [batch][8], or null
   int stage_stride;
   int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
@@ -447,6 +448,9 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 9:  // batched step: attention stamp buffer (device address; 0 = off)
       ws->att_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
       return B2D_OK;
+    case 10:  // sampler: phase stamp buffer (device address; 0 = off)
+      ws->sample_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
+      return B2D_OK;
   }
   return B2D_ERR_INVALID_ARG;
 }
@@ -519,7 +523,8 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
   B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
-                               params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st),
+                               params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st,
+                               ws->sample_trace),
            "sampler launch");
   return B2D_OK;
 }

@@ -28,6 +28,8 @@
 
 #include <cstdint>
 
+#include "b2d_ptx.cuh"
+
 namespace b2d {
 
 constexpr int kSamplerMaxVocab = 32768;
@@ -43,6 +45,7 @@ struct SampleArgs {
   int vocab, hist_cap;
   float temperature, rep_penalty;
   double top_p;
+  uint64_t* trace;         // diagnostics: global-timer stamps [batch][8] (thread 0 of each CTA), or null
 };
 
 struct SamplerSmem {
@@ -149,17 +152,18 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   }
   if (lane == 31) sm.red_d[warp] = incl;
   __syncthreads();
+  constexpr int kWarps = kSamplerThreads / 32;
   if (warp == 0) {
-    double w = sm.red_d[lane];
+    double w = lane < kWarps ? sm.red_d[lane] : 0.0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double v = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += v;
     }
-    sm.red_d[lane] = w;  // inclusive warp-total prefix
+    if (lane < kWarps) sm.red_d[lane] = w;  // inclusive warp-total prefix
   }
   __syncthreads();
-  const double total = sm.red_d[31];
+  const double total = sm.red_d[kWarps - 1];
   double run = (warp > 0 ? sm.red_d[warp - 1] : 0.0) + (incl - local);
   int found = 0x7fffffff;
   for (int i = i0; i < i1; ++i) {
@@ -177,29 +181,43 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   return k == 0x7fffffff ? n - 1 : k;
 }
 
+// Bitonic compare-exchange of (k, x) pairs: ascending by (key, id) when asc.
+__device__ __forceinline__ void cmp_swap(uint32_t& ka, uint32_t& xa, uint32_t& kb, uint32_t& xb, bool asc) {
+  const bool sw = (ka > kb || (ka == kb && xa > xb)) == asc;  // (branch-free)
+  const uint32_t k0 = sw ? kb : ka, k1 = sw ? ka : kb, x0 = sw ? xb : xa, x1 = sw ? xa : xb;
+  ka = k0; kb = k1; xa = x0; xb = x1;
+}
+
 // Bitonic steps with partner distance j < kSortChunk for stages kk_lo ..
 // kk_hi (powers of two) on every chunk of kSortChunk consecutive elements,
 // in registers; element e of a stage kk sorts ascending iff (e & kk) == 0.
+// A thread reads its chunk's 16-byte pieces starting at a rotation of its
+// own (conflict-free across the warp) and undoes the rotation with selects.
 constexpr int kSortChunk = 16;
 __device__ __forceinline__ void sort_chunks(SamplerSmem& sm, int kk_lo, int kk_hi) {
+  const int rk = (threadIdx.x >> 1) & 3, rx = (threadIdx.x >> 2) & 1;  // rotations of the key / id pieces
   for (int c = threadIdx.x; c < kSamplerMaxVocab / kSortChunk; c += kSamplerThreads) {
     const int base = c * kSortChunk;
     uint32_t k[kSortChunk], x[kSortChunk];
-    const uint4* k4 = reinterpret_cast<const uint4*>(sm.key + base);
+    {
+      const uint4* k4 = reinterpret_cast<const uint4*>(sm.key + base);
+      uint4 v[4];
 #pragma unroll
-    for (int q = 0; q < kSortChunk / 4; ++q) {
-      const uint4 v = k4[q];
-      k[4 * q] = v.x; k[4 * q + 1] = v.y; k[4 * q + 2] = v.z; k[4 * q + 3] = v.w;
-    }
-    const uint4* x4 = reinterpret_cast<const uint4*>(sm.idx + base);  // 8 ids per uint4
+      for (int q = 0; q < 4; ++q) v[q] = k4[(q + rk) & 3];  // v[q] = piece (q + rk) & 3
 #pragma unroll
-    for (int q = 0; q < kSortChunk / 8; ++q) {
-      const uint4 v = x4[q];
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      for (int q = 0; q < 4; ++q) {  // piece q = v[(q - rk) & 3]
+        const uint4 a0 = v[q], a1 = v[(q + 3) & 3], a2 = v[(q + 2) & 3], a3 = v[(q + 1) & 3];
+        const uint4 w = rk == 0 ? a0 : rk == 1 ? a1 : rk == 2 ? a2 : a3;
+        k[4 * q] = w.x; k[4 * q + 1] = w.y; k[4 * q + 2] = w.z; k[4 * q + 3] = w.w;
+      }
+      const uint4* x4 = reinterpret_cast<const uint4*>(sm.idx + base);  // 8 ids per piece
+      const uint4 y0 = x4[rx], y1 = x4[rx ^ 1];
+      const uint4 p0 = rx ? y1 : y0, p1 = rx ? y0 : y1;
+      const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        x[8 * q + 2 * h] = w[h] & 0xffffu;
-        x[8 * q + 2 * h + 1] = w[h] >> 16;
+      for (int h = 0; h < 8; ++h) {
+        x[2 * h] = wv[h] & 0xffffu;
+        x[2 * h + 1] = wv[h] >> 16;
       }
     }
     for (int kk = kk_lo; kk <= kk_hi; kk <<= 1) {
@@ -207,26 +225,59 @@ __device__ __forceinline__ void sort_chunks(SamplerSmem& sm, int kk_lo, int kk_h
       for (int j = kSortChunk / 2; j > 0; j >>= 1) {
         if (j >= kk) continue;  // stage kk has steps j = kk/2 .. 1
 #pragma unroll
-        for (int e = 0; e < kSortChunk; ++e) {
-          if (e & j) continue;
-          const bool asc = ((base + e) & kk) == 0;
-          const bool gt = k[e] > k[e + j] || (k[e] == k[e + j] && x[e] > x[e + j]);
-          if (gt == asc) {
-            const uint32_t tk = k[e], tx = x[e];
-            k[e] = k[e + j]; x[e] = x[e + j];
-            k[e + j] = tk; x[e + j] = tx;
-          }
-        }
+        for (int e = 0; e < kSortChunk; ++e)
+          if (!(e & j)) cmp_swap(k[e], x[e], k[e + j], x[e + j], ((base + e) & kk) == 0);
       }
     }
-    uint4* ko = reinterpret_cast<uint4*>(sm.key + base);
+    {
+      uint4 v[4];
 #pragma unroll
-    for (int q = 0; q < kSortChunk / 4; ++q) ko[q] = make_uint4(k[4 * q], k[4 * q + 1], k[4 * q + 2], k[4 * q + 3]);
-    uint4* xo = reinterpret_cast<uint4*>(sm.idx + base);
+      for (int q = 0; q < 4; ++q) v[q] = make_uint4(k[4 * q], k[4 * q + 1], k[4 * q + 2], k[4 * q + 3]);
+      uint4* k4 = reinterpret_cast<uint4*>(sm.key + base);
 #pragma unroll
-    for (int q = 0; q < kSortChunk / 8; ++q)
-      xo[q] = make_uint4(x[8 * q] | (x[8 * q + 1] << 16), x[8 * q + 2] | (x[8 * q + 3] << 16),
-                         x[8 * q + 4] | (x[8 * q + 5] << 16), x[8 * q + 6] | (x[8 * q + 7] << 16));
+      for (int q = 0; q < 4; ++q) {  // store piece (q + rk) & 3
+        const uint4 a0 = v[q], a1 = v[(q + 1) & 3], a2 = v[(q + 2) & 3], a3 = v[(q + 3) & 3];
+        k4[(q + rk) & 3] = rk == 0 ? a0 : rk == 1 ? a1 : rk == 2 ? a2 : a3;
+      }
+      const uint4 p0 = make_uint4(x[0] | (x[1] << 16), x[2] | (x[3] << 16), x[4] | (x[5] << 16), x[6] | (x[7] << 16));
+      const uint4 p1 = make_uint4(x[8] | (x[9] << 16), x[10] | (x[11] << 16), x[12] | (x[13] << 16),
+                                  x[14] | (x[15] << 16));
+      uint4* x4 = reinterpret_cast<uint4*>(sm.idx + base);
+      x4[rx] = rx ? p1 : p0;
+      x4[rx ^ 1] = rx ? p0 : p1;
+    }
+  }
+  __syncthreads();
+}
+
+// S consecutive bitonic steps of stage kk with distances jtop, jtop/2, ..,
+// d = jtop / 2^(S-1) (>= kSortChunk) in one shared-memory pass: a thread
+// loads groups of 2^S elements base + a*d, applies the S steps in registers
+// and stores them back.
+template <int S>
+__device__ __forceinline__ void sort_group_pass(SamplerSmem& sm, int kk, int jtop) {
+  constexpr int G = 1 << S;
+  const int d = jtop >> (S - 1), ld = __ffs(d) - 1;
+#pragma unroll 1
+  for (int gi = threadIdx.x; gi < kSamplerMaxVocab / G; gi += kSamplerThreads) {
+    const int base = ((gi >> ld) << (ld + S)) | (gi & (d - 1));
+    uint32_t k[G], x[G];
+#pragma unroll
+    for (int a = 0; a < G; ++a) {
+      k[a] = sm.key[base + a * d];
+      x[a] = sm.idx[base + a * d];
+    }
+    const bool asc = (base & kk) == 0;  // a*d < 2*jtop <= kk adds no carry into bit kk
+#pragma unroll
+    for (int m = G / 2; m > 0; m >>= 1)
+#pragma unroll
+      for (int a = 0; a < G; ++a)
+        if (!(a & m)) cmp_swap(k[a], x[a], k[a + m], x[a + m], asc);
+#pragma unroll
+    for (int a = 0; a < G; ++a) {
+      sm.key[base + a * d] = k[a];
+      sm.idx[base + a * d] = static_cast<uint16_t>(x[a]);
+    }
   }
   __syncthreads();
 }
@@ -238,6 +289,11 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   const int V = a.vocab;
   const float* lg = a.logits + static_cast<size_t>(b) * V;
   constexpr int PER = kSamplerMaxVocab / kSamplerThreads;
+  // stamps: 0 entry, 1 exponentials, 2 normalised, 3 sorted, 4 cutoff, 5 drawn
+  auto stamp = [&](int slot) {
+    if (a.trace != nullptr && t == 0) a.trace[static_cast<size_t>(b) * 8 + slot] = globaltimer_ns();
+  };
+  stamp(0);
 
   // ---- repetition penalty over the set of generated tokens (ref :32-39) ----
   const int hl = (a.history && a.hist_len) ? min(max(a.hist_len[b], 0), a.hist_cap) : 0;
@@ -313,6 +369,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
     }
   }
   __syncthreads();
+  stamp(1);
   // ---- normalise: p /= p.sum() (ref :51) ----
   const float S = pairwise_sum(sm, V, [&](int i) { return __uint_as_float(sm.key[i]); });
   const bool top = a.top_p < 1.0;
@@ -338,36 +395,20 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   // partner distance j < kSortChunk stay inside a thread's chunk of
   // kSortChunk consecutive elements and run in registers; wider steps are
   // shared-memory passes with every load of a batch issued before its stores.
+  stamp(2);
   sort_chunks(sm, 2, kSortChunk);  // stages kk = 2 .. kSortChunk entirely in registers
   for (int kk = 2 * kSortChunk; kk <= kSamplerMaxVocab; kk <<= 1) {
-    for (int j = kk >> 1, lj = __ffs(kk) - 2; j >= kSortChunk; j >>= 1, --lj) {  // lj = log2(j)
-      constexpr int PB = 8;  // pairs per batch
-#pragma unroll 1
-      for (int i0 = t; i0 < kSamplerMaxVocab / 2; i0 += PB * kSamplerThreads) {
-        uint32_t klo[PB], khi[PB], ilo[PB], ihi[PB];
-#pragma unroll
-        for (int q = 0; q < PB; ++q) {
-          const int i = i0 + q * kSamplerThreads;
-          const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
-          klo[q] = sm.key[lo]; khi[q] = sm.key[hi];
-          ilo[q] = sm.idx[lo]; ihi[q] = sm.idx[hi];
-        }
-#pragma unroll
-        for (int q = 0; q < PB; ++q) {
-          const int i = i0 + q * kSamplerThreads;
-          const int lo = ((i >> lj) << (lj + 1)) | (i & (j - 1)), hi = lo + j;
-          const bool asc = (lo & kk) == 0;
-          const bool gt = klo[q] > khi[q] || (klo[q] == khi[q] && ilo[q] > ihi[q]);
-          if (gt == asc) {
-            sm.key[lo] = khi[q]; sm.key[hi] = klo[q];
-            sm.idx[lo] = static_cast<uint16_t>(ihi[q]); sm.idx[hi] = static_cast<uint16_t>(ilo[q]);
-          }
-        }
-      }
-      __syncthreads();
+    // steps j = kk/2 .. kSortChunk, up to 4 per shared-memory pass
+    for (int j = kk >> 1; j >= kSortChunk;) {
+      const int left = __ffs(j) - __ffs(kSortChunk) + 1;  // steps j .. kSortChunk
+      if (left >= 4) { sort_group_pass<4>(sm, kk, j); j >>= 4; }
+      else if (left == 3) { sort_group_pass<3>(sm, kk, j); j >>= 3; }
+      else if (left == 2) { sort_group_pass<2>(sm, kk, j); j >>= 2; }
+      else { sort_group_pass<1>(sm, kk, j); j >>= 1; }
     }
     sort_chunks(sm, kk, kk);  // this stage's steps j < kSortChunk, in registers
   }
+  stamp(3);
   // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one.  The
   // running sum is a float, so float64(c) >= top_p  <=>  c >= thr with thr =
   // top_p rounded up to a float: the chain stays in float32 (the cumulative
@@ -416,15 +457,17 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   }
   __syncthreads();
   const int cut = sm.cutoff;
+  stamp(4);
   const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
   const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
   if (t == 0) a.out[b] = sm.idx[k];
+  stamp(5);
 }
 
 inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, const int32_t* history,
                                   int hist_cap, const int32_t* hist_len, const double* uniforms,
                                   double temperature, double top_p, double rep_penalty, int32_t* out,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, uint64_t* trace = nullptr) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -447,6 +490,7 @@ inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, con
   a.temperature = static_cast<float>(temperature);
   a.rep_penalty = static_cast<float>(rep_penalty);
   a.top_p = top_p;
+  a.trace = trace;
   sample_kernel<<<batch, kSamplerThreads, sizeof(SamplerSmem), st>>>(a);
   return cudaGetLastError();
 }

@@ -182,10 +182,14 @@ class DecodeEngine:
 
     def debug_tune(self, poll_ns: int | None = None, max_inflight: int | None = None,
                    pdl: bool | None = None, ksplit: int | None = None, att_cpc: int | None = None,
-                   gemm_trace: torch.Tensor | None = None, att_trace: torch.Tensor | None = None):
+                   gemm_trace: torch.Tensor | None = None, att_trace: torch.Tensor | None = None,
+                   sample_trace: torch.Tensor | None = None):
         """Diagnostic knobs: back-off between failed polls (ns), weight copies
         in flight per CTA; batched step: programmatic dependent launch on/off,
         forced K split, forced attention chunks per CTA (0 = automatic)."""
+        if sample_trace is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 10, sample_trace.data_ptr() if sample_trace.numel() else 0),
+                       "b2d_debug_tune")
         if att_trace is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 9, att_trace.data_ptr() if att_trace.numel() else 0),
                        "b2d_debug_tune")
