@@ -150,6 +150,55 @@ def test_paged_306m_long_context(engine306_batched, params306_f32):
     eng.check_device()
 
 
+def test_paged_306m_attention_splits(engine306_batched, params306_f32):
+    """Rows at ragged long positions (mid page, a page's last slot, the
+    context end) with every attention split count forced in turn: the last
+    step's logits match the float32 oracle (argmax where the margin allows)
+    for each count, and re-running a step at the same position is harmless
+    (the owner unit rewrites the same K/V)."""
+    from transformer_b200.config import CONFIG_306M
+    cfg = CONFIG_306M
+    rng = np.random.default_rng(15)
+    eng = engine306_batched
+    dev = eng.device
+    lens = [203, 336, cfg.context_len]  # last positions 202 (mid page), 335 (page end), 511
+    B = len(lens)
+    bps = cfg.context_len // PAGE_TOKENS
+    table, nb = _table(rng, B, bps)
+    pool = eng.new_kv_pool(nb)
+    table_d = torch.from_numpy(table).to(dev)
+    prompts = [rng.integers(0, cfg.vocab_size, n).astype(np.int32) for n in lens]
+    tok = torch.zeros(B, dtype=torch.int32, device=dev)
+    pos = torch.zeros(B, dtype=torch.int32, device=dev)
+    logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+    for t in range(max(lens) - 1):  # ragged ingestion up to each row's last position
+        tok.copy_(torch.from_numpy(np.array([p[t] if t < len(p) - 1 else 0 for p in prompts], np.int32)))
+        pos.copy_(torch.from_numpy(np.array([t if t < len(p) - 1 else -1 for p in prompts], np.int32)))
+        eng.step_paged(tok, pos, pool, table_d, logits)
+    refs = []
+    for p in prompts:
+        dec = CachedDecoder(params306_f32, cfg, 1)
+        for t, tk in enumerate(p):
+            r = dec.step([tk], [t])[0]
+        refs.append(r)
+    tok.copy_(torch.from_numpy(np.array([p[-1] for p in prompts], np.int32)))
+    pos.copy_(torch.from_numpy(np.array([n - 1 for n in lens], np.int32)))
+    nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+    try:
+        for splits in (0, 1, 2, 3, 8):
+            eng.debug_tune(att_cpc=splits)
+            eng.step_paged(tok, pos, pool, table_d, logits, nxt)
+            got, am = logits.cpu().numpy(), nxt.cpu().numpy()
+            for b in range(B):
+                assert_logits_close(got[b], refs[b], f"splits {splits} row {b}")
+                i, _, margin = top2(refs[b])
+                if margin > MARGIN:
+                    assert am[b] == i, f"splits {splits} row {b}: argmax {am[b]} vs {i}"
+    finally:
+        eng.debug_tune(att_cpc=0)
+    eng.check_device()
+
+
 def test_paged_matches_single_sequence_kernel(engine306_batched, engine306):
     """The batched path and the B=1 megakernel agree on the same sequence
     (both bf16 weights; activation rounding differs, so within tolerance)."""

@@ -431,7 +431,7 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
       if (value < 0 || value > b2d::kGemmMaxSplit) return B2D_ERR_INVALID_ARG;
       ws->force_ksplit = static_cast<int>(value);
       return B2D_OK;
-    case 5:  // batched step: force the attention's chunks per CTA (0 = automatic)
+    case 5:  // batched step: force the attention units per (sequence, kv head) (0 = automatic)
       if (value < 0 || value > 32) return B2D_ERR_INVALID_ARG;
       ws->force_att_cpc = static_cast<int>(value);
       return B2D_OK;

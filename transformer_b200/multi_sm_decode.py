@@ -186,7 +186,9 @@ class DecodeEngine:
                    sample_trace: torch.Tensor | None = None):
         """Diagnostic knobs: back-off between failed polls (ns), weight copies
         in flight per CTA; batched step: programmatic dependent launch on/off,
-        forced K split, forced attention chunks per CTA (0 = automatic)."""
+        forced K split, forced attention units per (sequence, kv head) (0 =
+        automatic); device stamp buffers for the projections, the attention
+        and the sampler (empty tensor = off)."""
         if sample_trace is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 10, sample_trace.data_ptr() if sample_trace.numel() else 0),
                        "b2d_debug_tune")
