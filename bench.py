@@ -438,11 +438,9 @@ def run_ours(args, rank, local_rank, world):
     for i, d in enumerate(waves):
         h_out[i].copy_(d.tok)
     p_e2e = pos
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for s in range(ne):
+
+    def e2e_step():
+        nonlocal p_e2e
         if p_e2e >= cfg.context_len:
             p_e2e = PROMPT_LEN
         for i, d in enumerate(waves):
@@ -453,6 +451,15 @@ def run_ours(args, rank, local_rank, world):
             h_out[i].copy_(d.tok, non_blocking=True)
         stream.synchronize()
         p_e2e += 1
+
+    for _ in range(2):  # warm-up: the call caches each wave's step graph on its second use
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(ne):
+        e2e_step()
     e2e_s = max_over_ranks(time.perf_counter() - t0, dev)
     e2e_value = TOTAL_SEQS * ne / e2e_s
     for d in waves:
@@ -506,8 +513,8 @@ def run_ours(args, rank, local_rank, world):
                      "algorithmic_bytes_per_step": alg_step},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                 "d2h_bytes_per_step": 4 * n_seq, "steps": ne,
-                "note": "per wave: pinned H2D of tokens+positions, b2d_decode_step_paged, D2H next tokens; "
-                        "one sync per step"},
+                "note": "per wave: pinned H2D of tokens+positions, b2d_decode_step_paged (replayed from its "
+                        "cached step graph after 2 untimed warm-up steps), D2H next tokens; one sync per step"},
         "clocks": clk,
     }
     line.update(extra)

@@ -159,7 +159,12 @@ B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_
  *   next_tok_dev      int32[batch] argmax
  * Needs a workspace created with max_batch >= 2.  Projections run on the
  * tensor cores (tcgen05); out-of-range tokens / table entries set the status
- * word read by b2d_last_error.
+ * word read by b2d_last_error.  From the second call with the same pointers,
+ * batch and pool shape, the step's kernel sequence is replayed from a CUDA
+ * graph cached in the workspace (16 argument sets, least recently used
+ * replaced): keep the argument buffers alive and reuse them between steps
+ * (their contents may change).  Free a pointer that a cached graph holds
+ * only after the step that used it has completed.
  */
 B2D_API b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev,
                                          const int32_t* pos_dev, int batch, void* kv_pool_dev,
@@ -246,7 +251,9 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * knob 9 = device address of a uint64 buffer [n_layers][8192 units][8] that
  * the batched step's attention fills with global-timer stamps (0 = off);
  * knob 10 = device address of a uint64 buffer [batch][8] of b2d_sample phase
- * stamps (0 = off).
+ * stamps (0 = off); knob 11 = b2d_decode_step_paged replays a cached CUDA
+ * graph for repeated argument sets (1, default) or launches directly (0).
+ * Every b2d_debug_tune call drops the cached graphs' validity.
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);
 B2D_API b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value);

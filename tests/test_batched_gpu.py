@@ -250,6 +250,46 @@ def test_paged_step_bitwise_reproducible(engine306_batched):
         assert torch.equal(lg, outs[0][0]) and torch.equal(nx, outs[0][1]) and torch.equal(pl, outs[0][2])
 
 
+def test_paged_step_graph_replay_matches_direct(engine306_batched):
+    """b2d_decode_step_paged replays a cached CUDA graph from the second call
+    with the same arguments: a greedy run through the cache (positions
+    advanced in the same device buffer) equals a run with direct launches
+    bit for bit, logits, tokens and cache rows."""
+    from transformer_b200.config import CONFIG_306M as cfg
+    eng = engine306_batched
+    dev = eng.device
+    rng = np.random.default_rng(22)
+    B, steps = 16, 6
+    table, nb = _table(rng, B, cfg.context_len // PAGE_TOKENS)
+    table_d = torch.from_numpy(table).to(dev)
+    shape = tuple(eng.new_kv_pool(nb).shape)
+    base = (torch.randn(shape, generator=torch.Generator().manual_seed(5)) * 0.5).to(torch.bfloat16)
+    tok0 = rng.integers(0, cfg.vocab_size, B).astype(np.int32)
+    pos0 = rng.integers(0, 300, B).astype(np.int32)
+    runs = []
+    try:
+        for graphs in (0, 1):
+            eng.debug_tune(graphs=bool(graphs))
+            pool = eng.new_kv_pool(nb)
+            pool.copy_(base.to(dev))
+            tok = torch.from_numpy(tok0).to(dev)
+            pos = torch.from_numpy(pos0).to(dev)
+            logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+            out = []
+            for _ in range(steps):
+                eng.step_paged(tok, pos, pool, table_d, logits, tok)
+                pos.add_(1)
+                out.append((logits.clone(), tok.clone()))
+            runs.append((out, pool.clone()))
+    finally:
+        eng.debug_tune(graphs=True)
+    eng.check_device()
+    (a, pa), (b, pb) = runs
+    for i, ((la, ta), (lb, tb)) in enumerate(zip(a, b)):
+        assert torch.equal(la, lb) and torch.equal(ta, tb), f"step {i}"
+    assert torch.equal(pa, pb)
+
+
 def test_paged_bad_inputs_set_status(engine_tiny_batched):
     """An out-of-range token or block-table entry is reported through the
     workspace status word (B2D_ERR_DEVICE_INPUT), not a fault."""

@@ -136,6 +136,21 @@ struct b2d_ws {
   int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
+  // b2d_decode_step_paged: CUDA graphs of the step's kernel sequence, one per
+  // argument set (LRU), captured on cap_stream and launched on the caller's.
+  struct StepGraph {
+    const void* ptr[6];    // tok, pos, pool, table, logits, next_tok
+    int batch, bps, nblk;
+    uint32_t tune;         // tune_gen at capture
+    int uses;              // calls seen with these arguments
+    int launches;          // kernels in the graph
+    uint64_t tick;         // last use
+    cudaGraphExec_t exec;
+  } graphs[16];
+  uint64_t graph_tick;
+  uint32_t tune_gen;       // bumped by every b2d_debug_tune call (cached graphs bake the knobs in)
+  bool no_graph;           // step through direct launches only
+  cudaStream_t cap_stream; // capture stream (created on first capture)
 };
 
 namespace {
@@ -350,6 +365,9 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
 b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   if (!ws) return B2D_OK;
   if (ws->m) cudaSetDevice(ws->m->device);
+  for (auto& g : ws->graphs)
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+  if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
   cudaFree(ws->H);
   cudaFree(ws->Hm);
   cudaFree(ws->qkv);
@@ -414,7 +432,12 @@ b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta) {
 
 b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
   if (!ws) return B2D_ERR_INVALID_ARG;
+  ++ws->tune_gen;  // cached step graphs hold the previous settings
   switch (knob) {
+    case 11:  // batched step: replay cached CUDA graphs (1, default) or launch directly (0)
+      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
+      ws->no_graph = value == 0;
+      return B2D_OK;
     case 1:  // back-off between failed polls, ns
       if (value < 0 || value > 100000) return B2D_ERR_INVALID_ARG;
       ws->poll_ns = static_cast<uint32_t>(value);
@@ -689,8 +712,62 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
       batch < 1 || batch > ws->max_batch || ws->max_batch < 2 || blocks_per_seq < 1 || num_blocks < 1)
     return B2D_ERR_INVALID_ARG;
   B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* lg = logits_dev ? logits_dev : ws->logits;
+  // The step is ~5 x n_layers dependent launches; from the second call with
+  // the same arguments on, it is replayed from a CUDA graph (one host call).
+  // Direct launches when graphs are off or the caller's stream is capturing
+  // (its own capture then records the kernels).
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (!ws->no_graph && cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone) {
+    const void* key[6] = {tok_dev, pos_dev, kv_pool_dev, block_table_dev, lg, next_tok_dev};
+    b2d_ws::StepGraph* g = nullptr;
+    for (auto& c : ws->graphs)
+      if (c.uses > 0 && std::equal(key, key + 6, c.ptr) && c.batch == batch && c.bps == blocks_per_seq &&
+          c.nblk == num_blocks && c.tune == ws->tune_gen) {
+        g = &c;
+        break;
+      }
+    if (!g) {  // least recently used entry
+      g = &ws->graphs[0];
+      for (auto& c : ws->graphs)
+        if (c.tick < g->tick) g = &c;
+      if (g->exec) cudaGraphExecDestroy(g->exec);
+      *g = b2d_ws::StepGraph{};
+      std::copy(key, key + 6, g->ptr);
+      g->batch = batch; g->bps = blocks_per_seq; g->nblk = num_blocks; g->tune = ws->tune_gen;
+    }
+    g->tick = ++ws->graph_tick;
+    if (g->uses++ > 0) {  // seen before: capture once (on a private stream; nothing runs), then replay
+      if (!g->exec) {
+        if (!ws->cap_stream) B2D_CUDA(cudaStreamCreateWithFlags(&ws->cap_stream, cudaStreamNonBlocking), "stream");
+        B2D_CUDA(cudaStreamBeginCapture(ws->cap_stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        b2d_status s = run_rows(m, ws, tok_dev, pos_dev, batch, kv_pool_dev, block_table_dev, blocks_per_seq,
+                                num_blocks, false, lg, next_tok_dev, ws->cap_stream);
+        cudaGraph_t graph = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(ws->cap_stream, &graph);
+        if (s == B2D_OK && e != cudaSuccess) s = cuda_fail(e, "end capture");
+        if (s == B2D_OK) {
+          const cudaError_t ei = cudaGraphInstantiate(&g->exec, graph, 0);
+          if (ei != cudaSuccess) {
+            g->exec = nullptr;
+            s = cuda_fail(ei, "graph instantiate");
+          }
+        }
+        if (graph) cudaGraphDestroy(graph);
+        if (s != B2D_OK) {
+          g->uses = 0;
+          return s;
+        }
+        g->launches = ws->last_launches;
+      }
+      ws->last_launches = g->launches;
+      B2D_CUDA(cudaGraphLaunch(g->exec, st), "graph launch");
+      return B2D_OK;
+    }
+  }
   return run_rows(m, ws, tok_dev, pos_dev, batch, kv_pool_dev, block_table_dev, blocks_per_seq, num_blocks, false,
-                  logits_dev ? logits_dev : ws->logits, next_tok_dev, static_cast<cudaStream_t>(stream));
+                  lg, next_tok_dev, st);
 }
 
 b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos, void* kv_dev,
