@@ -478,7 +478,7 @@ def run_ours(args, rank, local_rank, world):
             eng1.prefill(prompt_cfg2(), kvp)
         pf_ms = events_ms(lambda: [eng1.prefill(prompt_cfg2(), kvp) for _ in range(10)], stream, torch) / 10
         extra["config2_b1_long"]["prefill_384"] = {"ms": pf_ms, "tok_s": 384 / (pf_ms / 1000),
-                                                   "how": "b2d_prefill, 3 chunks of 128 positions, CUDA events"}
+                                                   "how": "b2d_prefill, one 384-row pass, CUDA events"}
         eng1.close()
         eng3 = DecodeEngine(w, max_batch=64)
         extra["config3_paged_b64"] = measure_cfg3(eng3, cfg, torch)

@@ -176,7 +176,7 @@ B2D_API b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t
  * Device prefill (replaces the JAX prefill of generate.py:68-89 /
  * model.py:194-231 for the decode cache): feeds n_tokens prompt tokens
  * (tok_dev, int32) at positions start_pos.. of ONE sequence through the
- * batched tensor-core step, 128 positions per chunk, writing their K/V into
+ * batched tensor-core step, up to 512 positions per chunk, writing their K/V into
  * kv_dev (one sequence's cache in the reference layout, b2d_kv_layout).
  * Outputs the logits of the last position (f32 [vocab], or NULL) and its
  * argmax (or NULL).  Each position's math is the decode step's at that

@@ -24,8 +24,10 @@ def _oracle_prefix(P, cfg, prompt):
 
 @pytest.mark.parametrize("n", [1, 5, 127, 128, 129])
 def test_prefill_tiny_chunk_boundaries(engine_tiny, params_tiny, n):
-    """Prompt lengths around the 128-position chunk: last logits and every
-    written cache row against the oracle; argmax where the margin allows."""
+    """Prompt lengths around 128 rows (a projection tile width) and a single
+    position: last logits (the output projection runs on the last row only)
+    and every written cache row against the oracle; argmax where the margin
+    allows."""
     from transformer_b200.config import CONFIG_TINY as cfg
     from transformer_b200.packing import unpack_kv_caches
     from transformer_b200.synth import params_f32
@@ -78,7 +80,7 @@ def test_prefill_continuation_then_decode(engine_tiny, params_tiny):
 
 
 def test_prefill_equals_stepwise_306m(engine306):
-    """Config 2's 384-token prompt (three chunks): device prefill against the
+    """Config 2's 384-token prompt (one 512-row chunk): device prefill against the
     one-position-per-step ingestion (both bf16 caches): last logits within the
     parity tolerance of each other, caches within bf16 rounding."""
     from transformer_b200.synth import prompt_cfg2

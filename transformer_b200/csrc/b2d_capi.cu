@@ -157,7 +157,7 @@ namespace {
 constexpr int kTraceCtas = 256;        // projection CTAs stamped per launch (diagnostics)
 constexpr int kTraceLaunches = 4 * 64 + 1;  // stamped projection launches per step (n_layers <= 64)
 constexpr int kAttTraceUnits = 8192;        // attention units stamped per launch (diagnostics)
-constexpr int kPrefillRows = 128;           // prompt positions per prefill chunk
+constexpr int kPrefillRows = 512;           // prompt positions per prefill chunk
 
 __global__ void iota_kernel(int32_t* out, int start, int n) {
   b2d::pdl_wait();
@@ -594,10 +594,11 @@ namespace {
 // ONE sequence whose cache `cache` is contiguous in the reference layout
 // (table = nullptr); the K/V of all rows are appended first, per layer.
 // logits == nullptr skips the output projection (earlier prefill chunks);
-// next_tok == nullptr skips the argmax.
+// next_tok == nullptr skips the argmax; last_row: the output projection
+// covers only the last row, written as logits row 0 (prefill).
 b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t* pos, int batch, void* cache,
                     const int32_t* table, int bps, int num_blocks, bool prefill, float* logits, int32_t* next_tok,
-                    cudaStream_t st) {
+                    cudaStream_t st, bool last_row = false) {
   b2d_status s = ensure_weight_maps(m);
   if (s != B2D_OK) return s;
   const b2d_config& c = m->cfg;
@@ -692,7 +693,14 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   }
   g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V;
   g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
+  if (last_row) {
+    g.N = 1;
+    g.n_base = batch - 1;
+    p_lg = b2d::gemm_plan(V, 1, D, 256);
+  }
   B2D_CUDA(gemm(m->wmaps[4 * c.n_layers], ws->xmap, b2d::EPI_F32, p_lg), "logits");
+  g.N = batch;
+  g.n_base = 0;
   if (next_tok) {
     B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
                       next_tok), "argmax");
@@ -784,10 +792,10 @@ b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_t
     B2D_CUDA(launch_k(iota_kernel, dim3((rows + 127) / 128), dim3(128), st, !ws->no_pdl, ws->prefill_pos,
                       start_pos + c0, rows), "positions");
     b2d_status s = run_rows(m, ws, tok_dev + c0, ws->prefill_pos, rows, kv_dev, nullptr, 0, 0, true,
-                            last && (logits_dev || next_tok_dev) ? ws->logits : nullptr, nullptr, st);
+                            last && (logits_dev || next_tok_dev) ? ws->logits : nullptr, nullptr, st, true);
     if (s != B2D_OK) return s;
     if (last) {
-      const float* lrow = ws->logits + size_t(rows - 1) * V;
+      const float* lrow = ws->logits;  // the last position's logits (row 0)
       if (logits_dev)
         B2D_CUDA(cudaMemcpyAsync(logits_dev, lrow, sizeof(float) * V, cudaMemcpyDeviceToDevice, st), "logits row");
       if (next_tok_dev)

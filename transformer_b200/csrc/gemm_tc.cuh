@@ -47,6 +47,7 @@ struct GemmArgs {
   int ldy = 0;
   uint32_t* err = nullptr;            // status word: set (if still 0) when a wait runs out
   int ksplit = 1;                     // 1..kGemmMaxSplit, <= K/64; > 1 needs a (1,1,ksplit) cluster launch
+  int n_base = 0;                     // X rows (and ss_in columns) start at this row; outputs at row 0
   // Folded RMSNorm (model.py:94-98): the next projection's input is
   // bf16(RMSNorm(h) * g) = r[n] * bf16(h * g) up to bf16 rounding, with
   // r[n] = rsqrt(mean(h[n]^2) + eps) applied to that projection's result.
@@ -189,7 +190,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
     pdl_wait();
     gemm_stamp(g, 2);
     for (int i = 0; i < pre; ++i)
-      tma_load_2d(sm + i * L::STAGE + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, n0, &full[i], pol_x);
+      tma_load_2d(sm + i * L::STAGE + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, g.n_base + n0, &full[i], pol_x);
     issued = pre;
     for (int i = pre; i < nk; ++i) {
       const int s = i % S;
@@ -197,7 +198,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
       uint8_t* a = sm + s * L::STAGE;
       mbar_arrive_expect_tx(&full[s], L::STAGE);
       tma_load_2d(a, &wmap, (kb0 + i) * kGemmBK, m0, &full[s], pol_w);
-      tma_load_2d(a + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, n0, &full[s], pol_x);
+      tma_load_2d(a + L::A_BYTES, &xmap, (kb0 + i) * kGemmBK, g.n_base + n0, &full[s], pol_x);
       issued = i + 1;
     }
   } else if (warp == 1 && lane == 0) {
@@ -226,7 +227,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
       float rs = 1.f;
       if (n0 + c < g.N) {
         float tot = 0.f;
-        for (int t = 0; t < g.ss_dim / kGemmBM; ++t) tot += __ldcg(g.ss_in + static_cast<size_t>(t) * g.ss_ld + n0 + c);
+        for (int t = 0; t < g.ss_dim / kGemmBM; ++t)
+          tot += __ldcg(g.ss_in + static_cast<size_t>(t) * g.ss_ld + g.n_base + n0 + c);
         rs = rsqrtf(tot / static_cast<float>(g.ss_dim) + g.norm_eps);
       }
       s_rs[c] = rs;
