@@ -261,11 +261,20 @@ def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
     ms = events_ms(run, stream, torch)
     eng.check_device()
     us = ms * 1000.0 / n_steps
+    # the same tokens from one launch (b2d_decode_steps), when they fit before the context end
+    one_launch = None
+    if P0 + 3 + n_steps <= cfg.context_len:
+        toks = torch.zeros(n_steps, dtype=torch.int32, device=dev)
+        ms1 = events_ms(lambda: eng.decode_steps(tok, posarr[3:4], kv, n_steps, tokens=toks, stream=stream),
+                        stream, torch)
+        eng.check_device()
+        one_launch = ms1 * 1000.0 / n_steps
     positions = [P0 + (i % span) for i in range(3, 3 + n_steps)]
     alg = float(np.mean([cfg.step_bytes([p]) for p in positions]))
     peak, kind = measured_peaks()
     ach = alg / (us * 1e-6) / 1e9
     return {"workload": label, "us_per_token": us, "tok_s": 1e6 / us, "steps": n_steps,
+            "us_per_token_one_launch": one_launch,
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
                          "traffic": profile_traffic()},

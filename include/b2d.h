@@ -148,6 +148,21 @@ B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_
                            float* logits_dev, int32_t* next_tok_dev, void* stream);
 
 /*
+ * Several greedy decode steps of one sequence (batch 1) in ONE launch: step s
+ * consumes the token produced by step s-1 (the first consumes *tok_dev) at
+ * position *pos_dev + s, appends its K/V to kv_dev and writes its argmax to
+ * tokens_dev[s] (int32[n_steps]); logits_dev (or NULL) receives the last
+ * step's logits.  The weights stream through the SMs without a break between
+ * steps.  Same math and results as n_steps calls of b2d_decode_step feeding
+ * next_tok back; *pos_dev + n_steps <= context_len (else the status word
+ * reports a bad position).  No counterpart in the reference's kernels (one
+ * launch per token, generate.py:112).
+ */
+B2D_API b2d_status b2d_decode_steps(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                                    int n_steps, void* kv_dev, int32_t* tokens_dev, float* logits_dev,
+                                    void* stream);
+
+/*
  * Batched decode step over a paged KV pool (no
  * reference counterpart: the reference's batched kernels were deleted).
  *   tok_dev / pos_dev int32[batch]; pos < 0 marks a sequence inactive for this

@@ -181,3 +181,65 @@ def test_wait_timeout_is_reported_not_hung(engine_tiny):
     kv = eng.new_kv()
     got, _ = _step(eng, 3, 0, kv)
     assert eng.last_error()[0] == _lib.B2D_OK and np.isfinite(got).all()
+
+
+@pytest.mark.parametrize("which", ["tiny", "306m"])
+def test_multi_step_equals_single_steps(which, engine_tiny, engine306):
+    """b2d_decode_steps (n greedy tokens in one launch) equals n launches of
+    b2d_decode_step with the argmax fed back: tokens, last logits and every
+    cache row bit for bit (same kernel math, fixed-order reductions)."""
+    eng = engine_tiny if which == "tiny" else engine306
+    cfg = eng.cfg
+    rng = np.random.default_rng(40)
+    prompt = rng.integers(0, cfg.vocab_size, 13).astype(np.int32)
+    n = 12 if which == "tiny" else 20
+    kv_a, kv_b = eng.new_kv(), eng.new_kv()
+    first = int(torch.argmax(eng.prefill(prompt, kv_a)).item())
+    eng.prefill(prompt, kv_b)
+    dev = eng.device
+    # n single launches, the device argmax fed back
+    tok = torch.tensor([first], dtype=torch.int32, device=dev)
+    pos = torch.tensor([len(prompt)], dtype=torch.int32, device=dev)
+    singles = []
+    for i in range(n):
+        eng.step(tok, pos, kv_a, eng.logits, tok)
+        singles.append(int(tok.item()))
+        pos += 1
+    last_single = eng.logits[0].clone()
+    # one launch
+    tok = torch.tensor([first], dtype=torch.int32, device=dev)
+    pos = torch.tensor([len(prompt)], dtype=torch.int32, device=dev)
+    logits = torch.zeros(cfg.vocab_size, dtype=torch.float32, device=dev)
+    toks = eng.decode_steps(tok, pos, kv_b, n, logits=logits)
+    eng.check_device()
+    assert toks.cpu().tolist() == singles
+    assert torch.equal(logits, last_single)
+    assert torch.equal(kv_a, kv_b)
+
+
+def test_multi_step_range_and_timeout(engine_tiny):
+    """A multi-step launch past the context is refused on the device (status
+    word, no write); a wait that cannot finish inside a multi-step launch is
+    reported as a timeout (failure injected on the host: one CTA fewer than
+    the split assumes) and the context stays usable."""
+    eng = engine_tiny
+    cfg = eng.cfg
+    dev = eng.device
+    kv = eng.new_kv()
+    tok = torch.tensor([3], dtype=torch.int32, device=dev)
+    pos = torch.tensor([cfg.context_len - 4], dtype=torch.int32, device=dev)
+    eng.reset()
+    eng.decode_steps(tok, pos, kv, 5)
+    st, word = eng.last_error()
+    assert st == _lib.B2D_ERR_DEVICE_INPUT and word == 0x202, (st, hex(word))
+    assert torch.count_nonzero(kv) == 0
+    eng.reset()
+    eng.debug_set(50_000_000, extra_ctas=1)
+    eng.decode_steps(tok, torch.zeros(1, dtype=torch.int32, device=dev), kv, 3)
+    st, word = eng.last_error()
+    assert st == _lib.B2D_ERR_DEVICE_TIMEOUT, (st, hex(word))
+    eng.debug_set(2_000_000_000, extra_ctas=0)
+    eng.reset()
+    kv = eng.new_kv()
+    toks = eng.decode_steps(tok, torch.zeros(1, dtype=torch.int32, device=dev), kv, 3)
+    assert eng.last_error()[0] == _lib.B2D_OK and all(0 <= t < cfg.vocab_size for t in toks.cpu().tolist())

@@ -478,15 +478,11 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
   return B2D_ERR_INVALID_ARG;
 }
 
-b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
-                           int batch, void* kv_dev, float* logits_dev, int32_t* next_tok_dev,
-                           void* stream) {
-  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_dev || !next_tok_dev || batch < 1 ||
-      batch > ws->max_batch)
-    return B2D_ERR_INVALID_ARG;
-  if (batch != 1) return B2D_ERR_UNSUPPORTED;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+namespace {
+// One cooperative launch of the B=1 kernel: n_steps greedy tokens.
+b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev, void* kv_dev,
+                     float* logits_dev, int32_t* next_tok_dev, int n_steps, int32_t* tok_out_dev,
+                     cudaStream_t st) {
   const b2d_config& c = m->cfg;
   b2d::DecodeArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -528,11 +524,36 @@ b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, con
   A.stage_stride = ws->stage_stride;
   A.poll_ns = ws->poll_ns;
   A.max_inflight = ws->max_inflight;
+  A.n_steps = n_steps;
+  A.tok_out = tok_out_dev;
   void* args[] = {&A};
   B2D_CUDA(cudaLaunchCooperativeKernel(m->ops->kernel, dim3(m->grid), dim3(b2d::kThreads), args,
                                        m->ops->smem, st),
            "decode launch");
   return B2D_OK;
+}
+}  // namespace
+
+b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                           int batch, void* kv_dev, float* logits_dev, int32_t* next_tok_dev,
+                           void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_dev || !next_tok_dev || batch < 1 ||
+      batch > ws->max_batch)
+    return B2D_ERR_INVALID_ARG;
+  if (batch != 1) return B2D_ERR_UNSUPPORTED;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  return launch_b1(m, ws, tok_dev, pos_dev, kv_dev, logits_dev, next_tok_dev, 1, nullptr,
+                   static_cast<cudaStream_t>(stream));
+}
+
+b2d_status b2d_decode_steps(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                            int n_steps, void* kv_dev, int32_t* tokens_dev, float* logits_dev, void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_dev || !tokens_dev || n_steps < 1 ||
+      n_steps > m->cfg.context_len)
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  return launch_b1(m, ws, tok_dev, pos_dev, kv_dev, logits_dev, tokens_dev + (n_steps - 1), n_steps, tokens_dev,
+                   static_cast<cudaStream_t>(stream));
 }
 
 b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab, const int32_t* history_dev,
@@ -863,7 +884,7 @@ b2d_status b2d_test_gemm(const void* w_dev, int M, int K, const void* x_dev, int
 // ---------------------------------------------------------------------------
 namespace b2d {
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;
-constexpr size_t kStaticCtlOffset = 0;          // Control (512 B)
+constexpr size_t kStaticCtlOffset = 0;          // Control (640 B)
 constexpr size_t kStaticArgmaxOffset = 1024;    // am_val[kStaticMaxGrid], am_idx[kStaticMaxGrid]
 constexpr int kStaticMaxGrid = 1024;
 constexpr size_t kStaticWordsOffset = 16384;    // exchange words

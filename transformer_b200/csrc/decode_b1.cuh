@@ -41,7 +41,7 @@ enum : uint32_t {
 };
 enum : uint32_t {
   SITE_H = 1, SITE_QKV = 2, SITE_ATT = 3, SITE_HM = 4, SITE_ACT = 5, SITE_FINAL = 6,
-  SITE_FULL = 7, SITE_EMPTY = 8, SITE_DRAIN = 9, SITE_VATT = 10,
+  SITE_FULL = 7, SITE_EMPTY = 8, SITE_DRAIN = 9, SITE_VATT = 10, SITE_TOKEN = 11,
 };
 
 struct Control {  // each word on its own 128-byte line
@@ -53,6 +53,8 @@ struct Control {  // each word on its own 128-byte line
   uint32_t pad2[31];
   uint32_t abort_flag;
   uint32_t pad3[31];
+  uint64_t tok_word;  // multi-step launches: (step flag << 32) | token of the step just finished
+  uint32_t pad4[30];
 };
 
 struct DecodeArgs {
@@ -68,6 +70,8 @@ struct DecodeArgs {
   __nv_bfloat16* kv;  // [L][2][NKV][ctx][DH]
   float* logits;      // [V] or null
   int32_t* next_tok;
+  int n_steps;        // greedy tokens per launch (>= 1): step s decodes at pos + s
+  int32_t* tok_out;   // [n_steps] the token of every step, or null
   uint64_t* words;    // exchange words
   Control* ctl;
   float* am_val;      // [grid]
@@ -153,6 +157,7 @@ struct Smem {
   float am_v[kConsumerWarps];
   int am_i[kConsumerWarps];
   int abort;
+  int tok_in;  // multi-step: this step's input token
 };
 
 // Fields read with 16-byte vector loads or written by bulk copies.
@@ -442,7 +447,7 @@ __device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float (&gr)[S::D
 
 // Producer: streams this CTA's weight ranges for the whole step.
 template <class S>
-__device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_t flag, uint64_t t0) {
+__device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_t flag, uint64_t t0, int nsteps) {
   const uint64_t pol = l2_policy_evict_first();
   const int G = A.grid_part;
   uint32_t seq = 0;
@@ -487,497 +492,531 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       issue(base + static_cast<size_t>(u) * unit_bytes, static_cast<uint32_t>(cnt * unit_bytes));
     }
   };
-  for (int l = 0; l < A.n_layers && ok; ++l) {
-    const uint8_t* lw = A.wbase + static_cast<size_t>(l) * A.layer_stride;
-    stream(lw + A.off_qkv, S::QKV, S::ROWB_D, S::RPS_D);
-    stream(lw + A.off_o, S::D, S::ROWB_D, S::RPS_D);
-    stream(lw + A.off_gu, S::DFF, 2 * S::ROWB_D, S::PPS);
-    stream(lw + A.off_down, S::D, S::ROWB_F, S::RPS_F);
-  }
-  if (ok) stream(A.wbase + A.off_emb, A.vocab, S::ROWB_D, S::RPS_D);
-  {
-    // Never leave with copies in flight: wait (bounded) for the last stages
-    // issued.  On the normal path they land before the consumers finish.
-    const uint32_t first = seq > kStages ? seq - kStages : 0;
-    const uint64_t td = globaltimer_ns();
-    for (uint32_t s = first; s < seq; ++s) {
-      while (!mbar_test(&sm.full[s % kStages], (s / kStages) & 1u)) {
-        if (globaltimer_ns() - td > A.wait_ns) break;
+  for (int step = 0; step < nsteps && ok; ++step) {  // the weight sequence repeats every step
+      for (int l = 0; l < A.n_layers && ok; ++l) {
+        const uint8_t* lw = A.wbase + static_cast<size_t>(l) * A.layer_stride;
+        stream(lw + A.off_qkv, S::QKV, S::ROWB_D, S::RPS_D);
+        stream(lw + A.off_o, S::D, S::ROWB_D, S::RPS_D);
+        stream(lw + A.off_gu, S::DFF, 2 * S::ROWB_D, S::PPS);
+        stream(lw + A.off_down, S::D, S::ROWB_F, S::RPS_F);
       }
+      if (ok) stream(A.wbase + A.off_emb, A.vocab, S::ROWB_D, S::RPS_D);
     }
-  }
-}
-
-// One attention unit: head h, KV positions [p0, p1) (reference :182-221).
-// Writes o (unnormalised), m, l as exchange words.
-//
-// Layout for latency: a warp owns 16 positions per pass, two lanes per
-// position (each lane holds half of the 64 dims), so QK needs one shuffle per
-// position instead of a full warp reduction; PV is lane-per-dim over
-// probabilities staged in shared memory.  The K/V of the unit's first pass
-// are requested at the start of the layer (att_prefetch), so their latency
-// hides behind the QKV phase.
-struct AttPre {
-  uint32_t vbytes;  // bytes of each of the pass's K and V copies in flight (0 = none)
-  float rc, rs;     // RoPE cos/sin (threads < 64)
-  int unit;         // unit the prefetch belongs to (-1 = none)
-};
-
-// Issue one pass (up to 128 positions from `base`) of unit (h, j): the cached
-// K and V rows into shared memory by two bulk copies (each contiguous in the
-// cache).  Position `pos` is new: it comes from q/k/v.
-template <class S>
-__device__ __forceinline__ void att_load_pass(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
-                                              int h, int j, int base) {
-  const int t = threadIdx.x;
-  const int g = h / S::GQA;
-  const int p1 = min(j * A.att_T + A.att_T, pos + 1);
-  const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
-  const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
-  const __nv_bfloat16* Vc = Kc + half;
-  const int ncached = max(0, min(min(base + 128, p1), pos) - base);
-  pre.vbytes = static_cast<uint32_t>(ncached) * S::DH * 2;
-  if (t == 0 && pre.vbytes) {
-    const uint64_t pol = l2_policy_evict_last();
-    mbar_arrive_expect_tx(&sm.att_bar, 2 * pre.vbytes);
-    bulk_g2s(sm.katt, Kc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
-    bulk_g2s(sm.vatt, Vc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
-  }
-}
-
-template <class S>
-__device__ __forceinline__ void att_prefetch(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
-                                             int u, int nsplit) {
-  const int t = threadIdx.x;
-  pre.unit = u;
-  att_load_pass<S>(A, sm, pre, l, pos, u / nsplit, u % nsplit, (u % nsplit) * A.att_T);
-  pre.rc = pre.rs = 0.f;
-  if (t < 64) {
-    pre.rc = __ldg(A.rcos + static_cast<size_t>(pos) * 32 + (t & 31));
-    pre.rs = __ldg(A.rsin + static_cast<size_t>(pos) * 32 + (t & 31));
-  }
-}
-
-template <class S>
-__device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm, uint32_t flag,
-                                               uint64_t t0, int l, int pos, int u, int nsplit,
-                                               int trace_slot, uint32_t& att_phase, AttPre& pre) {
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int h = u / nsplit, j = u % nsplit;
-  const int g = h / S::GQA;
-  const int p0 = j * A.att_T, p1 = min(p0 + A.att_T, pos + 1);
-  const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
-  const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
-  const __nv_bfloat16* Vc = Kc + half;
-  uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
-  const int qi = lane & 15, hf = lane >> 4;  // position within the warp's 16, dim half
-
-  if (pre.unit != u) att_prefetch<S>(A, sm, pre, l, pos, u, nsplit);
-  pre.unit = -1;
-  uint32_t& vbytes = pre.vbytes;
-  const float rc = pre.rc, rs = pre.rs;
-  auto load_pass = [&](int base) { att_load_pass<S>(A, sm, pre, l, pos, h, j, base); };
-  // Wait (bounded, ignoring the abort marker) for this pass's V copy; used on
-  // every path so the CTA never leaves with the copy in flight.
-  auto wait_v = [&]() -> bool {
-    if (!vbytes) return true;
-    const uint64_t ts0 = globaltimer_ns();
-    bool landed = false;
-    uint32_t n = 0;
-    while (!(landed = mbar_test(&sm.att_bar, att_phase & 1u))) {
-      if ((++n & 63u) == 0 && globaltimer_ns() - ts0 > 10000000ull) {
-        raise_error(A.ctl, ST_TIMEOUT | SITE_VATT, flag);
-        break;
-      }
-    }
-    ++att_phase;
-    vbytes = 0;
-    return landed;
-  };
-  // q head h, k/v of kv head g: 3 x 32 word pairs.
-  bool ok = gather_pairs<1>(
-      A, flag, t0, SITE_QKV,
-      [&](int) {
-        const int seg = t >> 5, e = (t & 31) * 2;
-        const int row = seg == 0 ? h * 64 : (seg == 1 ? S::NH * 64 + g * 64 : (S::NH + S::NKV) * 64 + g * 64);
-        return lw + S::D + row + e;
-      },
-      [&](int) { return t < 96; },
-      [&](int, float a, float b) { sm.qkv[2 * t] = a; sm.qkv[2 * t + 1] = b; });
-  ok = consumer_sync_and<kConsumers>(ok);
-  if (!ok) {
-    wait_v();
-    return false;
-  }
-  trace_stamp(A, trace_slot);
-  // RoPE (rotate-half, reference :154-173; f32 tables as model.py:101-107).
-  if (t < 64) {
-    const int i = t & 31;
-    const float* src = sm.qkv + (t < 32 ? 0 : 64);
-    const float lo = src[i], hi = src[i + 32];
-    float* dst = t < 32 ? sm.rq : sm.rk;
-    const float sc = t < 32 ? 0.125f : 1.0f;  // 1/sqrt(64) folded into q (exact)
-    dst[i] = (lo * rc - hi * rs) * sc;
-    dst[i + 32] = (lo * rs + hi * rc) * sc;
-  }
-  consumer_sync<kConsumers>();
-  const float4* q4 = reinterpret_cast<const float4*>(sm.rq + hf * 32);
-  const float vn0 = sm.qkv[128 + 2 * lane], vn1 = sm.qkv[128 + 2 * lane + 1];
-
-  float m = -INFINITY, lsum = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int base = p0; base < p1; base += 16 * kConsumerWarps) {
-    if (base != p0) load_pass(base);
-    if (!__all_sync(0xffffffffu, wait_v())) ok = false;  // K/V rows of this pass landed
-    const int pk = base + warp * 16 + qi;
-    float sdot = 0.f;
-    if (pk == pos) {
-#pragma unroll
-      for (int d = 0; d < 32; ++d) sdot = fmaf(sm.rq[hf * 32 + d], sm.rk[hf * 32 + d], sdot);
-    } else if (ok && pk < p1) {
-      // lane qi starts at chunk qi & 3 so a quarter-warp's 8 rows spread over banks
-      const uint4* kr = reinterpret_cast<const uint4*>(sm.katt[pk - base]) + hf * 4;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int cc = (c + qi) & 3;
-        const uint4 kw = kr[cc];
-        const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
-        sdot = fmaf(qa.x, bf16_lo(kw.x), sdot);
-        sdot = fmaf(qa.y, bf16_hi(kw.x), sdot);
-        sdot = fmaf(qa.z, bf16_lo(kw.y), sdot);
-        sdot = fmaf(qa.w, bf16_hi(kw.y), sdot);
-        sdot = fmaf(qb.x, bf16_lo(kw.z), sdot);
-        sdot = fmaf(qb.y, bf16_hi(kw.z), sdot);
-        sdot = fmaf(qb.z, bf16_lo(kw.w), sdot);
-        sdot = fmaf(qb.w, bf16_hi(kw.w), sdot);
-      }
-    }
-    sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
-    const bool valid = pk < p1;
-    float s = valid ? sdot : -INFINITY;
-    float mx = s;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float mn = fmaxf(m, mx);
-    const float pe = valid ? __expf(s - mn) : 0.f;
-    float ps = pe;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-    const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-    if (hf == 0) sm.wo[warp][qi] = pe;   // stage probabilities for PV
-    __syncwarp();
-    float a0 = 0.f, a1 = 0.f;
-    if (ok) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int pv = base + warp * 16 + i;
-        const float pi = sm.wo[warp][i];
-        float v0 = 0.f, v1 = 0.f;
-        if (pv == pos) {
-          v0 = vn0; v1 = vn1;
-        } else if (pv < p1) {
-          const uint32_t vw = reinterpret_cast<const uint32_t*>(sm.vatt[pv - base])[lane];
-          v0 = bf16_lo(vw); v1 = bf16_hi(vw);
+    {
+      // Never leave with copies in flight: wait (bounded) for the last stages
+      // issued.  On the normal path they land before the consumers finish.
+      const uint32_t first = seq > kStages ? seq - kStages : 0;
+      const uint64_t td = globaltimer_ns();
+      for (uint32_t s = first; s < seq; ++s) {
+        while (!mbar_test(&sm.full[s % kStages], (s / kStages) & 1u)) {
+          if (globaltimer_ns() - td > A.wait_ns) break;
         }
-        a0 = fmaf(pi, v0, a0);
-        a1 = fmaf(pi, v1, a1);
       }
     }
-    __syncwarp();
-    lsum = fmaf(lsum, alpha, ps);
-    o0 = fmaf(o0, alpha, a0);
-    o1 = fmaf(o1, alpha, a1);
-    m = mn;
-    // every warp is done reading the staged V before the next pass reuses it
-    ok = consumer_sync_and<kConsumers>(ok);
-    if (!ok) return false;
   }
-  // per-warp state -> shared, then warp 0 merges in fixed order
-  sm.wo[warp][2 * lane] = o0;
-  sm.wo[warp][2 * lane + 1] = o1;
-  if (lane == 0) { sm.wm[warp] = m; sm.wl[warp] = lsum; }
-  consumer_sync<kConsumers>();
-  if (warp == 0) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.wm[w]);
-    float L = 0.f, b0 = 0.f, b1 = 0.f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
-      const float e = sm.wl[w] > 0.f ? __expf(sm.wm[w] - M) : 0.f;
-      L = fmaf(sm.wl[w], e, L);
-      b0 = fmaf(sm.wo[w][2 * lane], e, b0);
-      b1 = fmaf(sm.wo[w][2 * lane + 1], e, b1);
+
+  // One attention unit: head h, KV positions [p0, p1) (reference :182-221).
+  // Writes o (unnormalised), m, l as exchange words.
+  //
+  // Layout for latency: a warp owns 16 positions per pass, two lanes per
+  // position (each lane holds half of the 64 dims), so QK needs one shuffle per
+  // position instead of a full warp reduction; PV is lane-per-dim over
+  // probabilities staged in shared memory.  The K/V of the unit's first pass
+  // are requested at the start of the layer (att_prefetch), so their latency
+  // hides behind the QKV phase.
+  struct AttPre {
+    uint32_t vbytes;  // bytes of each of the pass's K and V copies in flight (0 = none)
+    float rc, rs;     // RoPE cos/sin (threads < 64)
+    int unit;         // unit the prefetch belongs to (-1 = none)
+  };
+
+  // Issue one pass (up to 128 positions from `base`) of unit (h, j): the cached
+  // K and V rows into shared memory by two bulk copies (each contiguous in the
+  // cache).  Position `pos` is new: it comes from q/k/v.
+  template <class S>
+  __device__ __forceinline__ void att_load_pass(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
+                                                int h, int j, int base) {
+    const int t = threadIdx.x;
+    const int g = h / S::GQA;
+    const int p1 = min(j * A.att_T + A.att_T, pos + 1);
+    const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
+    const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
+    const __nv_bfloat16* Vc = Kc + half;
+    const int ncached = max(0, min(min(base + 128, p1), pos) - base);
+    pre.vbytes = static_cast<uint32_t>(ncached) * S::DH * 2;
+    if (t == 0 && pre.vbytes) {
+      const uint64_t pol = l2_policy_evict_last();
+      mbar_arrive_expect_tx(&sm.att_bar, 2 * pre.vbytes);
+      bulk_g2s(sm.katt, Kc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
+      bulk_g2s(sm.vatt, Vc + static_cast<size_t>(base) * S::DH, pre.vbytes, &sm.att_bar, pol);
     }
-    uint64_t* out = lw + A.w_att + static_cast<size_t>(h * nsplit + j) * kAttWords;
-    st_word(out + 2 * lane, b0, flag);
-    st_word(out + 2 * lane + 1, b1, flag);
-    if (lane == 0) {
-      st_word(out + 64, M, flag);
-      st_word(out + 65, L, flag);
+  }
+
+  template <class S>
+  __device__ __forceinline__ void att_prefetch(const DecodeArgs& A, Smem<S>& sm, AttPre& pre, int l, int pos,
+                                               int u, int nsplit) {
+    const int t = threadIdx.x;
+    pre.unit = u;
+    att_load_pass<S>(A, sm, pre, l, pos, u / nsplit, u % nsplit, (u % nsplit) * A.att_T);
+    pre.rc = pre.rs = 0.f;
+    if (t < 64) {
+      pre.rc = __ldg(A.rcos + static_cast<size_t>(pos) * 32 + (t & 31));
+      pre.rs = __ldg(A.rsin + static_cast<size_t>(pos) * 32 + (t & 31));
     }
   }
-  // The first head of the group, owning the split that holds `pos`, appends
-  // this position's K (post-RoPE) and V to the cache in bf16.
-  if (warp == 1 && (h % S::GQA) == 0 && pos >= p0 && pos < p1) {
-    __nv_bfloat162 kk = __floats2bfloat162_rn(sm.rk[2 * lane], sm.rk[2 * lane + 1]);
-    __nv_bfloat162 vv = __floats2bfloat162_rn(vn0, vn1);
-    __nv_bfloat16* kd = const_cast<__nv_bfloat16*>(Kc) + static_cast<size_t>(pos) * S::DH;
-    __nv_bfloat16* vd = const_cast<__nv_bfloat16*>(Vc) + static_cast<size_t>(pos) * S::DH;
-    reinterpret_cast<__nv_bfloat162*>(kd)[lane] = kk;
-    reinterpret_cast<__nv_bfloat162*>(vd)[lane] = vv;
-  }
-  consumer_sync<kConsumers>();
-  return true;
-}
 
-template <class S>
-__global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs A) {
-  extern __shared__ __align__(128) uint8_t decode_smem_raw[];
-  static_assert(SmemChecks<S>::ok, "");
-  Smem<S>& sm = *reinterpret_cast<Smem<S>*>(decode_smem_raw);
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int cta = blockIdx.x;
-  const int G = A.grid_part;
-  const uint64_t t0 = globaltimer_ns();
-
-  // A workspace holding an earlier device error stays halted until reset.
-  if (ld_relaxed_u32(&A.ctl->status) != 0u) return;
-  const int tok = __ldg(A.tok), pos = __ldg(A.pos);
-  if (tok < 0 || tok >= A.vocab || pos < 0 || pos >= A.ctx) {
-    if (cta == 0 && t == 0) atomicCAS(&A.ctl->status, 0u, ST_BAD_INPUT | (tok < 0 || tok >= A.vocab ? 1u : 2u));
-    return;
-  }
-  const uint32_t flag = ld_relaxed_u32(&A.ctl->gen) + 1u;
-
-  if (t == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kConsumerWarps);
-    }
-    mbar_init(&sm.att_bar, 1);
-    sm.abort = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    if (lane == 0) producer_loop<S>(A, sm, cta, flag, t0);
-    return;
-  }
-
-  Ring ring{sm.stage, sm.full, sm.empty, 0u};
-  bool ok = true;
-  uint32_t att_phase = 0;  // completed uses of sm.att_bar
-  AttPre pre;
-  pre.unit = -1;
-  pre.vbytes = 0;
-  trace_stamp(A, 0);
-  const int nsplit = (pos + A.att_T) / A.att_T;  // ceil((pos+1)/T)
-  const int n_units = S::NH * nsplit;
-
-  // Embedding row (reference :87-88).
-  {
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(A.wbase + A.off_emb) +
-                             static_cast<size_t>(tok) * S::D;
-    for (int i = t; i < S::D; i += kConsumers) sm.h[i] = __bfloat162float(e[i]);
-  }
-  consumer_sync<kConsumers>();
-
-  float gr[S::D / kConsumers];
-  for (int l = 0; l < A.n_layers; ++l) {
+  template <class S>
+  __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm, uint32_t flag,
+                                                 uint64_t t0, int l, int pos, int u, int nsplit,
+                                                 int trace_slot, uint32_t& att_phase, AttPre& pre) {
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int h = u / nsplit, j = u % nsplit;
+    const int g = h / S::GQA;
+    const int p0 = j * A.att_T, p1 = min(p0 + A.att_T, pos + 1);
+    const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
+    const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH;
+    const __nv_bfloat16* Vc = Kc + half;
     uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
-    load_gain<S>(A.ln1 + static_cast<size_t>(l) * S::D, gr);
-    if (cta < n_units) att_prefetch<S>(A, sm, pre, l, pos, cta, nsplit);  // K/V of this layer's unit
-    // ---- residual in: H_l (written by layer l-1's down phase) ----
-    if (l > 0) {
+    const int qi = lane & 15, hf = lane >> 4;  // position within the warp's 16, dim half
+
+    if (pre.unit != u) att_prefetch<S>(A, sm, pre, l, pos, u, nsplit);
+    pre.unit = -1;
+    uint32_t& vbytes = pre.vbytes;
+    const float rc = pre.rc, rs = pre.rs;
+    auto load_pass = [&](int base) { att_load_pass<S>(A, sm, pre, l, pos, h, j, base); };
+    // Wait (bounded, ignoring the abort marker) for this pass's V copy; used on
+    // every path so the CTA never leaves with the copy in flight.
+    auto wait_v = [&]() -> bool {
+      if (!vbytes) return true;
+      const uint64_t ts0 = globaltimer_ns();
+      bool landed = false;
+      uint32_t n = 0;
+      while (!(landed = mbar_test(&sm.att_bar, att_phase & 1u))) {
+        if ((++n & 63u) == 0 && globaltimer_ns() - ts0 > 10000000ull) {
+          raise_error(A.ctl, ST_TIMEOUT | SITE_VATT, flag);
+          break;
+        }
+      }
+      ++att_phase;
+      vbytes = 0;
+      return landed;
+    };
+    // q head h, k/v of kv head g: 3 x 32 word pairs.
+    bool ok = gather_pairs<1>(
+        A, flag, t0, SITE_QKV,
+        [&](int) {
+          const int seg = t >> 5, e = (t & 31) * 2;
+          const int row = seg == 0 ? h * 64 : (seg == 1 ? S::NH * 64 + g * 64 : (S::NH + S::NKV) * 64 + g * 64);
+          return lw + S::D + row + e;
+        },
+        [&](int) { return t < 96; },
+        [&](int, float a, float b) { sm.qkv[2 * t] = a; sm.qkv[2 * t + 1] = b; });
+    ok = consumer_sync_and<kConsumers>(ok);
+    if (!ok) {
+      wait_v();
+      return false;
+    }
+    trace_stamp(A, trace_slot);
+    // RoPE (rotate-half, reference :154-173; f32 tables as model.py:101-107).
+    if (t < 64) {
+      const int i = t & 31;
+      const float* src = sm.qkv + (t < 32 ? 0 : 64);
+      const float lo = src[i], hi = src[i + 32];
+      float* dst = t < 32 ? sm.rq : sm.rk;
+      const float sc = t < 32 ? 0.125f : 1.0f;  // 1/sqrt(64) folded into q (exact)
+      dst[i] = (lo * rc - hi * rs) * sc;
+      dst[i + 32] = (lo * rs + hi * rc) * sc;
+    }
+    consumer_sync<kConsumers>();
+    const float4* q4 = reinterpret_cast<const float4*>(sm.rq + hf * 32);
+    const float vn0 = sm.qkv[128 + 2 * lane], vn1 = sm.qkv[128 + 2 * lane + 1];
+
+    float m = -INFINITY, lsum = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int base = p0; base < p1; base += 16 * kConsumerWarps) {
+      if (base != p0) load_pass(base);
+      if (!__all_sync(0xffffffffu, wait_v())) ok = false;  // K/V rows of this pass landed
+      const int pk = base + warp * 16 + qi;
+      float sdot = 0.f;
+      if (pk == pos) {
+  #pragma unroll
+        for (int d = 0; d < 32; ++d) sdot = fmaf(sm.rq[hf * 32 + d], sm.rk[hf * 32 + d], sdot);
+      } else if (ok && pk < p1) {
+        // lane qi starts at chunk qi & 3 so a quarter-warp's 8 rows spread over banks
+        const uint4* kr = reinterpret_cast<const uint4*>(sm.katt[pk - base]) + hf * 4;
+  #pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = (c + qi) & 3;
+          const uint4 kw = kr[cc];
+          const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+          sdot = fmaf(qa.x, bf16_lo(kw.x), sdot);
+          sdot = fmaf(qa.y, bf16_hi(kw.x), sdot);
+          sdot = fmaf(qa.z, bf16_lo(kw.y), sdot);
+          sdot = fmaf(qa.w, bf16_hi(kw.y), sdot);
+          sdot = fmaf(qb.x, bf16_lo(kw.z), sdot);
+          sdot = fmaf(qb.y, bf16_hi(kw.z), sdot);
+          sdot = fmaf(qb.z, bf16_lo(kw.w), sdot);
+          sdot = fmaf(qb.w, bf16_hi(kw.w), sdot);
+        }
+      }
+      sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+      const bool valid = pk < p1;
+      float s = valid ? sdot : -INFINITY;
+      float mx = s;
+  #pragma unroll
+      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m, mx);
+      const float pe = valid ? __expf(s - mn) : 0.f;
+      float ps = pe;
+  #pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
+      if (hf == 0) sm.wo[warp][qi] = pe;   // stage probabilities for PV
+      __syncwarp();
+      float a0 = 0.f, a1 = 0.f;
+      if (ok) {
+  #pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int pv = base + warp * 16 + i;
+          const float pi = sm.wo[warp][i];
+          float v0 = 0.f, v1 = 0.f;
+          if (pv == pos) {
+            v0 = vn0; v1 = vn1;
+          } else if (pv < p1) {
+            const uint32_t vw = reinterpret_cast<const uint32_t*>(sm.vatt[pv - base])[lane];
+            v0 = bf16_lo(vw); v1 = bf16_hi(vw);
+          }
+          a0 = fmaf(pi, v0, a0);
+          a1 = fmaf(pi, v1, a1);
+        }
+      }
+      __syncwarp();
+      lsum = fmaf(lsum, alpha, ps);
+      o0 = fmaf(o0, alpha, a0);
+      o1 = fmaf(o1, alpha, a1);
+      m = mn;
+      // every warp is done reading the staged V before the next pass reuses it
+      ok = consumer_sync_and<kConsumers>(ok);
+      if (!ok) return false;
+    }
+    // per-warp state -> shared, then warp 0 merges in fixed order
+    sm.wo[warp][2 * lane] = o0;
+    sm.wo[warp][2 * lane + 1] = o1;
+    if (lane == 0) { sm.wm[warp] = m; sm.wl[warp] = lsum; }
+    consumer_sync<kConsumers>();
+    if (warp == 0) {
+      float M = -INFINITY;
+  #pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm.wm[w]);
+      float L = 0.f, b0 = 0.f, b1 = 0.f;
+  #pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float e = sm.wl[w] > 0.f ? __expf(sm.wm[w] - M) : 0.f;
+        L = fmaf(sm.wl[w], e, L);
+        b0 = fmaf(sm.wo[w][2 * lane], e, b0);
+        b1 = fmaf(sm.wo[w][2 * lane + 1], e, b1);
+      }
+      uint64_t* out = lw + A.w_att + static_cast<size_t>(h * nsplit + j) * kAttWords;
+      st_word(out + 2 * lane, b0, flag);
+      st_word(out + 2 * lane + 1, b1, flag);
+      if (lane == 0) {
+        st_word(out + 64, M, flag);
+        st_word(out + 65, L, flag);
+      }
+    }
+    // The first head of the group, owning the split that holds `pos`, appends
+    // this position's K (post-RoPE) and V to the cache in bf16.
+    if (warp == 1 && (h % S::GQA) == 0 && pos >= p0 && pos < p1) {
+      __nv_bfloat162 kk = __floats2bfloat162_rn(sm.rk[2 * lane], sm.rk[2 * lane + 1]);
+      __nv_bfloat162 vv = __floats2bfloat162_rn(vn0, vn1);
+      __nv_bfloat16* kd = const_cast<__nv_bfloat16*>(Kc) + static_cast<size_t>(pos) * S::DH;
+      __nv_bfloat16* vd = const_cast<__nv_bfloat16*>(Vc) + static_cast<size_t>(pos) * S::DH;
+      reinterpret_cast<__nv_bfloat162*>(kd)[lane] = kk;
+      reinterpret_cast<__nv_bfloat162*>(vd)[lane] = vv;
+    }
+    consumer_sync<kConsumers>();
+    return true;
+  }
+
+  template <class S>
+  __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs A) {
+    extern __shared__ __align__(128) uint8_t decode_smem_raw[];
+    static_assert(SmemChecks<S>::ok, "");
+    Smem<S>& sm = *reinterpret_cast<Smem<S>*>(decode_smem_raw);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int cta = blockIdx.x;
+    const int G = A.grid_part;
+    const uint64_t t0 = globaltimer_ns();
+
+    // A workspace holding an earlier device error stays halted until reset.
+    if (ld_relaxed_u32(&A.ctl->status) != 0u) return;
+    const int nsteps = A.n_steps > 1 ? A.n_steps : 1;
+    const int tok0 = __ldg(A.tok), pos0 = __ldg(A.pos);
+    if (tok0 < 0 || tok0 >= A.vocab || pos0 < 0 || pos0 + nsteps > A.ctx) {
+      if (cta == 0 && t == 0)
+        atomicCAS(&A.ctl->status, 0u, ST_BAD_INPUT | (tok0 < 0 || tok0 >= A.vocab ? 1u : 2u));
+      return;
+    }
+    // Step s writes its exchange words with flag0 + s; gen holds the last flag used.
+    const uint32_t flag0 = ld_relaxed_u32(&A.ctl->gen) + 1u;
+
+    if (t == 0) {
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&sm.full[s], 1);
+        mbar_init(&sm.empty[s], kConsumerWarps);
+      }
+      mbar_init(&sm.att_bar, 1);
+      sm.abort = 0;
+      fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+      if (lane == 0) producer_loop<S>(A, sm, cta, flag0, t0, nsteps);
+      return;
+    }
+
+    Ring ring{sm.stage, sm.full, sm.empty, 0u};
+    bool ok = true;
+    uint32_t att_phase = 0;  // completed uses of sm.att_bar
+    AttPre pre;
+    pre.unit = -1;
+    pre.vbytes = 0;
+    trace_stamp(A, 0);
+    const int tf = 1 + A.n_layers * kTracePerLayer;
+    float gr[S::D / kConsumers];
+    for (int step = 0; step < nsteps && ok; ++step) {
+    const uint32_t flag = flag0 + static_cast<uint32_t>(step);
+    const int pos = pos0 + step;
+    int tok = tok0;
+    if (step > 0) {  // the previous step's argmax, published by the CTA that finished it
+      if (t == 0) {
+        Waiter wt;
+        uint64_t w = ld_acquire_u64(&A.ctl->tok_word);
+        while (static_cast<uint32_t>(w >> 32) != flag - 1u) {
+          if (wt.expired(A, flag, t0, SITE_TOKEN)) {
+            ok = false;
+            break;
+          }
+          w = ld_acquire_u64(&A.ctl->tok_word);
+        }
+        sm.tok_in = static_cast<int>(static_cast<uint32_t>(w));
+      }
+      ok = consumer_sync_and<kConsumers>(ok);
+      if (!ok) break;
+      // K/V rows the previous step appended (other CTAs, generic stores) are read
+      // below by bulk copies (async proxy)
+      fence_proxy_async_all();
+      tok = sm.tok_in;
+    }
+    const int nsplit = (pos + A.att_T) / A.att_T;  // ceil((pos+1)/T)
+    const int n_units = S::NH * nsplit;
+
+    // Embedding row (reference :87-88).
+    {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(A.wbase + A.off_emb) +
+                               static_cast<size_t>(tok) * S::D;
+      for (int i = t; i < S::D; i += kConsumers) sm.h[i] = __bfloat162float(e[i]);
+    }
+    consumer_sync<kConsumers>();
+
+    for (int l = 0; l < A.n_layers; ++l) {
+      uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
+      load_gain<S>(A.ln1 + static_cast<size_t>(l) * S::D, gr);
+      if (cta < n_units) att_prefetch<S>(A, sm, pre, l, pos, cta, nsplit);  // K/V of this layer's unit
+      // ---- residual in: H_l (written by layer l-1's down phase) ----
+      if (l > 0) {
+        ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
+            A, flag, t0, SITE_H, [&](int i) { return lw + 2 * (t + i * kConsumers); },
+            [&](int i) { return t + i * kConsumers < S::D / 2; },
+            [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+      }
+      const int ts = 1 + l * kTracePerLayer;
+      trace_stamp(A, ts + 0);
+      rmsnorm_to_x<S>(sm, gr, A.eps);
+      trace_stamp(A, ts + 1);
+      // ---- QKV rows -> exchange words ----
+      {
+        const int a = split_begin(cta, S::QKV, G), b = split_begin(cta + 1, S::QKV, G);
+        ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
+                                                 [&](int u, float v, float) {
+                                                   if (lane == 0) st_word(lw + S::D + u, v, flag);
+                                                 });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+      }
+      trace_stamp(A, ts + 2);
+      trace_stamp(A, ts + 3);  // rewritten by a CTA that runs an attention unit
+      // ---- attention units ----
+      for (int u = cta; u < n_units && ok; u += G) {
+        ok = attention_unit<S>(A, sm, flag, t0, l, pos, u, nsplit, ts + 3, att_phase, pre);
+      }
+      if (!ok) break;
+      trace_stamp(A, ts + 4);
+      // ---- gather attention partials, merge splits -> x (bf16) ----
+      // Item 0 (threads < NH*nsplit): the (m, l) pair of unit t -> shared memory.
+      // Items 1..2*nsplit: this thread's 4 output dims of head t/16 per split.
+      {
+        float va[2 * kMaxSplits], vb[2 * kMaxSplits];
+        const int hh = t >> 4, d0 = (t & 15) * 4;
+        ok = gather_pairs<1 + 2 * kMaxSplits>(
+            A, flag, t0, SITE_ATT,
+            [&](int i) {
+              if (i == 0) return lw + A.w_att + static_cast<size_t>(t) * kAttWords + 64;
+              const int jj = (i - 1) >> 1, r = (i - 1) & 1;
+              return lw + A.w_att + static_cast<size_t>(hh * nsplit + jj) * kAttWords + d0 + 2 * r;
+            },
+            [&](int i) { return i == 0 ? t < n_units : (hh < S::NH && ((i - 1) >> 1) < nsplit); },
+            [&](int i, float a, float b) {
+              if (i == 0) { sm.ml[2 * t] = a; sm.ml[2 * t + 1] = b; }
+              else { va[i - 1] = a; vb[i - 1] = b; }
+            });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+        trace_stamp(A, ts + 5);
+        if (hh < S::NH) {
+          const float* ml = sm.ml + 2 * hh * nsplit;
+          float M = -INFINITY;
+          for (int jj = 0; jj < nsplit; ++jj) M = fmaxf(M, ml[2 * jj]);
+          float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  #pragma unroll
+          for (int jj = 0; jj < kMaxSplits; ++jj) {
+            if (jj < nsplit) {
+              const float e = __expf(ml[2 * jj] - M);
+              L = fmaf(ml[2 * jj + 1], e, L);
+              o[0] = fmaf(va[2 * jj], e, o[0]);
+              o[1] = fmaf(vb[2 * jj], e, o[1]);
+              o[2] = fmaf(va[2 * jj + 1], e, o[2]);
+              o[3] = fmaf(vb[2 * jj + 1], e, o[3]);
+            }
+          }
+          const float inv = 1.0f / fmaxf(L, 1e-10f);
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) sm.xf[xidx(hh * 64 + d0 + k)] = round_bf16(o[k] * inv);
+        }
+        consumer_sync<kConsumers>();
+      }
+      trace_stamp(A, ts + 6);
+      // ---- O rows: HM = H + attn @ Wo^T ----
+      {
+        const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
+        ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
+                                                 [&](int u, float v, float) {
+                                                   if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
+                                                 });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+      }
+      trace_stamp(A, ts + 7);
+      load_gain<S>(A.ln2 + static_cast<size_t>(l) * S::D, gr);
+      // ---- gather HM (the residual after attention) ----
       ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-          A, flag, t0, SITE_H, [&](int i) { return lw + 2 * (t + i * kConsumers); },
+          A, flag, t0, SITE_HM, [&](int i) { return lw + A.w_hm + 2 * (t + i * kConsumers); },
           [&](int i) { return t + i * kConsumers < S::D / 2; },
           [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
       ok = consumer_sync_and<kConsumers>(ok);
       if (!ok) break;
-    }
-    const int ts = 1 + l * kTracePerLayer;
-    trace_stamp(A, ts + 0);
-    rmsnorm_to_x<S>(sm, gr, A.eps);
-    trace_stamp(A, ts + 1);
-    // ---- QKV rows -> exchange words ----
-    {
-      const int a = split_begin(cta, S::QKV, G), b = split_begin(cta + 1, S::QKV, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                               [&](int u, float v, float) {
-                                                 if (lane == 0) st_word(lw + S::D + u, v, flag);
-                                               });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-    }
-    trace_stamp(A, ts + 2);
-    trace_stamp(A, ts + 3);  // rewritten by a CTA that runs an attention unit
-    // ---- attention units ----
-    for (int u = cta; u < n_units && ok; u += G) {
-      ok = attention_unit<S>(A, sm, flag, t0, l, pos, u, nsplit, ts + 3, att_phase, pre);
-    }
-    if (!ok) break;
-    trace_stamp(A, ts + 4);
-    // ---- gather attention partials, merge splits -> x (bf16) ----
-    // Item 0 (threads < NH*nsplit): the (m, l) pair of unit t -> shared memory.
-    // Items 1..2*nsplit: this thread's 4 output dims of head t/16 per split.
-    {
-      float va[2 * kMaxSplits], vb[2 * kMaxSplits];
-      const int hh = t >> 4, d0 = (t & 15) * 4;
-      ok = gather_pairs<1 + 2 * kMaxSplits>(
-          A, flag, t0, SITE_ATT,
-          [&](int i) {
-            if (i == 0) return lw + A.w_att + static_cast<size_t>(t) * kAttWords + 64;
-            const int jj = (i - 1) >> 1, r = (i - 1) & 1;
-            return lw + A.w_att + static_cast<size_t>(hh * nsplit + jj) * kAttWords + d0 + 2 * r;
-          },
-          [&](int i) { return i == 0 ? t < n_units : (hh < S::NH && ((i - 1) >> 1) < nsplit); },
-          [&](int i, float a, float b) {
-            if (i == 0) { sm.ml[2 * t] = a; sm.ml[2 * t + 1] = b; }
-            else { va[i - 1] = a; vb[i - 1] = b; }
-          });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-      trace_stamp(A, ts + 5);
-      if (hh < S::NH) {
-        const float* ml = sm.ml + 2 * hh * nsplit;
-        float M = -INFINITY;
-        for (int jj = 0; jj < nsplit; ++jj) M = fmaxf(M, ml[2 * jj]);
-        float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int jj = 0; jj < kMaxSplits; ++jj) {
-          if (jj < nsplit) {
-            const float e = __expf(ml[2 * jj] - M);
-            L = fmaf(ml[2 * jj + 1], e, L);
-            o[0] = fmaf(va[2 * jj], e, o[0]);
-            o[1] = fmaf(vb[2 * jj], e, o[1]);
-            o[2] = fmaf(va[2 * jj + 1], e, o[2]);
-            o[3] = fmaf(vb[2 * jj + 1], e, o[3]);
-          }
-        }
-        const float inv = 1.0f / fmaxf(L, 1e-10f);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sm.xf[xidx(hh * 64 + d0 + k)] = round_bf16(o[k] * inv);
+      trace_stamp(A, ts + 8);
+      rmsnorm_to_x<S>(sm, gr, A.eps);
+      trace_stamp(A, ts + 9);
+      // ---- gate/up pairs -> act = silu(g) * u ----
+      {
+        const int a = split_begin(cta, S::DFF, G), b = split_begin(cta + 1, S::DFF, G);
+        ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xf,
+                                                [&](int u, float gt, float up) {
+                                                  if (lane == 0) {
+                                                    const float act = gt * (1.0f / (1.0f + __expf(-gt))) * up;
+                                                    st_word(lw + A.w_act + u, act, flag);
+                                                  }
+                                                });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
       }
-      consumer_sync<kConsumers>();
+      trace_stamp(A, ts + 10);
+      // ---- gather act -> x (bf16), down rows: H_{l+1} = HM + act @ Wd^T ----
+      {
+        ok = gather_pairs<(S::DFF / 2 + kConsumers - 1) / kConsumers>(
+            A, flag, t0, SITE_ACT, [&](int i) { return lw + A.w_act + 2 * (t + i * kConsumers); },
+            [&](int i) { return t + i * kConsumers < S::DFF / 2; },
+            [&](int i, float a, float b) {
+              const int k = t + i * kConsumers;
+              sm.xf[xidx(2 * k)] = round_bf16(a);
+              sm.xf[xidx(2 * k + 1)] = round_bf16(b);
+            });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+        trace_stamp(A, ts + 11);
+        uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
+        const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
+        ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xf,
+                                                 [&](int u, float v, float) {
+                                                   if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
+                                                 });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+      }
+      trace_stamp(A, ts + 12);
     }
-    trace_stamp(A, ts + 6);
-    // ---- O rows: HM = H + attn @ Wo^T ----
-    {
-      const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                               [&](int u, float v, float) {
-                                                 if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
-                                               });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-    }
-    trace_stamp(A, ts + 7);
-    load_gain<S>(A.ln2 + static_cast<size_t>(l) * S::D, gr);
-    // ---- gather HM (the residual after attention) ----
-    ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-        A, flag, t0, SITE_HM, [&](int i) { return lw + A.w_hm + 2 * (t + i * kConsumers); },
-        [&](int i) { return t + i * kConsumers < S::D / 2; },
-        [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
-    ok = consumer_sync_and<kConsumers>(ok);
-    if (!ok) break;
-    trace_stamp(A, ts + 8);
-    rmsnorm_to_x<S>(sm, gr, A.eps);
-    trace_stamp(A, ts + 9);
-    // ---- gate/up pairs -> act = silu(g) * u ----
-    {
-      const int a = split_begin(cta, S::DFF, G), b = split_begin(cta + 1, S::DFF, G);
-      ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xf,
-                                              [&](int u, float gt, float up) {
-                                                if (lane == 0) {
-                                                  const float act = gt * (1.0f / (1.0f + __expf(-gt))) * up;
-                                                  st_word(lw + A.w_act + u, act, flag);
-                                                }
-                                              });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-    }
-    trace_stamp(A, ts + 10);
-    // ---- gather act -> x (bf16), down rows: H_{l+1} = HM + act @ Wd^T ----
-    {
-      ok = gather_pairs<(S::DFF / 2 + kConsumers - 1) / kConsumers>(
-          A, flag, t0, SITE_ACT, [&](int i) { return lw + A.w_act + 2 * (t + i * kConsumers); },
-          [&](int i) { return t + i * kConsumers < S::DFF / 2; },
-          [&](int i, float a, float b) {
-            const int k = t + i * kConsumers;
-            sm.xf[xidx(2 * k)] = round_bf16(a);
-            sm.xf[xidx(2 * k + 1)] = round_bf16(b);
-          });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-      trace_stamp(A, ts + 11);
-      uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
-      const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-      ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xf,
-                                               [&](int u, float v, float) {
-                                                 if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
-                                               });
-      ok = consumer_sync_and<kConsumers>(ok);
-      if (!ok) break;
-    }
-    trace_stamp(A, ts + 12);
-  }
-  const int tf = 1 + A.n_layers * kTracePerLayer;
 
-  if (ok) {
-    // ---- final norm + tied logits + argmax (reference :314-357) ----
-    uint64_t* fw = A.words + static_cast<size_t>(A.n_layers) * A.layer_words;
-    ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-        A, flag, t0, SITE_FINAL, [&](int i) { return fw + 2 * (t + i * kConsumers); },
-        [&](int i) { return t + i * kConsumers < S::D / 2; },
-        [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
-    ok = consumer_sync_and<kConsumers>(ok);
-  }
-  trace_stamp(A, tf + 0);
-  if (ok) {
-    load_gain<S>(A.lnf, gr);
-    rmsnorm_to_x<S>(sm, gr, A.eps);
-    float best_v = -INFINITY;
-    int best_i = 0x7fffffff;
-    const int a = split_begin(cta, A.vocab, G), b = split_begin(cta + 1, A.vocab, G);
-    ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                             [&](int u, float v, float) {
-                                               if (lane == 0 && A.logits) A.logits[u] = v;
-                                               if (v > best_v) { best_v = v; best_i = u; }
-                                             });
-    ok = consumer_sync_and<kConsumers>(ok);
-    trace_stamp(A, tf + 1);
     if (ok) {
-      if (lane == 0) { sm.am_v[warp] = best_v; sm.am_i[warp] = best_i; }
-      consumer_sync<kConsumers>();
-      if (t == 0) {
-        float bv = sm.am_v[0];
-        int bi = sm.am_i[0];
-        for (int w = 1; w < kConsumerWarps; ++w) {
-          if (sm.am_v[w] > bv || (sm.am_v[w] == bv && sm.am_i[w] < bi)) { bv = sm.am_v[w]; bi = sm.am_i[w]; }
-        }
-        A.am_val[cta] = bv;
-        A.am_idx[cta] = bi;
-        __threadfence();
-        const uint32_t ticket = atomicAdd(&A.ctl->arrive, 1u);
-        if (ticket == static_cast<uint32_t>(gridDim.x) - 1u) {
-          __threadfence();
-          float gv = -INFINITY;
-          int gi = 0x7fffffff;
-          for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
-            const float v = *reinterpret_cast<volatile float*>(&A.am_val[c]);
-            const int i = *reinterpret_cast<volatile int*>(&A.am_idx[c]);
-            if (v > gv || (v == gv && i < gi)) { gv = v; gi = i; }
+      // ---- final norm + tied logits + argmax (reference :314-357) ----
+      uint64_t* fw = A.words + static_cast<size_t>(A.n_layers) * A.layer_words;
+      ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
+          A, flag, t0, SITE_FINAL, [&](int i) { return fw + 2 * (t + i * kConsumers); },
+          [&](int i) { return t + i * kConsumers < S::D / 2; },
+          [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
+      ok = consumer_sync_and<kConsumers>(ok);
+    }
+    trace_stamp(A, tf + 0);
+    if (ok) {
+      load_gain<S>(A.lnf, gr);
+      rmsnorm_to_x<S>(sm, gr, A.eps);
+      float best_v = -INFINITY;
+      int best_i = 0x7fffffff;
+      const int a = split_begin(cta, A.vocab, G), b = split_begin(cta + 1, A.vocab, G);
+      ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
+                                               [&](int u, float v, float) {
+                                                 if (lane == 0 && A.logits) A.logits[u] = v;
+                                                 if (v > best_v) { best_v = v; best_i = u; }
+                                               });
+      ok = consumer_sync_and<kConsumers>(ok);
+      trace_stamp(A, tf + 1);
+      if (ok) {
+        if (lane == 0) { sm.am_v[warp] = best_v; sm.am_i[warp] = best_i; }
+        consumer_sync<kConsumers>();
+        if (t == 0) {
+          float bv = sm.am_v[0];
+          int bi = sm.am_i[0];
+          for (int w = 1; w < kConsumerWarps; ++w) {
+            if (sm.am_v[w] > bv || (sm.am_v[w] == bv && sm.am_i[w] < bi)) { bv = sm.am_v[w]; bi = sm.am_i[w]; }
           }
-          *A.next_tok = gi == 0x7fffffff ? 0 : gi;
-          A.ctl->arrive = 0u;
+          A.am_val[cta] = bv;
+          A.am_idx[cta] = bi;
           __threadfence();
-          st_relaxed_u32(&A.ctl->gen, flag);
+          const uint32_t ticket = atomicAdd(&A.ctl->arrive, 1u);
+          if (ticket == static_cast<uint32_t>(gridDim.x) - 1u) {
+            __threadfence();
+            float gv = -INFINITY;
+            int gi = 0x7fffffff;
+            for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+              const float v = *reinterpret_cast<volatile float*>(&A.am_val[c]);
+              const int i = *reinterpret_cast<volatile int*>(&A.am_idx[c]);
+              if (v > gv || (v == gv && i < gi)) { gv = v; gi = i; }
+            }
+            const int tk = gi == 0x7fffffff ? 0 : gi;
+            *A.next_tok = tk;
+            if (A.tok_out != nullptr) A.tok_out[step] = tk;
+            A.ctl->arrive = 0u;
+            __threadfence();
+            st_relaxed_u32(&A.ctl->gen, flag);
+            if (step + 1 < nsteps)  // the next step's input
+              st_release_u64(&A.ctl->tok_word, (static_cast<uint64_t>(flag) << 32) | static_cast<uint32_t>(tk));
+          }
         }
       }
     }
-  }
+  }  // step
   trace_stamp(A, tf + 2);
   if (!ok) {
     // a K/V staging copy requested for an attention unit that never ran

@@ -110,6 +110,30 @@ class DecodeEngine:
                                       _ptr(logits), _ptr(next_tok), _stream_ptr(stream))
         _lib.check(st, "b2d_decode_step")
 
+    def decode_steps(self, tok: torch.Tensor, pos: torch.Tensor, kv: torch.Tensor, n_steps: int,
+                     tokens: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                     stream=None) -> torch.Tensor:
+        """``n_steps`` greedy decode steps of one sequence in one launch
+        (``b2d_decode_steps``): step s feeds step s-1's argmax back at position
+        ``pos + s``.  Returns the device int32 [n_steps] tokens (async)."""
+        if n_steps < 1:
+            raise ValueError("n_steps must be >= 1")
+        for t, name in ((tok, "tok"), (pos, "pos")):
+            if t.dtype != torch.int32 or t.device != self.device or t.numel() < 1:
+                raise ValueError(f"{name} must be an int32 tensor on {self.device}")
+        if tokens is None:
+            tokens = torch.zeros(n_steps, dtype=torch.int32, device=self.device)
+        if tokens.dtype != torch.int32 or tokens.device != self.device or tokens.numel() < n_steps:
+            raise ValueError(f"tokens must be an int32 tensor on {self.device} with >= {n_steps} items")
+        if kv.dtype != torch.bfloat16 or kv.device != self.device or kv.numel() < self.kv_elems:
+            raise ValueError("kv must be a bf16 cache on the model device (see new_kv)")
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() < self.cfg.vocab_size):
+            raise ValueError("logits must be float32 [vocab]")
+        st = self.lib.b2d_decode_steps(self.model, self.ws, _ptr(tok), _ptr(pos), int(n_steps), _ptr(kv),
+                                       _ptr(tokens), _ptr(logits), _stream_ptr(stream))
+        _lib.check(st, "b2d_decode_steps")
+        return tokens[:n_steps]
+
     def new_kv_pool(self, num_blocks: int) -> torch.Tensor:
         """Zeroed paged KV pool: bf16 [n_layers, num_blocks, 2 (K|V), kv_heads,
         16, d_head]; block i of a sequence holds its positions 16i..16i+15."""
