@@ -5,7 +5,8 @@
 // it takes an even share x of the 16-position pages 0 .. pos[b]/16 of row b
 // (split by the row's actual length, so a launch captured once serves every
 // position) and runs its own online softmax over them for the GQA query heads
-// of g.  kPaWarps units per CTA, no CTA-wide synchronisation.
+// of g.  The splits (1, 2 or 4) units of a (row, kv head) are consecutive
+// warps of one CTA of W = max(2, splits) warps.
 //
 //   * page loads: each lane copies 4 + 4 16-byte pieces of the page's K and V
 //     rows (2 KB each, contiguous in the pool) with `cp.async` into a
@@ -23,9 +24,10 @@
 //     the V rows as B (`ldmatrix.trans`), 8 n-tiles of dimensions.
 //
 // A unit that covers its whole row writes the output directly; when a row is
-// split, each unit writes its (m, l, o) partial and the last unit to take the
-// (row, kv head) ticket merges them in split order.  Every reduction has a
-// fixed order: results are bitwise reproducible.  The unit holding position
+// split, each unit leaves its (m, l, o) partial in its own shared memory and,
+// after a named barrier of the row's warps, the first of them merges the
+// partials in split order.  Every reduction has a fixed order: results are
+// bitwise reproducible.  The unit holding position
 // pos[b] uses the new K (post-RoPE) / V rounded to bf16 (the cached values)
 // and, in append mode, writes them to the cache.  Math: model.py:
 // 100-131 (rotate-half RoPE, causal softmax over 0..p, GQA sharing).
@@ -37,13 +39,13 @@
 
 namespace b2d {
 
-constexpr int kPaWarps = 2;     // units (warps) per CTA
 constexpr int kPaStages = 4;    // pages in each warp's ring (consumed two at a time)
 constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
-constexpr int kPaMaxSplits = 8; // units per (row, kv head); <= the partial buffer's chunks
+constexpr int kPaMaxSplits = 4; // units per (row, kv head)
 constexpr int kPaWarpSmem = kPaStages * kPaStageElems * 2 + 256;  // ring + the new K / V row (bytes)
-constexpr int kPaSmem = kPaWarps * kPaWarpSmem;
+// warps per CTA for a split count (a row's units share a CTA)
+constexpr __host__ __device__ int pa_warps(int splits) { return splits > 2 ? splits : 2; }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -92,16 +94,17 @@ __device__ __forceinline__ const __nv_bfloat16* page_rows(const PagedAttnArgs& a
                       (kPageTokens * 64);
 }
 
-// grid ceil(rows * n_kv * splits / kPaWarps), kPaWarps * 32 threads, kPaSmem
-// bytes of dynamic shared memory; a.cpc = splits.  Unit u = blockIdx.x *
-// kPaWarps + warp is (b, g, x) with u = (b * n_kv + g) * splits + x.
-__global__ void __launch_bounds__(32 * kPaWarps) paged_attn_mma_kernel(const __grid_constant__ PagedAttnArgs a,
-                                                                       int n_rows) {
+// grid ceil(rows * n_kv * splits / W), W * 32 threads, W * kPaWarpSmem bytes
+// of dynamic shared memory; a.cpc = splits (1, 2 or 4), W = pa_warps(splits).
+// Unit u = blockIdx.x * W + warp is (b, g, x) with u = (b * n_kv + g) *
+// splits + x.
+template <int W>
+__global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_constant__ PagedAttnArgs a, int n_rows) {
   extern __shared__ __align__(16) uint8_t pa_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int splits = a.cpc;
-  const int u = blockIdx.x * kPaWarps + warp;
+  const int u = blockIdx.x * W + warp;
   if (u >= n_rows * a.n_kv * splits) return;
   const int x = u % splits, g = (u / splits) % a.n_kv, b = u / (splits * a.n_kv);
   // diagnostics: 0 entry, 1 loads issued, 2 past the programmatic wait, 3 query ready,
@@ -137,11 +140,9 @@ __global__ void __launch_bounds__(32 * kPaWarps) paged_attn_mma_kernel(const __g
   }
   const int npg = p / kPageTokens + 1;
   const int ppu = (npg + splits - 1) / splits;  // pages per unit
-  const int pg_lo = x * ppu;
-  if (pg_lo >= npg) return;  // no pages for this unit: no ticket either
+  const int pg_lo = min(x * ppu, npg);          // a unit past the row's pages has none (it still merges)
   const int pg_hi = min(pg_lo + ppu, npg);
-  const int nunits = (npg + ppu - 1) / ppu;  // units sharing this (row, kv head)
-  const bool owner = pg_hi == npg;
+  const bool owner = pg_lo < npg && pg_hi == npg;  // this unit's last page holds position p
   bool bad = tb != nullptr && npg > a.bps;
   if (tb != nullptr && !bad) {  // every page of the unit must exist
     if (lane >= pg_lo && lane < pg_hi) bad = tbl < 0 || tbl >= a.num_blocks;
@@ -350,7 +351,7 @@ __global__ void __launch_bounds__(32 * kPaWarps) paged_attn_mma_kernel(const __g
   l += __shfl_xor_sync(0xffffffffu, l, 2);
 
   // lane (gid < GQA, tig) holds head g*GQA + gid, dims 8j + 2tig, 8j + 2tig + 1 (j < 8)
-  if (nunits == 1) {
+  if (splits == 1) {
     if (head) {
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       __nv_bfloat162* out = reinterpret_cast<__nv_bfloat162*>(a.out + static_cast<size_t>(b) * a.ldo +
@@ -363,68 +364,47 @@ __global__ void __launch_bounds__(32 * kPaWarps) paged_attn_mma_kernel(const __g
     stamp(7);
     return;
   }
+  // Partial (m, l, o) of this unit in its own (drained) ring: [head][64] o, then m[4], l[4].
+  float* mine = reinterpret_cast<float*>(ring);
   if (head) {
-    float* part = a.part + ((static_cast<size_t>(b) * a.n_heads + g * GQA + gid) * a.max_chunks + x) * kAttPart;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      reinterpret_cast<float2*>(part + 4)[4 * j + tig] = make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
+      *reinterpret_cast<float2*>(mine + gid * 64 + 8 * j + 2 * tig) = make_float2(o[j][0] + o[j][2], o[j][1] + o[j][3]);
     if (tig == 0) {
-      part[0] = m;
-      part[1] = l;
+      mine[256 + gid] = m;
+      mine[260 + gid] = l;
     }
   }
   stamp(6);
-  __syncwarp();  // every lane's partial stores precede lane 0's release below
-  uint32_t last = 0;
-  if (lane == 0) {
-    uint32_t prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                 : "=r"(prev) : "l"(a.tickets + b * a.n_kv + g) : "memory");
-    last = prev == static_cast<uint32_t>(nunits - 1);
-  }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  __syncwarp();  // the other lanes' reads below follow lane 0's acquire
-  if (!last) {
-    stamp(7);
-    return;
-  }
-  if (lane == 0) a.tickets[b * a.n_kv + g] = 0u;
-  // Merge the units' partials in split order.  Lane (hh = lane / 8, c = lane % 8)
-  // takes head g*GQA + hh, dims 8c .. 8c+7; every load is issued before the math.
-  const int hh = lane >> 3, c8 = lane & 7;
-  if (hh < GQA) {
-    const float* ph = a.part + (static_cast<size_t>(b) * a.n_heads + g * GQA + hh) * a.max_chunks * kAttPart;
-    float2 ml[kPaMaxSplits];
-    float4 oa[kPaMaxSplits], ob[kPaMaxSplits];
-#pragma unroll
-    for (int j = 0; j < kPaMaxSplits; ++j)
-      if (j < nunits) {
-        ml[j] = __ldcg(reinterpret_cast<const float2*>(ph + j * kAttPart));
-        oa[j] = __ldcg(reinterpret_cast<const float4*>(ph + j * kAttPart + 4 + 8 * c8));
-        ob[j] = __ldcg(reinterpret_cast<const float4*>(ph + j * kAttPart + 8 + 8 * c8));
+  // the row's warps meet: with splits > 1 they are the whole CTA (splits == W); barrier 1
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * W) : "memory");
+  if (x == 0) {  // merge in split order: lane (hh = lane / 8, c = lane % 8) takes head hh, dims 8c .. 8c+7
+    const int hh = lane >> 3, c8 = lane & 7;
+    if (hh < GQA) {
+      float M = -INFINITY;
+      for (int j = 0; j < splits; ++j)
+        M = fmaxf(M, reinterpret_cast<const float*>(pa_smem + (warp + j) * kPaWarpSmem)[256 + hh]);
+      float L = 0.f, r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < splits; ++j) {
+        const float* pj = reinterpret_cast<const float*>(pa_smem + (warp + j) * kPaWarpSmem);
+        const float mj = pj[256 + hh];
+        const float wgt = mj == -INFINITY ? 0.f : __expf(mj - M);
+        L = fmaf(wgt, pj[260 + hh], L);
+        const float4 oa = *reinterpret_cast<const float4*>(pj + hh * 64 + 8 * c8);
+        const float4 ob = *reinterpret_cast<const float4*>(pj + hh * 64 + 8 * c8 + 4);
+        r[0] = fmaf(wgt, oa.x, r[0]); r[1] = fmaf(wgt, oa.y, r[1]);
+        r[2] = fmaf(wgt, oa.z, r[2]); r[3] = fmaf(wgt, oa.w, r[3]);
+        r[4] = fmaf(wgt, ob.x, r[4]); r[5] = fmaf(wgt, ob.y, r[5]);
+        r[6] = fmaf(wgt, ob.z, r[6]); r[7] = fmaf(wgt, ob.w, r[7]);
       }
-    float M = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kPaMaxSplits; ++j)
-      if (j < nunits) M = fmaxf(M, ml[j].x);
-    float L = 0.f, r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int j = 0; j < kPaMaxSplits; ++j)
-      if (j < nunits) {
-        const float wgt = ml[j].x == -INFINITY ? 0.f : __expf(ml[j].x - M);
-        L = fmaf(wgt, ml[j].y, L);
-        r[0] = fmaf(wgt, oa[j].x, r[0]); r[1] = fmaf(wgt, oa[j].y, r[1]);
-        r[2] = fmaf(wgt, oa[j].z, r[2]); r[3] = fmaf(wgt, oa[j].w, r[3]);
-        r[4] = fmaf(wgt, ob[j].x, r[4]); r[5] = fmaf(wgt, ob[j].y, r[5]);
-        r[6] = fmaf(wgt, ob[j].z, r[6]); r[7] = fmaf(wgt, ob[j].w, r[7]);
-      }
-    const float inv = L > 0.f ? 1.0f / L : 0.f;
-    uint4 pk;
-    pk.x = bf2_rn(r[0] * inv, r[1] * inv);
-    pk.y = bf2_rn(r[2] * inv, r[3] * inv);
-    pk.z = bf2_rn(r[4] * inv, r[5] * inv);
-    pk.w = bf2_rn(r[6] * inv, r[7] * inv);
-    *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + hh) * 64 + 8 * c8) = pk;
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      uint4 pk;
+      pk.x = bf2_rn(r[0] * inv, r[1] * inv);
+      pk.y = bf2_rn(r[2] * inv, r[3] * inv);
+      pk.z = bf2_rn(r[4] * inv, r[5] * inv);
+      pk.w = bf2_rn(r[6] * inv, r[7] * inv);
+      *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(b) * a.ldo + (g * GQA + hh) * 64 + 8 * c8) = pk;
+    }
   }
   stamp(7);
 }

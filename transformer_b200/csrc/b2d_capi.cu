@@ -122,8 +122,7 @@ struct b2d_ws {
   int32_t* prefill_pos;            // [kPrefillRows] positions of a prefill chunk
   int last_launches;               // kernels launched by the last batched step / prefill chunk
   int rows;                        // activation rows allocated (max_batch rounded up to the widest tile)
-  float *H, *Hm, *qkv, *logits, *att_part;
-  uint32_t* att_tickets;
+  float *H, *Hm, *qkv, *logits;
   float* ss;               // folded RMSNorm: per-tile sums of squares [d_model / 128][rows]
   bool no_pdl;             // diagnostics: launch without programmatic dependencies
   int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
@@ -133,7 +132,6 @@ struct b2d_ws {
   uint64_t* att_trace;     // diagnostics: attention stamps [layer][kAttTraceUnits][8], or null
   uint64_t* sample_trace;  // diagnostics: sampler phase stamps [batch][8], or null
   int stage_stride;
-  int att_chunks;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
   // b2d_decode_step_paged: CUDA graphs of the step's kernel sequence, one per
@@ -182,20 +180,27 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
-// launch_k with `smem` bytes of dynamic shared memory (the kernel's limit is
-// raised once per device).
-template <class... KArgs, class... Args>
-cudaError_t launch_k_smem(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, bool pdl,
-                          Args&&... args) {
+// The attention kernels' dynamic shared-memory limits, raised once per device.
+cudaError_t attn_smem_attrs() {
   static bool raised[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!raised[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    raised[dev] = true;
-  }
+  if (raised[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(b2d::paged_attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * b2d::kPaWarpSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(b2d::paged_attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             4 * b2d::kPaWarpSmem);
+  if (e == cudaSuccess) raised[dev] = true;
+  return e;
+}
+
+// launch_k with `smem` bytes of dynamic shared memory (the caller has raised
+// the kernel's limit where it exceeds the default).
+template <class... KArgs, class... Args>
+cudaError_t launch_k_smem(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, bool pdl,
+                          Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -327,7 +332,6 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     const size_t D = c.d_model, F = c.d_ff, Q = qkv, V = c.vocab_size;
     ws->rows = (ws->brows + 255) / 256 * 256;  // any tile width may be chosen (see gemm_plan)
     e = cudaMalloc(&ws->prefill_pos, sizeof(int32_t) * kPrefillRows);
-    ws->att_chunks = (c.context_len + b2d::kAttChunk - 1) / b2d::kAttChunk;
     if (e == cudaSuccess) e = cudaMalloc(&ws->H, sizeof(float) * D * ws->brows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->Hm, sizeof(float) * D * ws->brows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->qkv, sizeof(float) * Q * ws->brows);
@@ -338,10 +342,6 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     if (e == cudaSuccess) e = cudaMemset(ws->X, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->A, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->ACT, 0, 2 * F * ws->rows);
-    if (e == cudaSuccess)
-      e = cudaMalloc(&ws->att_part, sizeof(float) * size_t(ws->brows) * c.n_heads * ws->att_chunks * b2d::kAttPart);
-    if (e == cudaSuccess) e = cudaMalloc(&ws->att_tickets, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
-    if (e == cudaSuccess) e = cudaMemset(ws->att_tickets, 0, sizeof(uint32_t) * size_t(ws->brows) * c.n_kv_heads);
     if (e == cudaSuccess) e = cudaMalloc(&ws->ss, sizeof(float) * (D / b2d::kGemmBM) * ws->rows);
     for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
       const uint32_t box = 16u << i;
@@ -375,8 +375,6 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   cudaFree(ws->X);
   cudaFree(ws->A);
   cudaFree(ws->ACT);
-  cudaFree(ws->att_part);
-  cudaFree(ws->att_tickets);
   cudaFree(ws->ss);
   cudaFree(ws->prefill_pos);
   cudaFree(ws->words);
@@ -580,9 +578,7 @@ b2d_status ensure_weight_maps(b2d_model* m) {
   const b2d_config& c = m->cfg;
   const uint64_t D = c.d_model, F = c.d_ff, Q = uint64_t(c.n_heads + 2 * c.n_kv_heads) * 64;
   if (Q % b2d::kGemmBM || D % b2d::kGemmBM || (2 * F) % b2d::kGemmBM || c.vocab_size % b2d::kGemmBM ||
-      D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4 ||
-      c.context_len > 32 * b2d::kAttChunk ||  // the attention merge holds one chunk per lane
-      D > 2048)                               // the row RMSNorm holds a row in registers
+      D % b2d::kGemmBK || F % b2d::kGemmBK || c.n_heads / c.n_kv_heads > 4)  // 4 query heads per attention unit
     return B2D_ERR_UNSUPPORTED;
   CUtensorMap* maps = new (std::nothrow) CUtensorMap[4 * c.n_layers + 1];
   if (!maps) return B2D_ERR_NO_MEMORY;
@@ -672,13 +668,14 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
-  pa.part = ws->att_part; pa.tickets = ws->att_tickets; pa.max_chunks = ws->att_chunks;
   {  // units (warps) per (row, kv head): split rows only while the pairs alone leave SMs idle
     const int pairs = batch * c.n_kv_heads, target = 10 * m->grid;
-    const int cap = std::min(b2d::kPaMaxSplits, std::min(ws->att_chunks, (c.context_len + 15) / 16));
-    pa.cpc = std::max(1, std::min(cap, target / pairs));
-    if (ws->force_att_cpc) pa.cpc = std::min(cap, ws->force_att_cpc);
+    int sp = ws->force_att_cpc ? ws->force_att_cpc : std::max(1, target / pairs);
+    sp = std::min(sp, std::min(b2d::kPaMaxSplits, (c.context_len + 15) / 16));
+    pa.cpc = sp >= 4 ? 4 : sp >= 2 ? 2 : 1;  // a row's units share one CTA of pa_warps(splits) warps
   }
+  const int att_w = b2d::pa_warps(pa.cpc);
+  B2D_CUDA(attn_smem_attrs(), "attention attributes");
   const int att_units = batch * c.n_kv_heads * pa.cpc;
   // RMSNorm of the residual stream, folded: each residual projection writes
   // X = bf16(h * g_next) and per-tile sums of squares; the next projection
@@ -693,9 +690,14 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     pa.trace_units = kAttTraceUnits;
     if (prefill)  // every row's K/V in the cache before any row attends
       B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
-    B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel, dim3((att_units + b2d::kPaWarps - 1) / b2d::kPaWarps),
-                           dim3(32 * b2d::kPaWarps), b2d::kPaSmem, st, pdl, pa, batch),
-             "attention");
+    if (att_w == 2)
+      B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<2>, dim3((att_units + 1) / 2), dim3(64),
+                             2 * b2d::kPaWarpSmem, st, pdl, pa, batch),
+               "attention");
+    else
+      B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<4>, dim3((att_units + 3) / 4), dim3(128),
+                             4 * b2d::kPaWarpSmem, st, pdl, pa, batch),
+               "attention");
     launches_other += prefill ? 2 : 1;
     g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;
     g.ss_in = nullptr; g.xg_out = ws->X; g.xg_gain = ln2 + size_t(l) * D; g.ss_out = ws->ss;

@@ -73,10 +73,7 @@ struct PagedAttnArgs {
   __nv_bfloat16* out;          // [B][ldo] bf16: head h at columns h*64..
   int ldo;
   uint32_t* status;            // set when a block-table entry is out of range
-  float* part;                 // [B][n_heads][max_chunks][kAttPart] per-CTA partials
-  uint32_t* tickets;           // [B][n_kv]; zero between launches (the combining CTA resets it)
-  int max_chunks;              // partial slots per (row, head): >= cpc
-  int cpc;                     // CTAs per (row, kv head), each an even share of the row's pages
+  int cpc;                     // units per (row, kv head) (1, 2 or 4), each an even share of the row's pages
   // Cache addressing: table != nullptr -> the paged pool above; table ==
   // nullptr -> one sequence's contiguous cache in the reference layout
   // [layer][K|V][kv_head][ctx][64] (every row of the launch is a position of
@@ -127,8 +124,6 @@ __global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ P
   vd[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
 }
 
-constexpr int kAttChunk = 64;  // cached positions per attention partial slot (sizes the partial buffer)
-constexpr int kAttPart = 68;   // m, l, 2 pad, o[64]
 
 // next[b] = first index of the maximum of logits[b][0..V)  (one CTA per row)
 __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int ldl, int32_t* __restrict__ next) {
