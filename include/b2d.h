@@ -257,8 +257,8 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * (1..12, default 4); knob 3 = batched step with (1, default) or without (0)
  * programmatic dependent launch; knob 4 = batched step K split forced to
  * 1..8 (0 = automatic); knob 5 = batched attention units (warps) per
- * (sequence, kv head) forced to 1..32, capped at 8 and at the context's
- * 64-position chunks (0 = automatic); knob 6 = device address of a uint64
+ * (sequence, kv head) forced to 1..32, used as 1, 2 or 4 (rounded down,
+ * capped at 4; 0 = automatic); knob 6 = device address of a uint64
  * buffer [257 launches][256 CTAs][8] that the batched step's projections fill
  * with global-timer stamps (0 = off); knob 7 = device address of a uint64
  * buffer [grid][3][stride] for the B=1 step's weight stages (copy issued /
