@@ -85,9 +85,9 @@ def test_paged_tiny_ragged_all_positions(engine_tiny_batched, params_tiny):
 
 @pytest.mark.parametrize("cpc,ks", [(1, 1), (3, 2), (32, 8)])
 def test_paged_tiny_work_splits(engine_tiny_batched, params_tiny, cpc, ks):
-    """Forced attention chunks per CTA (one chunk per CTA with multi-CTA
-    merges, uneven groups, the whole sequence in one CTA) and K splits of the
-    projections give the same parity."""
+    """Forced attention units per (sequence, kv head) (1; 3 used as 2; 32
+    capped at 4: uneven page shares and units without pages included) and K
+    splits of the projections give the same parity."""
     from transformer_b200.config import CONFIG_TINY
     from transformer_b200.synth import params_f32
     eng = engine_tiny_batched

@@ -126,7 +126,7 @@ struct b2d_ws {
   float* ss;               // folded RMSNorm: per-tile sums of squares [d_model / 128][rows]
   bool no_pdl;             // diagnostics: launch without programmatic dependencies
   int force_ksplit;        // diagnostics: fixed K split (0 = automatic)
-  int force_att_cpc;       // diagnostics: fixed attention chunks per CTA (0 = automatic)
+  int force_att_cpc;       // diagnostics: fixed attention units per (sequence, kv head) (0 = automatic)
   uint64_t* gemm_trace;    // diagnostics: [launch][kTraceCtas][kGemmStamps] projection stamps, or null
   uint64_t* stage_trace;   // diagnostics: B=1 stage stamps [grid][3][stage_stride], or null
   uint64_t* att_trace;     // diagnostics: attention stamps [layer][kAttTraceUnits][8], or null
