@@ -131,6 +131,8 @@ struct b2d_ws {
   uint64_t* stage_trace;   // diagnostics: B=1 stage stamps [grid][3][stage_stride], or null
   uint64_t* att_trace;     // diagnostics: attention stamps [layer][kAttTraceUnits][8], or null
   uint64_t* sample_trace;  // diagnostics: sampler phase stamps [batch][8], or null
+  uint64_t* sample_scratch;  // top-p sort buffer [sample_rows][kSamplerMaxVocab]
+  int sample_rows;
   int stage_stride;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
@@ -367,6 +369,7 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   if (ws->m) cudaSetDevice(ws->m->device);
   for (auto& g : ws->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
+  cudaFree(ws->sample_scratch);
   if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
   cudaFree(ws->H);
   cudaFree(ws->Hm);
@@ -564,9 +567,22 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
   if (params->temperature > 0.0 && !uniforms_dev) return B2D_ERR_INVALID_ARG;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
+  if (params->temperature > 0.0 && params->top_p < 1.0 && batch > ws->sample_rows) {
+    // the top-p sort's scratch (256 KB per sequence), grown on first use outside capture
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    B2D_CUDA(cudaStreamIsCapturing(st, &cs), "capture status");
+    if (cs != cudaStreamCaptureStatusNone) return B2D_ERR_INVALID_ARG;
+    B2D_CUDA(cudaStreamSynchronize(st), "sync");
+    cudaFree(ws->sample_scratch);
+    ws->sample_scratch = nullptr;
+    ws->sample_rows = 0;
+    B2D_CUDA(cudaMalloc(&ws->sample_scratch, sizeof(uint64_t) * size_t(batch) * b2d::kSamplerMaxVocab),
+             "sampler scratch");
+    ws->sample_rows = batch;
+  }
   B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
                                params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st,
-                               ws->sample_trace),
+                               ws->sample_scratch, ws->sample_trace),
            "sampler launch");
   return B2D_OK;
 }

@@ -13,7 +13,8 @@
 //     reference's own np.exp is host dependent, up to 2 ulp on AVX-512);
 //   * normalisers: numpy's pairwise float32 summation (blocks of <= 128 with 8
 //     accumulators, halving at multiples of 8), evaluated as a tree;
-//   * top-p: order by descending probability, ties by ascending token id; the
+//   * top-p: order by descending probability, ties by ascending token id (a
+//     stable radix sort of the probabilities, which start in id order); the
 //     cutoff from a sequential float32 cumsum compared in float64 (numpy's
 //     searchsorted promotes the Python float);
 //   * choice: float64 prefix sums, divided by the total, first value > u.  The
@@ -46,6 +47,7 @@ struct SampleArgs {
   float temperature, rep_penalty;
   double top_p;
   uint64_t* trace;         // diagnostics: global-timer stamps [batch][8] (thread 0 of each CTA), or null
+  uint64_t* scratch;       // [batch][kSamplerMaxVocab] radix-sort buffer (key << 32 | id)
 };
 
 struct SamplerSmem {
@@ -60,6 +62,8 @@ struct SamplerSmem {
   int red_i[kSamplerThreads / 32];
   int cutoff;
   int token;
+  int rs_cnt[kSamplerThreads / 32][16];  // radix sort: digit counts / running offsets per warp
+  int rs_off[kSamplerThreads / 32][16];
 };
 
 __device__ __forceinline__ float key_to_p(uint32_t k) { return __uint_as_float(~k); }
@@ -181,105 +185,85 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   return k == 0x7fffffff ? n - 1 : k;
 }
 
-// Bitonic compare-exchange of (k, x) pairs: ascending by (key, id) when asc.
-__device__ __forceinline__ void cmp_swap(uint32_t& ka, uint32_t& xa, uint32_t& kb, uint32_t& xb, bool asc) {
-  const bool sw = (ka > kb || (ka == kb && xa > xb)) == asc;  // (branch-free)
-  const uint32_t k0 = sw ? kb : ka, k1 = sw ? ka : kb, x0 = sw ? xb : xa, x1 = sw ? xa : xb;
-  ka = k0; kb = k1; xa = x0; xb = x1;
+// Lanes of the warp whose 4-bit digit equals this lane's.
+__device__ __forceinline__ uint32_t same_digit_lanes(uint32_t d) {
+  uint32_t m = 0xffffffffu;
+#pragma unroll
+  for (int bit = 0; bit < 4; ++bit) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
+    m &= ((d >> bit) & 1u) ? bal : ~bal;
+  }
+  return m;
 }
 
-// Bitonic steps with partner distance j < kSortChunk for stages kk_lo ..
-// kk_hi (powers of two) on every chunk of kSortChunk consecutive elements,
-// in registers; element e of a stage kk sorts ascending iff (e & kk) == 0.
-// A thread reads its chunk's 16-byte pieces starting at a rotation of its
-// own (conflict-free across the warp) and undoes the rotation with selects.
-constexpr int kSortChunk = 16;
-__device__ __forceinline__ void sort_chunks(SamplerSmem& sm, int kk_lo, int kk_hi) {
-  const int rk = (threadIdx.x >> 1) & 3, rx = (threadIdx.x >> 2) & 1;  // rotations of the key / id pieces
-  for (int c = threadIdx.x; c < kSamplerMaxVocab / kSortChunk; c += kSamplerThreads) {
-    const int base = c * kSortChunk;
-    uint32_t k[kSortChunk], x[kSortChunk];
-    {
-      const uint4* k4 = reinterpret_cast<const uint4*>(sm.key + base);
-      uint4 v[4];
+// Stable LSD radix sort of (key, id) ascending by key: 8 passes of 4 bits,
+// alternating shared memory (sm.key / sm.idx) and the sequence's global
+// scratch (key << 32 | id); the result ends in shared memory.  Warp w owns
+// elements [1024 w, 1024 w + 1024) and visits them in index order (32 rounds
+// of 32 consecutive elements), so equal keys keep their order: the initial
+// order is by token id, hence ties end ascending by id, the order of the
+// (-p, id) comparison.  All threads of the block must call it.
+__device__ void radix_sort(SamplerSmem& sm, uint64_t* gbuf) {
+  static_assert(kSamplerMaxVocab == 32 * kSamplerThreads, "one 1024-element block per warp");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t below = (1u << lane) - 1u;
+  for (int pass = 0; pass < 8; ++pass) {
+    const int sh = 4 * pass;
+    const bool src_smem = (pass & 1) == 0;
+    if (lane < 16) sm.rs_cnt[warp][lane] = 0;
+    __syncwarp();
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) {  // digit counts of this warp's block
+      const int i = warp * 1024 + r * 32 + lane;
+      const uint32_t k = src_smem ? sm.key[i] : static_cast<uint32_t>(__ldcg(gbuf + i) >> 32);
+      atomicAdd(&sm.rs_cnt[warp][(k >> sh) & 15u], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {  // offsets: digit d's elements of warp w start at base(d) + sum over earlier warps
+      int tot = 0;
+      if (lane < 16)
+        for (int w = 0; w < kSamplerThreads / 32; ++w) {
+          const int c = sm.rs_cnt[w][lane];
+          sm.rs_off[w][lane] = tot;
+          tot += c;
+        }
+      int incl = tot;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) v[q] = k4[(q + rk) & 3];  // v[q] = piece (q + rk) & 3
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // piece q = v[(q - rk) & 3]
-        const uint4 a0 = v[q], a1 = v[(q + 3) & 3], a2 = v[(q + 2) & 3], a3 = v[(q + 1) & 3];
-        const uint4 w = rk == 0 ? a0 : rk == 1 ? a1 : rk == 2 ? a2 : a3;
-        k[4 * q] = w.x; k[4 * q + 1] = w.y; k[4 * q + 2] = w.z; k[4 * q + 3] = w.w;
+      for (int o = 1; o < 16; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
       }
-      const uint4* x4 = reinterpret_cast<const uint4*>(sm.idx + base);  // 8 ids per piece
-      const uint4 y0 = x4[rx], y1 = x4[rx ^ 1];
-      const uint4 p0 = rx ? y1 : y0, p1 = rx ? y0 : y1;
-      const uint32_t wv[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-#pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        x[2 * h] = wv[h] & 0xffffu;
-        x[2 * h + 1] = wv[h] >> 16;
+      if (lane < 16)
+        for (int w = 0; w < kSamplerThreads / 32; ++w) sm.rs_off[w][lane] += incl - tot;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int r = 0; r < 32; ++r) {  // scatter in index order
+      const int i = warp * 1024 + r * 32 + lane;
+      uint32_t k, x;
+      if (src_smem) {
+        k = sm.key[i];
+        x = sm.idx[i];
+      } else {
+        const uint64_t v = __ldcg(gbuf + i);
+        k = static_cast<uint32_t>(v >> 32);
+        x = static_cast<uint32_t>(v) & 0xffffu;
+      }
+      const uint32_t d = (k >> sh) & 15u;
+      const uint32_t m = same_digit_lanes(d);
+      const int dst = sm.rs_off[warp][d] + __popc(m & below);
+      __syncwarp();
+      if ((m & below) == 0) sm.rs_off[warp][d] += __popc(m);  // the group's lowest lane advances it
+      __syncwarp();
+      if (src_smem) {
+        __stcg(gbuf + dst, (static_cast<uint64_t>(k) << 32) | x);
+      } else {
+        sm.key[dst] = k;
+        sm.idx[dst] = static_cast<uint16_t>(x);
       }
     }
-    for (int kk = kk_lo; kk <= kk_hi; kk <<= 1) {
-#pragma unroll
-      for (int j = kSortChunk / 2; j > 0; j >>= 1) {
-        if (j >= kk) continue;  // stage kk has steps j = kk/2 .. 1
-#pragma unroll
-        for (int e = 0; e < kSortChunk; ++e)
-          if (!(e & j)) cmp_swap(k[e], x[e], k[e + j], x[e + j], ((base + e) & kk) == 0);
-      }
-    }
-    {
-      uint4 v[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) v[q] = make_uint4(k[4 * q], k[4 * q + 1], k[4 * q + 2], k[4 * q + 3]);
-      uint4* k4 = reinterpret_cast<uint4*>(sm.key + base);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // store piece (q + rk) & 3
-        const uint4 a0 = v[q], a1 = v[(q + 1) & 3], a2 = v[(q + 2) & 3], a3 = v[(q + 3) & 3];
-        k4[(q + rk) & 3] = rk == 0 ? a0 : rk == 1 ? a1 : rk == 2 ? a2 : a3;
-      }
-      const uint4 p0 = make_uint4(x[0] | (x[1] << 16), x[2] | (x[3] << 16), x[4] | (x[5] << 16), x[6] | (x[7] << 16));
-      const uint4 p1 = make_uint4(x[8] | (x[9] << 16), x[10] | (x[11] << 16), x[12] | (x[13] << 16),
-                                  x[14] | (x[15] << 16));
-      uint4* x4 = reinterpret_cast<uint4*>(sm.idx + base);
-      x4[rx] = rx ? p1 : p0;
-      x4[rx ^ 1] = rx ? p0 : p1;
-    }
+    __syncthreads();  // the pass's output is complete (global and shared) before the next pass reads it
   }
-  __syncthreads();
-}
-
-// S consecutive bitonic steps of stage kk with distances jtop, jtop/2, ..,
-// d = jtop / 2^(S-1) (>= kSortChunk) in one shared-memory pass: a thread
-// loads groups of 2^S elements base + a*d, applies the S steps in registers
-// and stores them back.
-template <int S>
-__device__ __forceinline__ void sort_group_pass(SamplerSmem& sm, int kk, int jtop) {
-  constexpr int G = 1 << S;
-  const int d = jtop >> (S - 1), ld = __ffs(d) - 1;
-#pragma unroll 1
-  for (int gi = threadIdx.x; gi < kSamplerMaxVocab / G; gi += kSamplerThreads) {
-    const int base = ((gi >> ld) << (ld + S)) | (gi & (d - 1));
-    uint32_t k[G], x[G];
-#pragma unroll
-    for (int a = 0; a < G; ++a) {
-      k[a] = sm.key[base + a * d];
-      x[a] = sm.idx[base + a * d];
-    }
-    const bool asc = (base & kk) == 0;  // a*d < 2*jtop <= kk adds no carry into bit kk
-#pragma unroll
-    for (int m = G / 2; m > 0; m >>= 1)
-#pragma unroll
-      for (int a = 0; a < G; ++a)
-        if (!(a & m)) cmp_swap(k[a], x[a], k[a + m], x[a + m], asc);
-#pragma unroll
-    for (int a = 0; a < G; ++a) {
-      sm.key[base + a * d] = k[a];
-      sm.idx[base + a * d] = static_cast<uint16_t>(x[a]);
-    }
-  }
-  __syncthreads();
 }
 
 __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const SampleArgs a) {
@@ -391,23 +375,9 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   }
 
   // ---- top-p (ref :53-63): sort by (descending p, ascending id) ----
-  // Bitonic sort ascending by (key, id) (key = ~bits of p).  Steps whose
-  // partner distance j < kSortChunk stay inside a thread's chunk of
-  // kSortChunk consecutive elements and run in registers; wider steps are
-  // shared-memory passes with every load of a batch issued before its stores.
+  // key = ~bits of p: ascending keys are descending probabilities.
   stamp(2);
-  sort_chunks(sm, 2, kSortChunk);  // stages kk = 2 .. kSortChunk entirely in registers
-  for (int kk = 2 * kSortChunk; kk <= kSamplerMaxVocab; kk <<= 1) {
-    // steps j = kk/2 .. kSortChunk, up to 4 per shared-memory pass
-    for (int j = kk >> 1; j >= kSortChunk;) {
-      const int left = __ffs(j) - __ffs(kSortChunk) + 1;  // steps j .. kSortChunk
-      if (left >= 4) { sort_group_pass<4>(sm, kk, j); j >>= 4; }
-      else if (left == 3) { sort_group_pass<3>(sm, kk, j); j >>= 3; }
-      else if (left == 2) { sort_group_pass<2>(sm, kk, j); j >>= 2; }
-      else { sort_group_pass<1>(sm, kk, j); j >>= 1; }
-    }
-    sort_chunks(sm, kk, kk);  // this stage's steps j < kSortChunk, in registers
-  }
+  radix_sort(sm, a.scratch + static_cast<size_t>(b) * kSamplerMaxVocab);
   stamp(3);
   // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one.  The
   // running sum is a float, so float64(c) >= top_p  <=>  c >= thr with thr =
@@ -467,7 +437,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
 inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, const int32_t* history,
                                   int hist_cap, const int32_t* hist_len, const double* uniforms,
                                   double temperature, double top_p, double rep_penalty, int32_t* out,
-                                  cudaStream_t st, uint64_t* trace = nullptr) {
+                                  cudaStream_t st, uint64_t* scratch, uint64_t* trace = nullptr) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -491,6 +461,7 @@ inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, con
   a.rep_penalty = static_cast<float>(rep_penalty);
   a.top_p = top_p;
   a.trace = trace;
+  a.scratch = scratch;
   sample_kernel<<<batch, kSamplerThreads, sizeof(SamplerSmem), st>>>(a);
   return cudaGetLastError();
 }
