@@ -67,6 +67,28 @@ def test_gemm_cluster_split_k(cuda, ks, epi):
         torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("ks", [1, 3])
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_96_row_tile(cuda, ks, epi):
+    """Batches of 65..96 rows take 96-row tiles (a TMEM allocation of 128
+    columns, 3 tiles for 256 rows): every epilogue, unsplit and split."""
+    g = torch.Generator(device="cpu").manual_seed(90 + 3 * ks + epi)
+    M, K, N = 512, 1024, 90
+    W = (torch.randn(M, K, generator=g) * 0.05).to(torch.bfloat16).to(cuda)
+    X = torch.randn(N, K, generator=g).to(torch.bfloat16).to(cuda)
+    R = torch.randn(N, M, generator=g).to(cuda) if epi == 1 else None
+    ldy = M // 2 if epi == 2 else None
+    out = _gemm(W, X, epi, resid=R, ldy=ldy, ksplit=ks)
+    full = X.float() @ W.float().T
+    if epi == 0:
+        torch.testing.assert_close(out, full, atol=1e-3, rtol=1e-3)
+    elif epi == 1:
+        torch.testing.assert_close(out, R + full, atol=1e-3, rtol=1e-3)
+    else:
+        ref = torch.nn.functional.silu(full[:, 0::2]) * full[:, 1::2]
+        torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+
 def test_gemm_residual_epilogue(cuda):
     g = torch.Generator(device="cpu").manual_seed(3)
     W = (torch.randn(1024, 1024, generator=g) * 0.05).to(torch.bfloat16).to(cuda)

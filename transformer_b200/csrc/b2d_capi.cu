@@ -135,7 +135,7 @@ struct b2d_ws {
   int sample_rows;
   int stage_stride;
   __nv_bfloat16 *X, *A, *ACT;
-  CUtensorMap xmap[5], amap[5], actmap[5];  // box rows 16 / 32 / 64 / 128 / 256
+  CUtensorMap xmap[6], amap[6], actmap[6];  // box rows 16 / 32 / 64 / 96 / 128 / 256 (bn_index)
   // b2d_decode_step_paged: CUDA graphs of the step's kernel sequence, one per
   // argument set (LRU), captured on cap_stream and launched on the caller's.
   struct StepGraph {
@@ -165,7 +165,7 @@ __global__ void iota_kernel(int32_t* out, int start, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = start + i;
 }
-inline int bn_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 128 ? 3 : 4; }
+inline int bn_index(int bn) { return bn == 16 ? 0 : bn == 32 ? 1 : bn == 64 ? 2 : bn == 96 ? 3 : bn == 128 ? 4 : 5; }
 
 // Launch with an optional programmatic dependency on the previous kernel of
 // the stream (the kernels call griddepcontrol.wait before reading its output).
@@ -345,8 +345,8 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
     if (e == cudaSuccess) e = cudaMemset(ws->A, 0, 2 * D * ws->rows);
     if (e == cudaSuccess) e = cudaMemset(ws->ACT, 0, 2 * F * ws->rows);
     if (e == cudaSuccess) e = cudaMalloc(&ws->ss, sizeof(float) * (D / b2d::kGemmBM) * ws->rows);
-    for (int i = 0; i < 5 && e == cudaSuccess; ++i) {
-      const uint32_t box = 16u << i;
+    for (int i = 0; i < 6 && e == cudaSuccess; ++i) {
+      const uint32_t box = static_cast<uint32_t>(b2d::kGemmWidths[i]);
       if (!b2d::make_kmajor_map(&ws->xmap[i], ws->X, D, ws->rows, box) ||
           !b2d::make_kmajor_map(&ws->amap[i], ws->A, D, ws->rows, box) ||
           !b2d::make_kmajor_map(&ws->actmap[i], ws->ACT, F, ws->rows, box))

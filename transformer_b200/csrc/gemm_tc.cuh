@@ -85,7 +85,8 @@ struct GemmSmem {
   static constexpr int BARS = STAGES * STAGE;
   static constexpr int RED_BYTES = BN * kGemmBM * 4;  // partial tile [BN][128] f32 (reuses the stages)
   static constexpr int BYTES = BARS + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // TMEM columns: a power of two >= 32 covering the tile's BN accumulator columns
+  static constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment for the swizzle atoms");
   static_assert(RED_BYTES <= BARS, "the partial tile must fit in the stage buffers");
   static_assert(BYTES <= 227 * 1024, "shared memory per CTA");
@@ -389,9 +390,14 @@ inline bool make_kmajor_map(CUtensorMap* map, const void* base, uint64_t inner, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tile widths (batch rows per tile), narrowest first.
+constexpr int kGemmWidths[] = {16, 32, 64, 96, 128, 256};
+// The next wider tile (256 stays 256).
+inline int gemm_bn_next(int bn) { return bn < 64 ? 2 * bn : bn == 64 ? 96 : bn == 96 ? 128 : 256; }
 // Batch rows per tile: the smallest width covering N, at most `cap`.
 inline int gemm_bn_for(int n, int cap = 256) {
-  const int bn = n <= 16 ? 16 : (n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : 256)));
+  int bn = 16;
+  while (bn < 256 && bn < n) bn = gemm_bn_next(bn);
   return bn < cap ? bn : cap;
 }
 
@@ -444,6 +450,7 @@ inline int gemm_max_clusters(int bn, int ks) {
     case 16: return gemm_max_clusters_t<16>(ks);
     case 32: return gemm_max_clusters_t<32>(ks);
     case 64: return gemm_max_clusters_t<64>(ks);
+    case 96: return gemm_max_clusters_t<96>(ks);
     case 128: return gemm_max_clusters_t<128>(ks);
     default: return gemm_max_clusters_t<256>(ks);
   }
@@ -460,7 +467,7 @@ struct GemmPlan {
 inline GemmPlan gemm_plan(int M, int N, int K, int bn_cap) {
   const int mt = M / kGemmBM;
   int bn = gemm_bn_for(N, bn_cap);
-  while (bn < 256 && mt * ((N + bn - 1) / bn) > gemm_max_clusters(bn, 1)) bn *= 2;
+  while (bn < 256 && mt * ((N + bn - 1) / bn) > gemm_max_clusters(bn, 1)) bn = gemm_bn_next(bn);
   const int tiles = mt * ((N + bn - 1) / bn);
   int ks = 1;
   for (int k = 2; k <= kGemmMaxSplit && k <= K / kGemmBK; ++k)
@@ -520,10 +527,10 @@ inline cudaError_t launch_gemm(const CUtensorMap& wm, const CUtensorMap& xm, con
     if (epi == EPI_RESID_F32) return launch_gemm_t<BNV, EPI_RESID_F32>(wm, xm, g, st, pdl); \
     return launch_gemm_t<BNV, EPI_SWIGLU_BF16>(wm, xm, g, st, pdl);                   \
   }
-  if (bn != 16 && bn != 32 && bn != 64 && bn != 128 && bn != 256) return cudaErrorInvalidValue;
   B2D_GEMM_CASE(16)
   B2D_GEMM_CASE(32)
   B2D_GEMM_CASE(64)
+  B2D_GEMM_CASE(96)
   B2D_GEMM_CASE(128)
   B2D_GEMM_CASE(256)
 #undef B2D_GEMM_CASE
