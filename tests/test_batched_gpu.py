@@ -120,6 +120,39 @@ def test_paged_306m_ragged(engine306_batched, params306_f32):
     _run_ragged(engine306_batched, params306_f32, CONFIG_306M, prompts, rng, check_every=4)
 
 
+def test_paged_306m_96_row_tiles(engine306_batched, params306_f32):
+    """80 sequences: every projection takes 96-row batch tiles (3 positions of
+    ragged prompts); four rows against the oracle, all rows finite."""
+    from transformer_b200.config import CONFIG_306M as cfg
+    rng = np.random.default_rng(16)
+    eng = engine306_batched
+    dev = eng.device
+    B, T = 80, 3
+    table, nb = _table(rng, B, cfg.context_len // PAGE_TOKENS)
+    pool = eng.new_kv_pool(nb)
+    table_d = torch.from_numpy(table).to(dev)
+    toks = rng.integers(0, cfg.vocab_size, (T, B)).astype(np.int32)
+    checked = [0, 31, 63, 79]
+    decs = {b: CachedDecoder(params306_f32, cfg, 1) for b in checked}
+    tok = torch.zeros(B, dtype=torch.int32, device=dev)
+    pos = torch.zeros(B, dtype=torch.int32, device=dev)
+    logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+    nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+    for t in range(T):
+        tok.copy_(torch.from_numpy(toks[t].copy()))
+        pos.fill_(t)
+        eng.step_paged(tok, pos, pool, table_d, logits, nxt)
+        got, am = logits.cpu().numpy(), nxt.cpu().numpy()
+        assert np.isfinite(got).all()
+        for b in checked:
+            ref = decs[b].step([toks[t, b]], [t])[0]
+            assert_logits_close(got[b], ref, f"row {b} pos {t}")
+            i, _, margin = top2(ref)
+            if margin > MARGIN:
+                assert am[b] == i
+    eng.check_device()
+
+
 def test_paged_306m_long_context(engine306_batched, params306_f32):
     """306M, positions near the end of the 512 context (config 2's length):
     ingested without checks, then the last 8 positions compared."""
