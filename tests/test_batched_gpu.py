@@ -120,19 +120,21 @@ def test_paged_306m_ragged(engine306_batched, params306_f32):
     _run_ragged(engine306_batched, params306_f32, CONFIG_306M, prompts, rng, check_every=4)
 
 
-def test_paged_306m_96_row_tiles(engine306_batched, params306_f32):
-    """80 sequences: every projection takes 96-row batch tiles (3 positions of
-    ragged prompts); four rows against the oracle, all rows finite."""
+@pytest.mark.parametrize("B", [80, 224])
+def test_paged_306m_96_row_tiles(engine306_batched, params306_f32, B):
+    """96-row batch tiles: at 80 sequences the output projection takes them,
+    at 224 the gate/up projection (its 64-row tiles would need a second
+    wave).  Three positions; four rows against the oracle, all rows finite."""
     from transformer_b200.config import CONFIG_306M as cfg
-    rng = np.random.default_rng(16)
+    rng = np.random.default_rng(16 + B)
     eng = engine306_batched
     dev = eng.device
-    B, T = 80, 3
+    T = 3
     table, nb = _table(rng, B, cfg.context_len // PAGE_TOKENS)
     pool = eng.new_kv_pool(nb)
     table_d = torch.from_numpy(table).to(dev)
     toks = rng.integers(0, cfg.vocab_size, (T, B)).astype(np.int32)
-    checked = [0, 31, 63, 79]
+    checked = [0, 31, B // 2 + 7, B - 1]
     decs = {b: CachedDecoder(params306_f32, cfg, 1) for b in checked}
     tok = torch.zeros(B, dtype=torch.int32, device=dev)
     pos = torch.zeros(B, dtype=torch.int32, device=dev)
