@@ -200,6 +200,42 @@ B2D_API b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t
 B2D_API b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos,
                                void* kv_dev, float* logits_dev, int32_t* next_tok_dev, void* stream);
 
+/*
+ * b2d_prefill into a paged KV pool (the layout of b2d_decode_step_paged):
+ * the sequence's positions are addressed through its block-table row
+ * table_row_dev (int32 [blocks_per_seq]; every entry that covers positions
+ * start_pos .. start_pos + n_tokens - 1 must name a block < num_blocks).
+ * Same math and outputs as b2d_prefill; admits a request into a running
+ * batch (the reference's serve.py / paged_kv.py, deleted upstream and
+ * described in knowledge/program.md:213-216, 257).
+ * start_pos + n_tokens <= min(context_len, 16 * blocks_per_seq).
+ */
+B2D_API b2d_status b2d_prefill_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens,
+                                     int start_pos, void* kv_pool_dev, const int32_t* table_row_dev,
+                                     int blocks_per_seq, int num_blocks, float* logits_dev,
+                                     int32_t* next_tok_dev, void* stream);
+
+/*
+ * Prefill of several sequences in one pass over the weights (chunked prefill
+ * for a continuous batch; the reference's prefill, model.py:194-231, takes
+ * one padded prompt at a time).  Row i feeds token tok_dev[i] at position
+ * pos_dev[i] of the sequence whose block-table row is table_dev[i][0..
+ * blocks_per_seq) (rows of one sequence carry the same table row).  Every
+ * row's K/V is written into the paged pool before any row attends, so a row
+ * sees the positions <= its own of its sequence that are in the pool or among
+ * this call's rows; a sequence longer than one call goes in several calls,
+ * earlier positions first.  Rows with pos < 0 are idle.  The last n_out rows
+ * (0 <= n_out <= n_rows; put each sequence's last prompt row there) get
+ * logits (f32 [n_out][vocab] in logits_dev, or NULL) and their argmax (int32
+ * [n_out] in next_tok_dev, or NULL); n_out = 0 writes the cache only.
+ * 1 <= n_rows <= b2d_prefill_rows_max() (512).
+ */
+B2D_API b2d_status b2d_prefill_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,
+                                    int n_rows, void* kv_pool_dev, const int32_t* table_dev, int blocks_per_seq,
+                                    int num_blocks, int n_out, float* logits_dev, int32_t* next_tok_dev,
+                                    void* stream);
+B2D_API int b2d_prefill_rows_max(void);
+
 /* Kernels launched by the last b2d_decode_step_paged (or prefill chunk). */
 B2D_API int b2d_batched_launches(const b2d_ws* ws);
 

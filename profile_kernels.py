@@ -12,6 +12,9 @@ arguments and results (``profile_kernels.py:44-87``): a host loop of
 uses this engine's algorithmic bytes (weights once, the KV rows actually read,
 one row written) and the measured HBM copy bandwidth.
 
+``--mode serve`` runs the continuous batcher (``transformer_b200.serve``) on
+a stream of requests and reports generated tokens per second, wall-clock.
+
 ``--mode paged`` runs the batched step over a paged KV pool with every
 sequence at ``--pos`` (the pool holds zeros: the step's work does not depend
 on the cached values), launched eagerly ``--warmup`` + ``--steps`` times; it is
@@ -156,9 +159,53 @@ def profile_paged(w, cfg, args, torch):
             "hbm_frac": alg / (us * 1e-6) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
 
+def profile_serve(w, cfg, args, torch):
+    """Continuous batching (``transformer_b200.serve``): ``--requests``
+    greedy requests with ``--prompt-len``-token prompts and generation lengths
+    uniform in [--gen-min, --gen-max] (seeded), ``--batch`` slots over a pool
+    of ``--num-blocks`` pages (default: enough for every slot's longest
+    sequence).  Wall-clock over the whole run (host scheduling, chunked
+    prefills, decode steps, one token read-back per step) after a warm-up run
+    of one request per slot."""
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    from transformer_b200.serve import PAGE_TOKENS, ContinuousBatcher
+    eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    rng = np.random.default_rng(5)
+    longest = args.prompt_len + args.gen_max - 1
+    nb = args.num_blocks or args.batch * ((longest + PAGE_TOKENS - 1) // PAGE_TOKENS)
+    cb = ContinuousBatcher(eng, args.batch, nb)
+    for _ in range(args.batch):
+        cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), 8)
+    cb.run()
+    cb.stats.clear()
+    gens = rng.integers(args.gen_min, args.gen_max + 1, args.requests)
+    rids = [cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), int(g)) for g in gens]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    out = cb.run()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    eng.check_device()
+    n_tok = sum(len(out[r]) for r in rids)
+    assert n_tok == int(gens.sum())
+    st = dict(cb.stats)
+    return {"mode": "serve", "requests": args.requests, "slots": args.batch, "num_blocks": nb,
+            "prompt_len": args.prompt_len, "gen": [args.gen_min, args.gen_max], "seconds": dt,
+            "generated_tok_s": n_tok / dt, "generated_tokens": n_tok,
+            "prompt_tok_s": args.requests * args.prompt_len / dt, "steps": st.get("steps", 0),
+            "mean_rows_per_step": (n_tok - args.requests) / max(1, st.get("steps", 1)),
+            "prefill_calls": st.get("prefill_calls", 0), "prefill_rows": st.get("prefill_rows", 0),
+            "preemptions": st.get("preemptions", 0)}
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["b1", "paged"], default="b1")
+    ap.add_argument("--mode", choices=["b1", "paged", "serve"], default="b1")
+    ap.add_argument("--requests", type=int, default=1024)
+    ap.add_argument("--prompt-len", type=int, default=64)
+    ap.add_argument("--gen-min", type=int, default=32)
+    ap.add_argument("--gen-max", type=int, default=256)
+    ap.add_argument("--num-blocks", type=int, default=0)
     ap.add_argument("--gen-len", type=int, default=128)
     ap.add_argument("--n-runs", type=int, default=10)
     ap.add_argument("--batch", type=int, default=64)
@@ -181,7 +228,8 @@ def main():
         params = synth_params(cfg, 0)
     w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
     out = {"memory": compute_memory_stats(cfg)}
-    out.update(profile_b1(w, cfg, args, torch) if args.mode == "b1" else profile_paged(w, cfg, args, torch))
+    prof = {"b1": profile_b1, "paged": profile_paged, "serve": profile_serve}[args.mode]
+    out.update(prof(w, cfg, args, torch))
     print(json.dumps(out))
     return 0
 

@@ -79,6 +79,11 @@ _SIGS = {
     "b2d_decode_step_paged": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int,
                                              _P, _P, _P]),
     "b2d_prefill": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P]),
+    "b2d_prefill_paged": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int,
+                                         ctypes.c_int, _P, _P, _P]),
+    "b2d_prefill_rows": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, _P, _P, _P]),
+    "b2d_prefill_rows_max": (ctypes.c_int, []),
     "b2d_batched_launches": (ctypes.c_int, [_P]),
     "b2d_sample": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_int, _P, _P,
                                   ctypes.POINTER(Sampling), _P, _P]),

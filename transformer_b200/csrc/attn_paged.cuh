@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     pdl_wait();
     pdl_launch();
   }
-  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.table_ld : nullptr;
   // The row's first 32 block-table entries, read alongside the position (lane i: page i).
   const int tbl = tb != nullptr && lane < a.bps ? __ldg(tb + lane) : 0;
   const int p = a.pos[b];

@@ -625,13 +625,16 @@ namespace {
 // sequences over a paged pool (`table` [batch][bps]); each row's new K/V is
 // appended by the attention kernel.  prefill = true: rows are positions of
 // ONE sequence whose cache `cache` is contiguous in the reference layout
-// (table = nullptr); the K/V of all rows are appended first, per layer.
+// (table = nullptr) or paged (table = its row); the K/V of all rows are
+// appended first, per layer.
 // logits == nullptr skips the output projection (earlier prefill chunks);
-// next_tok == nullptr skips the argmax; last_row: the output projection
-// covers only the last row, written as logits row 0 (prefill).
+// next_tok == nullptr skips the argmax; out_tail > 0: the output projection
+// and the argmax cover only the last out_tail rows, written as rows 0.. .
+// table_ld: entries between rows' table rows (default: bps for decode, 0 for
+// a prefill, whose rows then share the one table row `table` [bps]).
 b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t* pos, int batch, void* cache,
                     const int32_t* table, int bps, int num_blocks, bool prefill, float* logits, int32_t* next_tok,
-                    cudaStream_t st, bool last_row = false) {
+                    cudaStream_t st, int out_tail = 0, int table_ld = -1) {
   b2d_status s = ensure_weight_maps(m);
   if (s != B2D_OK) return s;
   const b2d_config& c = m->cfg;
@@ -680,6 +683,7 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   b2d::PagedAttnArgs pa{};
   pa.qkv = ws->qkv; pa.pos = pos; pa.pool = static_cast<__nv_bfloat16*>(cache);
   pa.table = table; pa.bps = bps; pa.num_blocks = num_blocks; pa.append = !prefill;
+  pa.table_ld = table_ld >= 0 ? table_ld : prefill ? 0 : bps;
   pa.n_heads = c.n_heads; pa.n_kv = c.n_kv_heads; pa.ctx = c.context_len;
   pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
@@ -732,16 +736,17 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   }
   g.M = V; g.K = D; g.y = logits; g.resid = nullptr; g.ldy = V;
   g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
-  if (last_row) {
-    g.N = 1;
-    g.n_base = batch - 1;
-    p_lg = b2d::gemm_plan(V, 1, D, 256);
+  const int n_out = out_tail > 0 ? out_tail : batch;
+  if (out_tail > 0) {
+    g.N = n_out;
+    g.n_base = batch - n_out;
+    p_lg = b2d::gemm_plan(V, n_out, D, 256);
   }
   B2D_CUDA(gemm(m->wmaps[4 * c.n_layers], ws->xmap, b2d::EPI_F32, p_lg), "logits");
   g.N = batch;
   g.n_base = 0;
   if (next_tok) {
-    B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(batch), dim3(1024), st, pdl, (const float*)logits, V, V,
+    B2D_CUDA(launch_k(b2d::argmax_rows_kernel, dim3(n_out), dim3(1024), st, pdl, (const float*)logits, V, V,
                       next_tok), "argmax");
     ++launches_other;
   }
@@ -817,21 +822,23 @@ b2d_status b2d_decode_step_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_de
                   lg, next_tok_dev, st);
 }
 
-b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos, void* kv_dev,
-                       float* logits_dev, int32_t* next_tok_dev, void* stream) {
-  if (!m || !ws || ws->m != m || !tok_dev || !kv_dev || n_tokens < 1 || start_pos < 0 ||
-      start_pos + n_tokens > m->cfg.context_len)
-    return B2D_ERR_INVALID_ARG;
+namespace {
+
+// Prompt positions start_pos.. of one sequence through run_rows, up to
+// kPrefillRows per chunk; `table` = nullptr: `cache` is that sequence's
+// contiguous cache, else the paged pool and `table` its block-table row.
+b2d_status prefill_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos, void* cache,
+                        const int32_t* table, int bps, int num_blocks, float* logits_dev, int32_t* next_tok_dev,
+                        cudaStream_t st) {
   B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int V = m->cfg.vocab_size;
   for (int c0 = 0; c0 < n_tokens; c0 += kPrefillRows) {
     const int rows = std::min(kPrefillRows, n_tokens - c0);
     const bool last = c0 + rows == n_tokens;
     B2D_CUDA(launch_k(iota_kernel, dim3((rows + 127) / 128), dim3(128), st, !ws->no_pdl, ws->prefill_pos,
                       start_pos + c0, rows), "positions");
-    b2d_status s = run_rows(m, ws, tok_dev + c0, ws->prefill_pos, rows, kv_dev, nullptr, 0, 0, true,
-                            last && (logits_dev || next_tok_dev) ? ws->logits : nullptr, nullptr, st, true);
+    b2d_status s = run_rows(m, ws, tok_dev + c0, ws->prefill_pos, rows, cache, table, bps, num_blocks, true,
+                            last && (logits_dev || next_tok_dev) ? ws->logits : nullptr, nullptr, st, 1);
     if (s != B2D_OK) return s;
     if (last) {
       const float* lrow = ws->logits;  // the last position's logits (row 0)
@@ -844,6 +851,43 @@ b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_t
   }
   return B2D_OK;
 }
+
+}  // namespace
+
+b2d_status b2d_prefill(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos, void* kv_dev,
+                       float* logits_dev, int32_t* next_tok_dev, void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !kv_dev || n_tokens < 1 || start_pos < 0 ||
+      start_pos + n_tokens > m->cfg.context_len)
+    return B2D_ERR_INVALID_ARG;
+  return prefill_rows(m, ws, tok_dev, n_tokens, start_pos, kv_dev, nullptr, 0, 0, logits_dev, next_tok_dev,
+                      static_cast<cudaStream_t>(stream));
+}
+
+b2d_status b2d_prefill_paged(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, int n_tokens, int start_pos,
+                             void* kv_pool_dev, const int32_t* table_row_dev, int blocks_per_seq, int num_blocks,
+                             float* logits_dev, int32_t* next_tok_dev, void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !kv_pool_dev || !table_row_dev || n_tokens < 1 || start_pos < 0 ||
+      blocks_per_seq < 1 || num_blocks < 1 || start_pos + n_tokens > m->cfg.context_len ||
+      start_pos + n_tokens > blocks_per_seq * b2d::kPageTokens)
+    return B2D_ERR_INVALID_ARG;
+  return prefill_rows(m, ws, tok_dev, n_tokens, start_pos, kv_pool_dev, table_row_dev, blocks_per_seq, num_blocks,
+                      logits_dev, next_tok_dev, static_cast<cudaStream_t>(stream));
+}
+
+b2d_status b2d_prefill_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev, int n_rows,
+                            void* kv_pool_dev, const int32_t* table_dev, int blocks_per_seq, int num_blocks,
+                            int n_out, float* logits_dev, int32_t* next_tok_dev, void* stream) {
+  if (!m || !ws || ws->m != m || !tok_dev || !pos_dev || !kv_pool_dev || !table_dev || n_rows < 1 ||
+      n_rows > kPrefillRows || blocks_per_seq < 1 || num_blocks < 1 || n_out < 0 || n_out > n_rows ||
+      (n_out == 0 && (logits_dev || next_tok_dev)))
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  float* lg = n_out == 0 || (!logits_dev && !next_tok_dev) ? nullptr : logits_dev ? logits_dev : ws->logits;
+  return run_rows(m, ws, tok_dev, pos_dev, n_rows, kv_pool_dev, table_dev, blocks_per_seq, num_blocks, true, lg,
+                  next_tok_dev, static_cast<cudaStream_t>(stream), n_out, blocks_per_seq);
+}
+
+int b2d_prefill_rows_max(void) { return kPrefillRows; }
 
 int b2d_batched_launches(const b2d_ws* ws) { return ws ? ws->last_launches : 0; }
 

@@ -66,8 +66,9 @@ struct PagedAttnArgs {
   const float* qkv;            // [B][(H+2KVH)*64] f32 (pre-RoPE q, k; v)
   const int32_t* pos;          // [B]
   __nv_bfloat16* pool;         // paged KV pool
-  const int32_t* table;        // [B][bps]
+  const int32_t* table;        // row b's entries at table + b * table_ld
   int bps, num_blocks, layer, n_heads, n_kv, ctx;
+  int table_ld;                // bps (decode: one table row per sequence) or 0 (prefill: rows share row 0)
   const float* rcos;           // [ctx][32]
   const float* rsin;
   __nv_bfloat16* out;          // [B][ldo] bf16: head h at columns h*64..
@@ -76,8 +77,8 @@ struct PagedAttnArgs {
   int cpc;                     // units per (row, kv head) (1, 2 or 4), each an even share of the row's pages
   // Cache addressing: table != nullptr -> the paged pool above; table ==
   // nullptr -> one sequence's contiguous cache in the reference layout
-  // [layer][K|V][kv_head][ctx][64] (every row of the launch is a position of
-  // that sequence, as in a prefill).
+  // [layer][K|V][kv_head][ctx][64].  In a prefill every row of the launch is a
+  // position of one sequence (table_ld = 0 with a paged pool).
   bool append;                 // the CTA holding a row's position writes its K/V (else done before)
   // diagnostics: global-timer stamps [unit][8] (units >= trace_units skipped), or nullptr
   uint64_t* trace;
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ P
   const int b = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
   const int p = a.pos[b];
   if (p < 0 || p >= a.ctx) return;
-  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.bps : nullptr;
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.table_ld : nullptr;
   if (tb != nullptr) {
     if (p / kPageTokens >= a.bps) return;
     const int e = tb[p / kPageTokens];

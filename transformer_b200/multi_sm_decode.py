@@ -141,6 +141,13 @@ class DecodeEngine:
         return torch.zeros(c.n_layers, num_blocks, 2, c.n_kv_heads, PAGE_TOKENS, c.d_head,
                            dtype=torch.bfloat16, device=self.device)
 
+    def _check_pool(self, pool: torch.Tensor) -> None:
+        c = self.cfg
+        if (pool.dtype != torch.bfloat16 or pool.device != self.device or not pool.is_contiguous() or pool.dim() != 6
+                or tuple(pool.shape[i] for i in (0, 2, 3, 4, 5)) != (c.n_layers, 2, c.n_kv_heads, PAGE_TOKENS,
+                                                                     c.d_head)):
+            raise ValueError("pool must be a paged KV pool of this model (see new_kv_pool)")
+
     def step_paged(self, tok: torch.Tensor, pos: torch.Tensor, pool: torch.Tensor,
                    block_table: torch.Tensor, logits: torch.Tensor | None = None,
                    next_tok: torch.Tensor | None = None, stream=None, batch: int | None = None) -> None:
@@ -158,10 +165,7 @@ class DecodeEngine:
             if t.dtype != torch.int32 or t.device != self.device or t.numel() < batch or not t.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous int32 tensor on {self.device} with >= {batch} items")
         c = self.cfg
-        if (pool.dtype != torch.bfloat16 or pool.device != self.device or not pool.is_contiguous() or pool.dim() != 6
-                or tuple(pool.shape[i] for i in (0, 2, 3, 4, 5)) != (c.n_layers, 2, c.n_kv_heads, PAGE_TOKENS,
-                                                                     c.d_head)):
-            raise ValueError("pool must be a paged KV pool of this model (see new_kv_pool)")
+        self._check_pool(pool)
         if (block_table.dtype != torch.int32 or block_table.device != self.device or block_table.dim() != 2
                 or block_table.shape[0] < batch or not block_table.is_contiguous()):
             raise ValueError("block_table must be a contiguous int32 [batch, blocks_per_seq] device tensor")
@@ -254,6 +258,71 @@ class DecodeEngine:
                                   _ptr(self.logits), _ptr(self.next_tok), _stream_ptr(stream))
         _lib.check(st, "b2d_prefill")
         return self.logits[0]
+
+    def prefill_paged(self, prompt, pool: torch.Tensor, table_row: torch.Tensor, start: int = 0,
+                      stream=None, next_tok: torch.Tensor | None = None) -> torch.Tensor:
+        """``b2d_prefill_paged``: as ``prefill``, into the paged pool ``pool``
+        (see ``new_kv_pool``) through one sequence's block-table row
+        ``table_row`` (device int32 [blocks_per_seq]).  Returns the last
+        position's logits (device [vocab]); the argmax goes to ``next_tok[0]``
+        (default: this engine's ``next_tok``)."""
+        prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
+        if prompt.size == 0:
+            raise ValueError("empty prompt")
+        self._check_pool(pool)
+        if (table_row.dtype != torch.int32 or table_row.device != self.device or table_row.dim() != 1
+                or not table_row.is_contiguous()):
+            raise ValueError("table_row must be a contiguous int32 [blocks_per_seq] device tensor")
+        if start < 0 or start + prompt.size > min(self.cfg.context_len, PAGE_TOKENS * table_row.numel()):
+            raise ValueError("prompt runs past the context or the table row")
+        nt = self.next_tok if next_tok is None else next_tok
+        if nt.dtype != torch.int32 or nt.device != self.device:
+            raise ValueError("next_tok must be an int32 device tensor")
+        toks = torch.from_numpy(prompt).to(self.device)
+        st = self.lib.b2d_prefill_paged(self.model, self.ws, _ptr(toks), int(prompt.size), int(start), _ptr(pool),
+                                        _ptr(table_row), table_row.numel(), pool.shape[1], _ptr(self.logits),
+                                        _ptr(nt), _stream_ptr(stream))
+        _lib.check(st, "b2d_prefill_paged")
+        return self.logits[0]
+
+    @property
+    def prefill_rows_max(self) -> int:
+        """Rows one ``prefill_rows`` call takes (one prefill chunk)."""
+        return int(self.lib.b2d_prefill_rows_max())
+
+    def prefill_rows(self, tok: torch.Tensor, pos: torch.Tensor, pool: torch.Tensor, table: torch.Tensor,
+                     n_out: int, logits: torch.Tensor | None = None, next_tok: torch.Tensor | None = None,
+                     n_rows: int | None = None, stream=None) -> None:
+        """``b2d_prefill_rows``: ``n_rows`` (<= 512) rows of tokens ``tok`` at
+        positions ``pos`` of the sequences whose block-table rows are
+        ``table`` [n_rows, blocks_per_seq] (device int32) through one pass
+        over the weights, writing their K/V into ``pool``; the last ``n_out``
+        rows get logits (float32 [n_out, vocab]) and / or argmax (int32
+        [n_out]) when those buffers are given (async, stream-ordered)."""
+        n_rows = n_rows or tok.numel()
+        if not 1 <= n_rows <= self.lib.b2d_prefill_rows_max():
+            raise ValueError(f"n_rows must be in [1, {self.lib.b2d_prefill_rows_max()}]")
+        if not 0 <= n_out <= n_rows:
+            raise ValueError("n_out must be in [0, n_rows]")
+        for t, name in ((tok, "tok"), (pos, "pos")):
+            if t.dtype != torch.int32 or t.device != self.device or t.numel() < n_rows or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous int32 tensor on {self.device} with >= {n_rows} items")
+        self._check_pool(pool)
+        if (table.dtype != torch.int32 or table.device != self.device or table.dim() != 2
+                or table.shape[0] < n_rows or not table.is_contiguous()):
+            raise ValueError("table must be a contiguous int32 [n_rows, blocks_per_seq] device tensor")
+        if logits is not None and (logits.dtype != torch.float32 or logits.device != self.device
+                                   or logits.numel() < n_out * self.cfg.vocab_size or not logits.is_contiguous()):
+            raise ValueError("logits must be contiguous float32 [n_out, vocab] on the model device")
+        if next_tok is not None and (next_tok.dtype != torch.int32 or next_tok.device != self.device
+                                     or next_tok.numel() < n_out):
+            raise ValueError("next_tok must be int32 [n_out] on the model device")
+        if n_out == 0 and (logits is not None or next_tok is not None):
+            raise ValueError("outputs given with n_out = 0")
+        st = self.lib.b2d_prefill_rows(self.model, self.ws, _ptr(tok), _ptr(pos), int(n_rows), _ptr(pool),
+                                       _ptr(table), table.shape[1], pool.shape[1], int(n_out), _ptr(logits),
+                                       _ptr(next_tok), _stream_ptr(stream))
+        _lib.check(st, "b2d_prefill_rows")
 
     def prefill_stepwise(self, prompt, kv: torch.Tensor, start: int = 0, stream=None) -> torch.Tensor:
         """Feed prompt tokens one decode step at a time (teacher forcing),

@@ -1,0 +1,403 @@
+"""Continuous batching over the paged KV pool.
+
+The reference's batched server and paged KV cache (``serve.py``,
+``kernels/paged_kv.py``) were deleted upstream; ``knowledge/program.md:213-216,
+257`` describes them: per-sequence position tracking, a ``PagePool`` of
+fixed-size KV pages, and batch slots refilled as sequences complete.  Here:
+
+* ``PagePool`` hands out the physical blocks of one paged pool (16 positions
+  each, the layout of ``b2d_decode_step_paged``) from a free list.
+* ``ContinuousBatcher`` keeps up to ``max_batch`` requests in slots.  Waiting
+  requests are admitted into free slots while the pool has the pages for
+  their prompts; their prompts go through ``b2d_prefill_rows`` together, up to
+  512 positions of any number of prompts per pass over the weights, writing
+  K/V through each slot's block-table row, and each prompt's last logits give
+  its first token (as ``generate.py:68-89``).  Each ``step()`` runs one
+  batched decode step over every slot (idle slots as ``pos = -1`` rows),
+  feeding each request its previous token at ``pos = prompt_len + i``
+  (``generate.py:92-123``).  A page
+  is taken when a request's next position starts one; when none is free the
+  most recently admitted request is preempted: its pages return to the pool
+  and it waits at the head of the queue, to be prefilled again over its prompt
+  and the tokens it has generated (its tokens so far are kept).
+
+Greedy requests (temperature 0, no repetition penalty, ``generate.py:102,
+115``) take the step's argmax; the others go through the device sampler with
+their generated tokens as history and one uniform per token from their own
+``numpy.random.RandomState(seed)``, the draw ``np.random.choice`` makes after
+``np.random.seed(seed)`` in the reference.
+"""
+
+from __future__ import annotations
+
+import collections
+import dataclasses
+
+import numpy as np
+import torch
+
+PAGE_TOKENS = 16  # positions per block (b2d_decode_step_paged's page)
+
+
+class PoolExhausted(RuntimeError):
+    pass
+
+
+class PagePool:
+    """Free list over the blocks 0..num_blocks-1 of one paged KV pool."""
+
+    def __init__(self, num_blocks: int):
+        if num_blocks < 1:
+            raise ValueError("num_blocks must be positive")
+        self.num_blocks = num_blocks
+        self._free = list(range(num_blocks - 1, -1, -1))  # pop() hands out low ids first
+        self._used = np.zeros(num_blocks, dtype=bool)
+
+    @property
+    def n_free(self) -> int:
+        return len(self._free)
+
+    def alloc(self, n: int) -> list[int]:
+        if n < 0:
+            raise ValueError("negative page count")
+        if n > len(self._free):
+            raise PoolExhausted(f"{n} pages wanted, {len(self._free)} free")
+        out = [self._free.pop() for _ in range(n)]
+        self._used[out] = True
+        return out
+
+    def free(self, blocks) -> None:
+        for b in blocks:
+            if not (0 <= b < self.num_blocks) or not self._used[b]:
+                raise ValueError(f"block {b} is not allocated")
+            self._used[b] = False
+            self._free.append(b)
+
+
+@dataclasses.dataclass
+class Request:
+    rid: int
+    prompt: np.ndarray
+    max_tokens: int
+    temperature: float = 0.0
+    top_p: float = 1.0
+    rep_penalty: float = 1.0
+    seed: int | None = None
+    out: list = dataclasses.field(default_factory=list)
+    blocks: list = dataclasses.field(default_factory=list)
+    slot: int = -1
+    admitted: int = -1       # admission order (the preemption victim is the latest)
+    preemptions: int = 0
+    rng: object = None
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature == 0.0 and self.rep_penalty == 1.0
+
+    def next_pos(self) -> int:
+        """Position of the token fed at this request's next decode step."""
+        return len(self.prompt) + len(self.out) - 1
+
+
+class ContinuousBatcher:
+    """Requests in ``max_batch`` slots over one paged pool of ``num_blocks``
+    blocks.  ``submit`` queues a request; ``step`` admits what fits and runs
+    one decode step, returning the ``(rid, token)`` pairs it produced
+    (admission's first tokens included); ``run`` steps until every request has
+    finished and returns ``{rid: tokens}``."""
+
+    def __init__(self, engine, max_batch: int, num_blocks: int, eos_id: int | None = None,
+                 hist_cap: int | None = None):
+        cfg = engine.cfg
+        self.eng = engine
+        self.ctx = cfg.context_len
+        self.vocab = cfg.vocab_size
+        self.bps = (self.ctx + PAGE_TOKENS - 1) // PAGE_TOKENS
+        if max_batch < 2 or max_batch > engine.max_batch:
+            raise ValueError(f"max_batch must be in [2, {engine.max_batch}] (the engine's workspace)")
+        if num_blocks < self.bps:
+            raise ValueError(f"num_blocks must hold one full-context sequence ({self.bps} blocks)")
+        self.max_batch, self.eos_id = max_batch, eos_id
+        self.pages = PagePool(num_blocks)
+        self.pool = engine.new_kv_pool(num_blocks)
+        dev = engine.device
+        self._cuda = dev.type == "cuda"
+        pin = self._cuda
+        # tok | pos | table rows, one host->device copy per step
+        n_stage = 2 * max_batch + max_batch * self.bps
+        self._h_stage = torch.zeros(n_stage, dtype=torch.int32, pin_memory=pin)
+        self._d_stage = torch.zeros(n_stage, dtype=torch.int32, device=dev)
+        self._h_tok = self._h_stage[:max_batch].numpy()
+        self._h_pos = self._h_stage[max_batch:2 * max_batch].numpy()
+        self._h_table = self._h_stage[2 * max_batch:].numpy().reshape(max_batch, self.bps)
+        self._d_tok = self._d_stage[:max_batch]
+        self._d_pos = self._d_stage[max_batch:2 * max_batch]
+        self._d_table = self._d_stage[2 * max_batch:].view(max_batch, self.bps)
+        self._d_next = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        # prefill chunks: tok | pos | table rows
+        self._rows_max = int(engine.prefill_rows_max)
+        cap = self._rows_max
+        self._hp_stage = torch.zeros(2 * cap + cap * self.bps, dtype=torch.int32, pin_memory=pin)
+        self._dp_stage = torch.zeros(2 * cap + cap * self.bps, dtype=torch.int32, device=dev)
+        self._hp_tok = self._hp_stage[:cap].numpy()
+        self._hp_pos = self._hp_stage[cap:2 * cap].numpy()
+        self._hp_table = self._hp_stage[2 * cap:].numpy().reshape(cap, self.bps)
+        self._dp_tok = self._dp_stage[:cap]
+        self._dp_pos = self._dp_stage[cap:2 * cap]
+        self._dp_table = self._dp_stage[2 * cap:].view(cap, self.bps)
+        self._dp_next = torch.zeros(cap, dtype=torch.int32, device=dev)
+        self._logits_rows = max(max_batch, cap)
+        self._h_next = torch.zeros(self._logits_rows, dtype=torch.int32, pin_memory=pin)
+        self._h_table[:] = 0
+        self._h_pos[:] = -1
+        self.slots: list[Request | None] = [None] * max_batch
+        self.waiting: collections.deque[Request] = collections.deque()
+        self.finished: dict[int, list] = {}
+        self._next_rid = 0
+        self._admit_tick = 0
+        self._hist_cap = hist_cap or self.ctx
+        self._sampler = None
+        self._logits = None
+        self.stats = collections.Counter()
+
+    # ---- requests --------------------------------------------------------
+    def submit(self, prompt, max_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
+               rep_penalty: float = 1.0, seed: int | None = None) -> int:
+        prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
+        if prompt.size == 0:
+            raise ValueError("empty prompt")
+        if max_tokens < 1:
+            raise ValueError("max_tokens must be >= 1")
+        if prompt.size + max_tokens - 1 > self.ctx:
+            raise ValueError(f"prompt ({prompt.size}) + max_tokens - 1 ({max_tokens - 1}) exceeds the context "
+                             f"({self.ctx})")
+        if prompt.min() < 0 or prompt.max() >= self.vocab:
+            raise ValueError("token id out of range")
+        if not (temperature >= 0.0 and top_p > 0.0 and rep_penalty > 0.0):
+            raise ValueError("bad sampling parameters")
+        if max_tokens > self._hist_cap:
+            raise ValueError("max_tokens exceeds the sampler history capacity")
+        rid = self._next_rid
+        self._next_rid += 1
+        r = Request(rid, prompt, int(max_tokens), float(temperature), float(top_p), float(rep_penalty), seed)
+        if not r.greedy:
+            r.rng = np.random.RandomState(seed)
+        self.waiting.append(r)
+        return rid
+
+    @property
+    def running(self) -> list[Request]:
+        return [r for r in self.slots if r is not None]
+
+    def idle(self) -> bool:
+        return not self.waiting and all(r is None for r in self.slots)
+
+    def run(self) -> dict[int, list]:
+        while not self.idle():
+            self.step()
+        return dict(self.finished)
+
+    # ---- one scheduling step --------------------------------------------
+    def step(self) -> list[tuple[int, int]]:
+        events: list[tuple[int, int]] = []
+        self._admit(events)
+        self._reserve_pages()
+        batch = 1 + max((i for i, r in enumerate(self.slots) if r is not None), default=-1)
+        if batch == 0:
+            return events
+        batch = max(batch, 2)  # the batched step takes at least two rows
+        for i in range(batch):
+            r = self.slots[i]
+            if r is None:
+                self._h_tok[i], self._h_pos[i] = 0, -1
+            else:
+                self._h_tok[i], self._h_pos[i] = r.out[-1], r.next_pos()
+        self._d_stage.copy_(self._h_stage, non_blocking=self._cuda)
+        need_logits = any(r is not None and not r.greedy for r in self.slots[:batch])
+        logits = self._logits_buf() if need_logits else None
+        self.eng.step_paged(self._d_tok, self._d_pos, self.pool, self._d_table, logits, self._d_next,
+                            batch=batch)
+        if need_logits:
+            toks = self._sample_rows(logits, self.slots[:batch], self._d_next)
+        else:
+            toks = self._fetch(self._d_next, batch)
+        self.stats["steps"] += 1
+        for i in range(batch):
+            r = self.slots[i]
+            if r is None:
+                continue
+            t = int(toks[i])
+            r.out.append(t)
+            events.append((r.rid, t))
+            self.stats["tokens"] += 1
+            self._maybe_finish(r)
+        return events
+
+    def _admit(self, events) -> None:
+        admitted = []
+        while self.waiting and None in self.slots:
+            r = self.waiting[0]
+            prefix = self._prefix(r)
+            need = (prefix.size + PAGE_TOKENS - 1) // PAGE_TOKENS
+            # keep one page of headroom for the running requests' next positions
+            headroom = 1 if any(s is not None for s in self.slots) else 0
+            if need + headroom > self.pages.n_free:
+                break
+            self.waiting.popleft()
+            slot = self.slots.index(None)
+            r.blocks = self.pages.alloc(need)
+            r.slot = slot
+            r.admitted = self._admit_tick
+            self._admit_tick += 1
+            self.slots[slot] = r
+            self._h_table[slot, :] = 0
+            self._h_table[slot, :need] = r.blocks
+            admitted.append((r, prefix))
+        if admitted:
+            self._prefill(admitted, events)
+
+    @staticmethod
+    def _prefix(r: Request) -> np.ndarray:
+        """Tokens whose K/V a (re)admitted request needs: its prompt, plus, after
+        a preemption, every generated token but the last (fed at the next step)."""
+        if not r.out:
+            return r.prompt
+        return np.concatenate([r.prompt, np.asarray(r.out[:-1], np.int32)])
+
+    def _prefill(self, admitted, events) -> None:
+        """The admitted prefixes in chunks of up to ``prefill_rows_max`` rows
+        (one pass over the weights each).  A new request's last row goes to its
+        chunk's tail, whose outputs give the first tokens; a readmitted
+        request's next token is already chosen."""
+        cap = self._rows_max
+        body: list[tuple[int, int, int]] = []       # (token, position, slot)
+        tail: list[tuple[int, int, int, Request]] = []
+
+        def flush():
+            rows = body + [t[:3] for t in tail]
+            n, n_out = len(rows), len(tail)
+            arr = np.asarray(rows, dtype=np.int64)
+            self._hp_tok[:n] = arr[:, 0]
+            self._hp_pos[:n] = arr[:, 1]
+            self._hp_table[:n] = self._h_table[arr[:, 2]]
+            self._dp_stage.copy_(self._hp_stage, non_blocking=self._cuda)
+            reqs = [t[3] for t in tail]
+            sampled = any(not q.greedy for q in reqs)
+            logits = self._logits_buf() if sampled else None
+            self.eng.prefill_rows(self._dp_tok, self._dp_pos, self.pool, self._dp_table, n_out,
+                                  logits=logits, next_tok=self._dp_next if n_out else None, n_rows=n)
+            self.stats["prefill_rows"] += n
+            self.stats["prefill_calls"] += 1
+            if n_out:
+                toks = (self._sample_rows(logits, reqs, self._dp_next) if sampled
+                        else self._fetch(self._dp_next, n_out))
+                for q, t in zip(reqs, toks):
+                    q.out.append(int(t))
+                    events.append((q.rid, int(t)))
+                    self.stats["tokens"] += 1
+                    self._maybe_finish(q)
+            elif self._cuda:  # the pinned staging is rewritten by the next chunk
+                torch.cuda.current_stream(self.eng.device).synchronize()
+            body.clear()
+            tail.clear()
+
+        for r, prefix in admitted:
+            n, wants_out = prefix.size, not r.out
+            for k in range(n):
+                if len(body) + len(tail) == cap:
+                    flush()
+                row = (int(prefix[k]), k, r.slot)
+                if k == n - 1 and wants_out:
+                    tail.append(row + (r,))
+                else:
+                    body.append(row)
+        if body or tail:
+            flush()
+
+    def _reserve_pages(self) -> None:
+        """Every running request gets the page its next position lands in,
+        preempting the most recently admitted requests while none is free."""
+        for r in sorted(self.running, key=lambda q: q.admitted):
+            if r.slot < 0:  # preempted below while serving an earlier request
+                continue
+            while r.next_pos() // PAGE_TOKENS >= len(r.blocks):
+                if self.pages.n_free == 0:
+                    victim = max(self.running, key=lambda q: q.admitted)
+                    self._preempt(victim)
+                    if victim is r:
+                        break
+                    continue
+                b = self.pages.alloc(1)[0]
+                self._h_table[r.slot, len(r.blocks)] = b
+                r.blocks.append(b)
+
+    def _preempt(self, r: Request) -> None:
+        self.pages.free(r.blocks)
+        r.blocks = []
+        self.slots[r.slot] = None
+        self._h_table[r.slot, :] = 0
+        r.slot = -1
+        r.preemptions += 1
+        self.stats["preemptions"] += 1
+        self.waiting.appendleft(r)
+
+    def _maybe_finish(self, r: Request) -> None:
+        if len(r.out) < r.max_tokens and (self.eos_id is None or r.out[-1] != self.eos_id):
+            return
+        self.pages.free(r.blocks)
+        r.blocks = []
+        self.slots[r.slot] = None
+        self._h_table[r.slot, :] = 0
+        r.slot = -1
+        self.finished[r.rid] = list(r.out)
+
+    # ---- device helpers --------------------------------------------------
+    def _fetch(self, d: torch.Tensor, n: int) -> np.ndarray:
+        h = self._h_next[:n]
+        h.copy_(d[:n], non_blocking=self._cuda)
+        if self._cuda:
+            torch.cuda.current_stream(self.eng.device).synchronize()
+        return h.numpy().copy()
+
+    def _logits_buf(self) -> torch.Tensor:
+        if self._logits is None:
+            self._logits = torch.empty(self._logits_rows, self.vocab, dtype=torch.float32, device=self.eng.device)
+        return self._logits
+
+    def _sample_rows(self, logits: torch.Tensor, rows, greedy_src: torch.Tensor) -> np.ndarray:
+        """Tokens for the requests ``rows`` (row i of ``logits``; None = idle):
+        sampled for non-greedy requests, with their generated tokens as history
+        and their next uniform; for greedy ones the argmax the step or the
+        prefill left in ``greedy_src``."""
+        from .generate import Sampler
+        if self._sampler is None:
+            self._sampler = Sampler(self.eng, self._logits_rows, self._hist_cap)
+        smp = self._sampler
+        batch = len(rows)
+        hist = np.zeros((batch, self._hist_cap), np.int32)
+        hlen = np.zeros(batch, np.int32)
+        u = np.zeros(batch, np.float64)
+        for i, r in enumerate(rows):
+            if r is None or r.greedy:
+                continue
+            n = len(r.out)
+            hist[i, :n] = r.out
+            hlen[i] = n
+            if r.temperature > 0.0:
+                u[i] = r.rng.random_sample()
+        smp.history[:batch].copy_(torch.from_numpy(hist))
+        smp.hist_len[:batch].copy_(torch.from_numpy(hlen))
+        smp.uniforms[:batch].copy_(torch.from_numpy(u))
+        out = np.zeros(batch, np.int32)
+        groups: dict = {}
+        for i, r in enumerate(rows):
+            if r is not None and not r.greedy:
+                groups.setdefault((r.temperature, r.top_p, r.rep_penalty), []).append(i)
+        greedy_rows = [i for i, r in enumerate(rows) if r is not None and r.greedy]
+        if greedy_rows:
+            out[greedy_rows] = self._fetch(greedy_src, batch)[greedy_rows]
+        for (temp, top_p, rp), idx in groups.items():
+            # one sampler launch per parameter set over all rows; keep this set's rows
+            got = smp.sample(logits[:batch], temp, top_p, rp, batch).cpu().numpy()
+            out[idx] = got[idx]
+        return out
