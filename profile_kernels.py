@@ -173,7 +173,7 @@ def profile_serve(w, cfg, args, torch):
     rng = np.random.default_rng(5)
     longest = args.prompt_len + args.gen_max - 1
     nb = args.num_blocks or args.batch * ((longest + PAGE_TOKENS - 1) // PAGE_TOKENS)
-    cb = ContinuousBatcher(eng, args.batch, nb)
+    cb = ContinuousBatcher(eng, args.batch, nb, admission=args.admission, fuse_prefill=not args.no_fuse)
     for _ in range(args.batch):
         cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), 8)
     cb.run()
@@ -195,7 +195,8 @@ def profile_serve(w, cfg, args, torch):
             "prompt_tok_s": args.requests * args.prompt_len / dt, "steps": st.get("steps", 0),
             "mean_rows_per_step": (n_tok - args.requests) / max(1, st.get("steps", 1)),
             "prefill_calls": st.get("prefill_calls", 0), "prefill_rows": st.get("prefill_rows", 0),
-            "preemptions": st.get("preemptions", 0)}
+            "mixed_steps": st.get("mixed_steps", 0), "preemptions": st.get("preemptions", 0),
+            "admission": args.admission, "fuse_prefill": not args.no_fuse}
 
 
 def main():
@@ -206,6 +207,8 @@ def main():
     ap.add_argument("--gen-min", type=int, default=32)
     ap.add_argument("--gen-max", type=int, default=256)
     ap.add_argument("--num-blocks", type=int, default=0)
+    ap.add_argument("--admission", choices=["reserve", "optimistic"], default="reserve")
+    ap.add_argument("--no-fuse", action="store_true", help="prefill admitted prompts in passes of their own")
     ap.add_argument("--gen-len", type=int, default=128)
     ap.add_argument("--n-runs", type=int, default=10)
     ap.add_argument("--batch", type=int, default=64)

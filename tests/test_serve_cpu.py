@@ -111,13 +111,18 @@ def test_page_pool():
     assert sorted(b) == [1, 3, 4] and pp.n_free == 0
 
 
-@pytest.mark.parametrize("seed,num_blocks", [(0, 4), (1, 6), (2, 9), (3, 40)])
-def test_batcher_matches_sequential(seed, num_blocks):
+@pytest.mark.parametrize("fuse", [True, False])
+@pytest.mark.parametrize("seed,num_blocks,admission", [(0, 4, "optimistic"), (1, 6, "optimistic"),
+                                                       (2, 9, "optimistic"), (3, 40, "optimistic"),
+                                                       (4, 6, "reserve"), (5, 9, "reserve")])
+def test_batcher_matches_sequential(seed, num_blocks, admission, fuse):
     """Requests of random lengths through 4 slots: every token stream equals
-    the one-at-a-time generation; small pools force preemptions."""
+    the one-at-a-time generation, prompts prefilled in fused passes or on
+    their own; small pools force preemptions under optimistic admission and
+    none under reserving admission."""
     rng = np.random.default_rng(seed)
-    eng = FakeEngine(ctx=64, vocab=97, max_batch=4)
-    cb = ContinuousBatcher(eng, 4, num_blocks)
+    eng = FakeEngine(ctx=64, vocab=97, max_batch=4, rows_max=64)
+    cb = ContinuousBatcher(eng, 4, num_blocks, admission=admission, fuse_prefill=fuse)
     want = {}
     for _ in range(14):
         n_prompt = int(rng.integers(1, 48))
@@ -130,10 +135,13 @@ def test_batcher_matches_sequential(seed, num_blocks):
     assert cb.pages.n_free == num_blocks
     assert cb.idle()
     assert cb.stats["tokens"] >= sum(len(v) for v in want.values())
-    if num_blocks <= 6:
+    if admission == "reserve":
+        assert cb.stats["preemptions"] == 0
+    elif num_blocks <= 6:
         assert cb.stats["preemptions"] > 0
-    if num_blocks == 40:
-        assert cb.stats["preemptions"] == 0 and max(eng.steps) == 4
+    if num_blocks == 40:  # room for every slot: several rows per pass on average
+        assert cb.stats["preemptions"] == 0 and cb.stats["tokens"] > 2 * cb.stats["steps"]
+    assert (cb.stats["mixed_steps"] > 0) == fuse
 
 
 def test_batcher_events_and_eos():
@@ -161,7 +169,7 @@ def test_batcher_prefill_chunks():
     outputs."""
     rng = np.random.default_rng(9)
     eng = FakeEngine(ctx=64, vocab=97, max_batch=4, rows_max=24)
-    cb = ContinuousBatcher(eng, 4, 16)
+    cb = ContinuousBatcher(eng, 4, 16, fuse_prefill=False)
     want = {}
     for n in (50, 3, 4, 30):
         pr = rng.integers(0, 97, n)
@@ -171,6 +179,20 @@ def test_batcher_prefill_chunks():
     assert max(r for r, _ in eng.prefill_calls) == 24 and len(eng.prefill_calls) == 4
     assert sum(o for _, o in eng.prefill_calls) == 4
     assert cb.run() == want
+
+
+def test_batcher_long_prompts_prefilled_on_their_own():
+    """With fused passes on, a prefix longer than one pass (here 24 rows) is
+    prefilled on its own in chunks while short prompts join the fused pass."""
+    rng = np.random.default_rng(10)
+    eng = FakeEngine(ctx=64, vocab=97, max_batch=4, rows_max=24)
+    cb = ContinuousBatcher(eng, 4, 16)
+    want = {}
+    for n in (50, 3, 4, 30, 2):
+        pr = rng.integers(0, 97, n)
+        want[cb.submit(pr, 6)] = _expected(pr, 6, 97)
+    assert cb.run() == want
+    assert cb.stats["mixed_steps"] > 0 and cb.stats["prefill_calls"] == 4  # 50 + 30 rows in 24-row chunks
 
 
 def test_batcher_single_token_and_full_context():

@@ -163,15 +163,18 @@ def _teacher_forced_greedy(P, cfg, prompt, out):
     return checked
 
 
-def test_batcher_greedy_tiny_vs_oracle(engine_tiny_batched, params_tiny):
+@pytest.mark.parametrize("fuse", [True, False])
+def test_batcher_greedy_tiny_vs_oracle(engine_tiny_batched, params_tiny, fuse):
     """12 requests through 4 slots over an 11-block pool (one 128-position
-    context is 8 blocks): slots refill as requests finish and requests are
-    preempted and readmitted; every stream is checked against the oracle."""
+    context is 8 blocks), optimistic admission: slots refill as requests
+    finish and requests are preempted and readmitted; prompts prefilled in
+    fused passes with the decode rows, or on their own.  Every stream is
+    checked against the oracle."""
     from transformer_b200.config import CONFIG_TINY as cfg
     from transformer_b200.synth import params_f32
     P = params_f32(params_tiny)
     rng = np.random.default_rng(21)
-    cb = ContinuousBatcher(engine_tiny_batched, 4, 11)
+    cb = ContinuousBatcher(engine_tiny_batched, 4, 11, admission="optimistic", fuse_prefill=fuse)
     prompts = {}
     for _ in range(12):
         n = int(rng.integers(1, 90))

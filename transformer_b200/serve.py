@@ -102,12 +102,20 @@ class Request:
 class ContinuousBatcher:
     """Requests in ``max_batch`` slots over one paged pool of ``num_blocks``
     blocks.  ``submit`` queues a request; ``step`` admits what fits and runs
-    one decode step, returning the ``(rid, token)`` pairs it produced
-    (admission's first tokens included); ``run`` steps until every request has
-    finished and returns ``{rid: tokens}``."""
+    one pass, returning the ``(rid, token)`` pairs it produced (admitted
+    requests' first tokens included); ``run`` steps until every request has
+    finished and returns ``{rid: tokens}``.
+
+    ``fuse_prefill``: a step that admits requests runs their prompt rows and
+    the running requests' decode rows in one ``b2d_prefill_rows`` pass (up to
+    512 rows; admission stops at that budget), instead of a prefill pass
+    followed by a decode step.  ``admission``: "reserve" admits a request only
+    while the pool can hold every admitted request at its longest (no
+    preemption); "optimistic" only needs the prompt's pages and one spare page
+    per running request, and preempts when the pool runs dry."""
 
     def __init__(self, engine, max_batch: int, num_blocks: int, eos_id: int | None = None,
-                 hist_cap: int | None = None):
+                 hist_cap: int | None = None, admission: str = "reserve", fuse_prefill: bool = True):
         cfg = engine.cfg
         self.eng = engine
         self.ctx = cfg.context_len
@@ -117,7 +125,10 @@ class ContinuousBatcher:
             raise ValueError(f"max_batch must be in [2, {engine.max_batch}] (the engine's workspace)")
         if num_blocks < self.bps:
             raise ValueError(f"num_blocks must hold one full-context sequence ({self.bps} blocks)")
+        if admission not in ("reserve", "optimistic"):
+            raise ValueError("admission must be 'reserve' or 'optimistic'")
         self.max_batch, self.eos_id = max_batch, eos_id
+        self.admission, self.fuse_prefill = admission, fuse_prefill
         self.pages = PagePool(num_blocks)
         self.pool = engine.new_kv_pool(num_blocks)
         dev = engine.device
@@ -199,13 +210,26 @@ class ContinuousBatcher:
 
     # ---- one scheduling step --------------------------------------------
     def step(self) -> list[tuple[int, int]]:
+        """Admit what fits, then one pass over the weights for every running
+        request (and, with ``fuse_prefill``, the admitted prompts' rows)."""
         events: list[tuple[int, int]] = []
-        self._admit(events)
+        n_run = sum(r is not None for r in self.slots)
+        budget = self._rows_max - n_run if self.fuse_prefill else None
+        fused, dedicated = self._admit(budget)
+        if dedicated:
+            self._prefill(dedicated, events)
         self._reserve_pages()
-        batch = 1 + max((i for i, r in enumerate(self.slots) if r is not None), default=-1)
-        if batch == 0:
-            return events
-        batch = max(batch, 2)  # the batched step takes at least two rows
+        fused = [(r, p) for r, p in fused if r.slot >= 0]  # not preempted since
+        if fused:
+            self._mixed_step(fused, events)
+        elif any(r is not None for r in self.slots):
+            self._decode_step(events)
+        return events
+
+    def _decode_step(self, events) -> None:
+        """b2d_decode_step_paged over slots 0..batch-1 (idle slots as pos = -1
+        rows; the step replays a CUDA graph while its arguments repeat)."""
+        batch = max(2, 1 + max(i for i, r in enumerate(self.slots) if r is not None))
         for i in range(batch):
             r = self.slots[i]
             if r is None:
@@ -222,26 +246,76 @@ class ContinuousBatcher:
         else:
             toks = self._fetch(self._d_next, batch)
         self.stats["steps"] += 1
-        for i in range(batch):
-            r = self.slots[i]
-            if r is None:
-                continue
+        self._emit([(i, r) for i, r in enumerate(self.slots[:batch]) if r is not None], toks, events)
+
+    def _mixed_step(self, fused, events) -> None:
+        """One b2d_prefill_rows pass: the admitted prefixes (body) plus, in the
+        tail, a decode row for every request that has tokens (running and
+        readmitted ones) and the last prompt row of every new request."""
+        toks, poss, slots = [], [], []
+        tail: list[Request] = []
+        t_tok, t_pos, t_slot = [], [], []
+        for r, prefix in fused:
+            n = prefix.size if r.out else prefix.size - 1  # a new request's last row is a tail row
+            toks.append(prefix[:n])
+            poss.append(np.arange(n, dtype=np.int32))
+            slots.append(np.full(n, r.slot, np.int32))
+            if not r.out:
+                tail.append(r)
+                t_tok.append(int(prefix[-1]))
+                t_pos.append(prefix.size - 1)
+                t_slot.append(r.slot)
+        for r in self.slots:
+            if r is not None and r.out:
+                tail.append(r)
+                t_tok.append(r.out[-1])
+                t_pos.append(r.next_pos())
+                t_slot.append(r.slot)
+        tok = np.concatenate(toks + [np.asarray(t_tok, np.int32)])
+        pos = np.concatenate(poss + [np.asarray(t_pos, np.int32)])
+        slot = np.concatenate(slots + [np.asarray(t_slot, np.int32)])
+        n, n_out = tok.size, len(tail)
+        assert n <= self._rows_max
+        self._hp_tok[:n] = tok
+        self._hp_pos[:n] = pos
+        self._hp_table[:n] = self._h_table[slot]
+        self._dp_stage.copy_(self._hp_stage, non_blocking=self._cuda)
+        sampled = any(not q.greedy for q in tail)
+        logits = self._logits_buf() if sampled else None
+        self.eng.prefill_rows(self._dp_tok, self._dp_pos, self.pool, self._dp_table, n_out,
+                              logits=logits, next_tok=self._dp_next, n_rows=n)
+        out = self._sample_rows(logits, tail, self._dp_next) if sampled else self._fetch(self._dp_next, n_out)
+        self.stats["steps"] += 1
+        self.stats["mixed_steps"] += 1
+        self.stats["prefill_rows"] += n - n_out + sum(1 for r, _ in fused if not r.out)
+        self._emit(list(enumerate(tail)), out, events)
+
+    def _emit(self, rows, toks, events) -> None:
+        for i, r in rows:
             t = int(toks[i])
             r.out.append(t)
             events.append((r.rid, t))
             self.stats["tokens"] += 1
             self._maybe_finish(r)
-        return events
 
-    def _admit(self, events) -> None:
-        admitted = []
+    def _admit(self, budget):
+        """Admit waiting requests in order while a slot and the pages for their
+        prefix (plus, for a readmitted request, its next position) are free,
+        and, when ``budget`` (rows of this step's fused pass) is not None,
+        while their rows fit it.  Returns (fused, dedicated): the admissions
+        for the fused pass, and those prefilled on their own (a prefix longer
+        than one pass, or fusing off)."""
+        fused, dedicated = [], []
         while self.waiting and None in self.slots:
             r = self.waiting[0]
             prefix = self._prefix(r)
-            need = (prefix.size + PAGE_TOKENS - 1) // PAGE_TOKENS
-            # keep one page of headroom for the running requests' next positions
-            headroom = 1 if any(s is not None for s in self.slots) else 0
-            if need + headroom > self.pages.n_free:
+            rows = prefix.size + (1 if r.out else 0)  # a readmitted request's decode row joins the pass
+            need = (rows + PAGE_TOKENS - 1) // PAGE_TOKENS
+            if not self._pages_allow(r, need):
+                break
+            own = budget is None or rows > self._rows_max
+            cost = 1 if own else rows  # rows it adds to this step's fused pass (own prefill: its decode row)
+            if budget is not None and cost > budget:
                 break
             self.waiting.popleft()
             slot = self.slots.index(None)
@@ -252,9 +326,25 @@ class ContinuousBatcher:
             self.slots[slot] = r
             self._h_table[slot, :] = 0
             self._h_table[slot, :need] = r.blocks
-            admitted.append((r, prefix))
-        if admitted:
-            self._prefill(admitted, events)
+            (dedicated if own else fused).append((r, prefix))
+            if budget is not None:
+                budget -= cost
+        return fused, dedicated
+
+    def _max_pages(self, r: Request) -> int:
+        return (len(r.prompt) + r.max_tokens - 1 + PAGE_TOKENS - 1) // PAGE_TOKENS
+
+    def _pages_allow(self, r: Request, need: int) -> bool:
+        """admission = "reserve": the pool must hold every running request and
+        this one at their longest (prompt + max_tokens - 1 positions), so no
+        request is ever preempted.  "optimistic": the prefix's pages plus one
+        free page per running request; the pool may run dry later, and then the
+        latest admissions are preempted."""
+        running = [q for q in self.slots if q is not None]
+        if self.admission == "reserve":
+            owed = sum(self._max_pages(q) - len(q.blocks) for q in running)
+            return self._max_pages(r) + owed <= self.pages.n_free
+        return need + len(running) <= self.pages.n_free or (not running and need <= self.pages.n_free)
 
     @staticmethod
     def _prefix(r: Request) -> np.ndarray:
