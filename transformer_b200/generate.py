@@ -11,9 +11,11 @@ Mirrors the reference's ``generate.py``:
   ``pos = prompt_len + i``; greedy (temperature 0 and no penalty) uses the
   kernel's argmax, everything else the sampler with the generated history.
 
-The prompt is ingested by the decode kernel itself, one position per launch
-(the reference prefills with JAX, ``model.py:194-231``; a device prefill is a
-separate, later component).
+The prompt goes through the device prefill (``b2d_prefill``: every prompt
+position in one pass of the batched tensor-core step, K/V written into the
+reference-layout cache), where the reference prefills with JAX
+(``model.py:194-231``).  For many concurrent requests see
+``transformer_b200.serve``.
 """
 
 from __future__ import annotations
