@@ -178,6 +178,7 @@ def profile_serve(w, cfg, args, torch):
         cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), 8)
     cb.run()
     cb.stats.clear()
+    cb.times.clear()
     gens = rng.integers(args.gen_min, args.gen_max + 1, args.requests)
     rids = [cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), int(g)) for g in gens]
     torch.cuda.synchronize()
@@ -196,7 +197,8 @@ def profile_serve(w, cfg, args, torch):
             "mean_rows_per_step": (n_tok - args.requests) / max(1, st.get("steps", 1)),
             "prefill_calls": st.get("prefill_calls", 0), "prefill_rows": st.get("prefill_rows", 0),
             "mixed_steps": st.get("mixed_steps", 0), "preemptions": st.get("preemptions", 0),
-            "admission": args.admission, "fuse_prefill": not args.no_fuse}
+            "admission": args.admission, "fuse_prefill": not args.no_fuse,
+            "seconds_by_pass": {k: round(v, 4) for k, v in cb.times.items()}}
 
 
 def main():

@@ -32,6 +32,7 @@ from __future__ import annotations
 
 import collections
 import dataclasses
+import time
 
 import numpy as np
 import torch
@@ -170,6 +171,7 @@ class ContinuousBatcher:
         self._sampler = None
         self._logits = None
         self.stats = collections.Counter()
+        self.times = collections.Counter()  # wall seconds per pass kind (each pass ends with a token read-back)
 
     # ---- requests --------------------------------------------------------
     def submit(self, prompt, max_tokens: int, temperature: float = 0.0, top_p: float = 1.0,
@@ -217,13 +219,18 @@ class ContinuousBatcher:
         budget = self._rows_max - n_run if self.fuse_prefill else None
         fused, dedicated = self._admit(budget)
         if dedicated:
+            t0 = time.perf_counter()
             self._prefill(dedicated, events)
+            self.times["prefill"] += time.perf_counter() - t0
         self._reserve_pages()
         fused = [(r, p) for r, p in fused if r.slot >= 0]  # not preempted since
+        t0 = time.perf_counter()
         if fused:
             self._mixed_step(fused, events)
+            self.times["mixed"] += time.perf_counter() - t0
         elif any(r is not None for r in self.slots):
             self._decode_step(events)
+            self.times["decode"] += time.perf_counter() - t0
         return events
 
     def _decode_step(self, events) -> None:
@@ -446,7 +453,9 @@ class ContinuousBatcher:
         h = self._h_next[:n]
         h.copy_(d[:n], non_blocking=self._cuda)
         if self._cuda:
+            t0 = time.perf_counter()
             torch.cuda.current_stream(self.eng.device).synchronize()
+            self.times["gpu_wait"] += time.perf_counter() - t0
         return h.numpy().copy()
 
     def _logits_buf(self) -> torch.Tensor:
