@@ -173,7 +173,8 @@ def profile_serve(w, cfg, args, torch):
     rng = np.random.default_rng(5)
     longest = args.prompt_len + args.gen_max - 1
     nb = args.num_blocks or args.batch * ((longest + PAGE_TOKENS - 1) // PAGE_TOKENS)
-    cb = ContinuousBatcher(eng, args.batch, nb, admission=args.admission, fuse_prefill=not args.no_fuse)
+    cb = ContinuousBatcher(eng, args.batch, nb, admission=args.admission, fuse_prefill=not args.no_fuse,
+                           pipeline=not args.no_pipeline, admit_batch=args.admit_batch or None)
     for _ in range(args.batch):
         cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), 8)
     cb.run()
@@ -196,8 +197,9 @@ def profile_serve(w, cfg, args, torch):
             "prompt_tok_s": args.requests * args.prompt_len / dt, "steps": st.get("steps", 0),
             "mean_rows_per_step": (n_tok - args.requests) / max(1, st.get("steps", 1)),
             "prefill_calls": st.get("prefill_calls", 0), "prefill_rows": st.get("prefill_rows", 0),
-            "mixed_steps": st.get("mixed_steps", 0), "preemptions": st.get("preemptions", 0),
-            "admission": args.admission, "fuse_prefill": not args.no_fuse,
+            "mixed_steps": st.get("mixed_steps", 0), "pipelined_steps": st.get("pipelined_steps", 0),
+            "preemptions": st.get("preemptions", 0), "admission": args.admission,
+            "fuse_prefill": not args.no_fuse, "pipeline": not args.no_pipeline, "admit_batch": cb.admit_batch,
             "seconds_by_pass": {k: round(v, 4) for k, v in cb.times.items()}}
 
 
@@ -211,6 +213,8 @@ def main():
     ap.add_argument("--num-blocks", type=int, default=0)
     ap.add_argument("--admission", choices=["reserve", "optimistic"], default="reserve")
     ap.add_argument("--no-fuse", action="store_true", help="prefill admitted prompts in passes of their own")
+    ap.add_argument("--no-pipeline", action="store_true", help="read every decode step's tokens before the next")
+    ap.add_argument("--admit-batch", type=int, default=0, help="free slots that trigger an admission (0: default)")
     ap.add_argument("--gen-len", type=int, default=128)
     ap.add_argument("--n-runs", type=int, default=10)
     ap.add_argument("--batch", type=int, default=64)

@@ -93,6 +93,8 @@ class FakeEngine:
             p = int(pos[b])
             if p >= 0:
                 next_tok[b] = self._next(pool, block_table[b].tolist(), p)
+            else:  # the device argmax also writes idle rows: a wrong token there
+                next_tok[b] = (7 * b + 3) % self.cfg.vocab_size
 
 
 def test_page_pool():
@@ -111,18 +113,20 @@ def test_page_pool():
     assert sorted(b) == [1, 3, 4] and pp.n_free == 0
 
 
+@pytest.mark.parametrize("pipe", [True, False])
 @pytest.mark.parametrize("fuse", [True, False])
 @pytest.mark.parametrize("seed,num_blocks,admission", [(0, 4, "optimistic"), (1, 6, "optimistic"),
                                                        (2, 9, "optimistic"), (3, 40, "optimistic"),
                                                        (4, 6, "reserve"), (5, 9, "reserve")])
-def test_batcher_matches_sequential(seed, num_blocks, admission, fuse):
+def test_batcher_matches_sequential(seed, num_blocks, admission, fuse, pipe):
     """Requests of random lengths through 4 slots: every token stream equals
     the one-at-a-time generation, prompts prefilled in fused passes or on
-    their own; small pools force preemptions under optimistic admission and
-    none under reserving admission."""
+    their own, decode steps pipelined (tokens fed back on the device) or not;
+    small pools force preemptions under optimistic admission and none under
+    reserving admission."""
     rng = np.random.default_rng(seed)
     eng = FakeEngine(ctx=64, vocab=97, max_batch=4, rows_max=64)
-    cb = ContinuousBatcher(eng, 4, num_blocks, admission=admission, fuse_prefill=fuse)
+    cb = ContinuousBatcher(eng, 4, num_blocks, admission=admission, fuse_prefill=fuse, pipeline=pipe)
     want = {}
     for _ in range(14):
         n_prompt = int(rng.integers(1, 48))
@@ -142,6 +146,7 @@ def test_batcher_matches_sequential(seed, num_blocks, admission, fuse):
     if num_blocks == 40:  # room for every slot: several rows per pass on average
         assert cb.stats["preemptions"] == 0 and cb.stats["tokens"] > 2 * cb.stats["steps"]
     assert (cb.stats["mixed_steps"] > 0) == fuse
+    assert (cb.stats["pipelined_steps"] > 0) == pipe
 
 
 def test_batcher_events_and_eos():

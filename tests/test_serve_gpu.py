@@ -163,18 +163,20 @@ def _teacher_forced_greedy(P, cfg, prompt, out):
     return checked
 
 
-@pytest.mark.parametrize("fuse", [True, False])
-def test_batcher_greedy_tiny_vs_oracle(engine_tiny_batched, params_tiny, fuse):
+@pytest.mark.parametrize("fuse,pipe", [(True, True), (False, True), (True, False)])
+def test_batcher_greedy_tiny_vs_oracle(engine_tiny_batched, params_tiny, fuse, pipe):
     """12 requests through 4 slots over an 11-block pool (one 128-position
     context is 8 blocks), optimistic admission: slots refill as requests
     finish and requests are preempted and readmitted; prompts prefilled in
-    fused passes with the decode rows, or on their own.  Every stream is
+    fused passes with the decode rows, or on their own; decode steps
+    pipelined (tokens fed back on the device) or not.  Every stream is
     checked against the oracle."""
     from transformer_b200.config import CONFIG_TINY as cfg
     from transformer_b200.synth import params_f32
     P = params_f32(params_tiny)
     rng = np.random.default_rng(21)
-    cb = ContinuousBatcher(engine_tiny_batched, 4, 11, admission="optimistic", fuse_prefill=fuse)
+    cb = ContinuousBatcher(engine_tiny_batched, 4, 11, admission="optimistic", fuse_prefill=fuse,
+                           pipeline=pipe)
     prompts = {}
     for _ in range(12):
         n = int(rng.integers(1, 90))
@@ -184,6 +186,7 @@ def test_batcher_greedy_tiny_vs_oracle(engine_tiny_batched, params_tiny, fuse):
     got = cb.run()
     engine_tiny_batched.check_device()
     assert cb.stats["preemptions"] > 0 and cb.pages.n_free == 11
+    assert (cb.stats["pipelined_steps"] > 0) == pipe
     checked = 0
     for rid, (pr, g) in prompts.items():
         assert len(got[rid]) == g

@@ -89,6 +89,7 @@ class Request:
     slot: int = -1
     admitted: int = -1       # admission order (the preemption victim is the latest)
     preemptions: int = 0
+    fed: int = 0             # decode rows issued (the first token comes from the prompt's last row)
     rng: object = None
 
     @property
@@ -96,8 +97,8 @@ class Request:
         return self.temperature == 0.0 and self.rep_penalty == 1.0
 
     def next_pos(self) -> int:
-        """Position of the token fed at this request's next decode step."""
-        return len(self.prompt) + len(self.out) - 1
+        """Position of the token fed at this request's next decode row."""
+        return len(self.prompt) + self.fed
 
 
 class ContinuousBatcher:
@@ -116,7 +117,8 @@ class ContinuousBatcher:
     per running request, and preempts when the pool runs dry."""
 
     def __init__(self, engine, max_batch: int, num_blocks: int, eos_id: int | None = None,
-                 hist_cap: int | None = None, admission: str = "reserve", fuse_prefill: bool = True):
+                 hist_cap: int | None = None, admission: str = "reserve", fuse_prefill: bool = True,
+                 pipeline: bool = True, admit_batch: int | None = None):
         cfg = engine.cfg
         self.eng = engine
         self.ctx = cfg.context_len
@@ -129,7 +131,8 @@ class ContinuousBatcher:
         if admission not in ("reserve", "optimistic"):
             raise ValueError("admission must be 'reserve' or 'optimistic'")
         self.max_batch, self.eos_id = max_batch, eos_id
-        self.admission, self.fuse_prefill = admission, fuse_prefill
+        self.admission, self.fuse_prefill, self.pipeline = admission, fuse_prefill, pipeline
+        self.admit_batch = admit_batch or max(1, max_batch // 32)
         self.pages = PagePool(num_blocks)
         self.pool = engine.new_kv_pool(num_blocks)
         dev = engine.device
@@ -162,6 +165,20 @@ class ContinuousBatcher:
         self._h_next = torch.zeros(self._logits_rows, dtype=torch.int32, pin_memory=pin)
         self._h_table[:] = 0
         self._h_pos[:] = -1
+        # pipelined decode steps: each slot's latest token stays on the device (the
+        # step reads and overwrites it); positions and table rows go through two
+        # pinned staging buffers, the tokens come back through two more
+        self._d_slot_tok = torch.zeros(max_batch, dtype=torch.int32, device=dev)
+        self._dq_stage = torch.zeros(max_batch + max_batch * self.bps, dtype=torch.int32, device=dev)
+        self._dq_pos = self._dq_stage[:max_batch]
+        self._dq_table = self._dq_stage[max_batch:].view(max_batch, self.bps)
+        self._hq_stage = [torch.zeros(max_batch + max_batch * self.bps, dtype=torch.int32, pin_memory=pin)
+                          for _ in range(2)]
+        self._hq_out = [torch.zeros(max_batch, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._hq_event = [torch.cuda.Event() for _ in range(2)] if self._cuda else [None, None]
+        self._ring = 0
+        self._inflight = None      # (ring index, [(slot, request)]) of the step whose tokens are unread
+        self._tok_dirty = True     # slots' latest tokens known only on the host
         self.slots: list[Request | None] = [None] * max_batch
         self.waiting: collections.deque[Request] = collections.deque()
         self.finished: dict[int, list] = {}
@@ -203,7 +220,7 @@ class ContinuousBatcher:
         return [r for r in self.slots if r is not None]
 
     def idle(self) -> bool:
-        return not self.waiting and all(r is None for r in self.slots)
+        return not self.waiting and self._inflight is None and all(r is None for r in self.slots)
 
     def run(self) -> dict[int, list]:
         while not self.idle():
@@ -213,8 +230,26 @@ class ContinuousBatcher:
     # ---- one scheduling step --------------------------------------------
     def step(self) -> list[tuple[int, int]]:
         """Admit what fits, then one pass over the weights for every running
-        request (and, with ``fuse_prefill``, the admitted prompts' rows)."""
+        request (and, with ``fuse_prefill``, the admitted prompts' rows).
+
+        With ``pipeline``, a decode step of greedy requests is issued without
+        waiting for its tokens: the next call issues the following step (the
+        tokens feed back on the device) before reading them, so the host's
+        scheduling overlaps the GPU.  Admissions, sampling, preemption and a
+        pool without a free page for every next position drain the pipeline
+        first."""
         events: list[tuple[int, int]] = []
+        if self._inflight is not None:
+            t0 = time.perf_counter()
+            if self._can_continue():
+                prev = self._inflight
+                self._issue_decode()
+                self._consume(prev, events)
+                self.times["decode"] += time.perf_counter() - t0
+                return events
+            prev, self._inflight = self._inflight, None
+            self._consume(prev, events)
+            self.times["decode"] += time.perf_counter() - t0
         n_run = sum(r is not None for r in self.slots)
         budget = self._rows_max - n_run if self.fuse_prefill else None
         fused, dedicated = self._admit(budget)
@@ -229,9 +264,100 @@ class ContinuousBatcher:
             self._mixed_step(fused, events)
             self.times["mixed"] += time.perf_counter() - t0
         elif any(r is not None for r in self.slots):
-            self._decode_step(events)
+            if self._pipelinable():
+                self._issue_decode()
+            else:
+                self._decode_step(events)
             self.times["decode"] += time.perf_counter() - t0
         return events
+
+    # ---- pipelined decode steps -----------------------------------------
+    def _pipelinable(self) -> bool:
+        return self.pipeline and all(r is None or r.greedy for r in self.slots)
+
+    def _admit_threshold(self) -> int:
+        """Free slots that trigger an admission: a few at a time while requests
+        run (each admission is a pass of its own and drains the pipeline)."""
+        if all(r is None for r in self.slots):
+            return 1
+        return max(1, min(self.admit_batch, len(self.waiting)))
+
+    def _can_continue(self) -> bool:
+        """Another decode step can be issued before the in-flight one's tokens
+        are read: every request is greedy, one has rows left, no admission is
+        due once the in-flight step's last tokens finish their requests, and a
+        free page exists for every next position that starts one."""
+        if not self._pipelinable():
+            return False
+        running = [r for r in self.slots if r is not None]
+        issuing = [r for r in running if r.fed < r.max_tokens - 1]
+        if not issuing:
+            return False
+        if self.waiting:
+            free_after = self.slots.count(None) + (len(running) - len(issuing))
+            if free_after >= self._admit_threshold():
+                return False
+        need = sum(1 for r in issuing if r.next_pos() // PAGE_TOKENS >= len(r.blocks))
+        return need <= self.pages.n_free
+
+    def _issue_decode(self) -> None:
+        """Launch one decode step over the slots whose requests have rows left
+        (tokens: each slot's latest, on the device), its tokens copied back
+        asynchronously."""
+        if self._tok_dirty:
+            h = np.zeros(self.max_batch, np.int32)
+            for i, r in enumerate(self.slots):
+                if r is not None and r.out:
+                    h[i] = r.out[-1]
+            self._d_slot_tok.copy_(torch.from_numpy(h))
+            self._tok_dirty = False
+        k = self._ring
+        self._ring ^= 1
+        hq = self._hq_stage[k].numpy()
+        pos = hq[:self.max_batch]
+        table = hq[self.max_batch:].reshape(self.max_batch, self.bps)
+        rows, batch = [], 2
+        for i, r in enumerate(self.slots):
+            if r is None or r.fed >= r.max_tokens - 1:
+                pos[i] = -1
+                continue
+            p = r.next_pos()
+            if p // PAGE_TOKENS >= len(r.blocks):  # free pages were checked by the caller
+                b = self.pages.alloc(1)[0]
+                self._h_table[i, len(r.blocks)] = b
+                r.blocks.append(b)
+            pos[i] = p
+            r.fed += 1
+            rows.append((i, r))
+            batch = max(batch, i + 1)
+        table[:batch] = self._h_table[:batch]
+        n = self.max_batch + batch * self.bps
+        self._dq_stage[:n].copy_(self._hq_stage[k][:n], non_blocking=self._cuda)
+        self.eng.step_paged(self._d_slot_tok, self._dq_pos, self.pool, self._dq_table, None, self._d_slot_tok,
+                            batch=batch)
+        self._hq_out[k][:batch].copy_(self._d_slot_tok[:batch], non_blocking=self._cuda)
+        if self._cuda:
+            self._hq_event[k].record()
+        self._inflight = (k, rows)
+        self.stats["steps"] += 1
+        self.stats["pipelined_steps"] += 1
+
+    def _consume(self, inflight, events) -> None:
+        """Read an issued step's tokens (waiting for that step only)."""
+        k, rows = inflight
+        if self._cuda:
+            t0 = time.perf_counter()
+            self._hq_event[k].synchronize()
+            self.times["gpu_wait"] += time.perf_counter() - t0
+        toks = self._hq_out[k].numpy()
+        for i, r in rows:
+            if r.slot != i:  # finished (end of sequence) while this step was in flight
+                continue
+            t = int(toks[i])
+            r.out.append(t)
+            events.append((r.rid, t))
+            self.stats["tokens"] += 1
+            self._maybe_finish(r)
 
     def _decode_step(self, events) -> None:
         """b2d_decode_step_paged over slots 0..batch-1 (idle slots as pos = -1
@@ -243,6 +369,7 @@ class ContinuousBatcher:
                 self._h_tok[i], self._h_pos[i] = 0, -1
             else:
                 self._h_tok[i], self._h_pos[i] = r.out[-1], r.next_pos()
+                r.fed += 1
         self._d_stage.copy_(self._h_stage, non_blocking=self._cuda)
         need_logits = any(r is not None and not r.greedy for r in self.slots[:batch])
         logits = self._logits_buf() if need_logits else None
@@ -278,6 +405,7 @@ class ContinuousBatcher:
                 t_tok.append(r.out[-1])
                 t_pos.append(r.next_pos())
                 t_slot.append(r.slot)
+                r.fed += 1
         tok = np.concatenate(toks + [np.asarray(t_tok, np.int32)])
         pos = np.concatenate(poss + [np.asarray(t_pos, np.int32)])
         slot = np.concatenate(slots + [np.asarray(t_slot, np.int32)])
@@ -298,6 +426,7 @@ class ContinuousBatcher:
         self._emit(list(enumerate(tail)), out, events)
 
     def _emit(self, rows, toks, events) -> None:
+        self._tok_dirty = True
         for i, r in rows:
             t = int(toks[i])
             r.out.append(t)
@@ -313,6 +442,8 @@ class ContinuousBatcher:
         for the fused pass, and those prefilled on their own (a prefix longer
         than one pass, or fusing off)."""
         fused, dedicated = [], []
+        if self.slots.count(None) < self._admit_threshold():
+            return fused, dedicated
         while self.waiting and None in self.slots:
             r = self.waiting[0]
             prefix = self._prefix(r)
@@ -331,6 +462,7 @@ class ContinuousBatcher:
             r.admitted = self._admit_tick
             self._admit_tick += 1
             self.slots[slot] = r
+            self._tok_dirty = True  # the slot's device token belongs to its previous request
             self._h_table[slot, :] = 0
             self._h_table[slot, :need] = r.blocks
             (dedicated if own else fused).append((r, prefix))
@@ -434,6 +566,7 @@ class ContinuousBatcher:
         self.slots[r.slot] = None
         self._h_table[r.slot, :] = 0
         r.slot = -1
+        r.fed = len(r.out) - 1  # no step is in flight here: every issued row has its token
         r.preemptions += 1
         self.stats["preemptions"] += 1
         self.waiting.appendleft(r)
