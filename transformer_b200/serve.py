@@ -296,7 +296,10 @@ class ContinuousBatcher:
         if self.waiting:
             free_after = self.slots.count(None) + (len(running) - len(issuing))
             if free_after >= self._admit_threshold():
-                return False
+                head = self.waiting[0]  # drain only for an admission the pool can take
+                rows = self._prefix(head).size + (1 if head.out else 0)
+                if self._pages_allow(head, (rows + PAGE_TOKENS - 1) // PAGE_TOKENS):
+                    return False
         need = sum(1 for r in issuing if r.next_pos() // PAGE_TOKENS >= len(r.blocks))
         return need <= self.pages.n_free
 
