@@ -12,6 +12,9 @@ arguments and results (``profile_kernels.py:44-87``): a host loop of
 uses this engine's algorithmic bytes (weights once, the KV rows actually read,
 one row written) and the measured HBM copy bandwidth.
 
+``--mode mixed`` times one fused pass of the batcher (decode rows plus prompt
+rows in one ``b2d_prefill_rows`` call), the small case for its ncu captures.
+
 ``--mode serve`` runs the continuous batcher (``transformer_b200.serve``) on
 a stream of requests and reports generated tokens per second, wall-clock.
 
@@ -159,6 +162,56 @@ def profile_paged(w, cfg, args, torch):
             "hbm_frac": alg / (us * 1e-6) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
 
+def profile_mixed(w, cfg, args, torch):
+    """One fused pass of the continuous batcher, timed alone: ``--batch``
+    decode rows at position ``--pos`` plus ``--prompts`` prompts of
+    ``--prompt-len`` rows, one ``b2d_prefill_rows`` call, eager launches
+    (``--warmup`` + ``--steps`` times; each pass rewrites the same cache
+    rows, so every pass does the same work)."""
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    from transformer_b200.serve import PAGE_TOKENS
+    eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    bps = (cfg.context_len + PAGE_TOKENS - 1) // PAGE_TOKENS
+    n_seq = args.batch + args.prompts
+    npg = max(args.pos // PAGE_TOKENS + 1, (args.prompt_len + PAGE_TOKENS - 1) // PAGE_TOKENS)
+    pool = eng.new_kv_pool(n_seq * npg)  # only the pages the rows reach
+    rng = np.random.default_rng(7)
+    table = np.zeros((n_seq, bps), np.int32)
+    table[:, :npg] = rng.permutation(n_seq * npg).astype(np.int32).reshape(n_seq, npg)
+    tok, pos, tab = [], [], []
+    for j in range(args.prompts):  # prompt rows but the last (body)
+        s_ = args.batch + j
+        tok += list(rng.integers(0, cfg.vocab_size, args.prompt_len - 1))
+        pos += list(range(args.prompt_len - 1))
+        tab += [table[s_]] * (args.prompt_len - 1)
+    for b in range(args.batch):  # decode rows (tail)
+        tok.append(int(rng.integers(0, cfg.vocab_size)))
+        pos.append(args.pos)
+        tab.append(table[b])
+    for j in range(args.prompts):  # each prompt's last row (tail)
+        tok.append(int(rng.integers(0, cfg.vocab_size)))
+        pos.append(args.prompt_len - 1)
+        tab.append(table[args.batch + j])
+    n, n_out = len(tok), args.batch + args.prompts
+    d_tok = torch.tensor(tok, dtype=torch.int32, device="cuda")
+    d_pos = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    d_tab = torch.from_numpy(np.stack(tab)).to("cuda")
+    nxt = torch.zeros(n_out, dtype=torch.int32, device="cuda")
+    for _ in range(args.warmup):
+        eng.prefill_rows(d_tok, d_pos, pool, d_tab, n_out, next_tok=nxt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        eng.prefill_rows(d_tok, d_pos, pool, d_tab, n_out, next_tok=nxt)
+    e1.record()
+    torch.cuda.synchronize()
+    eng.check_device()
+    us = e0.elapsed_time(e1) * 1000 / args.steps
+    return {"mode": "mixed", "rows": n, "decode_rows": args.batch, "pos": args.pos, "prompts": args.prompts,
+            "prompt_len": args.prompt_len, "us_per_pass": us, "launches": eng.lib.b2d_batched_launches(eng.ws)}
+
+
 def profile_serve(w, cfg, args, torch):
     """Continuous batching (``transformer_b200.serve``): ``--requests``
     greedy requests with ``--prompt-len``-token prompts and generation lengths
@@ -205,7 +258,8 @@ def profile_serve(w, cfg, args, torch):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["b1", "paged", "serve"], default="b1")
+    ap.add_argument("--mode", choices=["b1", "paged", "serve", "mixed"], default="b1")
+    ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--requests", type=int, default=1024)
     ap.add_argument("--prompt-len", type=int, default=64)
     ap.add_argument("--gen-min", type=int, default=32)
@@ -237,7 +291,7 @@ def main():
         params = synth_params(cfg, 0)
     w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
     out = {"memory": compute_memory_stats(cfg)}
-    prof = {"b1": profile_b1, "paged": profile_paged, "serve": profile_serve}[args.mode]
+    prof = {"b1": profile_b1, "paged": profile_paged, "serve": profile_serve, "mixed": profile_mixed}[args.mode]
     out.update(prof(w, cfg, args, torch))
     print(json.dumps(out))
     return 0
