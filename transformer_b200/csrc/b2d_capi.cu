@@ -702,15 +702,14 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   // (qkv, gate/up, logits) scales its result columns by rsqrt(mean + eps).
   for (int l = 0; l < c.n_layers; ++l) {
     // X = bf16(H * ln1[l]) and its statistics come from the embedding (l = 0) or the previous down projection
+    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q;
+    g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
+    B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
     pa.layer = l;
     pa.trace = ws->att_trace ? ws->att_trace + size_t(l) * kAttTraceUnits * 8 : nullptr;
     pa.trace_units = kAttTraceUnits;
-    g.M = Q; g.K = D; g.y = ws->qkv; g.resid = nullptr; g.ldy = Q;
-    g.ss_in = ws->ss; g.xg_out = nullptr; g.xg_gain = nullptr; g.ss_out = nullptr;
-    g.kv = pa;
-    g.kv_write = prefill;  // a prefill's rows: every row's K/V in the cache before any row attends
-    B2D_CUDA(gemm(m->wmaps[4 * l + 0], ws->xmap, b2d::EPI_F32, p_qkv), "qkv");
-    g.kv_write = 0;
+    if (prefill)  // every row's K/V in the cache before any row attends
+      B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
     if (att_w == 2)
       B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<2>, dim3((att_units + 1) / 2), dim3(64),
                              2 * b2d::kPaWarpSmem, st, pdl, pa, batch),
@@ -719,7 +718,7 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
       B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<4>, dim3((att_units + 3) / 4), dim3(128),
                              4 * b2d::kPaWarpSmem, st, pdl, pa, batch),
                "attention");
-    ++launches_other;
+    launches_other += prefill ? 2 : 1;
     g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;
     g.ss_in = nullptr; g.xg_out = ws->X; g.xg_gain = ln2 + size_t(l) * D; g.ss_out = ws->ss;
     B2D_CUDA(gemm(m->wmaps[4 * l + 1], ws->amap, b2d::EPI_RESID_F32, p_o), "o");

@@ -93,6 +93,39 @@ __device__ __forceinline__ __nv_bfloat16* kv_row(const PagedAttnArgs& a, const i
                        kPageTokens + pos % kPageTokens) * 64;
 }
 
+// Writes row b's K (post-RoPE) / V for kv head blockIdx.y at position pos[b]
+// (bf16, as cached).  grid (rows, n_kv), 32 threads.  Used before a prefill
+// launch of the attention (append = false) so that every row's K/V is in the
+// cache before any row attends.  Positions out of range / idle rows: skipped.
+__global__ void __launch_bounds__(32) kv_append_kernel(const __grid_constant__ PagedAttnArgs a) {
+  pdl_wait();
+  pdl_launch();
+  const int b = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
+  const int p = a.pos[b];
+  if (p < 0 || p >= a.ctx) return;
+  const int32_t* tb = a.table ? a.table + static_cast<size_t>(b) * a.table_ld : nullptr;
+  if (tb != nullptr) {
+    if (p / kPageTokens >= a.bps) return;
+    const int e = tb[p / kPageTokens];
+    if (e < 0 || e >= a.num_blocks) {
+      if (lane == 0) atomicCAS(a.status, 0u, 0x203u);
+      return;
+    }
+  }
+  const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
+  const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
+  const float* k = row + a.n_heads * 64 + g * 64;
+  const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
+  const float klo = k[lane], khi = k[lane + 32];
+  __nv_bfloat16* kd = kv_row(a, tb, p, 0, g);
+  __nv_bfloat16* vd = kv_row(a, tb, p, 1, g);
+  kd[lane] = __float2bfloat16_rn(klo * cs - khi * sn);
+  kd[lane + 32] = __float2bfloat16_rn(klo * sn + khi * cs);
+  vd[lane] = __float2bfloat16_rn(v[lane]);
+  vd[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
+}
+
+
 // next[b] = first index of the maximum of logits[b][0..V)  (one CTA per row)
 __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int ldl, int32_t* __restrict__ next) {
   __shared__ float rv[32];

@@ -27,7 +27,6 @@
 
 #include <cuda_bf16.h>
 
-#include "batched.cuh"
 #include "tc_ptx.cuh"
 
 namespace b2d {
@@ -65,11 +64,6 @@ struct GemmArgs {
   // diagnostics: global-timer stamps [cta][kGemmStamps] (CTAs >= trace_ctas skipped), or nullptr
   uint64_t* trace = nullptr;
   int trace_ctas = 0;
-  // Prefill (EPI_F32 qkv projection, kv_write != 0): after its stores, each
-  // CTA writes the K (post-RoPE) and V of its columns into the cache `kv`
-  // addresses, so every row's K/V is in the cache before the attention kernel.
-  PagedAttnArgs kv{};
-  int kv_write = 0;
 };
 
 // Stamp slots: 0 entry, 1 prologue done, 2 producer past the programmatic
@@ -123,49 +117,6 @@ __device__ __forceinline__ void gemm_store4(const GemmArgs& g, float4 v, int row
         __floats2bfloat162_rn(a0, a1);
   } else {
     *reinterpret_cast<float4*>(g.y + static_cast<size_t>(n) * g.ldy + row) = v;
-  }
-}
-
-// Prefill K/V append from the qkv projection's epilogue: the CTA has stored
-// the f32 rows of its columns j0..j1 for the tile's 128 features; after a
-// barrier its warps read the K and V head blocks back (64 features each, two
-// per tile, one warp per head block and column) and write them to the cache:
-// K rotated (model.py:110-117 rotate-half, f32 tables), both bf16 as cached
-// (model.py:194-231).  Positions out of range skip the row; a block-table
-// entry out of range sets the status.
-__device__ __noinline__ void gemm_kv_write(const GemmArgs& g, int m0, int n0, int j0, int j1, int warp, int lane,
-                                           bool got) {
-  __syncthreads();  // every thread arrives (got is per warp); the CTA's stores above are visible to all its threads
-  if (!got) return;
-  const PagedAttnArgs& a = g.kv;
-  const int kb = a.n_heads * 64, vb = (a.n_heads + a.n_kv) * 64, ve = vb + a.n_kv * 64;
-  if (m0 + kGemmBM <= kb || m0 >= ve) return;  // no K / V features in this tile
-  for (int u = warp; u < (j1 - j0) * 2; u += kGemmThreads / 32) {
-    const int n = n0 + j0 + u / 2, hb = m0 + 64 * (u % 2);  // output row, head block's first feature
-    if (n >= g.N || hb < kb || hb >= ve) continue;
-    const int p = a.pos[n];
-    if (p < 0 || p >= a.ctx) continue;
-    const int32_t* tb = a.table ? a.table + static_cast<size_t>(n) * a.table_ld : nullptr;
-    if (tb != nullptr) {
-      if (p / kPageTokens >= a.bps) continue;
-      const int e = tb[p / kPageTokens];
-      if (e < 0 || e >= a.num_blocks) {
-        if (lane == 0) atomicCAS(a.status, 0u, 0x203u);
-        continue;
-      }
-    }
-    const float* row = g.y + static_cast<size_t>(n) * g.ldy + hb;
-    const float lo = __ldcg(row + lane), hi = __ldcg(row + lane + 32);
-    if (hb < vb) {
-      const float cs = a.rcos[static_cast<size_t>(p) * 32 + lane], sn = a.rsin[static_cast<size_t>(p) * 32 + lane];
-      __nv_bfloat16* kd = kv_row(a, tb, p, 0, (hb - kb) / 64);
-      kd[lane] = __float2bfloat16_rn(lo * cs - hi * sn);
-      kd[lane + 32] = __float2bfloat16_rn(lo * sn + hi * cs);
-    } else {
-      __nv_bfloat16* vd = kv_row(a, tb, p, 1, (hb - vb) / 64);
-      vd[lane] = __float2bfloat16_rn(lo);
-      vd[lane + 32] = __float2bfloat16_rn(hi);
-    }
   }
 }
 
@@ -396,7 +347,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
     }
   }
   if (ks > 1) cluster_sync_all();  // no CTA leaves while another still reads its partial
-  if (EPI == EPI_F32 && g.kv_write != 0) gemm_kv_write(g, m0, n0, j0, j1, warp, lane, got);
   if (threadIdx.x == 0) gemm_stamp(g, 6);
   if (warp == 0 && lane == 0) {  // timeout paths: wait (bounded) for copies never consumed
     for (int i = issued > S ? issued - S : 0; i < issued; ++i) gemm_wait(&full[i % S], (i / S) & 1u, g.err);
