@@ -86,6 +86,15 @@ def test_host_argument_validation(lib):
     assert lib.b2d_debug_set(None, 1, 0) == _lib.B2D_ERR_INVALID_ARG
     assert lib.b2d_debug_tune(None, 1, 0) == _lib.B2D_ERR_INVALID_ARG
     assert lib.b2d_debug_trace(None, None, 0) == _lib.B2D_ERR_INVALID_ARG
+    # prefill entry points: null handles and buffers are rejected before any CUDA call
+    assert lib.b2d_prefill(None, None, None, 4, 0, None, None, None, None) == _lib.B2D_ERR_INVALID_ARG
+    assert lib.b2d_prefill_paged(None, None, None, 4, 0, None, None, 32, 64, None, None,
+                                 None) == _lib.B2D_ERR_INVALID_ARG
+    assert lib.b2d_prefill_rows(None, None, None, None, 8, None, None, 32, 64, 2, None, None,
+                                None) == _lib.B2D_ERR_INVALID_ARG
+    assert lib.b2d_prefill_rows_max() == 512
+    assert lib.b2d_decode_step_paged(None, None, None, None, 2, None, None, 32, 64, None, None,
+                                     None) == _lib.B2D_ERR_INVALID_ARG
 
 
 def test_product_path_has_no_oracle_import():
