@@ -141,6 +141,8 @@ def profile_paged(w, cfg, args, torch):
     from transformer_b200.batched import BatchedDecoder
     from transformer_b200.multi_sm_decode import DecodeEngine
     eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    if args.att_splits:
+        eng.debug_tune(att_cpc=args.att_splits)  # attention units per (sequence, kv head); 0 = automatic
     dec = BatchedDecoder(eng, args.batch, seed=args.batch)
     dec.pos.fill_(args.pos)
     dec.tok.copy_(torch.randint(0, cfg.vocab_size, (args.batch,), dtype=torch.int32))
@@ -157,7 +159,7 @@ def profile_paged(w, cfg, args, torch):
     us = e0.elapsed_time(e1) * 1000 / args.steps
     alg = cfg.step_bytes([args.pos] * args.batch)
     peak, kind = hbm_peak()
-    return {"mode": "paged", "batch": args.batch, "pos": args.pos, "steps": args.steps,
+    return {"mode": "paged", "batch": args.batch, "pos": args.pos, "steps": args.steps, "att_splits": args.att_splits,
             "us_per_step": us, "tok_s": args.batch * 1e6 / us, "algorithmic_bytes_per_step": alg,
             "hbm_frac": alg / (us * 1e-6) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
@@ -260,6 +262,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["b1", "paged", "serve", "mixed"], default="b1")
     ap.add_argument("--prompts", type=int, default=4)
+    ap.add_argument("--att-splits", type=int, default=0, help="--mode paged: force 1, 2 or 4 attention units")
     ap.add_argument("--requests", type=int, default=1024)
     ap.add_argument("--prompt-len", type=int, default=64)
     ap.add_argument("--gen-min", type=int, default=32)
