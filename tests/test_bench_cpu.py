@@ -1,0 +1,63 @@
+"""CPU: the parts of bench.py that need no GPU — the traffic figures it reads
+from the committed ncu summaries, the clock / throttle-reason parsing, and
+the reference arm's JSON line (the numpy oracle on a one-step sample)."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+from conftest import REPO
+
+sys.path.insert(0, REPO)
+import bench  # noqa: E402
+
+
+def test_profile_traffic_keys_parse():
+    """bench.py's roofline.traffic comes from these lines of profiles/."""
+    b1 = bench.profile_traffic()
+    step = bench.profile_traffic("paged_step_b256_pos80.md", "traffic_bytes_per_step")
+    assert isinstance(b1, int) and b1 > 600_000_000       # >= one pass over the 607 MB of weights
+    assert isinstance(step, int) and step > 1_000_000_000
+    assert bench.profile_traffic("no_such_summary.md") is None
+
+
+class _FakeProc:
+    def terminate(self):
+        pass
+
+    def wait(self, timeout=None):
+        return 0
+
+
+def test_clock_sampler_parses_reasons():
+    cs = bench.ClockSampler(0)
+    cs.proc = _FakeProc()
+    cs.lines = [
+        "0, 1965, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "0, 1890, 1965, 990.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1800, 1965, 999.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "garbage",
+    ]
+    got = cs.stop()
+    assert got["sm_mhz"] == 1890.0 and got["sm_max_mhz"] == 1965.0
+    assert got["reasons"] == ["sw_power_cap"] and got["samples"] == 3
+
+
+def test_reference_arm_line():
+    """`bench.py --impl reference` prints one JSON line with the contract's
+    keys, the oracle timed on a bounded sample (one decode step of 32
+    sequences here)."""
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0", "--cpu-sample-steps", "1"],
+                         capture_output=True, text=True, timeout=600, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "tok/s" and line["value"] > 0
+    assert line["metric"] == bench.METRIC and line["higher_is_better"] is True
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert line["config"]["workload"].startswith("serve (config 5)")
