@@ -216,7 +216,8 @@ def profile_mixed(w, cfg, args, torch):
 
 def profile_serve(w, cfg, args, torch):
     """Continuous batching (``transformer_b200.serve``): ``--requests``
-    greedy requests with ``--prompt-len``-token prompts and generation lengths
+    requests (greedy, or a ``--sampled-frac`` share sampled with config 4's
+    parameters) with ``--prompt-len``-token prompts and generation lengths
     uniform in [--gen-min, --gen-max] (seeded), ``--batch`` slots over a pool
     of ``--num-blocks`` pages (default: enough for every slot's longest
     sequence).  Wall-clock over the whole run (host scheduling, chunked
@@ -236,7 +237,10 @@ def profile_serve(w, cfg, args, torch):
     cb.stats.clear()
     cb.times.clear()
     gens = rng.integers(args.gen_min, args.gen_max + 1, args.requests)
-    rids = [cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), int(g)) for g in gens]
+    sampled = rng.random(args.requests) < args.sampled_frac  # config 4's parameters, a seed per request
+    rids = [cb.submit(rng.integers(0, cfg.vocab_size, args.prompt_len), int(g),
+                      **(dict(temperature=0.7, top_p=0.95, rep_penalty=1.2, seed=i) if sampled[i] else {}))
+            for i, g in enumerate(gens)]
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     out = cb.run()
@@ -255,6 +259,7 @@ def profile_serve(w, cfg, args, torch):
             "mixed_steps": st.get("mixed_steps", 0), "pipelined_steps": st.get("pipelined_steps", 0),
             "preemptions": st.get("preemptions", 0), "admission": args.admission,
             "fuse_prefill": not args.no_fuse, "pipeline": not args.no_pipeline, "admit_batch": cb.admit_batch,
+            "sampled_requests": int(sampled.sum()),
             "seconds_by_pass": {k: round(v, 4) for k, v in cb.times.items()}}
 
 
@@ -272,6 +277,8 @@ def main():
     ap.add_argument("--no-fuse", action="store_true", help="prefill admitted prompts in passes of their own")
     ap.add_argument("--no-pipeline", action="store_true", help="read every decode step's tokens before the next")
     ap.add_argument("--admit-batch", type=int, default=0, help="free slots that trigger an admission (0: default)")
+    ap.add_argument("--sampled-frac", type=float, default=0.0,
+                    help="--mode serve: fraction of requests sampled (T 0.7, top-p 0.95, rep 1.2)")
     ap.add_argument("--gen-len", type=int, default=128)
     ap.add_argument("--n-runs", type=int, default=10)
     ap.add_argument("--batch", type=int, default=64)
