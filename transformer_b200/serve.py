@@ -609,6 +609,20 @@ class ContinuousBatcher:
             self._sampler = Sampler(self.eng, self._logits_rows, self._hist_cap)
         smp = self._sampler
         batch = len(rows)
+        hist = np.zeros((batch, self._hist_cap), np.int32)
+        hlen = np.zeros(batch, np.int32)
+        u = np.zeros(batch, np.float64)
+        for i, r in enumerate(rows):
+            if r is None or r.greedy:
+                continue
+            n = len(r.out)
+            hist[i, :n] = r.out
+            hlen[i] = n
+            if r.temperature > 0.0:
+                u[i] = r.rng.random_sample()
+        smp.history[:batch].copy_(torch.from_numpy(hist))
+        smp.hist_len[:batch].copy_(torch.from_numpy(hlen))
+        smp.uniforms[:batch].copy_(torch.from_numpy(u))
         out = np.zeros(batch, np.int32)
         groups: dict = {}
         for i, r in enumerate(rows):
@@ -618,20 +632,7 @@ class ContinuousBatcher:
         if greedy_rows:
             out[greedy_rows] = self._fetch(greedy_src, batch)[greedy_rows]
         for (temp, top_p, rp), idx in groups.items():
-            # one sampler launch per parameter set, over that set's rows only
-            m = len(idx)
-            hist = np.zeros((m, self._hist_cap), np.int32)
-            hlen = np.zeros(m, np.int32)
-            u = np.zeros(m, np.float64)
-            for k, i in enumerate(idx):
-                r = rows[i]
-                hist[k, :len(r.out)] = r.out
-                hlen[k] = len(r.out)
-                if r.temperature > 0.0:
-                    u[k] = r.rng.random_sample()
-            smp.history[:m].copy_(torch.from_numpy(hist))
-            smp.hist_len[:m].copy_(torch.from_numpy(hlen))
-            smp.uniforms[:m].copy_(torch.from_numpy(u))
-            lg = logits[:batch] if m == batch else logits[torch.as_tensor(idx, device=logits.device)]
-            out[idx] = smp.sample(lg, temp, top_p, rp, m).cpu().numpy()[:m]
+            # one sampler launch per parameter set over all rows; keep this set's rows
+            got = smp.sample(logits[:batch], temp, top_p, rp, batch).cpu().numpy()
+            out[idx] = got[idx]
         return out
