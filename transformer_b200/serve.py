@@ -187,6 +187,8 @@ class ContinuousBatcher:
         self._hist_cap = hist_cap or self.ctx
         self._sampler = None
         self._logits = None
+        self._logits_c = None      # sampled rows gathered for the sampler
+        self._d_idx = None
         self.stats = collections.Counter()
         self.times = collections.Counter()  # wall seconds per pass kind (each pass ends with a token read-back)
 
@@ -609,20 +611,6 @@ class ContinuousBatcher:
             self._sampler = Sampler(self.eng, self._logits_rows, self._hist_cap)
         smp = self._sampler
         batch = len(rows)
-        hist = np.zeros((batch, self._hist_cap), np.int32)
-        hlen = np.zeros(batch, np.int32)
-        u = np.zeros(batch, np.float64)
-        for i, r in enumerate(rows):
-            if r is None or r.greedy:
-                continue
-            n = len(r.out)
-            hist[i, :n] = r.out
-            hlen[i] = n
-            if r.temperature > 0.0:
-                u[i] = r.rng.random_sample()
-        smp.history[:batch].copy_(torch.from_numpy(hist))
-        smp.hist_len[:batch].copy_(torch.from_numpy(hlen))
-        smp.uniforms[:batch].copy_(torch.from_numpy(u))
         out = np.zeros(batch, np.int32)
         groups: dict = {}
         for i, r in enumerate(rows):
@@ -632,7 +620,29 @@ class ContinuousBatcher:
         if greedy_rows:
             out[greedy_rows] = self._fetch(greedy_src, batch)[greedy_rows]
         for (temp, top_p, rp), idx in groups.items():
-            # one sampler launch per parameter set over all rows; keep this set's rows
-            got = smp.sample(logits[:batch], temp, top_p, rp, batch).cpu().numpy()
-            out[idx] = got[idx]
+            # one sampler launch per parameter set, over that set's rows only
+            # (gathered into a preallocated buffer when they are not all rows)
+            m = len(idx)
+            hist = np.zeros((m, self._hist_cap), np.int32)
+            hlen = np.zeros(m, np.int32)
+            u = np.zeros(m, np.float64)
+            for k, i in enumerate(idx):
+                r = rows[i]
+                hist[k, :len(r.out)] = r.out
+                hlen[k] = len(r.out)
+                if r.temperature > 0.0:
+                    u[k] = r.rng.random_sample()
+            smp.history[:m].copy_(torch.from_numpy(hist))
+            smp.hist_len[:m].copy_(torch.from_numpy(hlen))
+            smp.uniforms[:m].copy_(torch.from_numpy(u))
+            if m == batch:
+                lg = logits[:batch]
+            else:
+                if self._logits_c is None:
+                    self._logits_c = torch.empty_like(self._logits_buf())
+                    self._d_idx = torch.zeros(self._logits_rows, dtype=torch.int64, device=self.eng.device)
+                self._d_idx[:m].copy_(torch.as_tensor(idx, dtype=torch.int64))
+                lg = self._logits_c[:m]
+                torch.index_select(logits, 0, self._d_idx[:m], out=lg)
+            out[idx] = smp.sample(lg, temp, top_p, rp, m).cpu().numpy()[:m]
         return out
