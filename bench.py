@@ -10,8 +10,11 @@ replica per GPU, no collective on the data path).  Each rank keeps its
 most 256 (the batched tensor-core step, one CUDA graph per wave).  A step =
 one greedy token for every sequence of the job; `value` = 2048 * K tokens /
 max-over-ranks device time of the K timed steps (total work fixed as N grows:
-"strong" scaling).  Positions run 64.. upward (config 5's 256 decode steps
-fit; a longer run wraps back to 64).
+"strong" scaling).  Config 5 decodes positions 64..319; the K timed steps are
+spread evenly over that range (K >= 256: every position in turn), so the
+value represents the whole job rather than its cheapest, shortest-context
+steps.  A step's work (weights, KV pages read) depends only on its position,
+so each timed step is placed at its position directly.
 
 At N=1, rank 0 also measures the B=1 latency path (configs 1 and 2: the
 single-launch decode megakernel, us/token and its HBM roofline), config 3
@@ -25,8 +28,10 @@ step, and reads the next tokens back, all inside the timed region.
 
 `--impl reference` times the reference algorithm on the host cores: the
 reference needs JAX, which this image lacks, so the oracle's numpy
-restatement of model.py (KV-cached, float32) stands in for it, on a bounded
-sample of the same workload.
+restatement of model.py (KV-cached, float32) stands in for it.  Each of its
+K timed steps (after W warm-up steps) is a bounded sample of the workload:
+one greedy token for 32 of the 2048 sequences; `ms_per_step` is the measured
+time of such a sample step.
 """
 
 from __future__ import annotations
@@ -48,7 +53,19 @@ sys.path.insert(0, REPO)
 FALLBACK_HBM_GBS = 6650.0
 TOTAL_SEQS = 2048
 PROMPT_LEN = 64
+DECODE_STEPS = 256  # config 5: positions 64..319
 WAVE = 256
+REF_SAMPLE_SEQS = 32
+
+
+def timed_positions(k, first=PROMPT_LEN, n=DECODE_STEPS):
+    """Positions of the K timed steps: config 5's decode range first..first+n-1
+    spread evenly (every position in turn, wrapping, when k >= n)."""
+    if k >= n:
+        return [first + (i % n) for i in range(k)]
+    if k == 1:
+        return [first + n // 2]
+    return [first + int(round(i * (n - 1) / (k - 1))) for i in range(k)]
 
 
 def parse():
@@ -156,11 +173,12 @@ def oracle_params():
     return _PARAMS[0]
 
 
-def cpu_baseline_serve(steps, batch=32):
+def cpu_baseline_serve(steps, batch=REF_SAMPLE_SEQS, warmup=1):
     """Oracle (numpy restatement of model.py, KV-cached float32) on the host
     cores: `batch` sequences of the serve workload decoding at positions 64..
     (their caches hold seeded values in place of an ingested prompt: the step's
-    work does not depend on them)."""
+    work does not depend on them).  `warmup` untimed steps, then `steps` timed
+    ones; returns the baseline object with the measured ms per step."""
     from oracle.ref_forward import CachedDecoder
     from transformer_b200.config import CONFIG_306M as cfg
     from transformer_b200.synth import batch_cfg5
@@ -170,17 +188,21 @@ def cpu_baseline_serve(steps, batch=32):
     dec.K[:, :, :, :PROMPT_LEN] = rng.standard_normal(dec.K[:, :, :, :PROMPT_LEN].shape, dtype=np.float32)
     dec.V[:, :, :, :PROMPT_LEN] = rng.standard_normal(dec.V[:, :, :, :PROMPT_LEN].shape, dtype=np.float32)
     tok = batch_cfg5(cfg)[:batch, -1]
-    dec.step(tok, [PROMPT_LEN] * batch)  # warm-up
+    for i in range(warmup):
+        lg = dec.step(tok, [PROMPT_LEN + i] * batch)
+        tok = np.argmax(lg, axis=1)
+    p0 = PROMPT_LEN + warmup
     t0 = time.perf_counter()
     for i in range(steps):
-        lg = dec.step(tok, [PROMPT_LEN + 1 + i] * batch)
+        lg = dec.step(tok, [p0 + i] * batch)
         tok = np.argmax(lg, axis=1)
     dt = time.perf_counter() - t0
     cores = os.cpu_count()
     return {"value": steps * batch / dt, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} greedy decode steps of {batch} serve-workload sequences at positions "
-                      f"{PROMPT_LEN + 1}..{PROMPT_LEN + steps}, numpy float32 KV-cached restatement of "
-                      f"model.py, BLAS threads={cores}"}
+            "ms_per_step": 1000.0 * dt / steps,
+            "sample": f"{steps} timed greedy decode steps (after {warmup} untimed) of {batch} of the "
+                      f"{TOTAL_SEQS} serve-workload sequences at positions {p0}..{p0 + steps - 1}, numpy "
+                      f"float32 KV-cached restatement of model.py, BLAS threads={cores}"}
 
 
 def cpu_baseline_b1(steps):
@@ -213,21 +235,24 @@ def serve_config(world):
                         f"{TOTAL_SEQS // world} per GPU decoded in waves of <= {WAVE} on a paged KV pool "
                         f"(16-token blocks, random block tables), greedy",
             "model": "306M", "global_batch": TOTAL_SEQS, "seq_len": 512, "parallelism": f"replicas{world}",
+            "positions": f"timed steps spread evenly over config 5's decode positions {PROMPT_LEN}.."
+                         f"{PROMPT_LEN + DECODE_STEPS - 1}",
             "l2": "inputs larger than L2: 607 MB of weights per wave-step plus the KV pages"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    cb = cpu_baseline_serve(max(1, min(args.steps, args.cpu_sample_steps)))
+    cb = cpu_baseline_serve(max(1, args.steps), warmup=max(0, args.warmup))
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * TOTAL_SEQS / cb["value"], "higher_is_better": True, "scaling": "strong",
+            "n_gpus": args.gpus, "steps": max(1, args.steps), "warmup": max(0, args.warmup),
+            "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": serve_config(1),
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference needs JAX (absent); its numpy restatement (oracle) is timed instead, "
-                    "on a bounded sample of the workload"}
+            "note": f"reference needs JAX (absent); its numpy restatement (oracle) is timed instead; a step "
+                    f"is a bounded sample of the workload, one greedy token for {REF_SAMPLE_SEQS} of the "
+                    f"{TOTAL_SEQS} sequences, and ms_per_step is that sample step's measured time"}
     print(json.dumps(line))
     return 0
 
@@ -376,7 +401,7 @@ def run_ours(args, rank, local_rank, world):
     from transformer_b200.config import CONFIG_306M
     from transformer_b200.multi_sm_decode import DecodeEngine
     from transformer_b200.packing import prepare_decode_weights_nlayer
-    from transformer_b200.replicas import max_over_ranks, shard
+    from transformer_b200.replicas import all_ranks, max_over_ranks, shard
     from transformer_b200.synth import batch_cfg5, prompt_cfg1, prompt_cfg2, synth_params
 
     torch.cuda.set_device(local_rank)
@@ -398,23 +423,16 @@ def run_ours(args, rank, local_rank, world):
         d.ingest(list(all_prompts[b0:b1]))
         d.capture()
         waves.append(d)
-    pos = PROMPT_LEN
-
-    def one_step():
-        nonlocal pos
-        if pos >= cfg.context_len:  # wrap (only for runs longer than 448 steps)
-            for d in waves:
-                d.pos.fill_(PROMPT_LEN)
-            pos = PROMPT_LEN
-        for d in waves:
+    def one_step(p):
+        for d in waves:  # every wave's sequences at position p (the graph advances pos itself)
+            d.pos.fill_(p)
             d.replay()
-        pos += 1
 
-    for _ in range(args.warmup):
-        one_step()
+    for i in range(args.warmup):
+        one_step(PROMPT_LEN + i % DECODE_STEPS)
     torch.cuda.synchronize(dev)
     eng.check_device()
-    pos_t0 = pos
+    positions = timed_positions(args.steps)
     per_wave = eng.lib.b2d_batched_launches(eng.ws)  # kernels of one wave-step (the captured step's)
 
     # ---- device-timed region ----
@@ -424,16 +442,16 @@ def run_ours(args, rank, local_rank, world):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    ms = events_ms(lambda: [one_step() for _ in range(args.steps)], stream, torch)
+    ms = events_ms(lambda: [one_step(p) for p in positions], stream, torch)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clk = clocks.stop() if clocks else None
     eng.check_device()
-    ms = max_over_ranks(ms, dev)
+    rank_ms = all_ranks(ms, dev)
+    ms = max(rank_ms)
     ms_per_step = ms / args.steps
     value = TOTAL_SEQS * args.steps / (ms / 1000.0)
-    positions = [pos_t0 + i if pos_t0 + i < cfg.context_len else PROMPT_LEN for i in range(args.steps)]
     alg_step = float(np.mean([n_waves * cfg.step_bytes([p] * wave_b) for p in positions]))
     peak, peak_kind = measured_peaks()
     achieved = alg_step / (ms_per_step / 1000.0) / 1e9
@@ -446,29 +464,24 @@ def run_ours(args, rank, local_rank, world):
     d_in = [torch.zeros(2, wave_b, dtype=torch.int32, device=dev) for _ in waves]
     for i, d in enumerate(waves):
         h_out[i].copy_(d.tok)
-    p_e2e = pos
 
-    def e2e_step():
-        nonlocal p_e2e
-        if p_e2e >= cfg.context_len:
-            p_e2e = PROMPT_LEN
+    def e2e_step(p):
         for i, d in enumerate(waves):
             h_in[i][0].copy_(h_out[i])
-            h_in[i][1].fill_(p_e2e)
+            h_in[i][1].fill_(p)
             d_in[i].copy_(h_in[i], non_blocking=True)
             eng.step_paged(d_in[i][0], d_in[i][1], d.pool, d.table, d.logits, d.tok, stream)
             h_out[i].copy_(d.tok, non_blocking=True)
         stream.synchronize()
-        p_e2e += 1
 
-    for _ in range(2):  # warm-up: the call caches each wave's step graph on its second use
-        e2e_step()
+    for i in range(2):  # warm-up: the call caches each wave's step graph on its second use
+        e2e_step(PROMPT_LEN + i)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(ne):
-        e2e_step()
+    for p in timed_positions(ne):
+        e2e_step(p)
     e2e_s = max_over_ranks(time.perf_counter() - t0, dev)
     e2e_value = TOTAL_SEQS * ne / e2e_s
     for d in waves:
@@ -513,6 +526,7 @@ def run_ours(args, rank, local_rank, world):
         "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded prompts; no checkpoint on the box)",
         "config": serve_config(world),
         "gpu_launches": launches,
+        "rank_ms_per_step": [m / args.steps for m in rank_ms],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "scope": f"whole batched step per GPU ({per_wave} "
                      "kernels per wave: projections on tcgen05 with RMSNorm folded in, paged attention, embedding, argmax)",
@@ -523,7 +537,8 @@ def run_ours(args, rank, local_rank, world):
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                 "d2h_bytes_per_step": 4 * n_seq, "steps": ne,
                 "note": "per wave: pinned H2D of tokens+positions, b2d_decode_step_paged (replayed from its "
-                        "cached step graph after 2 untimed warm-up steps), D2H next tokens; one sync per step"},
+                        "cached step graph after 2 untimed warm-up steps), D2H next tokens; one sync per step; "
+                        "positions spread over 64..319 like the device-timed steps"},
         "clocks": clk,
     }
     line.update(extra)

@@ -264,7 +264,8 @@ B2D_API b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, in
  * GPU that loads it, until exit); a model whose exchange area does not fit
  * gets B2D_ERR_SCRATCH_LIMIT.  The caller passes the packed weights, the
  * inputs and the outputs exactly as for b2d_decode_step on the current
- * device.  The first call on a device looks up the array's device address,
+ * device (every pointer is checked to be device memory of the current device).
+ * The first call on a device looks up the array's device address,
  * so make it before any stream capture.  Each call clears the array on
  * `stream` before launching; calls that overlap on the GPU race on it.  No
  * model or workspace handle, no cudaMalloc/cudaFree, no host heap use.
@@ -273,6 +274,18 @@ B2D_API b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* wei
                                           uint64_t weights_bytes, const int32_t* tok_dev,
                                           const int32_t* pos_dev, void* kv_dev, float* logits_dev,
                                           int32_t* next_tok_dev, void* stream);
+/*
+ * Device status of the most recent b2d_decode_step_static call on the current
+ * device, without a workspace: synchronises `stream`, then reads the status
+ * word of the fixed array's control block.  Returns B2D_OK, or
+ * B2D_ERR_DEVICE_TIMEOUT / B2D_ERR_DEVICE_INPUT (a token or position out of
+ * range, read on the device) with the raw word in *detail.  Each static call
+ * clears that word before it launches, so a later call replaces an earlier
+ * call's error: check after every call whose inputs the host has not
+ * validated.  Allocates nothing.  No counterpart in the reference (it has no
+ * device status at all).
+ */
+B2D_API b2d_status b2d_static_last_error(void* stream, uint32_t* detail);
 
 /*
  * Test hook, not part of the reference surface: bound every in-kernel wait by

@@ -20,7 +20,8 @@ Fixtures (all small):
   tiny.npz          tiny model: forward logits, prefill logits + bf16 KV caches,
                     reference rms_norm / rope outputs, packed-format digests
   cfg1_greedy.npz   306M config 1: reference greedy stream (full-prefix
-                    recompute, f32), per-step top-1 / margin, logits at 2 steps
+                    recompute, f32), per-step top-1 / margin, full logits at
+                    18 steps (0, 1, every 8th, the last)
   cfg2_long.npz     306M config 2: same over a 384-token prompt to ctx 512
   sampling.npz      reference sample_token vs supplied-uniform restatement
   cfg4_sampled.npz  306M config 4: sampled token streams from the oracle
@@ -256,7 +257,8 @@ def make_cfg_greedy(ref, name, prompt, n_tokens):
     cfg = CONFIG_306M
     P, _ = ref_params(cfg)
     conf = ref_config(cfg)
-    keep = (0, 1, n_tokens - 1)
+    # full logits at 18 steps spread over the stream (0, 1, every 8th, the last)
+    keep = tuple(sorted({0, 1, n_tokens - 1, *range(8, n_tokens - 1, 8)}))
     toks, top1, margin, kept = greedy_full_recompute(ref_model, P, conf, prompt, n_tokens, keep)
     np.savez_compressed(os.path.join(HERE, name), prompt=prompt.astype(np.int32), tokens=toks,
                         top1=top1, margin=margin, logits_steps=np.array(keep, np.int32),

@@ -50,8 +50,8 @@ def test_reference_arm_line():
     """`bench.py --impl reference` prints one JSON line with the contract's
     keys, the oracle timed on a bounded sample (one decode step of 32
     sequences here)."""
-    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "0", "--cpu-sample-steps", "1"],
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "2",
+                          "--warmup", "1"],
                          capture_output=True, text=True, timeout=600, cwd=REPO)
     assert out.returncode == 0, out.stderr[-2000:]
     line = json.loads(out.stdout.strip().splitlines()[-1])
@@ -61,3 +61,19 @@ def test_reference_arm_line():
     assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["workload"].startswith("serve (config 5)")
+    # the line's step is the sample step it timed: K steps of ms_per_step fit in the run
+    assert line["steps"] == 2 and line["warmup"] == 1
+    assert abs(line["ms_per_step"] - line["cpu_baseline"]["ms_per_step"]) < 1e-9
+    assert abs(line["value"] - 1000.0 * bench.REF_SAMPLE_SEQS / line["ms_per_step"]) < 1e-6 * line["value"]
+
+
+def test_timed_positions_span_config5():
+    """The K timed steps of the headline cover config 5's decode positions
+    64..319 (evenly for K < 256, every position in turn from 256 on)."""
+    for k in (1, 2, 3, 20, 255):
+        p = bench.timed_positions(k)
+        assert len(p) == k and all(64 <= x <= 319 for x in p)
+        if k > 1:
+            assert p[0] == 64 and p[-1] == 319 and p == sorted(p)
+    assert bench.timed_positions(256) == list(range(64, 320))
+    assert bench.timed_positions(300)[256:] == list(range(64, 108))

@@ -9,7 +9,7 @@ import os
 import pytest
 import torch.multiprocessing as mp
 
-from transformer_b200.replicas import max_over_ranks, shard
+from transformer_b200.replicas import all_ranks, max_over_ranks, shard
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -44,7 +44,8 @@ def _worker(rank, world, port, out):
         # per-rank "elapsed" values; every rank must see the slowest
         got = max_over_ranks(10.0 + rank * 5.0)
         tokens = max_over_ranks(float(s.n))  # equal shares: the max equals any rank's share
-        out.put((rank, got, tokens, s.begin, s.end))
+        every = all_ranks(10.0 + rank * 5.0)  # per-rank step times, reported in rank order
+        out.put((rank, got, tokens, s.begin, s.end, every))
     finally:
         dist.destroy_process_group()
 
@@ -62,11 +63,13 @@ def test_max_over_ranks_gloo_world2():
     res = sorted(q.get(timeout=10) for _ in range(2))
     assert [r[1] for r in res] == [15.0, 15.0]
     assert [r[2] for r in res] == [1024.0, 1024.0]
-    assert res[0][3:] == (0, 1024) and res[1][3:] == (1024, 2048)
+    assert res[0][3:5] == (0, 1024) and res[1][3:5] == (1024, 2048)
+    assert [r[5] for r in res] == [[10.0, 15.0], [10.0, 15.0]]
 
 
 def test_max_over_ranks_without_group():
     assert max_over_ranks(3.5) == 3.5
+    assert all_ranks(3.5) == [3.5]
 
 
 def _dying_worker(rank, world, port, out):

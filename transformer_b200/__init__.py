@@ -9,7 +9,10 @@ logits and argmax), reached through the C ABI in ``include/b2d.h``
                        ``prepare_decode_weights_nlayer`` (kernels/fused_decode_nlayer.py)
 * ``generate``         ``sample_token`` / ``stream_tokens`` / ``generate_tokens``
                        (generate.py)
-* ``profile_kernels``  ``measure_decode`` / ``compute_memory_stats`` (profile_kernels.py)
+
+The reference's measurement functions (``measure_decode`` /
+``compute_memory_stats``, profile_kernels.py) live in the top-level
+``profile_kernels.py`` beside ``bench.py``, not in this package.
 
 Heavy imports (torch, the shared library) happen in those submodules, so
 ``config`` and ``synth`` stay importable on a CPU-only host.

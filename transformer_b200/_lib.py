@@ -89,6 +89,7 @@ _SIGS = {
                                   ctypes.POINTER(Sampling), _P, _P]),
     "b2d_decode_step_static": (ctypes.c_int, [ctypes.POINTER(Config), _P, ctypes.c_uint64, _P, _P, _P, _P,
                                               _P, _P]),
+    "b2d_static_last_error": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "b2d_debug_set": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int]),
     "b2d_debug_trace": (ctypes.c_int, [_P, _P, ctypes.c_int]),
     "b2d_debug_tune": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),

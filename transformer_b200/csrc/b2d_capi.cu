@@ -968,9 +968,9 @@ constexpr int kMaxDevices = 64;
 StaticDeviceState g_static_dev[kMaxDevices];
 std::mutex g_static_mu;
 
-b2d_status static_setup(int device, const ShapeOps* ops, int ops_index, StaticDeviceState** out) {
-  std::lock_guard<std::mutex> lock(g_static_mu);
-  StaticDeviceState& st = g_static_dev[device];
+// Looks up g_static_scratch's device address on `device` (current) once.
+// The caller holds g_static_mu.
+b2d_status static_lookup(int device, StaticDeviceState& st) {
   if (!st.ready) {
     void* p = nullptr;
     B2D_CUDA(cudaGetSymbolAddress(&p, g_static_scratch), "cudaGetSymbolAddress(g_static_scratch)");
@@ -984,6 +984,14 @@ b2d_status static_setup(int device, const ShapeOps* ops, int ops_index, StaticDe
     st.sms = sms;
     st.ready = true;
   }
+  return B2D_OK;
+}
+
+b2d_status static_setup(int device, const ShapeOps* ops, int ops_index, StaticDeviceState** out) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  StaticDeviceState& st = g_static_dev[device];
+  b2d_status s = static_lookup(device, st);
+  if (s != B2D_OK) return s;
   if (!(st.smem_set & (1 << ops_index))) {
     B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(ops->smem)),
@@ -1020,9 +1028,17 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   int device = 0;
   B2D_CUDA(cudaGetDevice(&device), "cudaGetDevice");
   if (device < 0 || device >= kMaxDevices) return B2D_ERR_UNSUPPORTED;
-  cudaPointerAttributes pa;
-  B2D_CUDA(cudaPointerGetAttributes(&pa, weights_dev), "cudaPointerGetAttributes");
-  if (pa.type != cudaMemoryTypeDevice || pa.device != device) return B2D_ERR_INVALID_ARG;
+  // Every buffer must be device memory of the current device: this entry
+  // point serves hosts with their own memory pools, where a host pointer or
+  // another GPU's buffer is an easy mistake that would otherwise reach the
+  // kernel unchecked.
+  const void* bufs[] = {weights_dev, tok_dev, pos_dev, kv_dev, next_tok_dev, logits_dev};
+  for (const void* b : bufs) {
+    if (b == nullptr) continue;  // only logits_dev may be null (checked above)
+    cudaPointerAttributes pa;
+    B2D_CUDA(cudaPointerGetAttributes(&pa, b), "cudaPointerGetAttributes");
+    if (pa.type != cudaMemoryTypeDevice || pa.device != device) return B2D_ERR_INVALID_ARG;
+  }
   StaticDeviceState* st = nullptr;
   const int ops_index = ops->d == 1024 ? 0 : 1;
   b2d_status s = static_setup(device, ops, ops_index, &st);
@@ -1071,4 +1087,33 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   B2D_CUDA(cudaLaunchCooperativeKernel(ops->kernel, dim3(st->sms), dim3(b2d::kThreads), args, ops->smem, cs),
            "static decode launch");
   return B2D_OK;
+}
+
+// Status of the last b2d_decode_step_static call on the current device: the
+// control block in the fixed array holds the kernel's status word (a bounded
+// wait that ran out, a token or position out of range read on the device).
+// Each static call clears that block before its launch, so this reports the
+// most recent call only.  Synchronises `stream` first; allocates nothing.
+extern "C" b2d_status b2d_static_last_error(void* stream, uint32_t* detail) {
+  if (detail) *detail = 0;
+  int device = 0;
+  B2D_CUDA(cudaGetDevice(&device), "cudaGetDevice");
+  if (device < 0 || device >= kMaxDevices) return B2D_ERR_UNSUPPORTED;
+  unsigned char* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    b2d_status s = static_lookup(device, g_static_dev[device]);
+    if (s != B2D_OK) return s;
+    scratch = g_static_dev[device].scratch;
+  }
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  uint32_t s = 0;
+  const b2d::Control* ctl = reinterpret_cast<const b2d::Control*>(scratch + b2d::kStaticCtlOffset);
+  B2D_CUDA(cudaMemcpyAsync(&s, &ctl->status, sizeof(s), cudaMemcpyDeviceToHost, cs), "read static status");
+  B2D_CUDA(cudaStreamSynchronize(cs), "cudaStreamSynchronize");
+  if (detail) *detail = s;
+  if (s == 0) return B2D_OK;
+  if ((s & 0xF00u) == b2d::ST_TIMEOUT) return B2D_ERR_DEVICE_TIMEOUT;
+  if ((s & 0xF00u) == b2d::ST_BAD_INPUT) return B2D_ERR_DEVICE_INPUT;
+  return B2D_ERR_DEVICE_HALTED;
 }
