@@ -45,14 +45,15 @@ using ShapeTiny = b2d::Shape<256, 768, 4, 2>;
 struct ShapeOps {
   int d, dff, nh, nkv;
   size_t smem;
-  const void* kernel;
-  size_t sampler_smem;
+  const void* kernel;        // the B=1 step
+  const void* kernel_trace;  // the same with diagnostic stamps (b2d_debug_trace, knobs 7/8)
 };
 
 template <class S>
 ShapeOps make_ops() {
   return ShapeOps{S::D, S::DFF, S::NH, S::NKV, sizeof(b2d::Smem<S>),
-                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S>), 0};
+                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, false>),
+                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, true>)};
 }
 
 const ShapeOps* find_ops(const b2d_config* c) {
@@ -272,9 +273,9 @@ b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint
   B2D_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "sm count");
   B2D_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device), "coop attr");
   if (!coop) return B2D_ERR_LAUNCH;
-  B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(ops->smem)),
-           "cudaFuncSetAttribute(smem)");
+  for (const void* k : {ops->kernel, ops->kernel_trace})
+    B2D_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ops->smem)),
+             "cudaFuncSetAttribute(smem)");
   if (sms < b2d::kMinGrid) return B2D_ERR_UNSUPPORTED;  // phase register budgets assume >= 128 SMs
   int per_sm = 0;
   B2D_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops->kernel, b2d::kThreads, ops->smem),
@@ -475,6 +476,7 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 10:  // sampler: phase stamp buffer (device address; 0 = off)
       ws->sample_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
       return B2D_OK;
+
   }
   return B2D_ERR_INVALID_ARG;
 }
@@ -528,8 +530,8 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   A.n_steps = n_steps;
   A.tok_out = tok_out_dev;
   void* args[] = {&A};
-  B2D_CUDA(cudaLaunchCooperativeKernel(m->ops->kernel, dim3(m->grid), dim3(b2d::kThreads), args,
-                                       m->ops->smem, st),
+  const void* kernel = A.trace || A.stage_trace ? m->ops->kernel_trace : m->ops->kernel;
+  B2D_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(m->grid), dim3(b2d::kThreads), args, m->ops->smem, st),
            "decode launch");
   return B2D_OK;
 }

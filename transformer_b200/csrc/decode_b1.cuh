@@ -94,11 +94,24 @@ struct DecodeArgs {
 };
 
 // Phase-stamp slots (per CTA): 0 = start, then per layer kTracePerLayer
-// stamps, then final gather / logits / end.
+// stamps, then final gather / logits / end.  Stamps exist only in the kernel
+// instantiated with TR = true (launched when a trace buffer is set), so the
+// production kernel carries no diagnostic branches.
 constexpr int kTracePerLayer = 13;
+template <bool TR>
 __device__ __forceinline__ void trace_stamp(const DecodeArgs& A, int slot) {
-  if (A.trace != nullptr && threadIdx.x == 0 && slot < A.trace_stride)
-    A.trace[static_cast<size_t>(blockIdx.x) * A.trace_stride + slot] = globaltimer_ns();
+  if constexpr (TR) {
+    if (A.trace != nullptr && threadIdx.x == 0 && slot < A.trace_stride)
+      A.trace[static_cast<size_t>(blockIdx.x) * A.trace_stride + slot] = globaltimer_ns();
+  }
+}
+// Weight-stage stamps (kind 0 issued, 1 seen full, 2 consumed), TR only.
+template <bool TR>
+__device__ __forceinline__ void stage_stamp(const DecodeArgs& A, int cta, int kind, uint32_t seq) {
+  if constexpr (TR) {
+    if (A.stage_trace != nullptr && seq < static_cast<uint32_t>(A.stage_stride))
+      A.stage_trace[(static_cast<size_t>(cta) * 3 + kind) * A.stage_stride + seq] = globaltimer_ns();
+  }
 }
 
 constexpr int kConsumerWarps = 8;
@@ -109,6 +122,8 @@ constexpr int kStages = 10;
 constexpr int kAttWords = 66;       // per attention unit: o[64], m, l
 constexpr int kMaxSplits = 4;       // attention units per head
 constexpr int kMinGrid = 128;       // fewest CTAs the phase register budgets assume
+// GEMV phases of a step, in streaming order (Smem::rng index / 2)
+enum Phase : int { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_VOCAB = 4, kPhases = 5 };
 
 template <int D_, int DFF_, int NH_, int NKV_>
 struct Shape {
@@ -120,7 +135,6 @@ struct Shape {
   static constexpr int ROWB_D = 2 * D;
   static constexpr int ROWB_F = 2 * DFF;
   static constexpr int RPS_D = kStageBytes / ROWB_D;        // rows of K=D per stage
-  static constexpr int PPS = kStageBytes / (2 * ROWB_D);    // gate/up pairs per stage
   static constexpr int RPS_F = kStageBytes / ROWB_F;        // down rows per stage
   static constexpr int XMAX = DFF > D ? DFF : D;
   // Units per warp per phase, for grids of at least kMinGrid CTAs.
@@ -128,9 +142,15 @@ struct Shape {
     return ((n + kMinGrid - 1) / kMinGrid + kConsumerWarps - 1) / kConsumerWarps;
   }
   static constexpr int J_QKV = units_per_warp(QKV), J_O = units_per_warp(D);
-  static constexpr int J_GU = units_per_warp(DFF), J_DOWN = units_per_warp(D);
+  static constexpr int J_GU = units_per_warp(2 * DFF), J_DOWN = units_per_warp(D);  // GU: single rows
+  // gate/up rows per CTA: the DFF / 2 act words (2 pairs = 4 rows each) split over >= kMinGrid CTAs
+  static constexpr int GU_ROWS_MAX = 4 * ((DFF / 2 + kMinGrid - 1) / kMinGrid);
+  static_assert(J_GU * kConsumerWarps >= GU_ROWS_MAX, "gate/up rows per warp");
+  static constexpr int NP_D = (D / 2 + kConsumers - 1) / kConsumers;        // residual word pairs per thread
+  static constexpr int NP_ACT = (DFF / 4 + kConsumers - 1) / kConsumers;    // act word pairs per thread
+  static_assert(DFF % 4 == 0, "act words hold two bf16 values, read in pairs");
   static_assert(D % 256 == 0 && DFF % 256 == 0, "row length must be a multiple of 256");
-  static_assert(RPS_D >= 1 && PPS >= 1 && RPS_F >= 1, "stage too small");
+  static_assert(RPS_D >= 1 && RPS_F >= 1, "stage too small");
   static_assert(NH % NKV == 0, "GQA");
   static_assert(NH * 16 <= kConsumers, "attention merge uses 16 threads per head");
   static_assert(NH * kMaxSplits <= kConsumers, "one thread per attention unit in the merge");
@@ -143,7 +163,7 @@ struct Smem {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   float h[S::D];          // residual stream (f32)
-  alignas(16) float xf[S::XMAX];  // GEMV input vector (bf16 values as f32), see xidx
+  alignas(16) __nv_bfloat16 xb[S::XMAX];  // GEMV input vector (bf16, natural order)
   alignas(128) __nv_bfloat16 katt[128][64];  // K rows of the attention unit's pass
   alignas(128) __nv_bfloat16 vatt[128][64];  // V rows of the attention unit's pass
   uint64_t att_bar;       // completes the K/V staging copies
@@ -156,6 +176,8 @@ struct Smem {
   float ml[2 * kConsumers];  // (m, l) of each attention unit
   float am_v[kConsumerWarps];
   int am_i[kConsumerWarps];
+  alignas(16) float gu_out[S::GU_ROWS_MAX];  // this CTA's gate/up dot products (gate j, up j, ...)
+  int rng[2 * kPhases];                      // this CTA's unit range [a, b) of each GEMV phase
   int abort;
   int tok_in;  // multi-step: this step's input token
 };
@@ -165,21 +187,14 @@ template <class S>
 struct SmemChecks {
   static_assert(offsetof(Smem<S>, stage) % 128 == 0, "stage alignment");
   static_assert(kStageBytes % 16 == 0, "stage size");
-  static_assert(offsetof(Smem<S>, xf) % 16 == 0, "xf alignment");
+  static_assert(offsetof(Smem<S>, xb) % 16 == 0, "xb alignment");
   static_assert(offsetof(Smem<S>, vatt) % 128 == 0 && offsetof(Smem<S>, katt) % 128 == 0, "K/V staging alignment");
   static_assert(offsetof(Smem<S>, rq) % 16 == 0, "rq alignment");
+  static_assert(offsetof(Smem<S>, gu_out) % 16 == 0, "gu_out alignment (read as float4)");
   static_assert(offsetof(Smem<S>, full) % 8 == 0 && offsetof(Smem<S>, att_bar) % 8 == 0, "mbarrier alignment");
   static_assert(sizeof(Smem<S>) <= 232448, "shared memory per CTA");
   static constexpr bool ok = true;
 };
-
-// Position of GEMV input element e in Smem::xf.  Lane l of a warp multiplies
-// weights e = k*256 + l*8 + j (j < 8); the layout puts j < 4 of all lanes
-// first, then j >= 4, so both of a lane's 16-byte reads are conflict-free.
-__device__ __forceinline__ int xidx(int e) {
-  const int k = e >> 8, r = e & 255, ln = r >> 3, j = r & 7;
-  return (k << 8) + ((j >> 2) << 7) + (ln << 2) + (j & 3);
-}
 
 __device__ __forceinline__ int split_begin(int c, int n, int g) {
   return static_cast<int>((static_cast<long long>(c) * n) / g);
@@ -221,11 +236,10 @@ struct Waiter {
 // aligned); valid(i) says whether this thread owns item i; store(i, a, b)
 // receives the payloads.  All owned loads are issued together, then the
 // thread spins on one pending pair at a time.  Returns false on timeout/abort.
-template <int N, class AddrF, class ValidF, class StoreF>
+template <int N, int GRP = 8, class AddrF, class ValidF, class StoreF>
 __device__ __forceinline__ bool gather_pairs(const DecodeArgs& A, uint32_t flag, uint64_t t0,
                                              uint32_t site, AddrF addr, ValidF valid, StoreF store) {
-  static_assert(N <= 32, "pending mask is 32 bits");
-  constexpr int GRP = 8;  // loads issued together per thread
+  static_assert(N <= 32, "pending mask is 32 bits");  // GRP: loads issued together per thread
   uint32_t pending = 0;
 #pragma unroll
   for (int i = 0; i < N; ++i)
@@ -316,96 +330,113 @@ __device__ __forceinline__ void release_n(Ring& r, int n) {
 
 constexpr int kGroupStages = kStages / 2;  // stages waited for together
 
-// One GEMV phase over this CTA's units [u_begin, u_end) (a unit is one row, or
-// a gate/up row pair when PAIR), streamed in stages of `per_stage` units.
-// Warp w owns units u_begin + w + 8j (j < MAXJ).  Each lane accumulates its
-// partial dot products for all of its units across the phase's stages (two
-// accumulators per row to shorten the FMA chain); the cross-lane reductions
-// of all units run together once, after the last stage, so their shuffle
-// latencies overlap.  out(u, dot0, dot1) is then called on every lane.
-template <int KI, int ROWB, bool PAIR, int MAXJ, class Out>
+// The GEMV input vector, read from Smem::xb (bf16, natural order).  Lane l
+// multiplies weight elements k*256 + l*8 + j (k < KI, j < 8), i.e. the 16-byte
+// chunk k*32 + l of the vector: one conflict-free 16-byte read per lane and K
+// step serves every row of the warp's units (the K loop is outermost).  The
+// unpacked bf16 pairs are exact f32 values.
+struct X4 {
+  uint64_t q[4];
+};
+struct XSmem {
+  const uint4* p;
+  __device__ __forceinline__ X4 chunk(int k) const {
+    const uint4 u = p[k * 32 + (threadIdx.x & 31)];
+    return X4{{bf2pack(u.x), bf2pack(u.y), bf2pack(u.z), bf2pack(u.w)}};
+  }
+};
+
+// acc += 8 bf16 weights (w) x the lane's 8 activations of one chunk.
+__device__ __forceinline__ void dot8r(const uint4 w, const X4& x, uint64_t& a0, uint64_t& a1) {
+  a0 = ffma2(bf2pack(w.x), x.q[0], a0);
+  a1 = ffma2(bf2pack(w.y), x.q[1], a1);
+  a0 = ffma2(bf2pack(w.z), x.q[2], a0);
+  a1 = ffma2(bf2pack(w.w), x.q[3], a1);
+}
+
+// One GEMV phase over this CTA's units [u_begin, u_end) (a unit is one row),
+// streamed in stages of PS units.  Warp w owns units u_begin + w + 8j
+// (j < MAXJ).  Each lane accumulates its partial dot products for all of its
+// units across the phase's stages (two accumulators per row to shorten the
+// FMA chain); the cross-lane reductions of all units run together once, after
+// the last stage, so their shuffle latencies overlap.  out(u, v) is then
+// called on every lane for each unit u < u_end of the warp.
+template <int KI, int ROWB, int PS, int MAXJ, bool TR, class Out>
 __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
-                                           int u_begin, int u_end, int per_stage,
-                                           const float* xsm, Out out) {
+                                           int u_begin, int u_end, const XSmem x, Out out, int sub = -1) {
+  // sub >= 0 (diagnostic kernel): stamps sub (stages acquired), sub + 1
+  // (products done), sub + 2 (reduced), sub + 3 (outputs stored)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int UNIT_BYTES = PAIR ? 2 * ROWB : ROWB;
-  constexpr int NR = PAIR ? 2 : 1;
-  const float4* xp = reinterpret_cast<const float4*>(xsm);
-  uint64_t acc[MAXJ][NR][2];
+  uint64_t acc[MAXJ][2];
 #pragma unroll
-  for (int j = 0; j < MAXJ; ++j)
-#pragma unroll
-    for (int r = 0; r < NR; ++r) acc[j][r][0] = acc[j][r][1] = 0ull;
+  for (int j = 0; j < MAXJ; ++j) acc[j][0] = acc[j][1] = 0ull;
   bool ok = true;
-  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * per_stage) {
-    const int ns = min(kGroupStages, (u_end - g0 + per_stage - 1) / per_stage);
+  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * PS) {
+    const int ns = min(kGroupStages, (u_end - g0 + PS - 1) / PS);
     ok = wait_full_n(A, ring, ns, flag, t0);
-    if (A.stage_trace != nullptr && threadIdx.x == 0 && ring.seq < static_cast<uint32_t>(A.stage_stride))
-      A.stage_trace[(static_cast<size_t>(blockIdx.x) * 3 + 1) * A.stage_stride + ring.seq] = globaltimer_ns();
+    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
+    if (sub >= 0 && g0 == u_begin) trace_stamp<TR>(A, sub);
     if (ok) {
+      const uint4* rp[MAXJ];  // this warp's rows in the group's stages (null: not in this group)
 #pragma unroll
       for (int j = 0; j < MAXJ; ++j) {
         const int u = u_begin + warp + kConsumerWarps * j;
-        const int st = (u - g0) / per_stage;  // stage of the group holding unit u
-        if (u >= g0 && st < ns && u < u_end) {
-          const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
-          const uint4* rp = reinterpret_cast<const uint4*>(
-              sb + static_cast<size_t>(u - g0 - st * per_stage) * UNIT_BYTES);
+        const int st = (u - g0) / PS;  // stage of the group holding unit u
+        rp[j] = nullptr;
+        if (u >= g0 && st < ns && u < u_end)
+          rp[j] = reinterpret_cast<const uint4*>(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages] +
+                                                 static_cast<size_t>(u - g0 - st * PS) * ROWB) +
+                  lane;
+      }
 #pragma unroll
-          for (int k = 0; k < KI; ++k) {
-            const float4 xa = xp[k * 64 + lane], xb = xp[k * 64 + 32 + lane];
+      for (int k = 0; k < KI; ++k) {
+        const X4 xc = x.chunk(k);
 #pragma unroll
-            for (int r = 0; r < NR; ++r)
-              dot8x2(rp[r * (ROWB / 16) + k * 32 + lane], xa, xb, acc[j][r][0], acc[j][r][1]);
-          }
-        }
+        for (int j = 0; j < MAXJ; ++j)
+          if (rp[j] != nullptr) dot8r(rp[j][k * 32], xc, acc[j][0], acc[j][1]);
       }
     }
-    if (A.stage_trace != nullptr && threadIdx.x == 0 && ring.seq < static_cast<uint32_t>(A.stage_stride))
-      A.stage_trace[(static_cast<size_t>(blockIdx.x) * 3 + 2) * A.stage_stride + ring.seq] = globaltimer_ns();
+    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
     release_n(ring, ns);
   }
   if (!ok) return false;
-  float v[MAXJ][NR];
+  if (sub >= 0) trace_stamp<TR>(A, sub + 1);
+  float v[MAXJ];
 #pragma unroll
-  for (int j = 0; j < MAXJ; ++j)
-#pragma unroll
-    for (int r = 0; r < NR; ++r) v[j][r] = f2sum(acc[j][r][0]) + f2sum(acc[j][r][1]);
+  for (int j = 0; j < MAXJ; ++j) v[j] = f2sum(acc[j][0]) + f2sum(acc[j][1]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int j = 0; j < MAXJ; ++j)
-#pragma unroll
-      for (int r = 0; r < NR; ++r) v[j][r] += __shfl_xor_sync(0xffffffffu, v[j][r], o);
+    for (int j = 0; j < MAXJ; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+  if (sub >= 0) trace_stamp<TR>(A, sub + 2);
 #pragma unroll
   for (int j = 0; j < MAXJ; ++j) {
     const int u = u_begin + warp + kConsumerWarps * j;
-    if (u < u_end) out(u, v[j][0], v[j][NR - 1]);
+    if (u < u_end) out(u, v[j]);
   }
+  if (sub >= 0) trace_stamp<TR>(A, sub + 3);
   return true;
 }
 
 // Same streaming for many units per warp (the logits): reduce per stage.
-template <int KI, int ROWB, class Out>
+template <int KI, int ROWB, int PS, class Out>
 __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
-                                                int u_begin, int u_end, int per_stage,
-                                                const float* xsm, Out out) {
+                                                int u_begin, int u_end, const XSmem x, Out out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float4* xp = reinterpret_cast<const float4*>(xsm);
   bool ok = true;
-  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * per_stage) {
-    const int g1 = min(g0 + kGroupStages * per_stage, u_end);
-    const int ns = (g1 - g0 + per_stage - 1) / per_stage;
+  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * PS) {
+    const int g1 = min(g0 + kGroupStages * PS, u_end);
+    const int ns = (g1 - g0 + PS - 1) / PS;
     ok = wait_full_n(A, ring, ns, flag, t0);
     if (ok) {
       const int first = g0 + ((warp - (g0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
       for (int u = first; u < g1; u += kConsumerWarps) {
-        const int st = (u - g0) / per_stage;
+        const int st = (u - g0) / PS;
         const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
-        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * per_stage) * ROWB);
+        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * PS) * ROWB);
         uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll
-        for (int k = 0; k < KI; ++k) dot8x2(rp[k * 32 + lane], xp[k * 64 + lane], xp[k * 64 + 32 + lane], a0, a1);
+        for (int k = 0; k < KI; ++k) dot8r(rp[k * 32 + lane], x.chunk(k), a0, a1);
         out(u, warp_sum(f2sum(a0) + f2sum(a1)), 0.f);
       }
     }
@@ -414,39 +445,77 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring,
   return ok;
 }
 
-// Norm gains for this thread's elements (t + k*256), loaded ahead of the
-// wait that precedes the norm so their latency is hidden.
-template <class S>
-__device__ __forceinline__ void load_gain(const float* g, float (&gr)[S::D / kConsumers]) {
-#pragma unroll
-  for (int k = 0; k < S::D / kConsumers; ++k) gr[k] = __ldg(g + threadIdx.x + k * kConsumers);
-}
-
-// x = bf16(h * rsqrt(mean(h^2) + eps) * g)  (RMSNorm, reference :121-126)
-template <class S>
-__device__ __forceinline__ void rmsnorm_to_x(Smem<S>& sm, const float (&gr)[S::D / kConsumers], float eps) {
-  static_assert(S::D % kConsumers == 0, "D must be a multiple of the consumer count");
+// Residual stream -> GEMV input: thread t holds the residual pairs
+// (elements 2k, 2k + 1, k = t + 256 i, i < NP) in hv.  Stores them into sm.h,
+// then x = bf16(h * rsqrt(mean(h^2) + eps) * g) into sm.xb (RMSNorm,
+// reference :121-126); the sum of squares is taken from the registers, so one
+// barrier publishes h and the per-warp sums together.  `ok` enters the
+// barrier's AND; returns the combined flag.
+template <class S, int NP>
+__device__ __forceinline__ bool norm_pairs(Smem<S>& sm, const float (&hv)[NP][2], const float2 (&g)[NP],
+                                           float eps, bool ok) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   float ss = 0.f;
 #pragma unroll
-  for (int i = t; i < S::D; i += kConsumers) ss = fmaf(sm.h[i], sm.h[i], ss);
+  for (int i = 0; i < NP; ++i) {
+    const int k = t + i * kConsumers;
+    if (k < S::D / 2) {
+      sm.h[2 * k] = hv[i][0];
+      sm.h[2 * k + 1] = hv[i][1];
+      ss = fmaf(hv[i][0], hv[i][0], ss);
+      ss = fmaf(hv[i][1], hv[i][1], ss);
+    }
+  }
   ss = warp_sum(ss);
   if (lane == 0) sm.red[warp] = ss;
-  consumer_sync<kConsumers>();
+  ok = consumer_sync_and<kConsumers>(ok);
+  if (!ok) return false;
   float tot = 0.f;
 #pragma unroll
   for (int w = 0; w < kConsumerWarps; ++w) tot += sm.red[w];
   const float r = rsqrtf(tot / static_cast<float>(S::D) + eps);
 #pragma unroll
-  for (int k = 0; k < S::D / kConsumers; ++k) {
-    const int i = t + k * kConsumers;
-    sm.xf[xidx(i)] = round_bf16(sm.h[i] * r * gr[k]);
+  for (int i = 0; i < NP; ++i) {
+    const int k = t + i * kConsumers;
+    if (k < S::D / 2)
+      reinterpret_cast<__nv_bfloat162*>(sm.xb)[k] = __floats2bfloat162_rn(hv[i][0] * r * g[i].x, hv[i][1] * r * g[i].y);
   }
   consumer_sync<kConsumers>();
+  return true;
+}
+
+// Norm gains of this thread's residual pairs (loaded ahead of the wait that
+// precedes the norm, so their latency is hidden).
+template <class S, int NP>
+__device__ __forceinline__ void load_gain_pairs(const float* gain, float2 (&g)[NP]) {
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int k = threadIdx.x + i * kConsumers;
+    g[i] = k < S::D / 2 ? __ldg(reinterpret_cast<const float2*>(gain) + k) : make_float2(0.f, 0.f);
+  }
+}
+
+// Gathers the residual stream (D f32 words at `src`, written by other CTAs)
+// and normalises it into sm.xb with gains `gain`.
+template <class S>
+__device__ __forceinline__ bool gather_norm(const DecodeArgs& A, Smem<S>& sm, const uint64_t* src, uint32_t flag,
+                                            uint64_t t0, uint32_t site, const float* gain) {
+  constexpr int NP = S::NP_D;
+  const int t = threadIdx.x;
+  float2 g[NP];
+  load_gain_pairs<S, NP>(gain, g);
+  float hv[NP][2];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) hv[i][0] = hv[i][1] = 0.f;
+  const bool ok = gather_pairs<NP>(
+      A, flag, t0, site, [&](int i) { return src + 2 * (t + i * kConsumers); },
+      [&](int i) { return t + i * kConsumers < S::D / 2; },
+      [&](int i, float a, float b) { hv[i][0] = a; hv[i][1] = b; });
+  return norm_pairs<S, NP>(sm, hv, g, A.eps, ok);
 }
 
 // Producer: streams this CTA's weight ranges for the whole step.
-template <class S>
+template <class S, bool TR>
 __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_t flag, uint64_t t0, int nsteps) {
   const uint64_t pol = l2_policy_evict_first();
   const int G = A.grid_part;
@@ -481,12 +550,13 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     }
     mbar_arrive_expect_tx(&sm.full[slot], bytes);
     bulk_g2s(sm.stage[slot], src, bytes, &sm.full[slot], pol);
-    if (A.stage_trace != nullptr && seq < static_cast<uint32_t>(A.stage_stride))
-      A.stage_trace[static_cast<size_t>(cta) * 3 * A.stage_stride + seq] = globaltimer_ns();
+    stage_stamp<TR>(A, cta, 0, seq);
     ++seq;
   };
-  auto stream = [&](const uint8_t* base, int n, int unit_bytes, int per_stage) {
-    const int a = split_begin(cta, n, G), b = split_begin(cta + 1, n, G);
+  // This CTA's units of a phase: n units split evenly in blocks of `blk`
+  // (the gate/up phase splits whole act words: 2 pairs = 4 rows).
+  auto stream = [&](const uint8_t* base, int n, int unit_bytes, int per_stage, int blk = 1) {
+    const int a = blk * split_begin(cta, n / blk, G), b = blk * split_begin(cta + 1, n / blk, G);
     for (int u = a; u < b && ok; u += per_stage) {
       const int cnt = min(per_stage, b - u);
       issue(base + static_cast<size_t>(u) * unit_bytes, static_cast<uint32_t>(cnt * unit_bytes));
@@ -497,7 +567,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
         const uint8_t* lw = A.wbase + static_cast<size_t>(l) * A.layer_stride;
         stream(lw + A.off_qkv, S::QKV, S::ROWB_D, S::RPS_D);
         stream(lw + A.off_o, S::D, S::ROWB_D, S::RPS_D);
-        stream(lw + A.off_gu, S::DFF, 2 * S::ROWB_D, S::PPS);
+        stream(lw + A.off_gu, 2 * S::DFF, S::ROWB_D, S::RPS_D, 4);
         stream(lw + A.off_down, S::D, S::ROWB_F, S::RPS_F);
       }
       if (ok) stream(A.wbase + A.off_emb, A.vocab, S::ROWB_D, S::RPS_D);
@@ -565,7 +635,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     }
   }
 
-  template <class S>
+  template <class S, bool TR>
   __device__ __forceinline__ bool attention_unit(const DecodeArgs& A, Smem<S>& sm, uint32_t flag,
                                                  uint64_t t0, int l, int pos, int u, int nsplit,
                                                  int trace_slot, uint32_t& att_phase, AttPre& pre) {
@@ -616,7 +686,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       wait_v();
       return false;
     }
-    trace_stamp(A, trace_slot);
+    trace_stamp<TR>(A, trace_slot);
     // RoPE (rotate-half, reference :154-173; f32 tables as model.py:101-107).
     if (t < 64) {
       const int i = t & 31;
@@ -737,7 +807,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     return true;
   }
 
-  template <class S>
+  template <class S, bool TR>
   __global__ void __launch_bounds__(kThreads, 1) decode_b1_kernel(const DecodeArgs A) {
     extern __shared__ __align__(128) uint8_t decode_smem_raw[];
     static_assert(SmemChecks<S>::ok, "");
@@ -768,10 +838,16 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       sm.abort = 0;
       fence_mbar_init();
     }
+    if (t < kPhases) {  // each phase's unit range for this CTA (the producer streams the same ranges)
+      const int n = t == PH_QKV ? S::QKV : t == PH_GU ? S::DFF / 2 : t == PH_VOCAB ? A.vocab : S::D;
+      const int blk = t == PH_GU ? 4 : 1;  // gate/up: whole act words of 4 rows
+      sm.rng[2 * t] = blk * split_begin(cta, n, G);
+      sm.rng[2 * t + 1] = blk * split_begin(cta + 1, n, G);
+    }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-      if (lane == 0) producer_loop<S>(A, sm, cta, flag0, t0, nsteps);
+      if (lane == 0) producer_loop<S, TR>(A, sm, cta, flag0, t0, nsteps);
       return;
     }
 
@@ -781,9 +857,8 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     AttPre pre;
     pre.unit = -1;
     pre.vbytes = 0;
-    trace_stamp(A, 0);
+    trace_stamp<TR>(A, 0);
     const int tf = 1 + A.n_layers * kTracePerLayer;
-    float gr[S::D / kConsumers];
     for (int step = 0; step < nsteps && ok; ++step) {
     const uint32_t flag = flag0 + static_cast<uint32_t>(step);
     const int pos = pos0 + step;
@@ -811,56 +886,58 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     const int nsplit = (pos + A.att_T) / A.att_T;  // ceil((pos+1)/T)
     const int n_units = S::NH * nsplit;
 
-    // Embedding row (reference :87-88).
-    {
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(A.wbase + A.off_emb) +
-                               static_cast<size_t>(tok) * S::D;
-      for (int i = t; i < S::D; i += kConsumers) sm.h[i] = __bfloat162float(e[i]);
-    }
-    consumer_sync<kConsumers>();
-
     for (int l = 0; l < A.n_layers; ++l) {
       uint64_t* lw = A.words + static_cast<size_t>(l) * A.layer_words;
-      load_gain<S>(A.ln1 + static_cast<size_t>(l) * S::D, gr);
       if (cta < n_units) att_prefetch<S>(A, sm, pre, l, pos, cta, nsplit);  // K/V of this layer's unit
-      // ---- residual in: H_l (written by layer l-1's down phase) ----
-      if (l > 0) {
-        ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-            A, flag, t0, SITE_H, [&](int i) { return lw + 2 * (t + i * kConsumers); },
-            [&](int i) { return t + i * kConsumers < S::D / 2; },
-            [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
-        ok = consumer_sync_and<kConsumers>(ok);
-        if (!ok) break;
-      }
-      const int ts = 1 + l * kTracePerLayer;
-      trace_stamp(A, ts + 0);
-      rmsnorm_to_x<S>(sm, gr, A.eps);
-      trace_stamp(A, ts + 1);
-      // ---- QKV rows -> exchange words ----
-      {
-        const int a = split_begin(cta, S::QKV, G), b = split_begin(cta + 1, S::QKV, G);
-        ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_QKV>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                                 [&](int u, float v, float) {
-                                                   if (lane == 0) st_word(lw + S::D + u, v, flag);
-                                                 });
-        ok = consumer_sync_and<kConsumers>(ok);
-        if (!ok) break;
-      }
-      trace_stamp(A, ts + 2);
-      trace_stamp(A, ts + 3);  // rewritten by a CTA that runs an attention unit
-      // ---- attention units ----
-      for (int u = cta; u < n_units && ok; u += G) {
-        ok = attention_unit<S>(A, sm, flag, t0, l, pos, u, nsplit, ts + 3, att_phase, pre);
+      // ---- residual in: the embedding row (reference :87-88) or H_l, written
+      // by layer l-1's down phase; RMSNorm1 -> x ----
+      if (l == 0) {
+        constexpr int NP = S::NP_D;
+        float2 g[NP];
+        load_gain_pairs<S, NP>(A.ln1, g);
+        const uint32_t* e = reinterpret_cast<const uint32_t*>(A.wbase + A.off_emb) +
+                            static_cast<size_t>(tok) * (S::D / 2);
+        float hv[NP][2];
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          const int k = t + i * kConsumers;
+          const uint32_t w2 = k < S::D / 2 ? __ldg(e + k) : 0u;
+          hv[i][0] = bf16_lo(w2);
+          hv[i][1] = bf16_hi(w2);
+        }
+        ok = norm_pairs<S, NP>(sm, hv, g, A.eps, true);
+      } else {
+        ok = gather_norm<S>(A, sm, lw, flag, t0, SITE_H, A.ln1 + static_cast<size_t>(l) * S::D);
       }
       if (!ok) break;
-      trace_stamp(A, ts + 4);
+      const int ts = 1 + l * kTracePerLayer;
+      trace_stamp<TR>(A, ts + 0);
+      trace_stamp<TR>(A, ts + 1);
+      // ---- QKV rows -> exchange words ----
+      {
+        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
+        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_QKV, TR>(
+            A, ring, flag, t0, sm.rng[2 * PH_QKV], sm.rng[2 * PH_QKV + 1], x, [&](int u, float v) {
+              if (lane == 0) st_word(lw + S::D + u, v, flag);
+            });
+        ok = consumer_sync_and<kConsumers>(ok);
+        if (!ok) break;
+      }
+      trace_stamp<TR>(A, ts + 2);
+      trace_stamp<TR>(A, ts + 3);  // rewritten by a CTA that runs an attention unit
+      // ---- attention units ----
+      for (int u = cta; u < n_units && ok; u += G) {
+        ok = attention_unit<S, TR>(A, sm, flag, t0, l, pos, u, nsplit, ts + 3, att_phase, pre);
+      }
+      if (!ok) break;
+      trace_stamp<TR>(A, ts + 4);
       // ---- gather attention partials, merge splits -> x (bf16) ----
       // Item 0 (threads < NH*nsplit): the (m, l) pair of unit t -> shared memory.
       // Items 1..2*nsplit: this thread's 4 output dims of head t/16 per split.
       {
         float va[2 * kMaxSplits], vb[2 * kMaxSplits];
         const int hh = t >> 4, d0 = (t & 15) * 4;
-        ok = gather_pairs<1 + 2 * kMaxSplits>(
+        ok = gather_pairs<1 + 2 * kMaxSplits, 3>(  // groups of 3: (m, l) + one split's 4 dims
             A, flag, t0, SITE_ATT,
             [&](int i) {
               if (i == 0) return lw + A.w_att + static_cast<size_t>(t) * kAttWords + 64;
@@ -874,7 +951,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
             });
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
-        trace_stamp(A, ts + 5);
+        trace_stamp<TR>(A, ts + 5);
         if (hh < S::NH) {
           const float* ml = sm.ml + 2 * hh * nsplit;
           float M = -INFINITY;
@@ -892,96 +969,92 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
             }
           }
           const float inv = 1.0f / fmaxf(L, 1e-10f);
-  #pragma unroll
-          for (int k = 0; k < 4; ++k) sm.xf[xidx(hh * 64 + d0 + k)] = round_bf16(o[k] * inv);
+          __nv_bfloat162* xo = reinterpret_cast<__nv_bfloat162*>(sm.xb) + (hh * 64 + d0) / 2;
+          xo[0] = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+          xo[1] = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
         }
         consumer_sync<kConsumers>();
       }
-      trace_stamp(A, ts + 6);
+      trace_stamp<TR>(A, ts + 6);
       // ---- O rows: HM = H + attn @ Wo^T ----
       {
-        const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-        ok = gemv_phase<S::KD, S::ROWB_D, false, S::J_O>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                                 [&](int u, float v, float) {
-                                                   if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
-                                                 });
+        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
+        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_O, TR>(
+            A, ring, flag, t0, sm.rng[2 * PH_O], sm.rng[2 * PH_O + 1], x, [&](int u, float v) {
+              if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
+            }, TR ? tf + 3 + 8 * l : -1);
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
       }
-      trace_stamp(A, ts + 7);
-      load_gain<S>(A.ln2 + static_cast<size_t>(l) * S::D, gr);
-      // ---- gather HM (the residual after attention) ----
-      ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-          A, flag, t0, SITE_HM, [&](int i) { return lw + A.w_hm + 2 * (t + i * kConsumers); },
-          [&](int i) { return t + i * kConsumers < S::D / 2; },
-          [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
-      ok = consumer_sync_and<kConsumers>(ok);
+      trace_stamp<TR>(A, ts + 7);
+      // ---- gather HM (the residual after attention); RMSNorm2 -> x ----
+      ok = gather_norm<S>(A, sm, lw + A.w_hm, flag, t0, SITE_HM, A.ln2 + static_cast<size_t>(l) * S::D);
       if (!ok) break;
-      trace_stamp(A, ts + 8);
-      rmsnorm_to_x<S>(sm, gr, A.eps);
-      trace_stamp(A, ts + 9);
-      // ---- gate/up pairs -> act = silu(g) * u ----
+      trace_stamp<TR>(A, ts + 8);
+      trace_stamp<TR>(A, ts + 9);
+      // ---- gate/up rows -> act = silu(g) * u; an exchange word holds two acts ----
       {
-        const int a = split_begin(cta, S::DFF, G), b = split_begin(cta + 1, S::DFF, G);
-        ok = gemv_phase<S::KD, S::ROWB_D, true, S::J_GU>(A, ring, flag, t0, a, b, S::PPS, sm.xf,
-                                                [&](int u, float gt, float up) {
-                                                  if (lane == 0) {
-                                                    const float act = gt * (1.0f / (1.0f + __expf(-gt))) * up;
-                                                    st_word(lw + A.w_act + u, act, flag);
-                                                  }
-                                                });
+        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
+        const int a = sm.rng[2 * PH_GU], b = sm.rng[2 * PH_GU + 1];
+        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_GU, TR>(
+            A, ring, flag, t0, a, b, x, [&](int u, float v) {
+              if (lane == 0) sm.gu_out[u - a] = v;
+            }, TR ? tf + 3 + 8 * l + 4 : -1);
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
+        // rows 4i .. 4i + 3 of the CTA's range: gate, up of pair 2m, gate, up of pair 2m + 1
+        if (t < (b - a) / 4) {
+          const float4 gu = reinterpret_cast<const float4*>(sm.gu_out)[t];
+          const float a0 = gu.x * (1.0f / (1.0f + __expf(-gu.x))) * gu.y;
+          const float a1 = gu.z * (1.0f / (1.0f + __expf(-gu.z))) * gu.w;
+          const __nv_bfloat162 pk = __floats2bfloat162_rn(a0, a1);
+          st_word(lw + A.w_act + a / 4 + t, __uint_as_float(*reinterpret_cast<const uint32_t*>(&pk)), flag);
+        }
       }
-      trace_stamp(A, ts + 10);
+      trace_stamp<TR>(A, ts + 10);
       // ---- gather act -> x (bf16), down rows: H_{l+1} = HM + act @ Wd^T ----
       {
-        ok = gather_pairs<(S::DFF / 2 + kConsumers - 1) / kConsumers>(
+        // word m holds act[2m] (low half) and act[2m + 1]; thread t reads word
+        // pairs p = t + 256 i, i.e. act[4p .. 4p + 3]
+        ok = gather_pairs<S::NP_ACT>(
             A, flag, t0, SITE_ACT, [&](int i) { return lw + A.w_act + 2 * (t + i * kConsumers); },
-            [&](int i) { return t + i * kConsumers < S::DFF / 2; },
-            [&](int i, float a, float b) {
-              const int k = t + i * kConsumers;
-              sm.xf[xidx(2 * k)] = round_bf16(a);
-              sm.xf[xidx(2 * k + 1)] = round_bf16(b);
+            [&](int i) { return t + i * kConsumers < S::DFF / 4; },
+            [&](int i, float a, float b) {  // the payloads are the bf16 pairs, in order
+              reinterpret_cast<uint2*>(sm.xb)[t + i * kConsumers] = make_uint2(__float_as_uint(a), __float_as_uint(b));
             });
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
-        trace_stamp(A, ts + 11);
+        trace_stamp<TR>(A, ts + 11);
+        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
         uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
-        const int a = split_begin(cta, S::D, G), b = split_begin(cta + 1, S::D, G);
-        ok = gemv_phase<S::KF, S::ROWB_F, false, S::J_DOWN>(A, ring, flag, t0, a, b, S::RPS_F, sm.xf,
-                                                 [&](int u, float v, float) {
-                                                   if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
-                                                 });
+        ok = gemv_phase<S::KF, S::ROWB_F, S::RPS_F, S::J_DOWN, TR>(
+            A, ring, flag, t0, sm.rng[2 * PH_DOWN], sm.rng[2 * PH_DOWN + 1], x, [&](int u, float v) {
+              if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
+            });
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
       }
-      trace_stamp(A, ts + 12);
+      trace_stamp<TR>(A, ts + 12);
     }
 
     if (ok) {
       // ---- final norm + tied logits + argmax (reference :314-357) ----
       uint64_t* fw = A.words + static_cast<size_t>(A.n_layers) * A.layer_words;
-      ok = gather_pairs<(S::D / 2 + kConsumers - 1) / kConsumers>(
-          A, flag, t0, SITE_FINAL, [&](int i) { return fw + 2 * (t + i * kConsumers); },
-          [&](int i) { return t + i * kConsumers < S::D / 2; },
-          [&](int i, float a, float b) { const int k = t + i * kConsumers; sm.h[2 * k] = a; sm.h[2 * k + 1] = b; });
-      ok = consumer_sync_and<kConsumers>(ok);
+      ok = gather_norm<S>(A, sm, fw, flag, t0, SITE_FINAL, A.lnf);
     }
-    trace_stamp(A, tf + 0);
+    trace_stamp<TR>(A, tf + 0);
     if (ok) {
-      load_gain<S>(A.lnf, gr);
-      rmsnorm_to_x<S>(sm, gr, A.eps);
+      const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
       float best_v = -INFINITY;
       int best_i = 0x7fffffff;
-      const int a = split_begin(cta, A.vocab, G), b = split_begin(cta + 1, A.vocab, G);
-      ok = gemv_phase_wide<S::KD, S::ROWB_D>(A, ring, flag, t0, a, b, S::RPS_D, sm.xf,
-                                               [&](int u, float v, float) {
-                                                 if (lane == 0 && A.logits) A.logits[u] = v;
-                                                 if (v > best_v) { best_v = v; best_i = u; }
-                                               });
+      ok = gemv_phase_wide<S::KD, S::ROWB_D, S::RPS_D>(A, ring, flag, t0, sm.rng[2 * PH_VOCAB],
+                                                       sm.rng[2 * PH_VOCAB + 1], x,
+                                                       [&](int u, float v, float) {
+                                                         if (lane == 0 && A.logits) A.logits[u] = v;
+                                                         if (v > best_v) { best_v = v; best_i = u; }
+                                                       });
       ok = consumer_sync_and<kConsumers>(ok);
-      trace_stamp(A, tf + 1);
+      trace_stamp<TR>(A, tf + 1);
       if (ok) {
         if (lane == 0) { sm.am_v[warp] = best_v; sm.am_i[warp] = best_i; }
         consumer_sync<kConsumers>();
@@ -1017,7 +1090,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       }
     }
   }  // step
-  trace_stamp(A, tf + 2);
+  trace_stamp<TR>(A, tf + 2);
   if (!ok) {
     // a K/V staging copy requested for an attention unit that never ran
     if (pre.vbytes) {
