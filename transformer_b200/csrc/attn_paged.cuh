@@ -36,6 +36,7 @@
 #include <cuda_bf16.h>
 
 #include "batched.cuh"
+#include "tc_ptx.cuh"
 
 namespace b2d {
 
@@ -44,6 +45,22 @@ constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
 constexpr int kPaMaxSplits = 4; // units per (row, kv head)
 constexpr int kPaWarpSmem = kPaStages * kPaStageElems * 2 + 256;  // ring + the new K / V row (bytes)
+// TMA page path (paged pool): a page's K and V rows land as two 2 KB tensor
+// copies with the 128-byte swizzle (16-byte chunk c of row r at chunk
+// c ^ (r % 8)), so the ldmatrix row reads are conflict-free without padding.
+constexpr int kPaPageBytes = 2 * kPageTokens * 128;                  // K then V, 4 KB
+constexpr int kPaWarpSmemTma = kPaStages * kPaPageBytes + 1024;      // ring + new K/V row + mbarriers (1024-aligned)
+constexpr uint64_t kPaWaitNs = 200000000ull;                          // bound on every page wait
+static_assert(kPaStages * kPaPageBytes + 256 + 8 * kPaStages <= kPaWarpSmemTma, "TMA ring layout");
+static_assert(kPaWarpSmemTma % 1024 == 0, "every warp's ring starts 1024-byte aligned");
+// Dynamic shared memory of a CTA of W warps.
+constexpr __host__ __device__ int pa_smem_bytes(int w, bool tma) {
+  return tma ? w * kPaWarpSmemTma + 1024 : w * kPaWarpSmem;
+}
+// Byte offset of 16-byte chunk c of row r inside a swizzled 16-row tile.
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
 // warps per CTA for a split count (a row's units share a CTA)
 constexpr __host__ __device__ int pa_warps(int splits) { return splits > 2 ? splits : 2; }
 
@@ -94,13 +111,19 @@ __device__ __forceinline__ const __nv_bfloat16* page_rows(const PagedAttnArgs& a
                       (kPageTokens * 64);
 }
 
-// grid ceil(rows * n_kv * splits / W), W * 32 threads, W * kPaWarpSmem bytes
-// of dynamic shared memory; a.cpc = splits (1, 2 or 4), W = pa_warps(splits).
-// Unit u = blockIdx.x * W + warp is (b, g, x) with u = (b * n_kv + g) *
-// splits + x.
-template <int W>
-__global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_constant__ PagedAttnArgs a, int n_rows) {
-  extern __shared__ __align__(16) uint8_t pa_smem[];
+// grid ceil(rows * n_kv * splits / W), W * 32 threads, pa_smem_bytes(W, TMA)
+// bytes of dynamic shared memory; a.cpc = splits (1, 2 or 4), W =
+// pa_warps(splits).  Unit u = blockIdx.x * W + warp is (b, g, x) with u =
+// (b * n_kv + g) * splits + x.  TMA = true needs a paged pool (a.table) and
+// kvmap: the pool as rows of 64 bf16 (128 B), boxes of 16 rows, 128-byte
+// swizzle; otherwise kvmap is unused and pages arrive by per-lane cp.async.
+template <int W, bool TMA>
+__global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_constant__ CUtensorMap kvmap,
+                                                                const __grid_constant__ PagedAttnArgs a, int n_rows) {
+  extern __shared__ __align__(16) uint8_t pa_smem_raw[];
+  constexpr int WS = TMA ? kPaWarpSmemTma : kPaWarpSmem;  // bytes per warp
+  uint8_t* pa_smem = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pa_smem_raw) + 1023) & ~uintptr_t(1023))
+                         : pa_smem_raw;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int splits = a.cpc;
@@ -114,9 +137,18 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     if (trace != nullptr && lane == 0) trace[slot] = globaltimer_ns();
   };
   stamp(0);
-  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * kPaWarpSmem);
-  __nv_bfloat16* skn = ring + kPaStages * kPaStageElems;  // the new position's K / V (bf16, as cached)
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * WS);
+  // the new position's K / V (bf16, as cached) after the ring
+  __nv_bfloat16* skn = TMA ? reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * WS + kPaStages * kPaPageBytes)
+                           : ring + kPaStages * kPaStageElems;
   __nv_bfloat16* svn = skn + 64;
+  uint64_t* pbar = reinterpret_cast<uint64_t*>(skn + 128);  // TMA: one mbarrier per ring slot
+  if (TMA && lane == 0) {
+    for (int i = 0; i < kPaStages; ++i) mbar_init(&pbar[i], 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&kvmap);
+  }
+  __syncwarp();
   const int GQA = a.n_heads / a.n_kv;
   const bool early = a.append;  // decode: the cache pages do not depend on the waited-for kernel
   if (!early) {
@@ -156,9 +188,21 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   // ---- page ring ----
   const int nw = bad ? 0 : pg_hi - pg_lo;
   const int rows_max = a.table == nullptr ? a.ctx : 1 << 30;  // contiguous cache: no row past the context
+  const uint64_t pol = l2_policy_evict_first();  // every K/V page is read once per step
   auto issue = [&](int k) {
     const int pg = pg_lo + k;  // (warp-uniform)
     const int blk = tb == nullptr ? 0 : pg < 32 ? __shfl_sync(0xffffffffu, tbl, pg) : tb[pg];
+    if constexpr (TMA) {
+      if (lane == 0) {
+        const int slot = k % kPaStages;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(ring) + slot * kPaPageBytes;
+        const int rk = (((a.layer * a.num_blocks + blk) * 2) * a.n_kv + g) * kPageTokens;  // K rows (host checks the range)
+        mbar_arrive_expect_tx(&pbar[slot], kPaPageBytes);
+        tma_load_2d(dst, &kvmap, 0, rk, &pbar[slot], pol);
+        tma_load_2d(dst + kPaPageBytes / 2, &kvmap, 0, rk + a.n_kv * kPageTokens, &pbar[slot], pol);
+      }
+      return;
+    }
     const __nv_bfloat16* ks = page_rows(a, blk, pg, 0, g);
     const __nv_bfloat16* vs = page_rows(a, blk, pg, 1, g);
     const uint32_t dst = smem_addr(ring + (k % kPaStages) * kPaStageElems);
@@ -174,8 +218,25 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
 #pragma unroll
   for (int k = 0; k < kPaStages; ++k) {
     if (k < nw) issue(k);
-    cp_async_commit();
+    if (!TMA) cp_async_commit();
   }
+  // TMA: waits for page k's copies (bounded; a timeout sets the status word and
+  // the page's data are not used for anything that is written out)
+  bool tma_ok = true;
+  auto wait_page = [&](int k) {
+    const uint32_t par = static_cast<uint32_t>(k / kPaStages) & 1u;
+    uint64_t* bar = &pbar[k % kPaStages];
+    if (mbar_test(bar, par)) return;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t n = 0;
+    while (!mbar_test(bar, par)) {
+      if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kPaWaitNs) {
+        if (lane == 0) atomicCAS(a.status, 0u, 0x10Cu);  // timeout | site 12 (attention pages)
+        tma_ok = false;
+        return;
+      }
+    }
+  };
   // RoPE factors of position p (model constants): lane (gid, tig) needs pairs
   // 2tig, 2tig+1 and 8+2tig, 9+2tig of k-steps 0, 1; the owner's K row needs lane.
   float2 rc[2][2], rs[2][2];
@@ -263,21 +324,43 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   for (int k = 0; k < nw; k += 2) {  // pages k, k + 1 (when present) as one block of 32 positions
     const int pg = pg_lo + k;
     const bool two = k + 1 < nw;
-    __nv_bfloat16* st0 = ring + (k % kPaStages) * kPaStageElems;
-    __nv_bfloat16* st1 = ring + ((k + 1) % kPaStages) * kPaStageElems;
-    cp_async_wait<kPaStages - 2>();
+    __nv_bfloat16* st0 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + (k % kPaStages) * kPaPageBytes)
+                             : ring + (k % kPaStages) * kPaStageElems;
+    __nv_bfloat16* st1 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + ((k + 1) % kPaStages) * kPaPageBytes)
+                             : ring + ((k + 1) % kPaStages) * kPaStageElems;
+    if constexpr (TMA) {
+      wait_page(k);
+      if (two) wait_page(k + 1);
+    } else {
+      cp_async_wait<kPaStages - 2>();
+    }
     __syncwarp();
     if (pg == npg - 1 || (two && pg + 1 == npg - 1)) {  // the page of position p: its row from the new
       __nv_bfloat16* st = pg == npg - 1 ? st0 : st1;   // K / V, V rows past p zeroed
       const int rp = p - (npg - 1) * kPageTokens;
-      if (lane < 8)
-        *reinterpret_cast<uint4*>(st + rp * kPaPitch + lane * 8) = reinterpret_cast<const uint4*>(skn)[lane];
-      else if (lane < 16)
-        *reinterpret_cast<uint4*>(st + (kPageTokens + rp) * kPaPitch + (lane - 8) * 8) =
-            reinterpret_cast<const uint4*>(svn)[lane - 8];
-      for (int i = lane; i < kPageTokens * 8; i += 32) {
-        const int r = i >> 3;
-        if (r > rp) *reinterpret_cast<uint4*>(st + (kPageTokens + r) * kPaPitch + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
+      if constexpr (TMA) {
+        uint8_t* sbt = reinterpret_cast<uint8_t*>(st);
+        if (lane < 8)
+          *reinterpret_cast<uint4*>(sbt + sw128(rp, lane)) = reinterpret_cast<const uint4*>(skn)[lane];
+        else if (lane < 16)
+          *reinterpret_cast<uint4*>(sbt + kPaPageBytes / 2 + sw128(rp, lane - 8)) =
+              reinterpret_cast<const uint4*>(svn)[lane - 8];
+        for (int i = lane; i < kPageTokens * 8; i += 32) {
+          const int r = i >> 3;
+          if (r > rp) *reinterpret_cast<uint4*>(sbt + kPaPageBytes / 2 + r * 128 + (i & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        // these generic stores precede the slot's next tensor copy (a later page)
+        fence_proxy_async_smem();
+      } else {
+        if (lane < 8)
+          *reinterpret_cast<uint4*>(st + rp * kPaPitch + lane * 8) = reinterpret_cast<const uint4*>(skn)[lane];
+        else if (lane < 16)
+          *reinterpret_cast<uint4*>(st + (kPageTokens + rp) * kPaPitch + (lane - 8) * 8) =
+              reinterpret_cast<const uint4*>(svn)[lane - 8];
+        for (int i = lane; i < kPageTokens * 8; i += 32) {
+          const int r = i >> 3;
+          if (r > rp) *reinterpret_cast<uint4*>(st + (kPageTokens + r) * kPaPitch + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
+        }
       }
       __syncwarp();
     }
@@ -292,7 +375,9 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
       for (int j = 0; j < 4; ++j) {
         if (j >= 2 && !two) continue;
         uint32_t b0, b1, b2, b3;  // (s2: dims +0, +8), (s2 + 1: dims +0, +8)
-        ldsm_x4((j < 2 ? sb0 : sb1) + 2u * ((8 * (j & 1) + mr) * kPaPitch + 16 * s2 + 8 * mi), b0, b1, b2, b3);
+        const int kr = 8 * (j & 1) + mr;  // K row of the page
+        ldsm_x4((j < 2 ? sb0 : sb1) + (TMA ? sw128(kr, 2 * s2 + mi) : 2u * (kr * kPaPitch + 16 * s2 + 8 * mi)), b0, b1, b2,
+                b3);
         mma_bf16(sc[j], qa[s2][0], qa[s2][1], qa[s2][2], qa[s2][3], b0, b1);
         mma_bf16(sc[j], qa[s2 + 1][0], qa[s2 + 1][1], qa[s2 + 1][2], qa[s2 + 1][3], b2, b3);
       }
@@ -333,19 +418,28 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         uint32_t b0, b1, b2, b3;  // (tile j: rows 0-7, 8-15), (tile j+1: rows 0-7, 8-15)
-        ldsm_x4_t(sb + 2u * ((kPageTokens + (mi & 1) * 8 + mr) * kPaPitch + 8 * (j + (mi >> 1))), b0, b1, b2, b3);
+        const int vr = (mi & 1) * 8 + mr;  // V row of the page
+        ldsm_x4_t(sb + (TMA ? kPaPageBytes / 2 + sw128(vr, j + (mi >> 1))
+                            : 2u * ((kPageTokens + vr) * kPaPitch + 8 * (j + (mi >> 1)))),
+                  b0, b1, b2, b3);
         mma_bf16(o[j], pa0, pa1, pa2, pa3, b0, b1);
         mma_bf16(o[j + 1], pa0, pa1, pa2, pa3, b2, b3);
       }
     }
     __syncwarp();  // every lane's reads of these stages are done before they are refilled
     if (k + kPaStages < nw) issue(k + kPaStages);
-    cp_async_commit();
+    if (!TMA) cp_async_commit();
     if (k + 1 + kPaStages < nw) issue(k + 1 + kPaStages);
-    cp_async_commit();
+    if (!TMA) cp_async_commit();
     if (k == 0) stamp(4);
   }
-  cp_async_wait<0>();
+  if (!TMA) cp_async_wait<0>();  // (TMA: every issued page was waited for in the loop)
+  if (TMA && !tma_ok) {
+    // a page wait ran out (status word set; this row's output is not meaningful):
+    // wait once more, bounded, for every slot's last copy so none is in flight at
+    // exit; the warp goes on to the row's barrier like the others
+    for (int k = max(0, nw - kPaStages); k < nw; ++k) wait_page(k);
+  }
   stamp(5);
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
@@ -383,10 +477,10 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     if (hh < GQA) {
       float M = -INFINITY;
       for (int j = 0; j < splits; ++j)
-        M = fmaxf(M, reinterpret_cast<const float*>(pa_smem + (warp + j) * kPaWarpSmem)[256 + hh]);
+        M = fmaxf(M, reinterpret_cast<const float*>(pa_smem + (warp + j) * WS)[256 + hh]);
       float L = 0.f, r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int j = 0; j < splits; ++j) {
-        const float* pj = reinterpret_cast<const float*>(pa_smem + (warp + j) * kPaWarpSmem);
+        const float* pj = reinterpret_cast<const float*>(pa_smem + (warp + j) * WS);
         const float mj = pj[256 + hh];
         const float wgt = mj == -INFINITY ? 0.f : __expf(mj - M);
         L = fmaf(wgt, pj[260 + hh], L);

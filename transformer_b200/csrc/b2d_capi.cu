@@ -152,6 +152,10 @@ struct b2d_ws {
   uint32_t tune_gen;       // bumped by every b2d_debug_tune call (cached graphs bake the knobs in)
   bool no_graph;           // step through direct launches only
   cudaStream_t cap_stream; // capture stream (created on first capture)
+  // paged attention: TMA view of the last paged pool used (rows of 64 bf16)
+  CUtensorMap kvmap;
+  const void* kvmap_pool;
+  int kvmap_nblk;
 };
 
 namespace {
@@ -190,11 +194,14 @@ cudaError_t attn_smem_attrs() {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (raised[dev]) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(b2d::paged_attn_mma_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       2 * b2d::kPaWarpSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(b2d::paged_attn_mma_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             4 * b2d::kPaWarpSmem);
+  cudaError_t e = cudaSuccess;
+  const std::pair<const void*, int> ks[] = {
+      {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<2, false>), b2d::pa_smem_bytes(2, false)},
+      {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<4, false>), b2d::pa_smem_bytes(4, false)},
+      {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<2, true>), b2d::pa_smem_bytes(2, true)},
+      {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<4, true>), b2d::pa_smem_bytes(4, true)}};
+  for (const auto& k : ks)
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k.first, cudaFuncAttributeMaxDynamicSharedMemorySize, k.second);
   if (e == cudaSuccess) raised[dev] = true;
   return e;
 }
@@ -698,6 +705,21 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   }
   const int att_w = b2d::pa_warps(pa.cpc);
   B2D_CUDA(attn_smem_attrs(), "attention attributes");
+  // Paged pool: pages arrive as TMA tensor copies (two 2 KB boxes per page)
+  // when the pool's rows of 64 bf16 are addressable with 32-bit coordinates.
+  CUtensorMap kvmap{};
+  const uint64_t pool_rows = uint64_t(c.n_layers) * uint64_t(num_blocks) * 2 * uint64_t(c.n_kv_heads) * b2d::kPageTokens;
+  const bool att_tma = table != nullptr && pool_rows <= 0x7fffffffull;
+  if (att_tma) {
+    if (ws->kvmap_pool != cache || ws->kvmap_nblk != num_blocks) {
+      if (!b2d::make_kmajor_map(&ws->kvmap, cache, 64, pool_rows, b2d::kPageTokens)) return B2D_ERR_CUDA;
+      ws->kvmap_pool = cache;
+      ws->kvmap_nblk = num_blocks;
+    }
+    kvmap = ws->kvmap;
+  }
+  auto* att_k2 = att_tma ? b2d::paged_attn_mma_kernel<2, true> : b2d::paged_attn_mma_kernel<2, false>;
+  auto* att_k4 = att_tma ? b2d::paged_attn_mma_kernel<4, true> : b2d::paged_attn_mma_kernel<4, false>;
   const int att_units = batch * c.n_kv_heads * pa.cpc;
   // RMSNorm of the residual stream, folded: each residual projection writes
   // X = bf16(h * g_next) and per-tile sums of squares; the next projection
@@ -713,12 +735,12 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     if (prefill)  // every row's K/V in the cache before any row attends
       B2D_CUDA(launch_k(b2d::kv_append_kernel, dim3(batch, c.n_kv_heads), dim3(32), st, pdl, pa), "kv append");
     if (att_w == 2)
-      B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<2>, dim3((att_units + 1) / 2), dim3(64),
-                             2 * b2d::kPaWarpSmem, st, pdl, pa, batch),
+      B2D_CUDA(launch_k_smem(att_k2, dim3((att_units + 1) / 2), dim3(64), b2d::pa_smem_bytes(2, att_tma), st, pdl,
+                             kvmap, pa, batch),
                "attention");
     else
-      B2D_CUDA(launch_k_smem(b2d::paged_attn_mma_kernel<4>, dim3((att_units + 3) / 4), dim3(128),
-                             4 * b2d::kPaWarpSmem, st, pdl, pa, batch),
+      B2D_CUDA(launch_k_smem(att_k4, dim3((att_units + 3) / 4), dim3(128), b2d::pa_smem_bytes(4, att_tma), st, pdl,
+                             kvmap, pa, batch),
                "attention");
     launches_other += prefill ? 2 : 1;
     g.M = D; g.K = D; g.y = ws->Hm; g.resid = ws->H; g.ldy = D;

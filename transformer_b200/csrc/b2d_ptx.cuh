@@ -90,6 +90,11 @@ __device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v) {
 // Orders this thread's (acquired) view of generic-proxy memory before its
 // later async-proxy (bulk copy) accesses.
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk / tensor copy) accesses of it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
