@@ -154,3 +154,36 @@ def test_cfg4_sampled_streams_teacher_forced(engine306, params306_f32):
                 ref = dec.step([int(toks[b, i])], [prompts.shape[1] + i])[0]
     total = steps * prompts.shape[0]
     print(f"cfg4: device draw equals the float32 oracle's stream at {same_as_stream}/{total} steps")
+
+
+@pytest.mark.parametrize("scale,ties", [(0.64, False), (3.0, False), (0.05, False), (4.0, True)])
+def test_topp_cutoff_equals_numpy_cumsum(engine306, scale, ties):
+    """The number of tokens top-p keeps equals numpy's: the first k + 1 with
+    float64(cumsum_f32(p_sorted)[k]) >= top_p (generate.py:58-60), where the
+    float32 cumsum is sequential.  The device evaluates that chain exactly but
+    in parallel (integer prefix sums within a binade of the running sum, with
+    binade crossings and exact rounding ties resolved one addition at a time),
+    so the count must match exactly.  Read from the sampler's diagnostic
+    stamp buffer (slot 6)."""
+    rng = np.random.default_rng(int(100 * scale) + ties)
+    smp = Sampler(engine306, 1, 8)
+    buf = torch.zeros(1, 8, dtype=torch.int64, device=engine306.device)
+    engine306.debug_tune(sample_trace=buf)
+    try:
+        for case in range(24):
+            logits = (rng.standard_normal(32000) * scale).astype(np.float32)
+            if ties:  # many exactly equal probabilities
+                logits = (np.round(logits * 4) / 4).astype(np.float32)
+            top_p = [0.5, 0.9, 0.95, 0.99, 0.999999, 0.3][case % 6]
+            temp = [1.0, 0.7][case % 2]
+            _device_sample(smp, logits, temp, top_p, 1.0, [], 0.5)
+            got = int(buf[0, 6].item()) & 0xffffffff
+            lg = logits / np.float32(temp) if temp != 1.0 else logits.copy()
+            lg = lg - lg.max()
+            p = OS.exp_f32(lg)
+            p = p / OS.pairwise_sum_f32(p)
+            order = np.lexsort((np.arange(p.size), -p))
+            want = min(int(np.searchsorted(np.cumsum(p[order], dtype=np.float32), top_p)) + 1, p.size)
+            assert got == want, (case, top_p, got, want)
+    finally:
+        engine306.debug_tune(sample_trace=torch.zeros(0, dtype=torch.int64))

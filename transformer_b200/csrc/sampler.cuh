@@ -62,6 +62,13 @@ struct SamplerSmem {
   int red_i[kSamplerThreads / 32];
   int cutoff;
   int token;
+  // top-p cutoff state: the exact float32 running sum c of the sorted
+  // probabilities before element ch_k, the result (0 = not found yet), and the
+  // first event of a parallel round (position, prefix before it, kind)
+  float ch_c;
+  int ch_k, ch_cut, ev_k, ev_kind;
+  long long ev_s, ch_tot;
+  long long scan64[kSamplerThreads / 32];
   int rs_cnt[kSamplerThreads / 32][16];  // radix sort: digit counts / running offsets per warp
   int rs_off[kSamplerThreads / 32][16];
 };
@@ -266,6 +273,163 @@ __device__ void radix_sort(SamplerSmem& sm, uint64_t* gbuf) {
   }
 }
 
+// numpy's top-p cutoff on the sorted probabilities p_k = key_to_p(key[k]):
+// the first k + 1 with float64(c_k) >= top_p, where c_k = fl32(c_{k-1} + p_k)
+// is numpy's sequential float32 cumsum (V if never).  float64(c) >= top_p is
+// c >= thr with thr = top_p rounded up to a float.
+//
+// The chain is evaluated exactly but in parallel.  While the running sum c
+// stays in one binade [2^E, 2^(E+1)) it is an integer multiple of u = 2^(E-23),
+// and fl32(c + p) = c + u * round(p / u) (round to nearest) unless p / u has a
+// fractional part of exactly 1/2 (then the tie goes to the even multiple,
+// which depends on c).  So a round of the block scales a chunk of 8 elements
+// per thread by 1/u, takes the integer prefix sums of the rounded values, and
+// finds the first element that (a) is a tie, (b) would carry the sum into the
+// next binade, or (c) reaches thr.  Events (a) and (b) are resolved with one
+// ordinary float32 addition and the next round starts after them; (c) ends.
+// The first kSeqHead elements, where c is small and changes binade often,
+// run sequentially (in blocks of 16 prefetched keys).  Sorted descending, every later p_k <= c, so p / u < 2^24.
+__device__ int topp_cutoff(SamplerSmem& sm, int V, double top_p, uint64_t* diag, int& rounds) {
+  constexpr int kSeqHead = 512, kPer = 8, kChunk = kPer * kSamplerThreads;
+  constexpr int kWarps = kSamplerThreads / 32;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float thr = __double2float_ru(top_p);
+  if (t == 0) {  // the head, 16 keys per block: the sum never decreases, so a
+                 // block whose end stays below thr needs no per-key test
+    const uint4* k4 = reinterpret_cast<const uint4*>(sm.key);
+    const int n0 = min(kSeqHead, V);  // a multiple of 16, or V
+    float c = 0.f;
+    int cut = 0, base = 0;
+    uint4 nxt[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) nxt[q] = k4[q];
+    for (; base < n0; base += 16) {
+      uint4 cur[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) nxt[q] = base + 16 + 4 * q < kSamplerMaxVocab ? k4[(base + 16) / 4 + q] : cur[q];
+      float e = c;
+      const int nk = min(16, n0 - base);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // keys at or past V decode to p = 0
+        e = __fadd_rn(e, 4 * q + 0 < nk ? key_to_p(cur[q].x) : 0.f);
+        e = __fadd_rn(e, 4 * q + 1 < nk ? key_to_p(cur[q].y) : 0.f);
+        e = __fadd_rn(e, 4 * q + 2 < nk ? key_to_p(cur[q].z) : 0.f);
+        e = __fadd_rn(e, 4 * q + 3 < nk ? key_to_p(cur[q].w) : 0.f);
+      }
+      if (e >= thr) {
+        for (int i = 0; i < nk; ++i) {
+          c = __fadd_rn(c, key_to_p(sm.key[base + i]));
+          if (c >= thr) {
+            cut = base + i + 1;
+            break;
+          }
+        }
+        break;
+      }
+      c = e;
+    }
+    sm.ch_c = c;
+    sm.ch_k = cut ? cut : n0;
+    sm.ch_cut = cut ? cut : (n0 == V ? V : 0);
+    if (diag) diag[0] = globaltimer_ns();
+  }
+  __syncthreads();
+  rounds = 0;
+  while (sm.ch_cut == 0) {
+    ++rounds;
+    const int k0 = sm.ch_k;
+    const float c = sm.ch_c;  // > 0: it holds p_0, the largest probability
+    int ex;
+    frexpf(c, &ex);  // c in [2^(ex-1), 2^ex): ulp u = 2^(ex-24)
+    const float scale = ldexpf(1.0f, 24 - ex);  // 1 / u, a power of two
+    const long long c0 = static_cast<long long>(__fmul_rn(c, scale));  // c / u, exact (< 2^24)
+    // T: the first running sum (in units of u) that reaches thr
+    const long long T = static_cast<long long>(ceil(static_cast<double>(thr) * static_cast<double>(scale)));
+    float y[kPer];
+    long long loc = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = k0 + kPer * t + j;
+      const float p = k < V ? key_to_p(sm.key[k]) : 0.f;
+      y[j] = __fmul_rn(p, scale);  // p / u, exact, < 2^24
+      const float q = floorf(y[j]);
+      loc += static_cast<long long>(q) + (y[j] - q > 0.5f ? 1 : 0);
+    }
+    // exclusive block scan of the per-thread sums (64-bit)
+    long long inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += v;
+    }
+    if (lane == 31) sm.scan64[warp] = inc;
+    if (t == 0) sm.ev_k = 0x7fffffff;
+    __syncthreads();
+    long long wt = lane < kWarps ? sm.scan64[lane] : 0;  // every warp scans the warp totals
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long v = __shfl_up_sync(0xffffffffu, wt, o);
+      if (lane >= o) wt += v;
+    }
+    const long long wbefore = warp > 0 ? __shfl_sync(0xffffffffu, wt, warp - 1) : 0;
+    long long S = c0 + wbefore + inc - loc;
+    int ev = 0x7fffffff, kind = 0;
+    long long ev_s = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = k0 + kPer * t + j;
+      if (k >= V || ev != 0x7fffffff) continue;
+      const float q = floorf(y[j]);
+      const float f = y[j] - q;
+      const long long qi = static_cast<long long>(q);
+      if (f == 0.5f || S + qi >= (1ll << 24) - 2) {  // exact tie, or the sum may leave the binade
+        ev = k; kind = 1; ev_s = S;
+        continue;
+      }
+      S += qi + (f > 0.5f ? 1 : 0);
+      if (S >= T) {  // threshold reached at k
+        ev = k; kind = 2; ev_s = S;
+      }
+    }
+    if (ev != 0x7fffffff) atomicMin(&sm.ev_k, ev);
+    __syncthreads();
+    if (ev != 0x7fffffff && ev == sm.ev_k) {  // the owner of the first event
+      sm.ev_kind = kind;
+      sm.ev_s = ev_s;
+    }
+    if (t == kSamplerThreads - 1) sm.ch_tot = S;  // the chunk's end (used when no event)
+    __syncthreads();
+    if (t == 0) {
+      const int k = sm.ev_k;
+      const float u = ldexpf(1.0f, ex - 24);
+      if (k == 0x7fffffff) {  // no event: the whole chunk stays in the binade, below thr
+        const int end = min(k0 + kChunk, V);
+        sm.ch_c = __fmul_rn(static_cast<float>(sm.ch_tot), u);  // < 2^24 units: exact
+        sm.ch_k = end;
+        if (end >= V) sm.ch_cut = V;
+      } else if (sm.ev_kind == 2) {
+        sm.ch_cut = k + 1;
+      } else {
+        const float cb = __fmul_rn(static_cast<float>(sm.ev_s), u);  // the exact sum before k
+        const float ck = __fadd_rn(cb, key_to_p(sm.key[k]));
+        if (ck >= thr) {
+          sm.ch_cut = k + 1;
+        } else {
+          sm.ch_c = ck;
+          sm.ch_k = k + 1;
+          if (k + 1 >= V) sm.ch_cut = V;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const int cut = sm.ch_cut;
+  __syncthreads();
+  return cut;
+}
+
 __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const SampleArgs a) {
   extern __shared__ __align__(16) uint8_t sampler_smem_raw[];
   SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(sampler_smem_raw);
@@ -273,7 +437,9 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   const int V = a.vocab;
   const float* lg = a.logits + static_cast<size_t>(b) * V;
   constexpr int PER = kSamplerMaxVocab / kSamplerThreads;
-  // stamps: 0 entry, 1 exponentials, 2 normalised, 3 sorted, 4 cutoff, 5 drawn
+  // stamps: 0 entry, 1 exponentials, 2 normalised, 3 sorted, 4 cutoff, 5 drawn;
+  // slot 6 = the top-p cutoff (tokens kept) | parallel rounds of the cutoff << 32,
+  // slot 7 = end of the cutoff's sequential head (global timer)
   auto stamp = [&](int slot) {
     if (a.trace != nullptr && t == 0) a.trace[static_cast<size_t>(b) * 8 + slot] = globaltimer_ns();
   };
@@ -379,54 +545,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   stamp(2);
   radix_sort(sm, a.scratch + static_cast<size_t>(b) * kSamplerMaxVocab);
   stamp(3);
-  // cutoff = first k with float64(cumsum_f32[k]) >= top_p, plus one.  The
-  // running sum is a float, so float64(c) >= top_p  <=>  c >= thr with thr =
-  // top_p rounded up to a float: the chain stays in float32 (the cumulative
-  // sum itself is sequential, as numpy's).
-  if (t == 0) {  // one thread runs the float32 chain in order, 16 keys per block
-    const float thr = __double2float_ru(a.top_p);
-    const uint4* k4 = reinterpret_cast<const uint4*>(sm.key);
-    const int n4 = (V + 3) / 4;  // keys past V decode to p = 0
-    constexpr int Q = 4;         // uint4 per block
-    auto load_blk = [&](int base, uint4 (&dst)[Q]) {
-#pragma unroll
-      for (int q = 0; q < Q; ++q) dst[q] = base + q < n4 ? k4[base + q] : make_uint4(~0u, ~0u, ~0u, ~0u);
-    };
-    float c = 0.f;
-    int cut = V;
-    uint4 nxt[Q];
-    load_blk(0, nxt);
-    for (int base = 0; base < n4; base += Q) {
-      uint4 cur[Q];
-#pragma unroll
-      for (int q = 0; q < Q; ++q) cur[q] = nxt[q];
-      load_blk(base + Q, nxt);  // the next block's keys are in flight during this block's chain
-      // The sum never decreases (p >= 0): the threshold is crossed inside this
-      // block iff it is crossed at its end; only then is the block rerun key by key.
-      float e = c;
-#pragma unroll
-      for (int q = 0; q < Q; ++q) {
-        e = __fadd_rn(e, key_to_p(cur[q].x));
-        e = __fadd_rn(e, key_to_p(cur[q].y));
-        e = __fadd_rn(e, key_to_p(cur[q].z));
-        e = __fadd_rn(e, key_to_p(cur[q].w));
-      }
-      if (e >= thr) {
-        for (int i = 0; i < 4 * Q; ++i) {
-          c = __fadd_rn(c, 4 * base + i < V ? key_to_p(sm.key[4 * base + i]) : 0.f);
-          if (c >= thr) {
-            cut = 4 * base + i + 1;
-            break;
-          }
-        }
-        break;
-      }
-      c = e;
-    }
-    sm.cutoff = min(cut, V);
-  }
-  __syncthreads();
-  const int cut = sm.cutoff;
+  int n_rounds = 0;
+  const int cut = topp_cutoff(sm, V, a.top_p, a.trace != nullptr ? a.trace + static_cast<size_t>(b) * 8 + 7 : nullptr, n_rounds);
+  if (a.trace != nullptr && t == 0)
+    a.trace[static_cast<size_t>(b) * 8 + 6] = static_cast<uint64_t>(cut) | (static_cast<uint64_t>(n_rounds) << 32);
   stamp(4);
   const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
   const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
