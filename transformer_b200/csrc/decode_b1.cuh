@@ -981,7 +981,13 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
         const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
         ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_O, TR>(
             A, ring, flag, t0, sm.rng[2 * PH_O], sm.rng[2 * PH_O + 1], x, [&](int u, float v) {
-              if (lane == 0) st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
+              if (lane == 0) {
+                st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
+                // Without this fence the residual words reach the 148 polling
+                // CTAs ~2-3 us after the store; with it the writer waits ~1 us
+                // for its store and the all-gather completes ~3 us sooner.
+                __threadfence();
+              }
             }, TR ? tf + 3 + 8 * l : -1);
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
@@ -1029,7 +1035,10 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
         uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
         ok = gemv_phase<S::KF, S::ROWB_F, S::RPS_F, S::J_DOWN, TR>(
             A, ring, flag, t0, sm.rng[2 * PH_DOWN], sm.rng[2 * PH_DOWN + 1], x, [&](int u, float v) {
-              if (lane == 0) st_word(nxt + u, sm.h[u] + v, flag);
+              if (lane == 0) {
+                st_word(nxt + u, sm.h[u] + v, flag);
+                __threadfence();  // as for the HM words (the next layer's H all-gather)
+              }
             });
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
