@@ -69,11 +69,16 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 // ---- exchange words -----------------------------------------------------
 // An exchange word is 8 bytes: low 32 bits payload (float bits), high 32 bits
-// the launch's flag.  A single 64-bit store is single-copy atomic, so a reader
-// that sees the current flag also sees the payload written with it.
+// the launch's flag.  It is written with one 64-bit atomic exchange (single-copy
+// atomic, so a reader that sees the current flag also sees the payload written
+// with it).  The atomic is performed at L2 at once and its old value is never
+// read, so the writer does not wait for it: measured on the B=1 step, a plain
+// relaxed store reached the polling CTAs 2-3 us later, and a fence after the
+// store made the writer itself wait ~1 us.
 __device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t flag) {
   const uint64_t w = (static_cast<uint64_t>(flag) << 32) | __float_as_uint(v);
-  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+  uint64_t old;
+  asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(w) : "memory");
 }
 // Two adjacent words (16-byte aligned); each 64-bit element is read atomically.
 __device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {

@@ -983,10 +983,6 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
             A, ring, flag, t0, sm.rng[2 * PH_O], sm.rng[2 * PH_O + 1], x, [&](int u, float v) {
               if (lane == 0) {
                 st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
-                // Without this fence the residual words reach the 148 polling
-                // CTAs ~2-3 us after the store; with it the writer waits ~1 us
-                // for its store and the all-gather completes ~3 us sooner.
-                __threadfence();
               }
             }, TR ? tf + 3 + 8 * l : -1);
         ok = consumer_sync_and<kConsumers>(ok);
@@ -1037,7 +1033,6 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
             A, ring, flag, t0, sm.rng[2 * PH_DOWN], sm.rng[2 * PH_DOWN + 1], x, [&](int u, float v) {
               if (lane == 0) {
                 st_word(nxt + u, sm.h[u] + v, flag);
-                __threadfence();  // as for the HM words (the next layer's H all-gather)
               }
             });
         ok = consumer_sync_and<kConsumers>(ok);
