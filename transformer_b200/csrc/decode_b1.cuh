@@ -117,7 +117,10 @@ __device__ __forceinline__ void stage_stamp(const DecodeArgs& A, int cta, int ki
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;
-constexpr int kStageBytes = 16896;  // 8 rows x 2 KB or 3 rows x 5.5 KB (306M shapes)
+// A stage holds whole weight rows at a pitch of the row plus 16 bytes (pitch =
+// 16 mod 128), so the 8 rows an ldmatrix reads fall in distinct banks.
+constexpr int kRowPad = 16;
+constexpr int kStageBytes = 16960;  // 8 rows of 2 KB or 3 rows of 5.5 KB, padded (306M shapes)
 constexpr int kStages = 10;
 constexpr int kAttWords = 66;       // per attention unit: o[64], m, l
 constexpr int kMaxSplits = 4;       // attention units per head
@@ -134,18 +137,20 @@ struct Shape {
   static constexpr int KF = DFF / 256;  // along K = DFF
   static constexpr int ROWB_D = 2 * D;
   static constexpr int ROWB_F = 2 * DFF;
-  static constexpr int RPS_D = kStageBytes / ROWB_D;        // rows of K=D per stage
-  static constexpr int RPS_F = kStageBytes / ROWB_F;        // down rows per stage
+  static constexpr int PITCH_D = ROWB_D + kRowPad, PITCH_F = ROWB_F + kRowPad;
+  static constexpr int RPS_D = kStageBytes / PITCH_D;       // rows of K=D per stage
+  static constexpr int RPS_F = kStageBytes / PITCH_F;       // down rows per stage
+  // 16-row MMA tiles per CTA of each layer phase (grids of >= kMinGrid CTAs)
+  static constexpr int tiles_for(int rows) { return ((rows + kMinGrid - 1) / kMinGrid + 15) / 16; }
+  static constexpr int MT_QKV = tiles_for(QKV), MT_O = tiles_for(D), MT_DOWN = tiles_for(D);
+  static constexpr int MT_GU = (4 * ((DFF / 2 + kMinGrid - 1) / kMinGrid) + 15) / 16;
+  static constexpr int MT_MAX = MT_GU > MT_QKV ? MT_GU : MT_QKV;
+  static_assert(D % 128 == 0 && DFF % 128 == 0, "K splits into 8 warp slices of whole 16-column steps");
+  static_assert(PITCH_D % 128 == 16 && PITCH_F % 128 == 16, "padded row pitch");
   static constexpr int XMAX = DFF > D ? DFF : D;
-  // Units per warp per phase, for grids of at least kMinGrid CTAs.
-  static constexpr int units_per_warp(int n) {
-    return ((n + kMinGrid - 1) / kMinGrid + kConsumerWarps - 1) / kConsumerWarps;
-  }
-  static constexpr int J_QKV = units_per_warp(QKV), J_O = units_per_warp(D);
-  static constexpr int J_GU = units_per_warp(2 * DFF), J_DOWN = units_per_warp(D);  // GU: single rows
   // gate/up rows per CTA: the DFF / 2 act words (2 pairs = 4 rows each) split over >= kMinGrid CTAs
   static constexpr int GU_ROWS_MAX = 4 * ((DFF / 2 + kMinGrid - 1) / kMinGrid);
-  static_assert(J_GU * kConsumerWarps >= GU_ROWS_MAX, "gate/up rows per warp");
+  static_assert(GU_ROWS_MAX <= 16 * ((4 * ((DFF / 2 + kMinGrid - 1) / kMinGrid) + 15) / 16), "gate/up tiles");
   static constexpr int NP_D = (D / 2 + kConsumers - 1) / kConsumers;        // residual word pairs per thread
   static constexpr int NP_ACT = (DFF / 4 + kConsumers - 1) / kConsumers;    // act word pairs per thread
   static_assert(DFF % 4 == 0, "act words hold two bf16 values, read in pairs");
@@ -177,6 +182,7 @@ struct Smem {
   float am_v[kConsumerWarps];
   int am_i[kConsumerWarps];
   alignas(16) float gu_out[S::GU_ROWS_MAX];  // this CTA's gate/up dot products (gate j, up j, ...)
+  float part[kConsumerWarps][S::MT_MAX * 16];  // GEMV: each warp's K-slice partial of every row
   int rng[2 * kPhases];                      // this CTA's unit range [a, b) of each GEMV phase
   int abort;
   int tok_in;  // multi-step: this step's input token
@@ -354,72 +360,81 @@ __device__ __forceinline__ void dot8r(const uint4 w, const X4& x, uint64_t& a0, 
   a1 = ffma2(bf2pack(w.w), x.q[3], a1);
 }
 
-// One GEMV phase over this CTA's units [u_begin, u_end) (a unit is one row),
-// streamed in stages of PS units.  Warp w owns units u_begin + w + 8j
-// (j < MAXJ).  Each lane accumulates its partial dot products for all of its
-// units across the phase's stages (two accumulators per row to shorten the
-// FMA chain); the cross-lane reductions of all units run together once, after
-// the last stage, so their shuffle latencies overlap.  out(u, v) is then
-// called on every lane for each unit u < u_end of the warp.
-template <int KI, int ROWB, int PS, int MAXJ, bool TR, class Out>
-__device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
-                                           int u_begin, int u_end, const XSmem x, Out out, int sub = -1) {
-  // sub >= 0 (diagnostic kernel): stamps sub (stages acquired), sub + 1
-  // (products done), sub + 2 (reduced), sub + 3 (outputs stored)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t acc[MAXJ][2];
+// One GEMV phase over this CTA's rows [u_begin, u_end) on warp-level tensor-core
+// MMAs (mma.m16n8k16, bf16 in, f32 accumulate).  All of the phase's stages are
+// resident at once (at most kStages); warp w takes the K slice [w K/8,
+// (w+1) K/8) of every 16-row tile: A = 16 weight rows (ldmatrix; rows past
+// u_end read a valid row and are ignored), B = the input vector in all 8
+// columns (two 32-bit shared reads per step, so every output column is the
+// dot product).  The warps' partials of each row meet in `part` (PSTRIDE
+// floats per warp) and thread r sums them in warp order (deterministic), then
+// calls out(u_begin + r, v).  Ends with the phase's closing barrier; returns
+// the AND of every warp's waits.
+template <int K, int PITCH, int PS, int MT, int PSTRIDE, bool TR, class Out>
+__device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, float* part, const __nv_bfloat16* xb,
+                                           uint32_t flag, uint64_t t0, int u_begin, int u_end, Out out) {
+  static_assert(MT * 16 <= PSTRIDE, "partial buffer");
+  constexpr int KS = K / 16 / kConsumerWarps;  // 16-column steps per warp
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int rows = u_end - u_begin;
+  const int ns = rows > 0 ? (rows + PS - 1) / PS : 0;
+  bool ok = rows <= MT * 16 && ns <= kStages;
+  if (ok && ns > 0) ok = wait_full_n(A, ring, ns, flag, t0);
+  if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
+  if (ok && rows > 0) {
+    // ldmatrix.x4 rows: lane l gives row (l & 7) + 8 ((l >> 3) & 1) of the tile, columns + 8 (l >> 4)
+    const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lk = 8 * (lane >> 4);
+    uint32_t rbase[MT];
 #pragma unroll
-  for (int j = 0; j < MAXJ; ++j) acc[j][0] = acc[j][1] = 0ull;
-  bool ok = true;
-  for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * PS) {
-    const int ns = min(kGroupStages, (u_end - g0 + PS - 1) / PS);
-    ok = wait_full_n(A, ring, ns, flag, t0);
-    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
-    if (sub >= 0 && g0 == u_begin) trace_stamp<TR>(A, sub);
-    if (ok) {
-      const uint4* rp[MAXJ];  // this warp's rows in the group's stages (null: not in this group)
+    for (int mt = 0; mt < MT; ++mt) {
+      const int r = min(mt * 16 + lr, rows - 1);  // rows past the range: any valid row
+      const int st = r / PS;
+      rbase[mt] = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages]) +
+                  static_cast<uint32_t>((r - st * PS) * PITCH + 2 * lk);
+    }
+    // two accumulator chains (even / odd steps) so consecutive MMAs do not wait on each other
+    float acc[2][MT][4];
 #pragma unroll
-      for (int j = 0; j < MAXJ; ++j) {
-        const int u = u_begin + warp + kConsumerWarps * j;
-        const int st = (u - g0) / PS;  // stage of the group holding unit u
-        rp[j] = nullptr;
-        if (u >= g0 && st < ns && u < u_end)
-          rp[j] = reinterpret_cast<const uint4*>(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages] +
-                                                 static_cast<size_t>(u - g0 - st * PS) * ROWB) +
-                  lane;
-      }
+    for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int k = 0; k < KI; ++k) {
-        const X4 xc = x.chunk(k);
+      for (int mt = 0; mt < MT; ++mt) acc[c][mt][0] = acc[c][mt][1] = acc[c][mt][2] = acc[c][mt][3] = 0.f;
+    const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xb);
+    const int k0 = warp * KS * 16;
+#pragma unroll 4
+    for (int s = 0; s < KS; ++s) {
+      const int k = k0 + 16 * s;
+      const uint32_t b0 = x32[(k + 2 * tig) >> 1], b1 = x32[(k + 8 + 2 * tig) >> 1];
 #pragma unroll
-        for (int j = 0; j < MAXJ; ++j)
-          if (rp[j] != nullptr) dot8r(rp[j][k * 32], xc, acc[j][0], acc[j][1]);
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(rbase[mt] + 2u * static_cast<uint32_t>(k), a0, a1, a2, a3);
+        mma_bf16(acc[s & 1][mt], a0, a1, a2, a3, b0, b1);
       }
     }
-    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
-    release_n(ring, ns);
+    if (tig == 0) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        part[warp * PSTRIDE + mt * 16 + gid] = acc[0][mt][0] + acc[1][mt][0];      // row gid of the tile
+        part[warp * PSTRIDE + mt * 16 + gid + 8] = acc[0][mt][2] + acc[1][mt][2];  // row gid + 8
+      }
+    }
   }
+  if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
+  if (ok) release_n(ring, ns);
+  ok = consumer_sync_and<kConsumers>(ok);
   if (!ok) return false;
-  if (sub >= 0) trace_stamp<TR>(A, sub + 1);
-  float v[MAXJ];
+  if (t < rows) {
+    float v = 0.f;
 #pragma unroll
-  for (int j = 0; j < MAXJ; ++j) v[j] = f2sum(acc[j][0]) + f2sum(acc[j][1]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int j = 0; j < MAXJ; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
-  if (sub >= 0) trace_stamp<TR>(A, sub + 2);
-#pragma unroll
-  for (int j = 0; j < MAXJ; ++j) {
-    const int u = u_begin + warp + kConsumerWarps * j;
-    if (u < u_end) out(u, v[j]);
+    for (int w = 0; w < kConsumerWarps; ++w) v += part[w * PSTRIDE + t];
+    out(u_begin + t, v);
   }
-  if (sub >= 0) trace_stamp<TR>(A, sub + 3);
   return true;
 }
 
 // Same streaming for many units per warp (the logits): reduce per stage.
-template <int KI, int ROWB, int PS, class Out>
+template <int KI, int PITCH, int PS, class Out>
 __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
                                                 int u_begin, int u_end, const XSmem x, Out out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -433,7 +448,7 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring,
       for (int u = first; u < g1; u += kConsumerWarps) {
         const int st = (u - g0) / PS;
         const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
-        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * PS) * ROWB);
+        const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * PS) * PITCH);
         uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll
         for (int k = 0; k < KI; ++k) dot8r(rp[k * 32 + lane], x.chunk(k), a0, a1);
@@ -516,7 +531,10 @@ __device__ __forceinline__ bool gather_norm(const DecodeArgs& A, Smem<S>& sm, co
 
 // Producer: streams this CTA's weight ranges for the whole step.
 template <class S, bool TR>
+// The whole producer warp runs it: lane 0 waits for ring slots and arms the
+// stages; the rows of a padded stage are copied by lanes 0..rows-1 in parallel.
 __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_t flag, uint64_t t0, int nsteps) {
+  const int lane = threadIdx.x & 31;
   const uint64_t pol = l2_policy_evict_first();
   const int G = A.grid_part;
   uint32_t seq = 0;
@@ -526,53 +544,69 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
   // exchange words.  Landed stages still accumulate in the ring.
   uint32_t landed = 0;
   const uint32_t cap = static_cast<uint32_t>(A.max_inflight);
-  auto issue = [&](const uint8_t* src, uint32_t bytes) {
+  // one stage: `cnt` rows of `rb` bytes each, from consecutive rows at src
+  auto issue = [&](const uint8_t* src, int cnt, uint32_t rb, uint32_t pitch) {
     const uint32_t slot = seq % kStages;
-    while (seq - landed >= cap) {
-      Waiter wt;
-      while (!mbar_test(&sm.full[landed % kStages], (landed / kStages) & 1u)) {
-        if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_FULL))) {
-          ok = false;
-          return;
+    bool good = true;
+    if (lane == 0) {
+      while (good && seq - landed >= cap) {
+        Waiter wt;
+        while (!mbar_test(&sm.full[landed % kStages], (landed / kStages) & 1u)) {
+          if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_FULL))) {
+            good = false;
+            break;
+          }
+        }
+        if (good) ++landed;
+      }
+      if (good && seq >= kStages) {
+        const uint32_t par = ((seq / kStages) - 1) & 1u;
+        Waiter wt;
+        while (!mbar_test(&sm.empty[slot], par)) {
+          if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_EMPTY))) {
+            good = false;
+            break;
+          }
         }
       }
-      ++landed;
+      if (good) mbar_arrive_expect_tx(&sm.full[slot], static_cast<uint32_t>(cnt) * rb);
     }
-    if (seq >= kStages) {
-      const uint32_t par = ((seq / kStages) - 1) & 1u;
-      Waiter wt;
-      while (!mbar_test(&sm.empty[slot], par)) {
-        if ((*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_EMPTY))) {
-          ok = false;
-          return;
-        }
-      }
+    if (!__shfl_sync(0xffffffffu, good ? 1 : 0, 0)) {
+      ok = false;
+      return;
     }
-    mbar_arrive_expect_tx(&sm.full[slot], bytes);
-    bulk_g2s(sm.stage[slot], src, bytes, &sm.full[slot], pol);
-    stage_stamp<TR>(A, cta, 0, seq);
+    if (pitch == rb) {  // unpadded: the stage's rows are one contiguous copy
+      if (lane == 0) bulk_g2s(sm.stage[slot], src, static_cast<uint32_t>(cnt) * rb, &sm.full[slot], pol);
+    } else {
+      for (int r = lane; r < cnt; r += 32)
+        bulk_g2s(sm.stage[slot] + static_cast<size_t>(r) * pitch, src + static_cast<size_t>(r) * rb, rb,
+                 &sm.full[slot], pol);
+    }
+    if (lane == 0) stage_stamp<TR>(A, cta, 0, seq);
     ++seq;
   };
   // This CTA's units of a phase: n units split evenly in blocks of `blk`
   // (the gate/up phase splits whole act words: 2 pairs = 4 rows).
-  auto stream = [&](const uint8_t* base, int n, int unit_bytes, int per_stage, int blk = 1) {
+  // `pad`: rows at the padded pitch (tensor-core phases) or packed (the logits).
+  auto stream = [&](const uint8_t* base, int n, int unit_bytes, int per_stage, int blk, bool pad) {
     const int a = blk * split_begin(cta, n / blk, G), b = blk * split_begin(cta + 1, n / blk, G);
     for (int u = a; u < b && ok; u += per_stage) {
       const int cnt = min(per_stage, b - u);
-      issue(base + static_cast<size_t>(u) * unit_bytes, static_cast<uint32_t>(cnt * unit_bytes));
+      issue(base + static_cast<size_t>(u) * unit_bytes, cnt, static_cast<uint32_t>(unit_bytes),
+            static_cast<uint32_t>(unit_bytes + (pad ? kRowPad : 0)));
     }
   };
   for (int step = 0; step < nsteps && ok; ++step) {  // the weight sequence repeats every step
       for (int l = 0; l < A.n_layers && ok; ++l) {
         const uint8_t* lw = A.wbase + static_cast<size_t>(l) * A.layer_stride;
-        stream(lw + A.off_qkv, S::QKV, S::ROWB_D, S::RPS_D);
-        stream(lw + A.off_o, S::D, S::ROWB_D, S::RPS_D);
-        stream(lw + A.off_gu, 2 * S::DFF, S::ROWB_D, S::RPS_D, 4);
-        stream(lw + A.off_down, S::D, S::ROWB_F, S::RPS_F);
+        stream(lw + A.off_qkv, S::QKV, S::ROWB_D, S::RPS_D, 1, true);
+        stream(lw + A.off_o, S::D, S::ROWB_D, S::RPS_D, 1, true);
+        stream(lw + A.off_gu, 2 * S::DFF, S::ROWB_D, S::RPS_D, 4, true);
+        stream(lw + A.off_down, S::D, S::ROWB_F, S::RPS_F, 1, true);
       }
-      if (ok) stream(A.wbase + A.off_emb, A.vocab, S::ROWB_D, S::RPS_D);
+      if (ok) stream(A.wbase + A.off_emb, A.vocab, S::ROWB_D, S::RPS_D, 1, false);
     }
-    {
+    if (lane == 0) {
       // Never leave with copies in flight: wait (bounded) for the last stages
       // issued.  On the normal path they land before the consumers finish.
       const uint32_t first = seq > kStages ? seq - kStages : 0;
@@ -847,7 +881,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-      if (lane == 0) producer_loop<S, TR>(A, sm, cta, flag0, t0, nsteps);
+      producer_loop<S, TR>(A, sm, cta, flag0, t0, nsteps);  // the whole producer warp
       return;
     }
 
@@ -915,12 +949,9 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       trace_stamp<TR>(A, ts + 1);
       // ---- QKV rows -> exchange words ----
       {
-        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
-        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_QKV, TR>(
-            A, ring, flag, t0, sm.rng[2 * PH_QKV], sm.rng[2 * PH_QKV + 1], x, [&](int u, float v) {
-              if (lane == 0) st_word(lw + S::D + u, v, flag);
-            });
-        ok = consumer_sync_and<kConsumers>(ok);
+        ok = gemv_phase<S::D, S::PITCH_D, S::RPS_D, S::MT_QKV, 16 * S::MT_MAX, TR>(
+            A, ring, &sm.part[0][0], sm.xb, flag, t0, sm.rng[2 * PH_QKV], sm.rng[2 * PH_QKV + 1],
+            [&](int u, float v) { st_word(lw + S::D + u, v, flag); });
         if (!ok) break;
       }
       trace_stamp<TR>(A, ts + 2);
@@ -978,14 +1009,9 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       trace_stamp<TR>(A, ts + 6);
       // ---- O rows: HM = H + attn @ Wo^T ----
       {
-        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
-        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_O, TR>(
-            A, ring, flag, t0, sm.rng[2 * PH_O], sm.rng[2 * PH_O + 1], x, [&](int u, float v) {
-              if (lane == 0) {
-                st_word(lw + A.w_hm + u, sm.h[u] + v, flag);
-              }
-            }, TR ? tf + 3 + 8 * l : -1);
-        ok = consumer_sync_and<kConsumers>(ok);
+        ok = gemv_phase<S::D, S::PITCH_D, S::RPS_D, S::MT_O, 16 * S::MT_MAX, TR>(
+            A, ring, &sm.part[0][0], sm.xb, flag, t0, sm.rng[2 * PH_O], sm.rng[2 * PH_O + 1],
+            [&](int u, float v) { st_word(lw + A.w_hm + u, sm.h[u] + v, flag); });
         if (!ok) break;
       }
       trace_stamp<TR>(A, ts + 7);
@@ -996,14 +1022,11 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
       trace_stamp<TR>(A, ts + 9);
       // ---- gate/up rows -> act = silu(g) * u; an exchange word holds two acts ----
       {
-        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
         const int a = sm.rng[2 * PH_GU], b = sm.rng[2 * PH_GU + 1];
-        ok = gemv_phase<S::KD, S::ROWB_D, S::RPS_D, S::J_GU, TR>(
-            A, ring, flag, t0, a, b, x, [&](int u, float v) {
-              if (lane == 0) sm.gu_out[u - a] = v;
-            }, TR ? tf + 3 + 8 * l + 4 : -1);
-        ok = consumer_sync_and<kConsumers>(ok);
+        ok = gemv_phase<S::D, S::PITCH_D, S::RPS_D, S::MT_GU, 16 * S::MT_MAX, TR>(
+            A, ring, &sm.part[0][0], sm.xb, flag, t0, a, b, [&](int u, float v) { sm.gu_out[u - a] = v; });
         if (!ok) break;
+        consumer_sync<kConsumers>();  // gu_out complete
         // rows 4i .. 4i + 3 of the CTA's range: gate, up of pair 2m, gate, up of pair 2m + 1
         if (t < (b - a) / 4) {
           const float4 gu = reinterpret_cast<const float4*>(sm.gu_out)[t];
@@ -1027,15 +1050,10 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
         ok = consumer_sync_and<kConsumers>(ok);
         if (!ok) break;
         trace_stamp<TR>(A, ts + 11);
-        const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
         uint64_t* nxt = A.words + static_cast<size_t>(l + 1) * A.layer_words;  // H_{l+1} at word 0
-        ok = gemv_phase<S::KF, S::ROWB_F, S::RPS_F, S::J_DOWN, TR>(
-            A, ring, flag, t0, sm.rng[2 * PH_DOWN], sm.rng[2 * PH_DOWN + 1], x, [&](int u, float v) {
-              if (lane == 0) {
-                st_word(nxt + u, sm.h[u] + v, flag);
-              }
-            });
-        ok = consumer_sync_and<kConsumers>(ok);
+        ok = gemv_phase<S::DFF, S::PITCH_F, S::RPS_F, S::MT_DOWN, 16 * S::MT_MAX, TR>(
+            A, ring, &sm.part[0][0], sm.xb, flag, t0, sm.rng[2 * PH_DOWN], sm.rng[2 * PH_DOWN + 1],
+            [&](int u, float v) { st_word(nxt + u, sm.h[u] + v, flag); });
         if (!ok) break;
       }
       trace_stamp<TR>(A, ts + 12);
