@@ -16,6 +16,7 @@
 #include "attn_paged.cuh"
 #include "batched.cuh"
 #include "decode_b1.cuh"
+#include "decode_b1c.cuh"
 #include "gemm_tc.cuh"
 #include "sampler.cuh"
 
@@ -45,15 +46,120 @@ using ShapeTiny = b2d::Shape<256, 768, 4, 2>;
 struct ShapeOps {
   int d, dff, nh, nkv;
   size_t smem;
-  const void* kernel;        // the B=1 step
+  const void* kernel;        // the B=1 step, flat grid (one CTA per SM)
   const void* kernel_trace;  // the same with diagnostic stamps (b2d_debug_trace, knobs 7/8)
+  size_t smem_c;
+  const void* kernel_c;        // the B=1 step on clusters of kCS CTAs (decode_b1c.cuh)
+  const void* kernel_c_trace;
+  int qbox, obox, gbox, dbox;  // the cluster kernel's q/k/v, Wo, gate/up, Wd tensor-copy rows
 };
 
 template <class S>
 ShapeOps make_ops() {
   return ShapeOps{S::D, S::DFF, S::NH, S::NKV, sizeof(b2d::Smem<S>),
                   reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, false>),
-                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, true>)};
+                  reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, true>),
+                  b2d::smem_c_bytes<S>(),
+                  reinterpret_cast<const void*>(&b2d::decode_b1c_kernel<S, false>),
+                  reinterpret_cast<const void*>(&b2d::decode_b1c_kernel<S, true>),
+                  b2d::ShapeC<S>::QPS, b2d::ShapeC<S>::OBOX, b2d::ShapeC<S>::PS, b2d::ShapeC<S>::DBOX};
+}
+
+// Tensor map of one projection over all layers: [n_layers][rows][inner] bf16
+// (row pitch inner * 2 bytes, layer pitch layer_stride), boxes of box_inner x
+// box_rows x 1.
+bool make_layer_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t layers,
+                    uint64_t layer_stride, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  auto enc = b2d::tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || (inner * 2) % 16 || layer_stride % 16) return false;
+  cuuint64_t dims[3] = {inner, rows, layers};
+  cuuint64_t strides[2] = {inner * 2, layer_stride};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Row-major projection [n_layers][rows][k] bf16 viewed as k-blocks: {64, rows,
+// k / 64, n_layers} with strides {k * 2, 128, layer_stride}; a box of
+// box_rows rows lands as [k / 64][box_rows][64], 128-byte swizzled.
+bool make_kblock_map(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint64_t layers,
+                     uint64_t layer_stride, uint32_t box_rows) {
+  auto enc = b2d::tensor_map_encoder();
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15u) || k % 64 || layer_stride % 16 || k / 64 > 256) return false;
+  cuuint64_t dims[4] = {64, rows, k / 64, layers};
+  cuuint64_t strides[3] = {k * 2, 128, layer_stride};
+  cuuint32_t box[4] = {64, box_rows, static_cast<cuuint32_t>(k / 64), 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The cluster kernel's weight views of the packed weights as stored: q/k/v
+// and gate/up rows in k-block boxes, Wo boxes of 64 columns (one head) x obox
+// rows (128-byte swizzled), Wd boxes of 8 columns (one act chunk) x dbox rows.
+bool make_b1c_maps(const b2d_config* c, const ShapeOps* ops, const uint8_t* w, const b2d_weights_layout_t& lay,
+                   b2d::MapsC* maps) {
+  const uint64_t d = c->d_model, f = c->d_ff, nl = c->n_layers;
+  const uint64_t qkv = uint64_t(c->n_heads + 2 * c->n_kv_heads) * c->d_head;
+  return make_kblock_map(&maps->qkv, w + lay.off_qkv, d, qkv, nl, lay.layer_stride, uint32_t(ops->qbox)) &&
+         make_layer_map(&maps->o, w + lay.off_o, d, d, nl, lay.layer_stride, 64, uint32_t(ops->obox),
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+         make_kblock_map(&maps->gu, w + lay.off_gu, d, 2 * f, nl, lay.layer_stride, uint32_t(ops->gbox)) &&
+         make_layer_map(&maps->down, w + lay.off_down, f, d, nl, lay.layer_stride, 8, uint32_t(ops->dbox),
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Clusters of the cluster kernel that fit co-resident (0 if none / unsupported).
+int b1c_max_clusters(const ShapeOps* ops) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = b2d::kCS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(b2d::kCS * 64);
+  cfg.blockDim = dim3(b2d::kThreads);
+  cfg.dynamicSmemBytes = ops->smem_c;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, ops->kernel_c, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// Grid of the cluster kernel for this shape on the current device, or 0 when
+// it does not fit (the flat kernel is used then).
+int b1c_grid(const ShapeOps* ops) {
+  const int nc = b1c_max_clusters(ops);
+  if (nc < ops->nh || nc * b2d::kCS < b2d::kMinGridC) return 0;
+  return nc * b2d::kCS;
+}
+
+// One cooperative launch of the cluster kernel.
+cudaError_t launch_b1c(const void* kernel, int grid, size_t smem, cudaStream_t st, const b2d::MapsC& maps,
+                       const b2d::DecodeArgs& A) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(b2d::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = b2d::kCS;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeCooperative;
+  at[1].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  void* args[] = {const_cast<b2d::MapsC*>(&maps), const_cast<b2d::DecodeArgs*>(&A)};
+  return cudaLaunchKernelExC(&cfg, kernel, args);
 }
 
 const ShapeOps* find_ops(const b2d_config* c) {
@@ -96,7 +202,9 @@ struct b2d_model {
   uint64_t wbytes;
   b2d_weights_layout_t lay;
   const ShapeOps* ops;
-  int grid;
+  int grid;               // SMs (the flat B=1 kernel's grid)
+  int b1_grid;            // the cluster B=1 kernel's grid (0 = the flat kernel is used)
+  b2d::MapsC b1_maps;     // its weight views
   // batched path: TMA descriptors of every projection (created on first use)
   bool maps_ready;
   CUtensorMap* wmaps;  // [4 * n_layers + 1]: per layer qkv, o, gu, down; then the embedding
@@ -113,7 +221,11 @@ struct b2d_ws {
   uint32_t layer_words, w_att, w_hm, w_act;
   int att_T;
   uint64_t wait_ns;
-  int grid_part;
+  int extra_ctas;          // test hook: work split over this many CTAs more than launched
+  bool force_flat;         // diagnostics: B=1 step on the flat kernel even where clusters fit
+  uint64_t* acc;           // cluster kernel: residual accumulators [2][2 n_layers][d_model]
+  size_t acc_words;
+  int b1_kind;             // kernel of the last B=1 launch: 0 none / flat, 1 cluster
   uint64_t* trace;
   int trace_stride;
   uint32_t poll_ns;
@@ -283,6 +395,9 @@ b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint
   for (const void* k : {ops->kernel, ops->kernel_trace})
     B2D_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ops->smem)),
              "cudaFuncSetAttribute(smem)");
+  for (const void* k : {ops->kernel_c, ops->kernel_c_trace})
+    B2D_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ops->smem_c)),
+             "cudaFuncSetAttribute(smem)");
   if (sms < b2d::kMinGrid) return B2D_ERR_UNSUPPORTED;  // phase register budgets assume >= 128 SMs
   int per_sm = 0;
   B2D_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ops->kernel, b2d::kThreads, ops->smem),
@@ -297,6 +412,8 @@ b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev, uint
   m->lay = lay;
   m->ops = ops;
   m->grid = sms;
+  m->b1_grid = b1c_grid(ops);
+  if (m->b1_grid > 0 && !make_b1c_maps(cfg, ops, m->w, lay, &m->b1_maps)) m->b1_grid = 0;
   m->maps_ready = false;
   m->wmaps = nullptr;
   *out = m;
@@ -309,7 +426,7 @@ b2d_status b2d_model_destroy(b2d_model* m) {
   return B2D_OK;
 }
 
-int b2d_model_grid(const b2d_model* m) { return m ? m->grid : 0; }
+int b2d_model_grid(const b2d_model* m) { return m ? (m->b1_grid > 0 ? m->b1_grid : m->grid) : 0; }
 
 b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   if (!out) return B2D_ERR_INVALID_ARG;
@@ -331,9 +448,11 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   ws->layer_words = (ws->layer_words + 1) & ~1u;
   ws->n_words = size_t(c.n_layers) * ws->layer_words + c.d_model;
   ws->wait_ns = 2000000000ull;  // 2 s bound on every in-kernel wait
-  ws->grid_part = m->grid;
   ws->max_inflight = 4;
+  ws->acc_words = size_t(2) * 2 * c.n_layers * c.d_model;
   cudaError_t e = cudaMalloc(&ws->words, ws->n_words * sizeof(uint64_t));
+  if (e == cudaSuccess) e = cudaMalloc(&ws->acc, ws->acc_words * sizeof(uint64_t));
+  if (e == cudaSuccess) e = cudaMemset(ws->acc, 0, ws->acc_words * sizeof(uint64_t));
   if (e == cudaSuccess) e = cudaMalloc(&ws->ctl, sizeof(b2d::Control));
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_val, sizeof(float) * m->grid);
   if (e == cudaSuccess) e = cudaMalloc(&ws->am_idx, sizeof(int32_t) * m->grid);
@@ -389,6 +508,7 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   cudaFree(ws->ss);
   cudaFree(ws->prefill_pos);
   cudaFree(ws->words);
+  cudaFree(ws->acc);
   cudaFree(ws->ctl);
   cudaFree(ws->am_val);
   cudaFree(ws->am_idx);
@@ -401,6 +521,7 @@ b2d_status b2d_workspace_reset(b2d_ws* ws, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   B2D_CUDA(cudaSetDevice(ws->m->device), "cudaSetDevice");
   B2D_CUDA(cudaMemsetAsync(ws->words, 0, ws->n_words * sizeof(uint64_t), st), "reset words");
+  B2D_CUDA(cudaMemsetAsync(ws->acc, 0, ws->acc_words * sizeof(uint64_t), st), "reset accumulators");
   B2D_CUDA(cudaMemsetAsync(ws->ctl, 0, sizeof(b2d::Control), st), "reset control");
   return B2D_OK;
 }
@@ -425,7 +546,7 @@ b2d_status b2d_last_error(b2d_ws* ws, void* stream, uint32_t* detail) {
 b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas) {
   if (!ws || wait_ns == 0 || extra_ctas < 0 || extra_ctas > 1024) return B2D_ERR_INVALID_ARG;
   ws->wait_ns = wait_ns;
-  ws->grid_part = ws->m->grid + extra_ctas;
+  ws->extra_ctas = extra_ctas;
   return B2D_OK;
 }
 
@@ -443,6 +564,10 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
   if (!ws) return B2D_ERR_INVALID_ARG;
   ++ws->tune_gen;  // cached step graphs hold the previous settings
   switch (knob) {
+    case 12:  // B=1 step: the flat kernel (1) or the cluster kernel where it fits (0, default)
+      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
+      ws->force_flat = value == 1;
+      return B2D_OK;
     case 11:  // batched step: replay cached CUDA graphs (1, default) or launch directly (0)
       if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
       ws->no_graph = value == 0;
@@ -514,6 +639,7 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   A.logits = logits_dev;
   A.next_tok = next_tok_dev;
   A.words = ws->words;
+  A.acc = ws->acc;
   A.ctl = ws->ctl;
   A.am_val = ws->am_val;
   A.am_idx = ws->am_idx;
@@ -525,7 +651,9 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   A.n_layers = c.n_layers;
   A.ctx = c.context_len;
   A.att_T = ws->att_T;
-  A.grid_part = ws->grid_part;
+  const bool clustered = m->b1_grid > 0 && !ws->force_flat;
+  const int grid = clustered ? m->b1_grid : m->grid;
+  A.grid_part = grid + ws->extra_ctas;
   A.wait_ns = ws->wait_ns;
   A.eps = c.rms_eps;
   A.trace = ws->trace;
@@ -536,9 +664,21 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   A.max_inflight = ws->max_inflight;
   A.n_steps = n_steps;
   A.tok_out = tok_out_dev;
+  const bool trace = A.trace || A.stage_trace;
+  if (clustered && ws->b1_kind != 1) {
+    // The cluster kernel finds the next step's accumulators zeroed by the
+    // step before it; after flat-kernel steps that is not so.
+    B2D_CUDA(cudaMemsetAsync(ws->acc, 0, ws->acc_words * sizeof(uint64_t), st), "clear accumulators");
+  }
+  ws->b1_kind = clustered ? 1 : 0;
+  if (clustered) {
+    B2D_CUDA(launch_b1c(trace ? m->ops->kernel_c_trace : m->ops->kernel_c, grid, m->ops->smem_c, st, m->b1_maps, A),
+             "decode launch");
+    return B2D_OK;
+  }
   void* args[] = {&A};
-  const void* kernel = A.trace || A.stage_trace ? m->ops->kernel_trace : m->ops->kernel;
-  B2D_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(m->grid), dim3(b2d::kThreads), args, m->ops->smem, st),
+  const void* kernel = trace ? m->ops->kernel_trace : m->ops->kernel;
+  B2D_CUDA(cudaLaunchCooperativeKernel(kernel, dim3(grid), dim3(b2d::kThreads), args, m->ops->smem, st),
            "decode launch");
   return B2D_OK;
 }
@@ -987,6 +1127,7 @@ struct StaticDeviceState {
   unsigned char* scratch;  // device address of g_static_scratch on this device
   int sms;
   int smem_set;            // bitmask of shape ops whose smem attribute is set
+  int c_grid[8];           // per shape ops: the cluster kernel's grid (0 = flat kernel)
 };
 constexpr int kMaxDevices = 64;
 StaticDeviceState g_static_dev[kMaxDevices];
@@ -1020,6 +1161,10 @@ b2d_status static_setup(int device, const ShapeOps* ops, int ops_index, StaticDe
     B2D_CUDA(cudaFuncSetAttribute(ops->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(ops->smem)),
              "cudaFuncSetAttribute(smem)");
+    B2D_CUDA(cudaFuncSetAttribute(ops->kernel_c, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(ops->smem_c)),
+             "cudaFuncSetAttribute(smem)");
+    st.c_grid[ops_index] = b1c_grid(ops);
     st.smem_set |= 1 << ops_index;
   }
   *out = &st;
@@ -1047,8 +1192,10 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   const uint32_t w_act = w_hm + uint32_t(cfg->d_model);
   const uint32_t layer_words = (w_act + uint32_t(cfg->d_ff) + 1) & ~1u;
   const size_t n_words = size_t(cfg->n_layers) * layer_words + cfg->d_model;
-  if (b2d::kStaticWordsOffset + n_words * sizeof(uint64_t) > b2d::kStaticScratchBytes)
-    return B2D_ERR_SCRATCH_LIMIT;
+  // the cluster kernel's accumulators follow the words
+  const size_t acc_offset = align256(b2d::kStaticWordsOffset + n_words * sizeof(uint64_t));
+  const size_t acc_bytes = size_t(2) * 2 * cfg->n_layers * cfg->d_model * sizeof(uint64_t);
+  if (acc_offset + acc_bytes > b2d::kStaticScratchBytes) return B2D_ERR_SCRATCH_LIMIT;
   int device = 0;
   B2D_CUDA(cudaGetDevice(&device), "cudaGetDevice");
   if (device < 0 || device >= kMaxDevices) return B2D_ERR_UNSUPPORTED;
@@ -1069,8 +1216,7 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   if (s != B2D_OK) return s;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   // Everything this call reads before writing starts from zero.
-  B2D_CUDA(cudaMemsetAsync(st->scratch, 0, b2d::kStaticWordsOffset + n_words * sizeof(uint64_t), cs),
-           "clear static scratch");
+  B2D_CUDA(cudaMemsetAsync(st->scratch, 0, acc_offset + acc_bytes, cs), "clear static scratch");
   const uint8_t* w = static_cast<const uint8_t*>(weights_dev);
   b2d::DecodeArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -1092,6 +1238,7 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   A.logits = logits_dev;
   A.next_tok = next_tok_dev;
   A.words = reinterpret_cast<uint64_t*>(st->scratch + b2d::kStaticWordsOffset);
+  A.acc = reinterpret_cast<uint64_t*>(st->scratch + acc_offset);
   A.ctl = reinterpret_cast<b2d::Control*>(st->scratch + b2d::kStaticCtlOffset);
   A.am_val = reinterpret_cast<float*>(st->scratch + b2d::kStaticArgmaxOffset);
   A.am_idx = reinterpret_cast<int32_t*>(st->scratch + b2d::kStaticArgmaxOffset + 4 * b2d::kStaticMaxGrid);
@@ -1103,10 +1250,17 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   A.n_layers = cfg->n_layers;
   A.ctx = cfg->context_len;
   A.att_T = 128 * ((cfg->context_len + 511) / 512);
-  A.grid_part = st->sms;
+  const int c_grid = st->c_grid[ops_index];
+  A.grid_part = c_grid > 0 ? c_grid : st->sms;
   A.wait_ns = 2000000000ull;
   A.eps = cfg->rms_eps;
   A.max_inflight = 4;
+  if (c_grid > 0) {
+    b2d::MapsC maps;  // encoded on the host per call: no allocation
+    if (!make_b1c_maps(cfg, ops, w, lay, &maps)) return B2D_ERR_INVALID_ARG;
+    B2D_CUDA(launch_b1c(ops->kernel_c, c_grid, ops->smem_c, cs, maps, A), "static decode launch");
+    return B2D_OK;
+  }
   void* args[] = {&A};
   B2D_CUDA(cudaLaunchCooperativeKernel(ops->kernel, dim3(st->sms), dim3(b2d::kThreads), args, ops->smem, cs),
            "static decode launch");

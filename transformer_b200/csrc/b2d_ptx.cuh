@@ -67,6 +67,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy) : "memory");
 }
 
+// ---- 16-byte asynchronous copies (LSU path, not the tensor-copy unit) -------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) { cp_async16(smem_addr(dst), src); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---- exchange words -----------------------------------------------------
 // An exchange word is 8 bytes: low 32 bits payload (float bits), high 32 bits
 // the launch's flag.  It is written with one 64-bit atomic exchange (single-copy
@@ -110,6 +122,67 @@ __device__ __forceinline__ void st_relaxed_u32(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ uint32_t word_flag(uint64_t w) { return static_cast<uint32_t>(w >> 32); }
 __device__ __forceinline__ float word_val(uint64_t w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+// ---- fixed-point accumulator words ----------------------------------------
+// A residual-stream element that several CTAs contribute to is an 8-byte
+// accumulator: bits 58..63 count the contributions, bits 0..57 hold the sum
+// of (value * 2^32 + 2^51) over them.  Every contribution is one 64-bit
+// atomic add, so the sum is exact and independent of the order in which the
+// adds land (integer addition), and a reader that sees the expected count has
+// the complete sum.  |value| < 2^19 per contribution; at most 63
+// contributions (63 * 2^52 < 2^58, so the biased sum never carries into the
+// count).
+constexpr int kAccCountShift = 58;
+constexpr uint64_t kAccBias = 1ull << 51;
+constexpr float kAccLimit = 524288.f;  // 2^19
+__device__ __forceinline__ void red_add_u64(uint64_t* p, uint64_t v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// value -> fixed point (round to nearest); false when out of range or NaN.
+__device__ __forceinline__ bool acc_fix(float v, int64_t& q) {
+  const bool in = fabsf(v) < kAccLimit;
+  q = in ? __float2ll_rn(v * 4294967296.f) : 0;
+  return in;
+}
+// One contribution of fixed-point q (|q| < 2^51).
+__device__ __forceinline__ void acc_add(uint64_t* p, int64_t q) {
+  red_add_u64(p, (1ull << kAccCountShift) + static_cast<uint64_t>(q + static_cast<int64_t>(kAccBias)));
+}
+__device__ __forceinline__ uint32_t acc_count(uint64_t w) { return static_cast<uint32_t>(w >> kAccCountShift); }
+// The exact fixed-point sum of a word whose count is n.
+__device__ __forceinline__ int64_t acc_sum(uint64_t w, uint32_t n) {
+  return static_cast<int64_t>(w & ((1ull << kAccCountShift) - 1)) - static_cast<int64_t>(n) * static_cast<int64_t>(kAccBias);
+}
+// Nearest f32 of a fixed-point sum.
+__device__ __forceinline__ float acc_value(int64_t s) { return __ll2float_rn(s) * 2.3283064365386963e-10f; }
+
+// ---- distributed shared memory (cluster) signalling ---------------------------
+// Asynchronous store into cluster CTA shared memory (addresses from mapa)
+// that completes `bytes` of a transaction on the receiver's mbarrier: the
+// receiver arms the phase with arrive.expect_tx(total bytes) and its wait
+// completes once every pushed byte has landed.  No fence on the sender.
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(addr), "f"(v),
+               "r"(bar) : "memory");
+}
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(a), "f"(b), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void st_async_f32x4(uint32_t addr, float4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar) : "memory");
+}
+// Phase test with cluster-scope acquire (the phase of a barrier that peers push to).
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
 
 // ---- named barrier among the consumer warps -----------------------------
 template <int NT>

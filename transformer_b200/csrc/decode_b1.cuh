@@ -73,6 +73,7 @@ struct DecodeArgs {
   int n_steps;        // greedy tokens per launch (>= 1): step s decodes at pos + s
   int32_t* tok_out;   // [n_steps] the token of every step, or null
   uint64_t* words;    // exchange words
+  uint64_t* acc;      // cluster kernel: residual accumulators [2 parities][2 n_layers][D]
   Control* ctl;
   float* am_val;      // [grid]
   int32_t* am_idx;
@@ -120,7 +121,9 @@ constexpr int kThreads = kConsumers + 32;
 // A stage holds whole weight rows at a pitch of the row plus 16 bytes (pitch =
 // 16 mod 128), so the 8 rows an ldmatrix reads fall in distinct banks.
 constexpr int kRowPad = 16;
-constexpr int kStageBytes = 16960;  // 8 rows of 2 KB or 3 rows of 5.5 KB, padded (306M shapes)
+// 8 rows of 2 KB or 3 rows of 5.5 KB, padded (306M shapes); a multiple of
+// 1024 so that stages can take 128-byte-swizzled tensor copies
+constexpr int kStageBytes = 17408;
 constexpr int kStages = 10;
 constexpr int kAttWords = 66;       // per attention unit: o[64], m, l
 constexpr int kMaxSplits = 4;       // attention units per head

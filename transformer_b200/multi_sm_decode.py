@@ -211,13 +211,17 @@ class DecodeEngine:
     def debug_tune(self, poll_ns: int | None = None, max_inflight: int | None = None,
                    pdl: bool | None = None, ksplit: int | None = None, att_cpc: int | None = None,
                    gemm_trace: torch.Tensor | None = None, att_trace: torch.Tensor | None = None,
-                   sample_trace: torch.Tensor | None = None, graphs: bool | None = None):
+                   sample_trace: torch.Tensor | None = None, graphs: bool | None = None,
+                   flat: bool | None = None):
         """Diagnostic knobs: back-off between failed polls (ns), weight copies
         in flight per CTA; batched step: programmatic dependent launch on/off,
         forced K split, forced attention units per (sequence, kv head) (0 =
         automatic); device stamp buffers for the projections, the attention
         and the sampler (empty tensor = off); graph replay of repeated
-        batched steps on / off."""
+        batched steps on / off; B=1 step on the flat one-CTA-per-SM kernel
+        (True) or on the cluster kernel where it fits (False, default)."""
+        if flat is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 12, int(bool(flat))), "b2d_debug_tune")
         if graphs is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 11, int(bool(graphs))), "b2d_debug_tune")
         if sample_trace is not None:
