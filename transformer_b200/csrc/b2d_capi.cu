@@ -45,6 +45,7 @@ using ShapeTiny = b2d::Shape<256, 768, 4, 2>;
 // Shape-specialised entry points.
 struct ShapeOps {
   int d, dff, nh, nkv;
+  int (*chunk_begin)(int c, int G);  // the cluster kernel's act-chunk split
   size_t smem;
   const void* kernel;        // the B=1 step, flat grid (one CTA per SM)
   const void* kernel_trace;  // the same with diagnostic stamps (b2d_debug_trace, knobs 7/8)
@@ -55,8 +56,11 @@ struct ShapeOps {
 };
 
 template <class S>
+int chunk_begin_host(int c, int G) { return b2d::chunk_begin<S>(c, G); }
+
+template <class S>
 ShapeOps make_ops() {
-  return ShapeOps{S::D, S::DFF, S::NH, S::NKV, sizeof(b2d::Smem<S>),
+  return ShapeOps{S::D, S::DFF, S::NH, S::NKV, &chunk_begin_host<S>, sizeof(b2d::Smem<S>),
                   reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, false>),
                   reinterpret_cast<const void*>(&b2d::decode_b1_kernel<S, true>),
                   b2d::smem_c_bytes<S>(),
@@ -138,7 +142,10 @@ int b1c_max_clusters(const ShapeOps* ops) {
 int b1c_grid(const ShapeOps* ops) {
   const int nc = b1c_max_clusters(ops);
   if (nc < ops->nh || nc * b2d::kCS < b2d::kMinGridC) return 0;
-  return nc * b2d::kCS;
+  const int grid = nc * b2d::kCS;
+  for (int c = 0; c < grid; ++c)  // the kernel's per-CTA gate/up budget
+    if (ops->chunk_begin(c + 1, grid) - ops->chunk_begin(c, grid) > b2d::kMaxChunksC) return 0;
+  return grid;
 }
 
 // One cooperative launch of the cluster kernel.
@@ -577,7 +584,7 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
       ws->poll_ns = static_cast<uint32_t>(value);
       return B2D_OK;
     case 2:  // bulk copies in flight per CTA
-      if (value < 1 || value > b2d::kStages) return B2D_ERR_INVALID_ARG;
+      if (value < 1 || value > b2d::kStagesC) return B2D_ERR_INVALID_ARG;  // the larger ring
       ws->max_inflight = static_cast<int>(value);
       return B2D_OK;
     case 3:  // batched step: programmatic dependent launch on (1) / off (0)

@@ -288,17 +288,21 @@ __device__ __forceinline__ bool gather_pairs(const DecodeArgs& A, uint32_t flag,
   return true;
 }
 
-// Consumer-side view of the stage ring.
-struct Ring {
-  uint8_t (*stage)[kStageBytes];
+// Consumer-side view of a stage ring of NS stages of SB bytes.
+template <int NS, int SB>
+struct RingT {
+  static constexpr int kN = NS;
+  uint8_t (*stage)[SB];
   uint64_t* full;
   uint64_t* empty;
   uint32_t seq;
 };
+using Ring = RingT<kStages, kStageBytes>;
 
 // Warp-uniform: every lane acquires the stage itself; lane 0 decides timeouts.
-__device__ __forceinline__ bool wait_full(const DecodeArgs& A, Ring& r, uint32_t flag, uint64_t t0) {
-  const uint32_t slot = r.seq % kStages, par = (r.seq / kStages) & 1u;
+template <class R>
+__device__ __forceinline__ bool wait_full(const DecodeArgs& A, R& r, uint32_t flag, uint64_t t0) {
+  const uint32_t slot = r.seq % R::kN, par = (r.seq / R::kN) & 1u;
   const int lane = threadIdx.x & 31;
   Waiter wt;
   while (true) {
@@ -314,12 +318,13 @@ __device__ __forceinline__ bool wait_full(const DecodeArgs& A, Ring& r, uint32_t
 // stages are already resident (the usual case: the producer runs ~20 us
 // ahead) costs one barrier round trip instead of one per stage; __syncwarp
 // then orders every lane after the acquiring lanes.
-__device__ __forceinline__ bool wait_full_n(const DecodeArgs& A, Ring& r, int n, uint32_t flag, uint64_t t0) {
+template <class R>
+__device__ __forceinline__ bool wait_full_n(const DecodeArgs& A, R& r, int n, uint32_t flag, uint64_t t0) {
   const int lane = threadIdx.x & 31;
   const uint32_t sq = r.seq + static_cast<uint32_t>(lane);
   Waiter wt;
   while (true) {
-    const bool done = lane >= n || mbar_test(&r.full[sq % kStages], (sq / kStages) & 1u);
+    const bool done = lane >= n || mbar_test(&r.full[sq % R::kN], (sq / R::kN) & 1u);
     if (__all_sync(0xffffffffu, done)) break;
     const bool exp = lane == 0 ? wt.expired(A, flag, t0, SITE_FULL) : false;
     if (__shfl_sync(0xffffffffu, exp ? 1 : 0, 0)) return false;
@@ -330,14 +335,14 @@ __device__ __forceinline__ bool wait_full_n(const DecodeArgs& A, Ring& r, int n,
 
 // Warp-uniform: this warp is done with stages seq .. seq+n-1 (lane i arrives
 // on stage seq+i's empty barrier).
-__device__ __forceinline__ void release_n(Ring& r, int n) {
+template <class R>
+__device__ __forceinline__ void release_n(R& r, int n) {
   const int lane = threadIdx.x & 31;
   __syncwarp();
-  if (lane < n) mbar_arrive(&r.empty[(r.seq + static_cast<uint32_t>(lane)) % kStages]);
+  if (lane < n) mbar_arrive(&r.empty[(r.seq + static_cast<uint32_t>(lane)) % R::kN]);
   r.seq += static_cast<uint32_t>(n);
 }
 
-constexpr int kGroupStages = kStages / 2;  // stages waited for together
 
 // The GEMV input vector, read from Smem::xb (bf16, natural order).  Lane l
 // multiplies weight elements k*256 + l*8 + j (k < KI, j < 8), i.e. the 16-byte
@@ -437,9 +442,10 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, floa
 }
 
 // Same streaming for many units per warp (the logits): reduce per stage.
-template <int KI, int PITCH, int PS, class Out>
-__device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring, uint32_t flag, uint64_t t0,
+template <int KI, int PITCH, int PS, class R, class Out>
+__device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, R& ring, uint32_t flag, uint64_t t0,
                                                 int u_begin, int u_end, const XSmem x, Out out) {
+  constexpr int kGroupStages = R::kN / 2;  // stages waited for together
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   bool ok = true;
   for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * PS) {
@@ -450,7 +456,7 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, Ring& ring,
       const int first = g0 + ((warp - (g0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
       for (int u = first; u < g1; u += kConsumerWarps) {
         const int st = (u - g0) / PS;
-        const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages];
+        const uint8_t* sb = ring.stage[(ring.seq + static_cast<uint32_t>(st)) % R::kN];
         const uint4* rp = reinterpret_cast<const uint4*>(sb + static_cast<size_t>(u - g0 - st * PS) * PITCH);
         uint64_t a0 = 0ull, a1 = 0ull;
 #pragma unroll

@@ -47,6 +47,17 @@ namespace b2d {
 
 constexpr int kCS = 4;            // CTAs per cluster
 constexpr int kMinGridC = 120;    // fewest CTAs the per-CTA budgets assume
+// Act chunks are split over the CTAs in proportion to a weight: 1 for a CTA
+// of a head cluster (which also streams 48 q/k/v rows and a Wo block per
+// layer), kChunkWeight for the others, so that every CTA streams about the
+// same bytes per layer.
+constexpr int kChunkWeight = 3;
+constexpr int kMaxChunksC = 4;    // act chunks per CTA at most (the host checks its grid against it)
+// Weight ring: every stage is one 16 KB tensor copy, so 12 of them fit.
+constexpr int kStagesC = 12;
+constexpr int kStageBytesC = 16384;
+using RingC = RingT<kStagesC, kStageBytesC>;
+constexpr int kAttRows = 64;      // K/V positions staged per attention pass
 enum : uint32_t {
   ST_RANGE = 0x300u,              // | site: a residual contribution out of the accumulator range
   SITE_QKVX = 12, SITE_ATTX = 13, SITE_DRED = 14,
@@ -60,19 +71,19 @@ struct ShapeC {
   static constexpr int OBOX = OROWS < 128 ? OROWS : 128;    // Wo rows per tensor copy (one stage)
   static constexpr int OBOXES = OROWS / OBOX;
   static constexpr int CHUNKS = S::DFF / 8;                 // act chunks of 8 units
-  static constexpr int MAXCH = (CHUNKS + kMinGridC - 1) / kMinGridC;
+  static constexpr int MAXCH = kMaxChunksC;
   static constexpr int GU_ROWS = 16 * MAXCH;
   static constexpr int DBOX = S::D < 256 ? S::D : 256;      // Wd rows per tensor copy
   static constexpr int DBOXES = S::D / DBOX;
-  static constexpr int PS = 8192 / S::D;                    // K = D rows per 16 KB stage (k-block layout)
+  static constexpr int PS = kStageBytesC / S::ROWB_D;       // K = D rows per stage (k-block layout; logits)
   static constexpr int QPS = QROWS < PS ? QROWS : PS;       // rows per stage of the q / k / v ranges
   static constexpr int MT_QKV = (QKV_ROWS + 15) / 16, MT_GU = (GU_ROWS + 15) / 16;
   static constexpr int MT_MAX = MT_QKV > MT_GU ? MT_QKV : MT_GU;
   static_assert(64 % kCS == 0 && QROWS % QPS == 0, "q/k/v rows fill whole stages");
-  static_assert(OROWS % 16 == 0 && OROWS % OBOX == 0 && OBOX * 128 <= kStageBytes, "Wo boxes");
-  static_assert(S::D % DBOX == 0 && S::D * 16 <= kStageBytes, "one act chunk's Wd columns fill one stage");
-  static_assert(S::D % 64 == 0 && PS >= 1 && PS * 2 * S::D <= kStageBytes, "k-block stages");
-  static_assert(S::DFF % 8 == 0 && 2 * MAXCH <= kStages, "gate/up stages resident together");
+  static_assert(OROWS % 16 == 0 && OROWS % OBOX == 0 && OBOX * 128 <= kStageBytesC, "Wo boxes");
+  static_assert(S::D % DBOX == 0 && S::D * 16 <= kStageBytesC, "one act chunk's Wd columns fill one stage");
+  static_assert(S::D % 64 == 0 && PS >= 1 && PS * S::ROWB_D <= kStageBytesC, "k-block stages");
+  static_assert(S::DFF % 8 == 0 && 2 * MAXCH <= kStagesC, "gate/up stages resident together");
   static_assert(S::D / 4 <= kConsumers && OROWS <= kConsumers, "one thread per pushed quad / owned row");
   static_assert(S::GQA * S::NKV == S::NH, "GQA");
   // bytes each CTA receives per layer through each cluster barrier
@@ -84,15 +95,27 @@ struct ShapeC {
 template <class S>
 struct SmemC {
   using C = ShapeC<S>;
-  alignas(1024) uint8_t stage[kStages][kStageBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  alignas(1024) uint8_t stage[kStagesC][kStageBytesC];
+  uint64_t full[kStagesC];
+  uint64_t empty[kStagesC];
   uint64_t qkv_bar;   // q/k/v pushes of the cluster (kQkvBytes per layer)
   uint64_t attp_bar;  // attention partial pushes (kAttpBytes)
   uint64_t dred_bar;  // down partial pushes (kDredBytes)
   alignas(16) __nv_bfloat16 xb[S::D];          // GEMV input (bf16)
-  alignas(128) __nv_bfloat16 katt[128][64];
-  alignas(128) __nv_bfloat16 vatt[128][64];
+  // The attention's K/V rows and the MLP's down partials are never live at
+  // once: a peer pushes its down partials only after this CTA's attention of
+  // the layer fed the HM accumulators it waited for, and the next layer's K/V
+  // copies start after the barrier that ends this layer.
+  union alignas(128) {
+    struct {  // K/V rows of one pass: row r's 16-byte chunk c at r * 128 + ((c ^ (r & 7)) << 4)
+      __nv_bfloat16 k[kAttRows][64];
+      __nv_bfloat16 v[kAttRows][64];
+    } att;
+    struct {
+      float pd[S::D];               // this CTA's down partial
+      float pr[kCS][C::OROWS];      // the cluster's down partials of this CTA's rows
+    } dn;
+  } u;
   alignas(16) float qkv[3 * 64];               // head q, kv-group k, v (pushed by the cluster)
   alignas(16) float rq[64];
   alignas(16) float rk[64];
@@ -100,10 +123,7 @@ struct SmemC {
   float wm[kConsumerWarps], wl[kConsumerWarps];
   float red[kConsumerWarps];
   alignas(16) float attp[kCS][68];             // attention partials (o[64], m, l) by sender rank
-  alignas(16) float pd[S::D];                  // this CTA's down partial
-  alignas(16) float pr[kCS][C::OROWS];         // the cluster's down partials of this CTA's rows
   int64_t fix[C::OROWS];                       // exact residual sums of this CTA's rows (cluster 0)
-  alignas(16) float gu_out[C::GU_ROWS];
   float act[8 * C::MAXCH];
   float part[kConsumerWarps][C::MT_MAX * 16];
   float am_v[kConsumerWarps];
@@ -116,13 +136,21 @@ constexpr size_t smem_c_bytes() { return sizeof(SmemC<S>) + 1024; }  // + base a
 template <class S>
 struct SmemCChecks {
   static_assert(offsetof(SmemC<S>, stage) == 0, "stages first (1024-aligned base)");
-  static_assert(offsetof(SmemC<S>, xb) % 16 == 0 && offsetof(SmemC<S>, pd) % 16 == 0 &&
-                offsetof(SmemC<S>, pr) % 16 == 0 && offsetof(SmemC<S>, attp) % 16 == 0, "vector fields");
-  static_assert(offsetof(SmemC<S>, katt) % 128 == 0 && offsetof(SmemC<S>, vatt) % 128 == 0, "K/V staging");
+  static_assert(offsetof(SmemC<S>, xb) % 16 == 0 && offsetof(SmemC<S>, u) % 128 == 0 &&
+                offsetof(SmemC<S>, attp) % 16 == 0, "vector fields");
   static_assert(offsetof(SmemC<S>, full) % 8 == 0, "mbarriers");
   static_assert(smem_c_bytes<S>() <= 232448, "shared memory per CTA");
   static constexpr bool ok = true;
 };
+
+// First act chunk of CTA c when G CTAs share the CHUNKS chunks (weights as
+// above; CTAs c >= gridDim.x exist only in the failure-injection test).
+template <class S>
+__device__ __host__ __forceinline__ int chunk_begin(int c, int G) {
+  const int nh = S::NH * kCS;
+  const auto w = [nh](int x) { return static_cast<long long>(x <= nh ? x : nh + kChunkWeight * (x - nh)); };
+  return static_cast<int>(static_cast<long long>(ShapeC<S>::CHUNKS) * w(c) / w(G));
+}
 
 // Accumulator word of residual element `row` after sublayer `which` (0 = HM_l,
 // after attention; 1 = H_{l+1}, after the MLP) of layer l, parity `par`.
@@ -243,12 +271,12 @@ __device__ void producer_c(const DecodeArgs& A, SmemC<S>& sm, const MapsC& maps,
   bool ok = true;
   // Arms the next ring slot for `bytes` (warp-uniform); -1 when the launch aborted.
   auto arm = [&](uint32_t bytes) -> int {
-    const uint32_t slot = seq % kStages;
+    const uint32_t slot = seq % kStagesC;
     bool good = true;
     if (lane == 0) {
       while (good && seq - landed >= cap) {
         Waiter wt;
-        while (!mbar_test(&sm.full[landed % kStages], (landed / kStages) & 1u)) {
+        while (!mbar_test(&sm.full[landed % kStagesC], (landed / kStagesC) & 1u)) {
           if (*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_FULL)) {
             good = false;
             break;
@@ -256,8 +284,8 @@ __device__ void producer_c(const DecodeArgs& A, SmemC<S>& sm, const MapsC& maps,
         }
         if (good) ++landed;
       }
-      if (good && seq >= kStages) {
-        const uint32_t par = ((seq / kStages) - 1) & 1u;
+      if (good && seq >= kStagesC) {
+        const uint32_t par = ((seq / kStagesC) - 1) & 1u;
         Waiter wt;
         while (!mbar_test(&sm.empty[slot], par)) {
           if (*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_EMPTY)) {
@@ -317,52 +345,57 @@ __device__ void producer_c(const DecodeArgs& A, SmemC<S>& sm, const MapsC& maps,
         }
       }
     }
-    if (ok) rows(A.wbase + A.off_emb + static_cast<size_t>(v0) * S::ROWB_D, v1 - v0, S::RPS_D);
+    if (ok) rows(A.wbase + A.off_emb + static_cast<size_t>(v0) * S::ROWB_D, v1 - v0, C::PS);
   }
   if (lane == 0) {
     // never leave with copies in flight (bounded)
-    const uint32_t first = seq > kStages ? seq - kStages : 0;
+    const uint32_t first = seq > kStagesC ? seq - kStagesC : 0;
     const uint64_t td = globaltimer_ns();
     for (uint32_t s = first; s < seq; ++s) {
-      while (!mbar_test(&sm.full[s % kStages], (s / kStages) & 1u)) {
+      while (!mbar_test(&sm.full[s % kStagesC], (s / kStagesC) & 1u)) {
         if (globaltimer_ns() - td > A.wait_ns) break;
       }
     }
   }
 }
 
-// K/V staging of one attention pass: cached positions [base, min(base + 128,
-// p1, pos)) of kv head g, layer l, into katt / vatt by 16-byte cp.async
-// copies from every consumer thread.  They bypass the tensor-copy unit, whose
-// queue holds the weight stream.  Each thread waits for its own copies
-// (cp.async.wait_all) before the barrier that publishes them.
+// K/V staging of one attention pass: cached positions [base, min(base +
+// kAttRows, p1, pos)) of kv head g, layer l, into sm.u.att by 16-byte cp.async
+// copies from every consumer thread (row r's chunk c at r * 128 + ((c ^ (r &
+// 7)) << 4)).  They bypass the tensor-copy unit, whose queue holds the weight
+// stream.  Each thread waits for its own copies (cp.async.wait_all) before the
+// barrier that publishes them.
 template <class S>
 __device__ __forceinline__ void att_issue_c(const DecodeArgs& A, SmemC<S>& sm, int l, int g, int pos, int base,
                                             int p1) {
   const size_t half = static_cast<size_t>(S::NKV) * A.ctx * S::DH;
   const __nv_bfloat16* Kc = A.kv + static_cast<size_t>(l) * 2 * half + static_cast<size_t>(g) * A.ctx * S::DH +
                             static_cast<size_t>(base) * S::DH;
-  const int ncached = max(0, min(min(base + 128, p1), pos) - base);
+  const int ncached = max(0, min(min(base + kAttRows, p1), pos) - base);
   for (int i = threadIdx.x; i < ncached * 8; i += kConsumers) {  // 8 chunks of 16 bytes per row
-    cp_async16(&sm.katt[0][0] + 8 * i, Kc + 8 * i);
-    cp_async16(&sm.vatt[0][0] + 8 * i, Kc + half + 8 * i);
+    const int r = i >> 3, c = i & 7;
+    const int off = r * 64 + ((c ^ (r & 7)) << 3);
+    cp_async16(&sm.u.att.k[0][0] + off, Kc + 8 * i);
+    cp_async16(&sm.u.att.v[0][0] + off, Kc + half + 8 * i);
   }
   cp_async_commit();
 }
 
 // The attention of head h over this CTA's positions [p0, p1) (reference
-// :182-221), from q/k/v in sm.qkv: RoPE, then passes of up to 128 positions
-// (a warp owns 16 per pass, two lanes per position), online softmax.
-// Returns the unnormalised partial in warp 0's registers: lane l holds o[2l],
-// o[2l + 1] in (b0, b1), and M, L.  The K/V rows of the first pass were
-// issued with the layer (att_issue_c).
+// :182-221), from q/k/v in sm.qkv: RoPE, then passes of kAttRows positions.
+// A warp owns 8 positions of a pass, four lanes per position (16 dims each),
+// so a score is a 16-term dot product and two shuffles; online softmax per
+// warp; PV with lane l on dims 2l, 2l + 1.  Returns the unnormalised partial
+// in warp 0's registers: lane l holds o[2l], o[2l + 1] in (b0, b1), and M, L.
+// The K/V rows of the first pass were issued with the layer (att_issue_c).
 template <class S, bool TR>
 __device__ __forceinline__ void attention_slice(const DecodeArgs& A, SmemC<S>& sm, int l, int pos, int h, int p0,
                                                 int p1, float rc, float rs, float& b0, float& b1, float& Mo,
                                                 float& Lo, int ts) {
+  static_assert(kAttRows == 8 * kConsumerWarps, "a pass is 8 positions per warp");
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int g = h / S::GQA;
-  const int qi = lane & 15, hf = lane >> 4;
+  const int qi = lane >> 2, q4 = lane & 3;  // position within the warp's 8, dim quarter
   cp_async_wait_all();  // this thread's share of the first pass's K/V rows (issued with the layer)
   // RoPE (rotate-half, reference :154-173; f32 tables as model.py:101-107).
   if (t < 64) {
@@ -376,62 +409,74 @@ __device__ __forceinline__ void attention_slice(const DecodeArgs& A, SmemC<S>& s
   }
   consumer_sync<kConsumers>();
   trace_stamp<TR>(A, ts + 10);
-  const float4* q4 = reinterpret_cast<const float4*>(sm.rq + hf * 32);
+  float qv[16];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) qv[d] = sm.rq[16 * q4 + d];
   const float vn0 = sm.qkv[128 + 2 * lane], vn1 = sm.qkv[128 + 2 * lane + 1];
   float m = -INFINITY, lsum = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int base = p0; base < p1; base += 16 * kConsumerWarps) {
-    if (base != p0) {  // later passes (contexts past 128 positions per CTA)
+  for (int base = p0; base < p1; base += kAttRows) {
+    if (base != p0) {  // later passes
       att_issue_c<S>(A, sm, l, g, pos, base, p1);
       cp_async_wait_all();
       consumer_sync<kConsumers>();
     }
-    const int pk = base + warp * 16 + qi;
-    float sdot = 0.f;
+    const int r = warp * 8 + qi, pk = base + r;
+    float sa = 0.f, sb = 0.f;
     if (pk == pos) {
 #pragma unroll
-      for (int d = 0; d < 32; ++d) sdot = fmaf(sm.rq[hf * 32 + d], sm.rk[hf * 32 + d], sdot);
-    } else if (pk < p1) {
-      const uint4* kr = reinterpret_cast<const uint4*>(sm.katt[pk - base]) + hf * 4;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int cc = (c + qi) & 3;
-        const uint4 kw = kr[cc];
-        const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
-        sdot = fmaf(qa.x, bf16_lo(kw.x), sdot);
-        sdot = fmaf(qa.y, bf16_hi(kw.x), sdot);
-        sdot = fmaf(qa.z, bf16_lo(kw.y), sdot);
-        sdot = fmaf(qa.w, bf16_hi(kw.y), sdot);
-        sdot = fmaf(qb.x, bf16_lo(kw.z), sdot);
-        sdot = fmaf(qb.y, bf16_hi(kw.z), sdot);
-        sdot = fmaf(qb.z, bf16_lo(kw.w), sdot);
-        sdot = fmaf(qb.w, bf16_hi(kw.w), sdot);
+      for (int d = 0; d < 16; d += 2) {
+        sa = fmaf(qv[d], sm.rk[16 * q4 + d], sa);
+        sb = fmaf(qv[d + 1], sm.rk[16 * q4 + d + 1], sb);
       }
+    } else if (pk < p1) {
+      const uint4* kr = reinterpret_cast<const uint4*>(sm.u.att.k[r]);
+      const uint4 k0 = kr[(2 * q4) ^ qi], k1 = kr[(2 * q4 + 1) ^ qi];  // (r & 7) == qi
+      sa = fmaf(qv[0], bf16_lo(k0.x), sa);
+      sb = fmaf(qv[1], bf16_hi(k0.x), sb);
+      sa = fmaf(qv[2], bf16_lo(k0.y), sa);
+      sb = fmaf(qv[3], bf16_hi(k0.y), sb);
+      sa = fmaf(qv[4], bf16_lo(k0.z), sa);
+      sb = fmaf(qv[5], bf16_hi(k0.z), sb);
+      sa = fmaf(qv[6], bf16_lo(k0.w), sa);
+      sb = fmaf(qv[7], bf16_hi(k0.w), sb);
+      sa = fmaf(qv[8], bf16_lo(k1.x), sa);
+      sb = fmaf(qv[9], bf16_hi(k1.x), sb);
+      sa = fmaf(qv[10], bf16_lo(k1.y), sa);
+      sb = fmaf(qv[11], bf16_hi(k1.y), sb);
+      sa = fmaf(qv[12], bf16_lo(k1.z), sa);
+      sb = fmaf(qv[13], bf16_hi(k1.z), sb);
+      sa = fmaf(qv[14], bf16_lo(k1.w), sa);
+      sb = fmaf(qv[15], bf16_hi(k1.w), sb);
     }
-    sdot += __shfl_xor_sync(0xffffffffu, sdot, 16);
+    float sdot = sa + sb;
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
+    sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
     const bool valid = pk < p1;
     const float s = valid ? sdot : -INFINITY;
     float mx = s;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float mn = fmaxf(m, mx);
     const float pe = valid ? __expf(s - mn) : 0.f;
     float ps = pe;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    for (int o = 4; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
     const float alpha = m == -INFINITY ? 0.f : __expf(m - mn);
-    if (hf == 0) sm.wo[warp][qi] = pe;
+    if (q4 == 0) sm.wo[warp][qi] = pe;  // stage probabilities for PV
     __syncwarp();
+    if (base == p0) trace_stamp<TR>(A, ts + 11);
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int pv = base + warp * 16 + i;
+    for (int i = 0; i < 8; ++i) {
+      const int rv = warp * 8 + i, pv = base + rv;
       const float pi = sm.wo[warp][i];
       float v0 = 0.f, v1 = 0.f;
       if (pv == pos) {
         v0 = vn0;
         v1 = vn1;
       } else if (pv < p1) {
-        const uint32_t vw = reinterpret_cast<const uint32_t*>(sm.vatt[pv - base])[lane];
+        const uint32_t vw =
+            reinterpret_cast<const uint32_t*>(sm.u.att.v[rv])[(((lane >> 2) ^ (rv & 7)) << 2) + (lane & 3)];
         v0 = bf16_lo(vw);
         v1 = bf16_hi(vw);
       }
@@ -445,7 +490,7 @@ __device__ __forceinline__ void attention_slice(const DecodeArgs& A, SmemC<S>& s
     m = mn;
     consumer_sync<kConsumers>();  // staged K/V read by every warp before a later pass reuses them
   }
-  trace_stamp<TR>(A, ts + 11);
+  trace_stamp<TR>(A, ts + 12);
   sm.wo[warp][2 * lane] = o0;
   sm.wo[warp][2 * lane + 1] = o1;
   if (lane == 0) {
@@ -470,7 +515,6 @@ __device__ __forceinline__ void attention_slice(const DecodeArgs& A, SmemC<S>& s
     Mo = M;
     Lo = L;
   }
-  trace_stamp<TR>(A, ts + 12);
   // The first head of the group appends this position's K (post-RoPE) and V
   // to the cache in bf16 (the CTA whose positions include pos).
   if (warp == 1 && (h % S::GQA) == 0 && pos >= p0 && pos < p1) {
@@ -487,21 +531,26 @@ __device__ __forceinline__ void attention_slice(const DecodeArgs& A, SmemC<S>& s
 // gemv_phase (decode_b1.cuh) but reading k-block stages: a stage holds RB
 // consecutive rows as [K/64][RB][64] bf16 with the 128-byte swizzle (16-byte
 // chunk c of row r at ((c ^ (r & 7)) << 4) within the row's 128 bytes).
-// Warp w takes K slice [w K/8, (w+1) K/8) of every 16-row tile; thread r sums
-// the warps' partials in warp order and calls out(r, v).  Ends with the
-// phase's closing barrier; returns the AND of every warp's waits.
-template <int K, int RB, int MT, int PSTRIDE, bool TR, class Out>
-__device__ __forceinline__ bool gemv_phase_sw(const DecodeArgs& A, Ring& ring, float* part, const __nv_bfloat16* xb,
+// Warp w takes K slice [w K/8, (w+1) K/8) of every 16-row tile that holds
+// rows; the input fragments of the whole slice are loaded first and the
+// weight fragments one K step ahead of their MMAs (ldmatrix latency is ~100
+// cycles).  Thread r sums the warps' partials in warp order and calls
+// out(r, v); with SWIGLU, rows (2j, 2j + 1) are gate and up of unit j and
+// out(j, silu(gate) * up) is called instead.  Returns the AND of every
+// warp's waits (after the phase's closing barrier).
+template <int K, int RB, int MT, int PSTRIDE, bool TR, bool SWIGLU, class Out>
+__device__ __forceinline__ bool gemv_phase_sw(const DecodeArgs& A, RingC& ring, float* part, const __nv_bfloat16* xb,
                                               uint32_t flag, uint64_t t0, int rows, Out out) {
   static_assert(MT * 16 <= PSTRIDE, "partial buffer");
   constexpr int KS = K / 16 / kConsumerWarps;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int gid = lane >> 2, tig = lane & 3;
   const int ns = rows > 0 ? (rows + RB - 1) / RB : 0;
-  bool ok = rows <= MT * 16 && ns <= kStages;
+  bool ok = rows <= MT * 16 && ns <= kStagesC;
   if (ok && ns > 0) ok = wait_full_n(A, ring, ns, flag, t0);
   if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
   if (ok && rows > 0) {
+    const int nt = (rows + 15) >> 4;  // tiles holding rows
     const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lk = 8 * (lane >> 4);
     uint32_t rbase[MT];
     uint32_t rsw[MT];
@@ -509,34 +558,52 @@ __device__ __forceinline__ bool gemv_phase_sw(const DecodeArgs& A, Ring& ring, f
     for (int mt = 0; mt < MT; ++mt) {
       const int r = min(mt * 16 + lr, rows - 1);  // rows past the range: any valid row
       const int st = r / RB, rr = r - st * RB;
-      rbase[mt] = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStages]) +
+      rbase[mt] = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStagesC]) +
                   static_cast<uint32_t>(rr * 128);
       rsw[mt] = static_cast<uint32_t>(rr & 7);
     }
-    float acc[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
     const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xb);
     const int k0 = warp * KS * 16;
-#pragma unroll 4
-    for (int s = 0; s < KS; ++s) {
-      const int k = k0 + 16 * s;
-      const uint32_t b0 = x32[(k + 2 * tig) >> 1], b1 = x32[(k + 8 + 2 * tig) >> 1];
-      const int kl = k + lk;
-      const uint32_t kb_off = static_cast<uint32_t>((kl >> 6) * RB * 128);
-      const uint32_t c = static_cast<uint32_t>((kl >> 3) & 7);
+    uint32_t bx[KS][2];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(rbase[mt] + kb_off + ((c ^ rsw[mt]) << 4), a0, a1, a2, a3);
-        mma_bf16(acc[mt], a0, a1, a2, a3, b0, b1);
+    for (int s = 0; s < KS; ++s) {
+      bx[s][0] = x32[(k0 + 16 * s + 2 * tig) >> 1];
+      bx[s][1] = x32[(k0 + 16 * s + 8 + 2 * tig) >> 1];
+    }
+    auto a_addr = [&](int mt, int s) {
+      const int kl = k0 + 16 * s + lk;
+      return rbase[mt] + static_cast<uint32_t>((kl >> 6) * RB * 128) +
+             ((static_cast<uint32_t>((kl >> 3) & 7) ^ rsw[mt]) << 4);
+    };
+    float acc[MT][4];
+    uint32_t af[2][MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+      if (mt < nt) ldsm_x4(a_addr(mt, 0), af[0][mt][0], af[0][mt][1], af[0][mt][2], af[0][mt][3]);
+    }
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      if (s + 1 < KS) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          if (mt < nt)
+            ldsm_x4(a_addr(mt, s + 1), af[(s + 1) & 1][mt][0], af[(s + 1) & 1][mt][1], af[(s + 1) & 1][mt][2],
+                    af[(s + 1) & 1][mt][3]);
       }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        if (mt < nt)
+          mma_bf16(acc[mt], af[s & 1][mt][0], af[s & 1][mt][1], af[s & 1][mt][2], af[s & 1][mt][3], bx[s][0],
+                   bx[s][1]);
     }
     if (tig == 0) {
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        part[warp * PSTRIDE + mt * 16 + gid] = acc[mt][0];
-        part[warp * PSTRIDE + mt * 16 + gid + 8] = acc[mt][2];
+        if (mt < nt) {
+          part[warp * PSTRIDE + mt * 16 + gid] = acc[mt][0];
+          part[warp * PSTRIDE + mt * 16 + gid + 8] = acc[mt][2];
+        }
       }
     }
   }
@@ -544,10 +611,189 @@ __device__ __forceinline__ bool gemv_phase_sw(const DecodeArgs& A, Ring& ring, f
   if (ok) release_n(ring, ns);
   ok = consumer_sync_and<kConsumers>(ok);
   if (!ok) return false;
+  float v = 0.f;
   if (t < rows) {
-    float v = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) v += part[w * PSTRIDE + t];
+  }
+  if constexpr (SWIGLU) {
+    const float up = __shfl_down_sync(0xffffffffu, v, 1);  // rows come in (gate, up) pairs
+    if ((t & 1) == 0 && t < rows) out(t >> 1, v * (1.0f / (1.0f + __expf(-v))) * up);
+  } else if (t < rows) {
+    out(t, v);
+  }
+  return true;
+}
+
+// The layer's input GEMVs fused with the residual gather and RMSNorm
+// (reference :121-126): warp w needs only its K slice [w K/8, (w+1) K/8) of
+// the normalised input, so it polls just those residual words, writes
+// bf16(h * gain) for its slice into sm.xb and runs its MMAs at once, while
+// other slices may still be arriving.  The norm's scalar factor r = rsqrt(
+// mean(h^2) + eps) multiplies the summed rows in the epilogue (W (h g) r
+// equals W (h r g) up to where the bf16 rounding of the input falls).
+// The residual comes from accumulator words (`words`, complete at `target`
+// contributions; all of a lane's pending pairs are loaded before any is
+// checked, so a poll costs one round trip) or, when words is null, from the
+// bf16 embedding row `emb`.  keep(row, s_row, s_row+1) receives the exact
+// fixed-point sums of each pair once.  Weight stages and the epilogue as
+// gemv_phase_sw.
+template <int K, int RB, int MT, int PSTRIDE, bool TR, bool SWIGLU, class SM, class Keep, class Out>
+__device__ __forceinline__ bool gemv_x_sw(const DecodeArgs& A, RingC& ring, SM& sm, uint32_t flag, uint64_t t0,
+                                          uint32_t site, const float* gain, float eps, int rows,
+                                          const uint64_t* words, uint32_t target, const uint32_t* emb, Keep keep,
+                                          Out out) {
+  static_assert(MT * 16 <= PSTRIDE, "partial buffer");
+  constexpr int KS = K / 16 / kConsumerWarps;
+  constexpr int PPW = K / 2 / kConsumerWarps;  // residual pairs per warp slice
+  constexpr int NPL = (PPW + 31) / 32;          // pairs per lane
+  static_assert(NPL <= 32, "pending mask");
+  float* part = &sm.part[0][0];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int k0 = warp * KS * 16;
+  // ---- this warp's slice of the residual -> bf16(h * gain) in sm.xb ----
+  float2 g[NPL];
+  uint32_t pending = 0;
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int p = lane + 32 * j;
+    g[j] = p < PPW ? __ldg(reinterpret_cast<const float2*>(gain) + k0 / 2 + p) : make_float2(0.f, 0.f);
+    if (p < PPW) pending |= 1u << j;
+  }
+  float hs[NPL][2];  // the lane's pairs, summed in a fixed order once all arrived
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) hs[j][0] = hs[j][1] = 0.f;
+  bool ok = true;
+  Waiter wt;
+  while (pending) {
+    uint64_t wa[NPL], wb[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int p = k0 / 2 + lane + 32 * j;
+      if (pending & (1u << j)) {
+        if (words != nullptr) {
+          ld_words2(words + 2 * p, wa[j], wb[j]);
+        } else {  // embedding pair: exact bf16 values, always in the accumulator range
+          const uint32_t w2 = __ldg(emb + p);
+          int64_t qa = 0, qb = 0;
+          acc_fix(bf16_lo(w2), qa);
+          acc_fix(bf16_hi(w2), qb);
+          wa[j] = (static_cast<uint64_t>(target) << kAccCountShift) + static_cast<uint64_t>(qa + target * static_cast<int64_t>(kAccBias));
+          wb[j] = (static_cast<uint64_t>(target) << kAccCountShift) + static_cast<uint64_t>(qb + target * static_cast<int64_t>(kAccBias));
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+      const int p = k0 / 2 + lane + 32 * j;
+      if ((pending & (1u << j)) && acc_count(wa[j]) == target && acc_count(wb[j]) == target) {
+        const int64_t sa = acc_sum(wa[j], target), sb = acc_sum(wb[j], target);
+        const float h0 = acc_value(sa), h1 = acc_value(sb);
+        keep(2 * p, sa, sb);
+        hs[j][0] = h0;
+        hs[j][1] = h1;
+        reinterpret_cast<__nv_bfloat162*>(sm.xb)[p] = __floats2bfloat162_rn(h0 * g[j].x, h1 * g[j].y);
+        pending &= ~(1u << j);
+      }
+    }
+    if (!pending) break;
+    if (A.poll_ns) __nanosleep(A.poll_ns);
+    if (wt.expired(A, flag, t0, site)) {
+      ok = false;
+      break;
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    ss = fmaf(hs[j][0], hs[j][0], ss);
+    ss = fmaf(hs[j][1], hs[j][1], ss);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) sm.red[warp] = ss;
+  __syncwarp();  // the warp's slice of sm.xb, written by its lanes
+  if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
+  // ---- the warp's K slice of every row tile ----
+  const int ns = rows > 0 ? (rows + RB - 1) / RB : 0;
+  ok = ok && rows <= MT * 16 && ns <= kStagesC;
+  if (ok && ns > 0) ok = wait_full_n(A, ring, ns, flag, t0);
+  if (ok && rows > 0) {
+    const int nt = (rows + 15) >> 4;  // tiles holding rows
+    const int lr = (lane & 7) + 8 * ((lane >> 3) & 1), lk = 8 * (lane >> 4);
+    uint32_t rbase[MT];
+    uint32_t rsw[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int r = min(mt * 16 + lr, rows - 1);  // rows past the range: any valid row
+      const int st = r / RB, rr = r - st * RB;
+      rbase[mt] = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(st)) % kStagesC]) +
+                  static_cast<uint32_t>(rr * 128);
+      rsw[mt] = static_cast<uint32_t>(rr & 7);
+    }
+    const uint32_t* x32 = reinterpret_cast<const uint32_t*>(sm.xb);
+    uint32_t bx[KS][2];
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      bx[s][0] = x32[(k0 + 16 * s + 2 * tig) >> 1];
+      bx[s][1] = x32[(k0 + 16 * s + 8 + 2 * tig) >> 1];
+    }
+    auto a_addr = [&](int mt, int s) {
+      const int kl = k0 + 16 * s + lk;
+      return rbase[mt] + static_cast<uint32_t>((kl >> 6) * RB * 128) +
+             ((static_cast<uint32_t>((kl >> 3) & 7) ^ rsw[mt]) << 4);
+    };
+    float acc[MT][4];
+    uint32_t af[2][MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+      if (mt < nt) ldsm_x4(a_addr(mt, 0), af[0][mt][0], af[0][mt][1], af[0][mt][2], af[0][mt][3]);
+    }
+#pragma unroll
+    for (int s = 0; s < KS; ++s) {
+      if (s + 1 < KS) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          if (mt < nt)
+            ldsm_x4(a_addr(mt, s + 1), af[(s + 1) & 1][mt][0], af[(s + 1) & 1][mt][1], af[(s + 1) & 1][mt][2],
+                    af[(s + 1) & 1][mt][3]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+        if (mt < nt)
+          mma_bf16(acc[mt], af[s & 1][mt][0], af[s & 1][mt][1], af[s & 1][mt][2], af[s & 1][mt][3], bx[s][0],
+                   bx[s][1]);
+    }
+    if (tig == 0) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        if (mt < nt) {
+          part[warp * PSTRIDE + mt * 16 + gid] = acc[mt][0];
+          part[warp * PSTRIDE + mt * 16 + gid + 8] = acc[mt][2];
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
+  if (ok) release_n(ring, ns);
+  ok = consumer_sync_and<kConsumers>(ok);
+  if (!ok) return false;
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) tot += sm.red[w];
+  const float r = rsqrtf(tot / static_cast<float>(K) + eps);
+  float v = 0.f;
+  if (t < rows) {
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) v += part[w * PSTRIDE + t];
+    v *= r;
+  }
+  if constexpr (SWIGLU) {
+    const float up = __shfl_down_sync(0xffffffffu, v, 1);  // rows come in (gate, up) pairs
+    if ((t & 1) == 0 && t < rows) out(t >> 1, v * (1.0f / (1.0f + __expf(-v))) * up);
+  } else if (t < rows) {
     out(t, v);
   }
   return true;
@@ -557,7 +803,7 @@ __device__ __forceinline__ bool gemv_phase_sw(const DecodeArgs& A, Ring& ring, f
 // head h's columns, 128-byte swizzled) times the head output in sm.xb[0..64).
 // Warp w takes 16-row tiles w, w + 8, ...; out(r, v) per row.
 template <class S, class Out>
-__device__ __forceinline__ bool o_phase(const DecodeArgs& A, Ring& ring, const __nv_bfloat16* xo, uint32_t flag,
+__device__ __forceinline__ bool o_phase(const DecodeArgs& A, RingC& ring, const __nv_bfloat16* xo, uint32_t flag,
                                         uint64_t t0, Out out) {
   using C = ShapeC<S>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -567,7 +813,7 @@ __device__ __forceinline__ bool o_phase(const DecodeArgs& A, Ring& ring, const _
     const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xo);
     for (int tile = warp; tile < C::OROWS / 16; tile += kConsumerWarps) {
       const int box = (tile * 16) / C::OBOX;
-      const uint32_t sb = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(box)) % kStages]);
+      const uint32_t sb = smem_addr(ring.stage[(ring.seq + static_cast<uint32_t>(box)) % kStagesC]);
       const int lr = tile * 16 - box * C::OBOX + (lane & 7) + 8 * ((lane >> 3) & 1);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -617,12 +863,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   const uint32_t flag0 = ld_relaxed_u32(&A.ctl->gen) + 1u;
   // this CTA's act chunks and logits rows (the host keeps G >= kMinGridC, so nch <= MAXCH)
-  const int a8 = split_begin(cta, C::CHUNKS, G), nch = split_begin(cta + 1, C::CHUNKS, G) - a8;
+  const int a8 = chunk_begin<S>(cta, G), nch = chunk_begin<S>(cta + 1, G) - a8;
   const int v0 = split_begin(cta, A.vocab, G), v1 = split_begin(cta + 1, A.vocab, G);
   ok = ok && nch <= C::MAXCH;
 
   if (t == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStagesC; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], kConsumerWarps);
     }
@@ -645,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
 
-  Ring ring{sm.stage, sm.full, sm.empty, 0u};
+  RingC ring{sm.stage, sm.full, sm.empty, 0u};
   uint32_t xphase = 0;  // completed phases of each cluster barrier (one per layer)
   constexpr int NP = S::NP_D;
   const int own0 = rank * C::OROWS;    // residual rows this CTA adds to the accumulators
@@ -693,55 +939,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* hn = acc_word(A, par, l, 1, S::D);
       if (head >= 0) {
         if (ok) att_issue_c<S>(A, sm, l, head / S::GQA, pos, p0, p1);  // K/V of this layer's slice
-        // ---- residual in: the embedding row (reference :87-88) or H_l; RMSNorm1 -> x ----
-        {
-          float2 g[NP];
-          load_gain_pairs<S, NP>(A.ln1 + static_cast<size_t>(l) * S::D, g);
-          float hv[NP][2];
-#pragma unroll
-          for (int i = 0; i < NP; ++i) hv[i][0] = hv[i][1] = 0.f;
-          bool got = ok;
-          if (ok && l == 0) {
-            const uint32_t* e = reinterpret_cast<const uint32_t*>(A.wbase + A.off_emb) +
-                                static_cast<size_t>(tok) * (S::D / 2);
-#pragma unroll
-            for (int i = 0; i < NP; ++i) {
-              const int k = t + i * kConsumers;
-              const uint32_t w2 = k < S::D / 2 ? __ldg(e + k) : 0u;
-              hv[i][0] = bf16_lo(w2);
-              hv[i][1] = bf16_hi(w2);
-              const int row = 2 * k;
-              if (keeper && k < S::D / 2 && row >= own0 && row < own0 + C::OROWS) {
-                int64_t qa = 0, qb = 0;
-                acc_fix(hv[i][0], qa);  // bf16 values: always in range
-                acc_fix(hv[i][1], qb);
-                sm.fix[row - own0] = qa;
-                sm.fix[row + 1 - own0] = qb;
-              }
-            }
-          } else if (ok) {
-            got = gather_acc<S, NP>(A, acc_word(A, par, l - 1, 1, S::D), n_clusters, flag, t0, SITE_H, hv,
-                                    [&](int row, int64_t sa, int64_t sb) {
-                                      if (keeper && row >= own0 && row < own0 + C::OROWS) {
-                                        sm.fix[row - own0] = sa;
-                                        sm.fix[row + 1 - own0] = sb;
-                                      }
-                                    });
-          }
-          ok = norm_x<S, NP>(sm, hv, g, A.eps, got) && ok;
-        }
+        // ---- residual in: the embedding row (reference :87-88) or H_l; RMSNorm1;
+        // q / k / v rows -> every CTA of the cluster ----
         trace_stamp<TR>(A, ts + 0);
-        // ---- q / k / v rows -> every CTA of the cluster ----
         if (ok) {
           const uint32_t qkv_base = smem_addr(sm.qkv);
-          ok = gemv_phase_sw<S::D, C::QPS, C::MT_QKV, 16 * C::MT_MAX, TR>(
-              A, ring, &sm.part[0][0], sm.xb, flag, t0, C::QKV_ROWS, [&](int u, float v) {
-                const int comp = u / C::QROWS, idx = rank * C::QROWS + (u % C::QROWS);
-                const uint32_t a = qkv_base + static_cast<uint32_t>(4 * (comp * 64 + idx));
-                const uint32_t bar = smem_addr(&sm.qkv_bar);
+          auto push = [&](int u, float v) {
+            const int comp = u / C::QROWS, idx = rank * C::QROWS + (u % C::QROWS);
+            const uint32_t a = qkv_base + static_cast<uint32_t>(4 * (comp * 64 + idx));
+            const uint32_t bar = smem_addr(&sm.qkv_bar);
 #pragma unroll
-                for (int d = 0; d < kCS; ++d) st_async_f32(mapa_shared(a, d), v, mapa_shared(bar, d));
-              });
+            for (int d = 0; d < kCS; ++d) st_async_f32(mapa_shared(a, d), v, mapa_shared(bar, d));
+          };
+          auto keep_fix = [&](int row, int64_t sa, int64_t sb) {
+            if (keeper && row >= own0 && row < own0 + C::OROWS) {
+              sm.fix[row - own0] = sa;
+              sm.fix[row + 1 - own0] = sb;
+            }
+          };
+          const float* g1 = A.ln1 + static_cast<size_t>(l) * S::D;
+          const uint32_t* e = reinterpret_cast<const uint32_t*>(A.wbase + A.off_emb) +
+                              static_cast<size_t>(tok) * (S::D / 2);
+          ok = gemv_x_sw<S::D, C::QPS, C::MT_QKV, 16 * C::MT_MAX, TR, false>(
+              A, ring, sm, flag, t0, SITE_H, g1, A.eps, C::QKV_ROWS, l == 0 ? nullptr : acc_word(A, par, l - 1, 1, S::D),
+              l == 0 ? 1u : n_clusters, e, keep_fix, push);
         }
         trace_stamp<TR>(A, ts + 1);
         if (ok) {
@@ -800,33 +1021,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = consumer_sync_and<kConsumers>(ok);
         trace_stamp<TR>(A, ts + 5);
       }
-      // ---- HM (the residual after attention); RMSNorm2 -> x ----
-      {
-        float2 g[NP];
-        load_gain_pairs<S, NP>(A.ln2 + static_cast<size_t>(l) * S::D, g);
-        float hv[NP][2];
-#pragma unroll
-        for (int i = 0; i < NP; ++i) hv[i][0] = hv[i][1] = 0.f;
-        bool got = ok;
-        if (ok)
-          got = gather_acc<S, NP>(A, hm, S::NH, flag, t0, SITE_HM, hv, [&](int row, int64_t sa, int64_t sb) {
-            if (keeper && row >= own0 && row < own0 + C::OROWS) {
-              sm.fix[row - own0] = sa;
-              sm.fix[row + 1 - own0] = sb;
-            }
-          });
-        ok = norm_x<S, NP>(sm, hv, g, A.eps, got) && ok;
-      }
+      // ---- HM (the residual after attention); RMSNorm2; gate/up rows of this
+      // CTA's act chunks -> act = silu(g) * u (bf16) ----
       trace_stamp<TR>(A, ts + 6);
-      // ---- gate/up rows of this CTA's act chunks -> act = silu(g) * u (bf16) ----
       if (ok) {
-        ok = gemv_phase_sw<S::D, C::PS, C::MT_GU, 16 * C::MT_MAX, TR>(
-            A, ring, &sm.part[0][0], sm.xb, flag, t0, 16 * nch, [&](int u, float v) { sm.gu_out[u] = v; });
-        consumer_sync<kConsumers>();
-        if (t < 8 * nch) {  // rows 2j, 2j + 1: gate and up of unit j
-          const float gt = sm.gu_out[2 * t], up = sm.gu_out[2 * t + 1];
-          sm.act[t] = round_bf16(gt * (1.0f / (1.0f + __expf(-gt))) * up);
-        }
+        ok = gemv_x_sw<S::D, C::PS, C::MT_GU, 16 * C::MT_MAX, TR, true>(
+            A, ring, sm, flag, t0, SITE_HM, A.ln2 + static_cast<size_t>(l) * S::D, A.eps, 16 * nch, hm, S::NH,
+            nullptr,
+            [&](int row, int64_t sa, int64_t sb) {
+              if (keeper && row >= own0 && row < own0 + C::OROWS) {
+                sm.fix[row - own0] = sa;
+                sm.fix[row + 1 - own0] = sb;
+              }
+            },
+            [&](int j, float a) { sm.act[j] = round_bf16(a); });
         consumer_sync<kConsumers>();
       }
       trace_stamp<TR>(A, ts + 7);
@@ -838,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float p = 0.f;
             for (int ch = 0; ch < nch; ++ch) {
               const uint4 w = *reinterpret_cast<const uint4*>(
-                  ring.stage[(ring.seq + static_cast<uint32_t>(ch)) % kStages] + static_cast<size_t>(r) * 16);
+                  ring.stage[(ring.seq + static_cast<uint32_t>(ch)) % kStagesC] + static_cast<size_t>(r) * 16);
               const float* a = sm.act + 8 * ch;
               p = fmaf(a[0], bf16_lo(w.x), p);
               p = fmaf(a[1], bf16_hi(w.x), p);
@@ -849,15 +1057,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               p = fmaf(a[6], bf16_lo(w.w), p);
               p = fmaf(a[7], bf16_hi(w.w), p);
             }
-            sm.pd[r] = p;
+            sm.u.dn.pd[r] = p;
           }
           release_n(ring, nch);
         }
         ok = consumer_sync_and<kConsumers>(ok);
         if (ok && t < S::D / 4) {  // quad t: rows 4t .. 4t + 3, owned by cluster CTA 4t / OROWS
           const int d = (4 * t) / C::OROWS;
-          const float4 v = reinterpret_cast<const float4*>(sm.pd)[t];
-          st_async_f32x4(mapa_shared(smem_addr(&sm.pr[rank][4 * t - d * C::OROWS]), d), v,
+          const float4 v = reinterpret_cast<const float4*>(sm.u.dn.pd)[t];
+          st_async_f32x4(mapa_shared(smem_addr(&sm.u.dn.pr[rank][4 * t - d * C::OROWS]), d), v,
                          mapa_shared(smem_addr(&sm.dred_bar), d));
         }
       }
@@ -871,13 +1079,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && t < C::OROWS) {
         float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < kCS; ++k) s += sm.pr[k][t];
+        for (int k = 0; k < kCS; ++k) s += sm.u.dn.pr[k][t];
         int64_t q;
         acc_contrib(A, s, keeper ? sm.fix[t] : 0, flag, SITE_H, q);
         acc_add(hn + own0 + t, q);
       }
       trace_stamp<TR>(A, ts + 9);
       ++xphase;
+      if (head >= 0) consumer_sync<kConsumers>();  // down partials read before the next layer's K/V copies
     }
 
     // ---- final norm + tied logits + argmax (reference :314-357) ----
