@@ -1041,24 +1041,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- Wd column blocks x act -> partial of every output row -> the cluster ----
       if (ok) {
         ok = wait_full_n(A, ring, nch, flag, t0);
+        if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
         if (ok) {
-          for (int r = t; r < S::D; r += kConsumers) {
-            float p = 0.f;
-            for (int ch = 0; ch < nch; ++ch) {
-              const uint4 w = *reinterpret_cast<const uint4*>(
-                  ring.stage[(ring.seq + static_cast<uint32_t>(ch)) % kStagesC] + static_cast<size_t>(r) * 16);
-              const float* a = sm.act + 8 * ch;
-              p = fmaf(a[0], bf16_lo(w.x), p);
-              p = fmaf(a[1], bf16_hi(w.x), p);
-              p = fmaf(a[2], bf16_lo(w.y), p);
-              p = fmaf(a[3], bf16_hi(w.y), p);
-              p = fmaf(a[4], bf16_lo(w.z), p);
-              p = fmaf(a[5], bf16_hi(w.z), p);
-              p = fmaf(a[6], bf16_lo(w.w), p);
-              p = fmaf(a[7], bf16_hi(w.w), p);
+          // thread t: rows t + kConsumers i, independent accumulators; chunk by chunk
+          constexpr int RPT = (S::D + kConsumers - 1) / kConsumers;
+          float p[RPT];
+#pragma unroll
+          for (int i = 0; i < RPT; ++i) p[i] = 0.f;
+#pragma unroll
+          for (int ch = 0; ch < C::MAXCH; ++ch) {
+            if (ch < nch) {
+              const uint8_t* stg = ring.stage[(ring.seq + static_cast<uint32_t>(ch)) % kStagesC];
+              float a[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a[j] = sm.act[8 * ch + j];
+#pragma unroll
+              for (int i = 0; i < RPT; ++i) {
+                const int r = t + i * kConsumers;
+                if (r < S::D) {
+                  const uint4 w = *reinterpret_cast<const uint4*>(stg + static_cast<size_t>(r) * 16);
+                  p[i] = fmaf(a[0], bf16_lo(w.x), p[i]);
+                  p[i] = fmaf(a[1], bf16_hi(w.x), p[i]);
+                  p[i] = fmaf(a[2], bf16_lo(w.y), p[i]);
+                  p[i] = fmaf(a[3], bf16_hi(w.y), p[i]);
+                  p[i] = fmaf(a[4], bf16_lo(w.z), p[i]);
+                  p[i] = fmaf(a[5], bf16_hi(w.z), p[i]);
+                  p[i] = fmaf(a[6], bf16_lo(w.w), p[i]);
+                  p[i] = fmaf(a[7], bf16_hi(w.w), p[i]);
+                }
+              }
             }
-            sm.u.dn.pd[r] = p;
           }
+#pragma unroll
+          for (int i = 0; i < RPT; ++i)
+            if (t + i * kConsumers < S::D) sm.u.dn.pd[t + i * kConsumers] = p[i];
+          if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
           release_n(ring, nch);
         }
         ok = consumer_sync_and<kConsumers>(ok);
