@@ -121,7 +121,9 @@ B2D_API b2d_status b2d_kv_layout(const b2d_config* cfg, b2d_kv_layout_t* out);
 B2D_API b2d_status b2d_model_create(const b2d_config* cfg, const void* weights_dev,
                             uint64_t weights_bytes, int device, b2d_model** out);
 B2D_API b2d_status b2d_model_destroy(b2d_model* m);
-/* Number of CTAs the decode kernel launches (one per SM). */
+/* Number of CTAs the B=1 decode kernel launches: whole clusters of 4 CTAs
+ * that fit co-resident (the cluster kernel), or one per SM (the flat kernel,
+ * used where the cluster grid does not fit). */
 B2D_API int b2d_model_grid(const b2d_model* m);
 
 /* Workspace: inter-CTA exchange words, control words.  Allocated once here;
@@ -316,7 +318,9 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * the batched step's attention fills with global-timer stamps (0 = off);
  * knob 10 = device address of a uint64 buffer [batch][8] of b2d_sample phase
  * stamps (0 = off); knob 11 = b2d_decode_step_paged replays a cached CUDA
- * graph for repeated argument sets (1, default) or launches directly (0).
+ * graph for repeated argument sets (1, default) or launches directly (0);
+ * knob 12 = the B=1 step on the flat kernel (1) or on the cluster kernel
+ * where it fits (0, default).
  * Every b2d_debug_tune call drops the cached graphs' validity.
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);

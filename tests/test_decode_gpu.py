@@ -104,6 +104,59 @@ def test_cfg2_long_context_parity_306m(engine306):
     assert not mism, f"argmax differs at steps {mism}"
 
 
+def test_cluster_kernel_selected(engine306):
+    """On a B200 the B=1 step runs on the cluster kernel: its grid is whole
+    clusters of 4 CTAs that fit co-resident (fewer CTAs than SMs), and the
+    flat kernel (one CTA per SM) is only the fallback."""
+    sms = torch.cuda.get_device_properties(engine306.device).multi_processor_count
+    assert engine306.grid % 4 == 0 and engine306.grid < sms, (engine306.grid, sms)
+
+
+def test_flat_kernel_parity_306m(engine306):
+    """The flat one-CTA-per-SM kernel (used where the cluster grid does not
+    fit) keeps config 1 parity: the same teacher-forced checks, with the flat
+    kernel forced through the diagnostic knob on a second workspace."""
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    eng = DecodeEngine(engine306.w)
+    try:
+        eng.debug_tune(flat=True)
+        errs, mism = _teacher_forced_306(eng, golden("cfg1_greedy.npz"), set())
+        assert not mism, f"argmax differs at steps {mism}"
+    finally:
+        eng.close()
+
+
+def test_flat_and_cluster_kernels_agree(engine306):
+    """Both B=1 kernels decode the same greedy stream from the same cache;
+    their logits differ only by summation order (fixed-point residual sums
+    and split-K projections in the cluster kernel), well inside the oracle
+    tolerance.  Switching kernels on one workspace is allowed (the host
+    clears the cluster kernel's accumulators when it takes over)."""
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    g = golden("cfg1_greedy.npz")
+    eng = DecodeEngine(engine306.w)
+    try:
+        streams, logits = [], []
+        for flat in (False, True, False):
+            eng.debug_tune(flat=flat)
+            kv = eng.new_kv()
+            lg = eng.prefill(g["prompt"], kv)
+            tok = int(torch.argmax(lg).item())
+            toks, lgs = [tok], []
+            for i in range(24):
+                lg_np, tok = _step(eng, tok, len(g["prompt"]) + i, kv)
+                toks.append(tok)
+                lgs.append(lg_np)
+            eng.check_device()
+            streams.append(toks)
+            logits.append(np.stack(lgs))
+        assert streams[0] == streams[1] == streams[2]
+        assert np.array_equal(logits[0], logits[2])  # the cluster kernel is deterministic across a switch
+        assert np.abs(logits[0] - logits[1]).max() < 0.05
+    finally:
+        eng.close()
+
+
 def test_free_run_greedy_prefix(engine306):
     """Free-running greedy decode on the device: report the prefix that matches
     the reference stream (a near-tie can fork it; teacher-forced parity above

@@ -456,7 +456,7 @@ b2d_status b2d_workspace_create(b2d_model* m, int max_batch, b2d_ws** out) {
   ws->n_words = size_t(c.n_layers) * ws->layer_words + c.d_model;
   ws->wait_ns = 2000000000ull;  // 2 s bound on every in-kernel wait
   ws->max_inflight = 4;
-  ws->acc_words = size_t(2) * 2 * c.n_layers * c.d_model;
+  ws->acc_words = size_t(2) * 2 * c.n_layers * c.d_model * b2d::kAccStride;
   cudaError_t e = cudaMalloc(&ws->words, ws->n_words * sizeof(uint64_t));
   if (e == cudaSuccess) e = cudaMalloc(&ws->acc, ws->acc_words * sizeof(uint64_t));
   if (e == cudaSuccess) e = cudaMemset(ws->acc, 0, ws->acc_words * sizeof(uint64_t));
@@ -1199,10 +1199,13 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   const uint32_t w_act = w_hm + uint32_t(cfg->d_model);
   const uint32_t layer_words = (w_act + uint32_t(cfg->d_ff) + 1) & ~1u;
   const size_t n_words = size_t(cfg->n_layers) * layer_words + cfg->d_model;
-  // the cluster kernel's accumulators follow the words
-  const size_t acc_offset = align256(b2d::kStaticWordsOffset + n_words * sizeof(uint64_t));
-  const size_t acc_bytes = size_t(2) * 2 * cfg->n_layers * cfg->d_model * sizeof(uint64_t);
-  if (acc_offset + acc_bytes > b2d::kStaticScratchBytes) return B2D_ERR_SCRATCH_LIMIT;
+  // The flat kernel uses exchange words, the cluster kernel residual
+  // accumulators: whichever runs takes the area after the argmax partials.
+  const size_t words_bytes = n_words * sizeof(uint64_t);
+  const size_t acc_bytes = size_t(2) * 2 * cfg->n_layers * cfg->d_model * b2d::kAccStride * sizeof(uint64_t);
+  // refused before any device work when neither kernel's area fits
+  if (b2d::kStaticWordsOffset + std::min(words_bytes, acc_bytes) > b2d::kStaticScratchBytes)
+    return B2D_ERR_SCRATCH_LIMIT;
   int device = 0;
   B2D_CUDA(cudaGetDevice(&device), "cudaGetDevice");
   if (device < 0 || device >= kMaxDevices) return B2D_ERR_UNSUPPORTED;
@@ -1221,9 +1224,12 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   const int ops_index = ops->d == 1024 ? 0 : 1;
   b2d_status s = static_setup(device, ops, ops_index, &st);
   if (s != B2D_OK) return s;
+  const int c_grid = st->c_grid[ops_index];
+  const size_t used = b2d::kStaticWordsOffset + (c_grid > 0 ? acc_bytes : words_bytes);
+  if (used > b2d::kStaticScratchBytes) return B2D_ERR_SCRATCH_LIMIT;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
   // Everything this call reads before writing starts from zero.
-  B2D_CUDA(cudaMemsetAsync(st->scratch, 0, acc_offset + acc_bytes, cs), "clear static scratch");
+  B2D_CUDA(cudaMemsetAsync(st->scratch, 0, used, cs), "clear static scratch");
   const uint8_t* w = static_cast<const uint8_t*>(weights_dev);
   b2d::DecodeArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -1245,7 +1251,7 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   A.logits = logits_dev;
   A.next_tok = next_tok_dev;
   A.words = reinterpret_cast<uint64_t*>(st->scratch + b2d::kStaticWordsOffset);
-  A.acc = reinterpret_cast<uint64_t*>(st->scratch + acc_offset);
+  A.acc = reinterpret_cast<uint64_t*>(st->scratch + b2d::kStaticWordsOffset);
   A.ctl = reinterpret_cast<b2d::Control*>(st->scratch + b2d::kStaticCtlOffset);
   A.am_val = reinterpret_cast<float*>(st->scratch + b2d::kStaticArgmaxOffset);
   A.am_idx = reinterpret_cast<int32_t*>(st->scratch + b2d::kStaticArgmaxOffset + 4 * b2d::kStaticMaxGrid);
@@ -1257,7 +1263,6 @@ extern "C" b2d_status b2d_decode_step_static(const b2d_config* cfg, const void* 
   A.n_layers = cfg->n_layers;
   A.ctx = cfg->context_len;
   A.att_T = 128 * ((cfg->context_len + 511) / 512);
-  const int c_grid = st->c_grid[ops_index];
   A.grid_part = c_grid > 0 ? c_grid : st->sms;
   A.wait_ns = 2000000000ull;
   A.eps = cfg->rms_eps;

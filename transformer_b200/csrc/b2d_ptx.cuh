@@ -96,6 +96,11 @@ __device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t flag) {
 __device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -152,10 +152,23 @@ __device__ __host__ __forceinline__ int chunk_begin(int c, int G) {
   return static_cast<int>(static_cast<long long>(ShapeC<S>::CHUNKS) * w(c) / w(G));
 }
 
-// Accumulator word of residual element `row` after sublayer `which` (0 = HM_l,
+// Accumulator words of a residual vector after sublayer `which` (0 = HM_l,
 // after attention; 1 = H_{l+1}, after the MLP) of layer l, parity `par`.
+// Element r's word sits at r * kAccStride.  Packed (1) is faster than one
+// word per 32-byte sector (4): measured, the polls of 4x the sectors cost
+// more than the atomic adds gain.
+constexpr int kAccStride = 1;
 __device__ __forceinline__ uint64_t* acc_word(const DecodeArgs& A, uint32_t par, int l, int which, int d) {
-  return A.acc + (static_cast<size_t>(par) * A.n_layers * 2 + static_cast<size_t>(2 * l + which)) * d;
+  return A.acc + (static_cast<size_t>(par) * A.n_layers * 2 + static_cast<size_t>(2 * l + which)) * d * kAccStride;
+}
+// The words of elements 2i and 2i + 1.
+__device__ __forceinline__ void acc_ld2(const uint64_t* v, int i, uint64_t& a, uint64_t& b) {
+  if constexpr (kAccStride == 1) {
+    ld_words2(v + 2 * i, a, b);  // one 16-byte load
+  } else {
+    a = ld_relaxed_u64(v + 2 * i * kAccStride);
+    b = ld_relaxed_u64(v + (2 * i + 1) * kAccStride);
+  }
 }
 
 // Waits until every word of a residual vector (D accumulator words at src)
@@ -175,7 +188,7 @@ __device__ __forceinline__ bool gather_acc(const DecodeArgs& A, const uint64_t* 
     uint64_t a[NP], b[NP];
 #pragma unroll
     for (int i = 0; i < NP; ++i)
-      if (pending & (1u << i)) ld_words2(src + 2 * (t + i * kConsumers), a[i], b[i]);
+      if (pending & (1u << i)) acc_ld2(src, t + i * kConsumers, a[i], b[i]);
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
       if ((pending & (1u << i)) && acc_count(a[i]) == target && acc_count(b[i]) == target) {
@@ -673,7 +686,7 @@ __device__ __forceinline__ bool gemv_x_sw(const DecodeArgs& A, RingC& ring, SM& 
       const int p = k0 / 2 + lane + 32 * j;
       if (pending & (1u << j)) {
         if (words != nullptr) {
-          ld_words2(words + 2 * p, wa[j], wb[j]);
+          acc_ld2(words, p, wa[j], wb[j]);
         } else {  // embedding pair: exact bf16 values, always in the accumulator range
           const uint32_t w2 = __ldg(emb + p);
           int64_t qa = 0, qb = 0;
@@ -920,7 +933,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tok = sm.tok_in;
     }
     if (ok) {  // zero this CTA's share of the other parity's accumulators (the next step's)
-      const size_t n2 = static_cast<size_t>(A.n_layers) * S::D;  // word pairs per parity
+      const size_t n2 = static_cast<size_t>(A.n_layers) * S::D * kAccStride;  // word pairs per parity
       uint4* z = reinterpret_cast<uint4*>(A.acc + static_cast<size_t>(par ^ 1u) * 2 * n2);
       const size_t za = (n2 * cta) / gridDim.x, zb = (n2 * (cta + 1)) / gridDim.x;
       for (size_t i = za + t; i < zb; i += kConsumers) z[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -1015,7 +1028,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = o_phase<S>(A, ring, sm.xb, flag, t0, [&](int r, float v) {
             int64_t q;
             acc_contrib(A, v, keeper ? sm.fix[r] : 0, flag, SITE_HM, q);
-            acc_add(hm + own0 + r, q);
+            acc_add(hm + (own0 + r) * kAccStride, q);
           });
         }
         ok = consumer_sync_and<kConsumers>(ok);
@@ -1099,7 +1112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kCS; ++k) s += sm.u.dn.pr[k][t];
         int64_t q;
         acc_contrib(A, s, keeper ? sm.fix[t] : 0, flag, SITE_H, q);
-        acc_add(hn + own0 + t, q);
+        acc_add(hn + (own0 + t) * kAccStride, q);
       }
       trace_stamp<TR>(A, ts + 9);
       ++xphase;
