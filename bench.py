@@ -95,7 +95,7 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic(name="decode_b1_cfg1.md", key="traffic_bytes_per_launch"):
+def profile_traffic(name, key="traffic_bytes_per_launch"):
     """DRAM bytes (per launch / per step) from a committed ncu summary."""
     p = os.path.join(REPO, "profiles", name)
     if not os.path.exists(p):
@@ -302,7 +302,11 @@ def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
             "us_per_token_one_launch": one_launch,
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
-                         "traffic": profile_traffic()},
+                         "traffic": profile_traffic("decode_b1_cfg1.md"),
+                         "traffic_note": "ncu cannot replay the cooperative cluster launch (LaunchFailed), so "
+                                         "the cluster kernel has no DRAM counters; the flat kernel streaming "
+                                         "the same weights read 1.014x the algorithmic bytes "
+                                         "(profiles/decode_b1_flat_cfg1.md)"},
             "gpu_launches": n_steps}
 
 

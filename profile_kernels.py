@@ -137,6 +137,65 @@ def profile_b1(w, cfg, args, torch):
             "peak_gbs": peak, "peak_source": kind, "first_tokens": tokens[:8]}
 
 
+# Phases of the cluster kernel's per-layer stamps (slot pairs; `head` = only
+# the CTAs of head clusters run the phase).  Slot numbers follow the stamps in
+# csrc/decode_b1c.cuh.
+_B1C_PHASES = [
+    ("H gather + RMSNorm1 + q/k/v GEMV + push", 0, 1, True),
+    ("q/k/v exchange (cluster)", 1, 2, True),
+    ("attention: RoPE", 2, 10, True),
+    ("attention: scores + softmax", 10, 11, True),
+    ("attention: P.V (+ later passes)", 11, 12, True),
+    ("attention: warp merge + K/V append + push", 12, 3, True),
+    ("partial exchange + merge (cluster)", 3, 4, True),
+    ("Wo GEMV + HM adds", 4, 5, True),
+    ("HM gather + RMSNorm2 + gate/up GEMV + SwiGLU", 6, 7, False),
+    ("Wd partial + push", 7, 8, False),
+    ("cluster reduce + H adds", 8, 9, False),
+]
+
+
+def profile_b1_trace(w, cfg, args, torch):
+    """Per-phase timing of the B=1 step from the kernel's global-timer stamps
+    (b2d_debug_trace): per layer (layers 2..L-2), per phase, the critical
+    increment (latest CTA at the phase end minus latest at its start) and
+    the mean per-CTA duration; the stamped kernel is ~8% slower than the
+    plain one."""
+    from transformer_b200.multi_sm_decode import DecodeEngine, _ptr
+    from transformer_b200.synth import prompt_cfg1
+    eng = DecodeEngine(w)
+    kv = eng.new_kv()
+    eng.prefill(prompt_cfg1(cfg), kv)
+    tok = torch.tensor([5], dtype=torch.int32, device=eng.device)
+    pos = torch.tensor([args.pos], dtype=torch.int32, device=eng.device)
+    for _ in range(3):
+        eng.step(tok, pos, kv, eng.logits, eng.next_tok)
+    per, nl = 13, cfg.n_layers
+    stride = eng.trace_slots()
+    buf = torch.zeros(eng.grid, stride, dtype=torch.int64, device=eng.device)
+    eng.lib.b2d_debug_trace(eng.ws, _ptr(buf), stride)
+    eng.step(tok, pos, kv, eng.logits, eng.next_tok)
+    torch.cuda.synchronize()
+    eng.lib.b2d_debug_trace(eng.ws, None, 0)
+    eng.check_device()
+    t = buf.cpu().numpy().astype(np.int64)
+    nh = 4 * cfg.n_heads
+    layers = range(2, nl - 1)
+    phases = {}
+    for name, a, b, head in _B1C_PHASES:
+        rows = slice(0, nh) if head else slice(None)
+        crit = np.mean([(t[rows, 1 + l * per + b].max() - t[rows, 1 + l * per + a].max()) / 1e3 for l in layers])
+        mean = np.mean([np.mean(t[rows, 1 + l * per + b] - t[rows, 1 + l * per + a]) / 1e3 for l in layers])
+        phases[name] = {"crit_us": round(float(crit), 2), "mean_us": round(float(mean), 2)}
+    tf = 1 + nl * per
+    layer = np.mean([(t[:, 1 + l * per + 9].max() - t[:, 1 + (l - 1) * per + 9].max()) / 1e3 for l in layers])
+    return {"mode": "b1-trace", "pos": args.pos, "grid": eng.grid, "layer_us": round(float(layer), 2),
+            "phases": phases,
+            "final_gather_norm_us": round(float((t[:, tf].max() - t[:, 1 + (nl - 1) * per + 9].max()) / 1e3), 2),
+            "logits_argmax_us": round(float((t[:, tf + 1].max() - t[:, tf].max()) / 1e3), 2),
+            "step_us_stamped": round(float((t[:, tf + 2].max() - t[:, 0].min()) / 1e3), 1)}
+
+
 def profile_paged(w, cfg, args, torch):
     from transformer_b200.batched import BatchedDecoder
     from transformer_b200.multi_sm_decode import DecodeEngine
@@ -265,7 +324,7 @@ def profile_serve(w, cfg, args, torch):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["b1", "paged", "serve", "mixed"], default="b1")
+    ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "serve", "mixed"], default="b1")
     ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--att-splits", type=int, default=0, help="--mode paged: force 1, 2 or 4 attention units")
     ap.add_argument("--requests", type=int, default=1024)
@@ -301,7 +360,8 @@ def main():
         params = synth_params(cfg, 0)
     w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
     out = {"memory": compute_memory_stats(cfg)}
-    prof = {"b1": profile_b1, "paged": profile_paged, "serve": profile_serve, "mixed": profile_mixed}[args.mode]
+    prof = {"b1": profile_b1, "b1-trace": profile_b1_trace, "paged": profile_paged, "serve": profile_serve,
+            "mixed": profile_mixed}[args.mode]
     out.update(prof(w, cfg, args, torch))
     print(json.dumps(out))
     return 0

@@ -30,12 +30,14 @@ def _p(t):
 
 
 def test_static_step_rejects_models_beyond_its_fixed_scratch():
-    """A model whose exchange area exceeds the fixed array is refused with
-    B2D_ERR_SCRATCH_LIMIT before any device work (no GPU needed)."""
+    """A model whose scratch exceeds the fixed array for either B=1 kernel
+    (the flat kernel's exchange words, the cluster kernel's residual
+    accumulators) is refused with B2D_ERR_SCRATCH_LIMIT before any device
+    work (no GPU needed)."""
     from transformer_b200 import build
     build.build()
     lib = _lib.load()
-    big = _lib.make_config(ModelConfig(n_layers=64))  # ~5.4 MB of exchange words
+    big = _lib.make_config(ModelConfig(n_layers=160))  # ~13.6 MB of exchange words, 5.2 MB of accumulators
     fake = ctypes.c_void_p(0x100000)  # never dereferenced: rejected first
     st = lib.b2d_decode_step_static(ctypes.byref(big), fake, ctypes.c_uint64(1 << 40), fake, fake, fake, None,
                                     fake, None)
