@@ -442,10 +442,10 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, floa
 }
 
 // Same streaming for many units per warp (the logits): reduce per stage.
-template <int KI, int PITCH, int PS, class R, class Out>
+template <int KI, int PITCH, int PS, class R, int GROUP = R::kN / 2, class Out>
 __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, R& ring, uint32_t flag, uint64_t t0,
                                                 int u_begin, int u_end, const XSmem x, Out out) {
-  constexpr int kGroupStages = R::kN / 2;  // stages waited for together
+  constexpr int kGroupStages = GROUP;  // stages waited for (and released) together
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   bool ok = true;
   for (int g0 = u_begin; g0 < u_end && ok; g0 += kGroupStages * PS) {

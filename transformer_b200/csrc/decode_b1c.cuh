@@ -1137,7 +1137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const XSmem x{reinterpret_cast<const uint4*>(sm.xb)};
       float best_v = -INFINITY;
       int best_i = 0x7fffffff;
-      ok = gemv_phase_wide<S::KD, S::ROWB_D, S::RPS_D>(A, ring, flag, t0, v0, v1, x, [&](int u, float v, float) {
+      // released two stages at a time, so up to 10 of the 12 slots can be in flight
+      ok = gemv_phase_wide<S::KD, S::ROWB_D, S::RPS_D, RingC, 2>(A, ring, flag, t0, v0, v1, x, [&](int u, float v, float) {
         if (lane == 0 && A.logits) A.logits[u] = v;
         if (v > best_v) {
           best_v = v;
