@@ -40,7 +40,7 @@
 
 namespace b2d {
 
-constexpr int kPaStages = 6;    // pages in each warp's ring (consumed two at a time)
+constexpr int kPaStages = 4;    // pages in each warp's ring (consumed two at a time)
 constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
 constexpr int kPaMaxSplits = 4; // units per (row, kv head)

@@ -47,11 +47,13 @@ namespace b2d {
 
 constexpr int kCS = 4;            // CTAs per cluster
 constexpr int kMinGridC = 120;    // fewest CTAs the per-CTA budgets assume
-// Act chunks are split over the CTAs in proportion to a weight: 1 for a CTA
-// of a head cluster (which also streams 48 q/k/v rows and a Wo block per
-// layer), kChunkWeight for the others, so that every CTA streams about the
-// same bytes per layer.
-constexpr int kChunkWeight = 3;
+// Act chunks are split over the CTAs in proportion to a weight:
+// kChunkWeightHead for a CTA of a head cluster (which also streams 48 q/k/v
+// rows and a Wo block per layer), kChunkWeightOther for the others.  Measured
+// at 132 CTAs: 1 : 3 (head CTAs 1-2 chunks, others 3-4) 266 us/token; 4 : 5
+// (at most 3 chunks everywhere) 316 us: a head CTA with 3 chunks no longer
+// fits its layer in the weight ring and waits for its down stages.
+constexpr int kChunkWeightHead = 1, kChunkWeightOther = 3;
 constexpr int kMaxChunksC = 4;    // act chunks per CTA at most (the host checks its grid against it)
 // Weight ring: every stage is one 16 KB tensor copy, so 12 of them fit.
 constexpr int kStagesC = 12;
@@ -148,7 +150,10 @@ struct SmemCChecks {
 template <class S>
 __device__ __host__ __forceinline__ int chunk_begin(int c, int G) {
   const int nh = S::NH * kCS;
-  const auto w = [nh](int x) { return static_cast<long long>(x <= nh ? x : nh + kChunkWeight * (x - nh)); };
+  const auto w = [nh](int x) {
+    return static_cast<long long>(x <= nh ? kChunkWeightHead * x
+                                          : kChunkWeightHead * nh + kChunkWeightOther * (x - nh));
+  };
   return static_cast<int>(static_cast<long long>(ShapeC<S>::CHUNKS) * w(c) / w(G));
 }
 
