@@ -155,6 +155,46 @@ def test_paged_306m_96_row_tiles(engine306_batched, params306_f32, B):
     eng.check_device()
 
 
+def test_paged_306m_640_rows_shallow_rings(engine306, params306_f32):
+    """640 sequences (2560 attention units, far more than the warps that fit
+    at once): the attention runs with shallower page rings.  Three positions;
+    four rows against the oracle, all rows finite.  Each row owns one block
+    (positions < 16 read only page 0)."""
+    from transformer_b200.config import CONFIG_306M as cfg
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    B, T = 640, 3
+    eng = DecodeEngine(engine306.w, max_batch=B)
+    try:
+        dev = eng.device
+        rng = np.random.default_rng(640)
+        table = np.zeros((B, cfg.context_len // PAGE_TOKENS), np.int32)
+        table[:, 0] = rng.permutation(B).astype(np.int32)
+        pool = eng.new_kv_pool(B)
+        table_d = torch.from_numpy(table).to(dev)
+        toks = rng.integers(0, cfg.vocab_size, (T, B)).astype(np.int32)
+        checked = [0, 97, 333, B - 1]
+        decs = {b: CachedDecoder(params306_f32, cfg, 1) for b in checked}
+        tok = torch.zeros(B, dtype=torch.int32, device=dev)
+        pos = torch.zeros(B, dtype=torch.int32, device=dev)
+        logits = torch.zeros(B, cfg.vocab_size, dtype=torch.float32, device=dev)
+        nxt = torch.zeros(B, dtype=torch.int32, device=dev)
+        for t in range(T):
+            tok.copy_(torch.from_numpy(toks[t].copy()))
+            pos.fill_(t)
+            eng.step_paged(tok, pos, pool, table_d, logits, nxt)
+            got, am = logits.cpu().numpy(), nxt.cpu().numpy()
+            assert np.isfinite(got).all()
+            for b in checked:
+                ref = decs[b].step([toks[t, b]], [t])[0]
+                assert_logits_close(got[b], ref, f"row {b} pos {t}")
+                i, _, margin = top2(ref)
+                if margin > MARGIN:
+                    assert am[b] == i
+        eng.check_device()
+    finally:
+        eng.close()
+
+
 def test_paged_306m_long_context(engine306_batched, params306_f32):
     """306M, positions near the end of the 512 context (config 2's length):
     ingested without checks, then the last 8 positions compared."""

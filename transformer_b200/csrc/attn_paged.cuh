@@ -40,7 +40,8 @@
 
 namespace b2d {
 
-constexpr int kPaStages = 4;    // pages in each warp's ring (consumed two at a time)
+constexpr int kPaStages = 6;    // pages in each warp's ring (consumed two at a time)
+constexpr int kPaStagesShallow = 4;  // the ring when units far outnumber warp slots (more warps per SM)
 constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
 constexpr int kPaMaxSplits = 4; // units per (row, kv head)
@@ -54,9 +55,16 @@ constexpr uint64_t kPaWaitNs = 200000000ull;                          // bound o
 static_assert(kPaStages * kPaPageBytes + 256 + 8 * kPaStages <= kPaWarpSmemTma, "TMA ring layout");
 static_assert(kPaWarpSmemTma % 1024 == 0, "every warp's ring starts 1024-byte aligned");
 // Dynamic shared memory of a CTA of W warps.
-constexpr __host__ __device__ int pa_smem_bytes(int w, bool tma) {
-  return tma ? w * kPaWarpSmemTma + 1024 : w * kPaWarpSmem;
+// Bytes per warp for a ring of `stages` pages.
+constexpr __host__ __device__ int pa_warp_smem(bool tma, int stages) {
+  return tma ? stages * kPaPageBytes + 1024 : stages * kPaStageElems * 2 + 256;
 }
+constexpr __host__ __device__ int pa_smem_bytes(int w, bool tma, int stages = kPaStages) {
+  return tma ? w * pa_warp_smem(true, stages) + 1024 : w * pa_warp_smem(false, stages);
+}
+static_assert(pa_warp_smem(true, kPaStages) == kPaWarpSmemTma && pa_warp_smem(false, kPaStages) == kPaWarpSmem,
+              "ring sizes");
+static_assert(pa_warp_smem(true, kPaStagesShallow) % 1024 == 0, "every warp's ring starts 1024-byte aligned");
 // Byte offset of 16-byte chunk c of row r inside a swizzled 16-row tile.
 __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
@@ -90,11 +98,11 @@ __device__ __forceinline__ const __nv_bfloat16* page_rows(const PagedAttnArgs& a
 // (b * n_kv + g) * splits + x.  TMA = true needs a paged pool (a.table) and
 // kvmap: the pool as rows of 64 bf16 (128 B), boxes of 16 rows, 128-byte
 // swizzle; otherwise kvmap is unused and pages arrive by per-lane cp.async.
-template <int W, bool TMA>
+template <int W, bool TMA, int STAGES = kPaStages>
 __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_constant__ CUtensorMap kvmap,
                                                                 const __grid_constant__ PagedAttnArgs a, int n_rows) {
   extern __shared__ __align__(16) uint8_t pa_smem_raw[];
-  constexpr int WS = TMA ? kPaWarpSmemTma : kPaWarpSmem;  // bytes per warp
+  constexpr int WS = pa_warp_smem(TMA, STAGES);  // bytes per warp
   uint8_t* pa_smem = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pa_smem_raw) + 1023) & ~uintptr_t(1023))
                          : pa_smem_raw;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,12 +120,12 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   stamp(0);
   __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * WS);
   // the new position's K / V (bf16, as cached) after the ring
-  __nv_bfloat16* skn = TMA ? reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * WS + kPaStages * kPaPageBytes)
-                           : ring + kPaStages * kPaStageElems;
+  __nv_bfloat16* skn = TMA ? reinterpret_cast<__nv_bfloat16*>(pa_smem + warp * WS + STAGES * kPaPageBytes)
+                           : ring + STAGES * kPaStageElems;
   __nv_bfloat16* svn = skn + 64;
   uint64_t* pbar = reinterpret_cast<uint64_t*>(skn + 128);  // TMA: one mbarrier per ring slot
   if (TMA && lane == 0) {
-    for (int i = 0; i < kPaStages; ++i) mbar_init(&pbar[i], 1);
+    for (int i = 0; i < STAGES; ++i) mbar_init(&pbar[i], 1);
     fence_mbar_init();
     tma_prefetch_desc(&kvmap);
   }
@@ -167,7 +175,7 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     const int blk = tb == nullptr ? 0 : pg < 32 ? __shfl_sync(0xffffffffu, tbl, pg) : tb[pg];
     if constexpr (TMA) {
       if (lane == 0) {
-        const int slot = k % kPaStages;
+        const int slot = k % STAGES;
         uint8_t* dst = reinterpret_cast<uint8_t*>(ring) + slot * kPaPageBytes;
         const int rk = (((a.layer * a.num_blocks + blk) * 2) * a.n_kv + g) * kPageTokens;  // K rows (host checks the range)
         mbar_arrive_expect_tx(&pbar[slot], kPaPageBytes);
@@ -178,7 +186,7 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     }
     const __nv_bfloat16* ks = page_rows(a, blk, pg, 0, g);
     const __nv_bfloat16* vs = page_rows(a, blk, pg, 1, g);
-    const uint32_t dst = smem_addr(ring + (k % kPaStages) * kPaStageElems);
+    const uint32_t dst = smem_addr(ring + (k % STAGES) * kPaStageElems);
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int i = lane + 32 * r, row = i >> 3, c16 = i & 7;
@@ -189,7 +197,7 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     }
   };
 #pragma unroll
-  for (int k = 0; k < kPaStages; ++k) {
+  for (int k = 0; k < STAGES; ++k) {
     if (k < nw) issue(k);
     if (!TMA) cp_async_commit();
   }
@@ -197,8 +205,8 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   // the page's data are not used for anything that is written out)
   bool tma_ok = true;
   auto wait_page = [&](int k) {
-    const uint32_t par = static_cast<uint32_t>(k / kPaStages) & 1u;
-    uint64_t* bar = &pbar[k % kPaStages];
+    const uint32_t par = static_cast<uint32_t>(k / STAGES) & 1u;
+    uint64_t* bar = &pbar[k % STAGES];
     if (mbar_test(bar, par)) return;
     const uint64_t t0 = globaltimer_ns();
     uint32_t n = 0;
@@ -292,20 +300,20 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   const bool head = gid < GQA;
   // ldmatrix lane addressing: matrix mi = lane / 8, row lane % 8
   const int mi = lane >> 3, mr = lane & 7;
-  static_assert(kPaStages % 2 == 0, "pages are consumed in pairs");
+  static_assert(STAGES % 2 == 0, "pages are consumed in pairs");
 #pragma unroll 1
   for (int k = 0; k < nw; k += 2) {  // pages k, k + 1 (when present) as one block of 32 positions
     const int pg = pg_lo + k;
     const bool two = k + 1 < nw;
-    __nv_bfloat16* st0 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + (k % kPaStages) * kPaPageBytes)
-                             : ring + (k % kPaStages) * kPaStageElems;
-    __nv_bfloat16* st1 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + ((k + 1) % kPaStages) * kPaPageBytes)
-                             : ring + ((k + 1) % kPaStages) * kPaStageElems;
+    __nv_bfloat16* st0 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + (k % STAGES) * kPaPageBytes)
+                             : ring + (k % STAGES) * kPaStageElems;
+    __nv_bfloat16* st1 = TMA ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ring) + ((k + 1) % STAGES) * kPaPageBytes)
+                             : ring + ((k + 1) % STAGES) * kPaStageElems;
     if constexpr (TMA) {
       wait_page(k);
       if (two) wait_page(k + 1);
     } else {
-      cp_async_wait<kPaStages - 2>();
+      cp_async_wait<STAGES - 2>();
     }
     __syncwarp();
     if (pg == npg - 1 || (two && pg + 1 == npg - 1)) {  // the page of position p: its row from the new
@@ -400,9 +408,9 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
       }
     }
     __syncwarp();  // every lane's reads of these stages are done before they are refilled
-    if (k + kPaStages < nw) issue(k + kPaStages);
+    if (k + STAGES < nw) issue(k + STAGES);
     if (!TMA) cp_async_commit();
-    if (k + 1 + kPaStages < nw) issue(k + 1 + kPaStages);
+    if (k + 1 + STAGES < nw) issue(k + 1 + STAGES);
     if (!TMA) cp_async_commit();
     if (k == 0) stamp(4);
   }
@@ -411,7 +419,7 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
     // a page wait ran out (status word set; this row's output is not meaningful):
     // wait once more, bounded, for every slot's last copy so none is in flight at
     // exit; the warp goes on to the row's barrier like the others
-    for (int k = max(0, nw - kPaStages); k < nw; ++k) wait_page(k);
+    for (int k = max(0, nw - STAGES); k < nw; ++k) wait_page(k);
   }
   stamp(5);
   l += __shfl_xor_sync(0xffffffffu, l, 1);
