@@ -42,6 +42,7 @@ namespace b2d {
 
 constexpr int kPaStages = 6;    // pages in each warp's ring (consumed two at a time)
 constexpr int kPaStagesShallow = 4;  // the ring when units far outnumber warp slots (more warps per SM)
+constexpr int kPaStagesSplit = 2;    // the ring of rows split in two so that their units fit one wave
 constexpr int kPaPitch = 72;    // bf16 per staged row: 144 B
 constexpr int kPaStageElems = 2 * kPageTokens * kPaPitch;  // K rows then V rows
 constexpr int kPaMaxSplits = 4; // units per (row, kv head)
@@ -64,7 +65,8 @@ constexpr __host__ __device__ int pa_smem_bytes(int w, bool tma, int stages = kP
 }
 static_assert(pa_warp_smem(true, kPaStages) == kPaWarpSmemTma && pa_warp_smem(false, kPaStages) == kPaWarpSmem,
               "ring sizes");
-static_assert(pa_warp_smem(true, kPaStagesShallow) % 1024 == 0, "every warp's ring starts 1024-byte aligned");
+static_assert(pa_warp_smem(true, kPaStagesShallow) % 1024 == 0 && pa_warp_smem(true, kPaStagesSplit) % 1024 == 0,
+              "every warp's ring starts 1024-byte aligned");
 // Byte offset of 16-byte chunk c of row r inside a swizzled 16-row tile.
 __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));

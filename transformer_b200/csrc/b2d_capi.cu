@@ -320,7 +320,9 @@ cudaError_t attn_smem_attrs() {
       {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<2, true>), b2d::pa_smem_bytes(2, true)},
       {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<4, true>), b2d::pa_smem_bytes(4, true)},
       {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<2, true, b2d::kPaStagesShallow>),
-       b2d::pa_smem_bytes(2, true, b2d::kPaStagesShallow)}};
+       b2d::pa_smem_bytes(2, true, b2d::kPaStagesShallow)},
+      {reinterpret_cast<const void*>(&b2d::paged_attn_mma_kernel<2, true, b2d::kPaStagesSplit>),
+       b2d::pa_smem_bytes(2, true, b2d::kPaStagesSplit)}};
   for (const auto& k : ks)
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k.first, cudaFuncAttributeMaxDynamicSharedMemorySize, k.second);
   if (e == cudaSuccess) raised[dev] = true;
@@ -846,14 +848,6 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
   pa.rcos = reinterpret_cast<const float*>(m->w + m->lay.off_cos);
   pa.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   pa.out = ws->A; pa.ldo = D; pa.status = status;
-  {  // units (warps) per (row, kv head): split rows only while the pairs alone leave SMs idle
-    const int pairs = batch * c.n_kv_heads, target = 10 * m->grid;
-    int sp = ws->force_att_cpc ? ws->force_att_cpc : std::max(1, target / pairs);
-    sp = std::min(sp, std::min(b2d::kPaMaxSplits, (c.context_len + 15) / 16));
-    pa.cpc = sp >= 4 ? 4 : sp >= 2 ? 2 : 1;  // a row's units share one CTA of pa_warps(splits) warps
-  }
-  const int att_w = b2d::pa_warps(pa.cpc);
-  B2D_CUDA(attn_smem_attrs(), "attention attributes");
   // Paged pool: pages arrive as TMA tensor copies (two 2 KB boxes per page)
   // when the pool's rows of 64 bf16 are addressable with 32-bit coordinates.
   CUtensorMap kvmap{};
@@ -867,16 +861,39 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     }
     kvmap = ws->kvmap;
   }
-  const int att_units = batch * c.n_kv_heads * pa.cpc;
-  // Units far beyond the warps that fit at once (a one-wave batch of 2048):
-  // shallower page rings let more warps share an SM (measured: one wave of
-  // 2048 457k -> 490k tok/s; waves of 256 are faster with the deeper ring).
-  const bool att_shallow = att_tma && att_w == 2 && att_units > 16 * m->grid;
-  auto* att_k2 = att_tma ? (att_shallow ? b2d::paged_attn_mma_kernel<2, true, b2d::kPaStagesShallow>
-                                        : b2d::paged_attn_mma_kernel<2, true>)
-                         : b2d::paged_attn_mma_kernel<2, false>;
+  // Units (warps) per (row, kv head) and each unit's page ring (measured at
+  // B=256 / 2048, TMA pages):
+  //  * rows split while the (row, kv head) pairs alone leave SMs idle, with
+  //    6-page rings (8 warps per SM);
+  //  * rows left whole by that rule whose split units fit one wave only with
+  //    2-page rings (22 warps per SM): split in two with 2-page rings (B=256:
+  //    1170 -> 1155 us per step at position 190, 1282 -> 1262 at 300);
+  //  * units far beyond the warp slots (a one-wave batch of 2048): 4-page
+  //    rings (457k -> 487k tok/s; 6-page rings are faster for waves of 256).
+  const int pairs = batch * c.n_kv_heads;
+  int att_stages = b2d::kPaStages;
+  {
+    const int target = 10 * m->grid;
+    int sp = ws->force_att_cpc ? ws->force_att_cpc : std::max(1, target / pairs);
+    sp = std::min(sp, std::min(b2d::kPaMaxSplits, (c.context_len + 15) / 16));
+    pa.cpc = sp >= 4 ? 4 : sp >= 2 ? 2 : 1;  // a row's units share one CTA of pa_warps(splits) warps
+    if (att_tma && pa.cpc == 1 && !ws->force_att_cpc && 2 * pairs > 8 * m->grid && 2 * pairs <= 22 * m->grid &&
+        c.context_len >= 2 * b2d::kPageTokens) {
+      pa.cpc = 2;
+      att_stages = b2d::kPaStagesSplit;
+    } else if (att_tma && pa.cpc == 1 && pairs > 16 * m->grid) {
+      att_stages = b2d::kPaStagesShallow;
+    }
+  }
+  const int att_w = b2d::pa_warps(pa.cpc);
+  B2D_CUDA(attn_smem_attrs(), "attention attributes");
+  const int att_units = pairs * pa.cpc;
+  auto* att_k2 = !att_tma ? b2d::paged_attn_mma_kernel<2, false>
+                 : att_stages == b2d::kPaStagesSplit ? b2d::paged_attn_mma_kernel<2, true, b2d::kPaStagesSplit>
+                 : att_stages == b2d::kPaStagesShallow ? b2d::paged_attn_mma_kernel<2, true, b2d::kPaStagesShallow>
+                                                      : b2d::paged_attn_mma_kernel<2, true>;
   auto* att_k4 = att_tma ? b2d::paged_attn_mma_kernel<4, true> : b2d::paged_attn_mma_kernel<4, false>;
-  const int att_smem2 = att_shallow ? b2d::pa_smem_bytes(2, true, b2d::kPaStagesShallow) : b2d::pa_smem_bytes(2, att_tma);
+  const int att_smem2 = b2d::pa_smem_bytes(2, att_tma, att_stages);
   // RMSNorm of the residual stream, folded: each residual projection writes
   // X = bf16(h * g_next) and per-tile sums of squares; the next projection
   // (qkv, gate/up, logits) scales its result columns by rsqrt(mean + eps).
