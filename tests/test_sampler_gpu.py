@@ -187,3 +187,45 @@ def test_topp_cutoff_equals_numpy_cumsum(engine306, scale, ties):
             assert got == want, (case, top_p, got, want)
     finally:
         engine306.debug_tune(sample_trace=torch.zeros(0, dtype=torch.int64))
+
+
+@pytest.mark.parametrize("vocab", [32000, 32768, 5000, 4097, 100])
+def test_cluster_and_one_cta_samplers_agree(engine306, vocab):
+    """Top-p draws run on a cluster of 8 CTAs per sequence where the batch
+    fits one wave of clusters (the default), or on one CTA per sequence
+    (knob 13).  Both return the same tokens and the same top-p cutoff counts,
+    and the tokens equal the CPU restatement's.  The vocabularies leave
+    cluster CTAs full, partly filled and empty (a CTA holds 4096 ids)."""
+    rng = np.random.default_rng(vocab)
+    B = 4
+    dev = engine306.device
+    smp = Sampler(engine306, B, 64)
+    buf = torch.zeros(B, 8, dtype=torch.int64, device=dev)
+    engine306.debug_tune(sample_trace=buf)
+    try:
+        for case in range(6):
+            temp, top_p, rp = [(0.7, 0.95, 1.2), (1.0, 0.5, 1.0), (1.3, 0.999, 1.1)][case % 3]
+            logits = (rng.standard_normal((B, vocab)) * [0.64, 3.0, 0.05][case % 3]).astype(np.float32)
+            if case % 2:  # exactly equal probabilities
+                logits = (np.round(logits * 4) / 4).astype(np.float32)
+            hists = [rng.integers(0, vocab, int(rng.integers(0, 40))).astype(np.int32) for _ in range(B)]
+            us = rng.random(B)
+            smp.hist_len.zero_()
+            for b in range(B):
+                smp.history[b, :len(hists[b])].copy_(torch.as_tensor(hists[b]))
+                smp.hist_len[b] = len(hists[b])
+            smp.uniforms[:B].copy_(torch.as_tensor(us))
+            lg = torch.from_numpy(logits).to(dev)
+            runs = {}
+            for single in (False, True):
+                engine306.debug_tune(sample_single=single)
+                buf.zero_()
+                tok = smp.sample(lg, temp, top_p, rp, B).cpu().numpy().copy()
+                runs[single] = (tok, buf[:, 6].cpu().numpy() & 0xffffffff)
+            assert (runs[False][0] == runs[True][0]).all(), (case, runs)
+            assert (runs[False][1] == runs[True][1]).all(), (case, runs)
+            for b in range(B):
+                want = OS.sample_token(logits[b], temp, top_p, rp, list(hists[b]), us[b])
+                assert runs[False][0][b] == want or _boundary(logits[b], temp, top_p, rp, list(hists[b]), us[b])
+    finally:
+        engine306.debug_tune(sample_single=False, sample_trace=torch.zeros(0, dtype=torch.int64))

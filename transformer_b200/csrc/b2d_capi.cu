@@ -253,6 +253,7 @@ struct b2d_ws {
   uint64_t* sample_trace;  // diagnostics: sampler phase stamps [batch][8], or null
   uint64_t* sample_scratch;  // top-p sort buffer [sample_rows][kSamplerMaxVocab]
   int sample_rows;
+  bool sample_single;      // diagnostics: top-p draws on one CTA per sequence even where clusters fit
   int stage_stride;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[6], amap[6], actmap[6];  // box rows 16 / 32 / 64 / 96 / 128 / 256 (bn_index)
@@ -619,6 +620,10 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 10:  // sampler: phase stamp buffer (device address; 0 = off)
       ws->sample_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
       return B2D_OK;
+    case 13:  // sampler: top-p draws on one CTA per sequence (1) or on clusters where they fit (0, default)
+      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
+      ws->sample_single = value == 1;
+      return B2D_OK;
 
   }
   return B2D_ERR_INVALID_ARG;
@@ -742,7 +747,7 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
   }
   B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
                                params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st,
-                               ws->sample_scratch, ws->sample_trace),
+                               ws->sample_scratch, ws->sample_trace, !ws->sample_single),
            "sampler launch");
   return B2D_OK;
 }

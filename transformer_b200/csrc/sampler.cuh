@@ -1,4 +1,5 @@
-// sampler.cuh — device sampler, one CTA per sequence (sm_100a).
+// sampler.cuh — device sampler: one CTA per sequence, or for top-p draws a
+// cluster of 8 CTAs per sequence while the batch fits one wave (sm_100a).
 //
 // Replaces the reference's host numpy sampler, generate.py:28-65 sample_token:
 // repetition penalty over the set of generated tokens, temperature, softmax,
@@ -30,12 +31,18 @@
 #include <cstdint>
 
 #include "b2d_ptx.cuh"
+#include "tc_ptx.cuh"
 
 namespace b2d {
 
 constexpr int kSamplerMaxVocab = 32768;
 constexpr int kSamplerThreads = 1024;
 constexpr int kTreeNodes = 1024;  // heap-indexed pairwise-sum tree (depth <= 9)
+// Cluster sampler: one cluster of kSampleCluster CTAs per sequence, CTA r
+// holding sort positions [r * kSliceElems, (r + 1) * kSliceElems).
+constexpr int kSampleCluster = 8;
+constexpr int kSliceElems = kSamplerMaxVocab / kSampleCluster;
+static_assert(kSliceElems == 4 * kSamplerThreads, "four positions per thread");
 
 struct SampleArgs {
   const float* logits;     // [batch][vocab]
@@ -71,23 +78,29 @@ struct SamplerSmem {
   long long scan64[kSamplerThreads / 32];
   int rs_cnt[kSamplerThreads / 32][16];  // radix sort: digit counts / running offsets per warp
   int rs_off[kSamplerThreads / 32][16];
+  // cluster sampler: values every CTA of the cluster pushes into every CTA
+  // (slot = the pushing CTA's rank)
+  float cl_max[kSampleCluster];
+  uint32_t cl_and[kSampleCluster], cl_or[kSampleCluster];
+  int cl_cnt[kSampleCluster][16];
+  uint32_t red_and[kSamplerThreads / 32], red_or[kSamplerThreads / 32];
 };
 
 __device__ __forceinline__ float key_to_p(uint32_t k) { return __uint_as_float(~k); }
 
-// numpy's pairwise float32 sum of get(0..n-1), evaluated level by level over
-// a heap-indexed tree of its recursion; returns 0 + sum like np.sum.  All
-// threads of the block must call it.
-template <class Get>
-__device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
+// numpy's pairwise float32 sum, evaluated as a heap-indexed tree of its
+// recursion: every node longer than 128 splits at n2 = n/2 rounded down to a
+// multiple of 8; a leaf (<= 128) is numpy's 8-accumulator block sum.
+// tree_split builds the nodes of the range [0, n) (all threads of the block).
+__device__ void tree_split(SamplerSmem& sm, int n) {
   const int t = threadIdx.x;
+  for (int i = t; i < kTreeNodes; i += blockDim.x) sm.node_len[i] = -1;
+  __syncthreads();
   if (t == 0) {
-    for (int i = 0; i < kTreeNodes; ++i) sm.node_len[i] = -1;
     sm.node_start[1] = 0;
     sm.node_len[1] = n;
   }
   __syncthreads();
-  // top-down: split every node longer than 128 (n2 = n/2 rounded down to 8)
   for (int d = 0; d < 9; ++d) {
     const int first = 1 << d, count = 1 << d;
     for (int i = t; i < count; i += blockDim.x) {
@@ -104,32 +117,33 @@ __device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
     }
     __syncthreads();
   }
-  // leaves (len <= 128): numpy's 8-accumulator block sum
-  for (int nd = 1 + t; nd < kTreeNodes; nd += blockDim.x) {
-    const int len = sm.node_len[nd];
-    if (len < 0 || len > 128) continue;
-    const int s0 = sm.node_start[nd];
-    float res;
-    if (len < 8) {
-      res = 0.f;
-      for (int i = 0; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
-    } else {
-      float r[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) r[j] = get(s0 + j);
-      int i = 8;
-      for (; i < len - (len % 8); i += 8) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], get(s0 + i + j));
-      }
-      res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                      __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
-      for (; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
-    }
-    sm.node_val[nd] = res;
+}
+
+// numpy's block sum of get(s0 .. s0 + len - 1), len <= 128.
+template <class Get>
+__device__ float leaf_sum(int s0, int len, Get get) {
+  if (len < 8) {
+    float res = 0.f;
+    for (int i = 0; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+    return res;
   }
-  __syncthreads();
-  // bottom-up: internal node = left + right
+  float r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r[j] = get(s0 + j);
+  int i = 8;
+  for (; i < len - (len % 8); i += 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], get(s0 + i + j));
+  }
+  float res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                        __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+  for (; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+  return res;
+}
+
+// Bottom-up: internal node = left + right; returns 0 + root like np.sum.
+__device__ float tree_combine(SamplerSmem& sm) {
+  const int t = threadIdx.x;
   for (int d = 8; d >= 0; --d) {
     const int first = 1 << d, count = 1 << d;
     for (int i = t; i < count; i += blockDim.x) {
@@ -142,6 +156,17 @@ __device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
   const float total = __fadd_rn(0.f, sm.node_val[1]);
   __syncthreads();
   return total;
+}
+
+// numpy's pairwise float32 sum of get(0..n-1) (n <= 2^16, so the tree's leaves
+// are at most 128 long); all threads of the block must call it.
+template <class Get>
+__device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
+  tree_split(sm, n);
+  for (int nd = 1 + threadIdx.x; nd < kTreeNodes; nd += blockDim.x)
+    if (sm.node_len[nd] >= 0 && sm.node_len[nd] <= 128) sm.node_val[nd] = leaf_sum(sm.node_start[nd], sm.node_len[nd], get);
+  __syncthreads();
+  return tree_combine(sm);
 }
 
 // Block-wide float64 prefix sums of get(0..n-1) (thread-contiguous chunks);
@@ -175,11 +200,20 @@ __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   }
   __syncthreads();
   const double total = sm.red_d[kWarps - 1];
-  double run = (warp > 0 ? sm.red_d[warp - 1] : 0.0) + (incl - local);
+  const double run0 = (warp > 0 ? sm.red_d[warp - 1] : 0.0) + (incl - local);
+  // The running sums never decrease and a correctly rounded division is
+  // monotone in its dividend, so only the chunk whose end already exceeds u
+  // can hold the first crossing: one division per chunk, then per element
+  // in that chunk alone.
+  double run = run0;
+  for (int i = i0; i < i1; ++i) run += static_cast<double>(get(i));
   int found = 0x7fffffff;
-  for (int i = i0; i < i1; ++i) {
-    run += static_cast<double>(get(i));
-    if (run / total > u) { found = i; break; }
+  if (i1 > i0 && run / total > u) {
+    run = run0;
+    for (int i = i0; i < i1; ++i) {
+      run += static_cast<double>(get(i));
+      if (run / total > u) { found = i; break; }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) found = min(found, __shfl_xor_sync(0xffffffffu, found, o));
@@ -556,10 +590,301 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
   stamp(5);
 }
 
+// The top-p sampler on a cluster of kSampleCluster CTAs per sequence
+// (temperature > 0, top_p < 1).  Same arithmetic, and so the same token, as
+// sample_kernel; the work that scales with the vocabulary is spread over the
+// cluster:
+//   * CTA r takes token ids [r * kSliceElems, (r + 1) * kSliceElems):
+//     penalty, temperature, its max (exchanged), float64 exp;
+//   * the pairwise sum's leaves are summed where they start (reading a
+//     neighbour's exponentials through distributed shared memory where a leaf
+//     crosses a slice), broadcast to every CTA, and combined identically in
+//     each;
+//   * the stable LSD radix sort (4-bit digits) keeps sort positions [r *
+//     kSliceElems, ...) in CTA r: each pass counts digits per warp, exchanges
+//     the CTA's 16 totals, and scatters every element straight into the CTA
+//     that holds its destination position.  Digits that are equal for every
+//     key (from the keys' AND / OR, exchanged with the first pass's counts)
+//     are skipped: such a pass is the identity;
+//   * the sorted keys and ids are gathered into CTA 0, which runs the top-p
+//     cutoff, the renormalisation and the draw alone.
+// Every thread of every CTA passes every cluster barrier (no early exit
+// before the gather), and no wait depends on data.  Before the gather, CTA
+// r's shared key array holds two sort buffers and its exponentials.
+__device__ __forceinline__ uint64_t* cl_sort_buf(SamplerSmem& sm, int which) {
+  return reinterpret_cast<uint64_t*>(sm.key) + which * kSliceElems;
+}
+__device__ __forceinline__ float* cl_exp_buf(SamplerSmem& sm) {
+  return reinterpret_cast<float*>(sm.key + 4 * kSliceElems);
+}
+
+__global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(const SampleArgs a) {
+  extern __shared__ __align__(16) uint8_t sampler_smem_raw[];
+  SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(sampler_smem_raw);
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int b = blockIdx.x / kSampleCluster, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int V = a.vocab;
+  const int i0 = rank * kSliceElems;
+  const int nloc = max(0, min(kSliceElems, V - i0));  // positions (and ids) this CTA holds
+  const float* lg = a.logits + static_cast<size_t>(b) * V;
+  const bool lead = rank == 0;
+  constexpr int kWarps = kSamplerThreads / 32;
+  auto stamp = [&](int slot) {
+    if (a.trace != nullptr && lead && t == 0) a.trace[static_cast<size_t>(b) * 8 + slot] = globaltimer_ns();
+  };
+  cluster_sync_all();  // every CTA of the cluster runs before any writes into another
+  stamp(0);
+
+  // ---- penalty, temperature, max (ref :32-49) ----
+  const int hl = (a.history && a.hist_len) ? min(max(a.hist_len[b], 0), a.hist_cap) : 0;
+  const bool penalize = a.rep_penalty != 1.0f && hl > 0;
+  if (penalize) {
+    for (int i = t; i < kSliceElems / 32; i += kSamplerThreads) sm.seen[i] = 0u;
+    __syncthreads();
+    for (int i = t; i < hl; i += kSamplerThreads) {
+      const int tok = a.history[static_cast<size_t>(b) * a.hist_cap + i] - i0;
+      if (tok >= 0 && tok < nloc) atomicOr(&sm.seen[tok >> 5], 1u << (tok & 31));
+    }
+    __syncthreads();
+  }
+  float v[4];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = t + r * kSamplerThreads;
+    float x = -INFINITY;
+    if (j < nloc) {
+      x = lg[i0 + j];
+      if (penalize && (sm.seen[j >> 5] >> (j & 31)) & 1u)
+        x = x > 0.f ? __fdiv_rn(x, a.rep_penalty) : __fmul_rn(x, a.rep_penalty);
+      if (a.temperature != 1.0f) x = __fdiv_rn(x, a.temperature);
+    }
+    v[r] = x;
+    mx = fmaxf(mx, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) sm.red_f[warp] = mx;
+  __syncthreads();
+  if (t < kSampleCluster) {
+    float m = sm.red_f[0];
+    for (int w = 1; w < kWarps; ++w) m = fmaxf(m, sm.red_f[w]);
+    st_dsmem_f32(mapa_shared(smem_addr(&sm.cl_max[rank]), t), m);
+  }
+  cluster_sync_all();
+  mx = sm.cl_max[0];
+#pragma unroll
+  for (int c = 1; c < kSampleCluster; ++c) mx = fmaxf(mx, sm.cl_max[c]);
+  float* E = cl_exp_buf(sm);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = t + r * kSamplerThreads;
+    if (j < nloc) E[j] = __double2float_rn(exp(static_cast<double>(__fsub_rn(v[r], mx))));
+  }
+  cluster_sync_all();  // every slice's exponentials are readable
+  stamp(1);
+
+  // ---- normalise: p /= p.sum() (ref :51), the pairwise leaves spread ----
+  tree_split(sm, V);
+  const uint32_t e_base = smem_addr(E);
+  for (int nd = 1 + t; nd < kTreeNodes; nd += kSamplerThreads) {
+    const int len = sm.node_len[nd], s0 = sm.node_start[nd];
+    if (len < 0 || len > 128 || s0 < i0 || s0 >= i0 + nloc) continue;
+    const float res = leaf_sum(s0, len, [&](int i) {
+      return ld_dsmem_f32(mapa_shared(e_base + 4u * static_cast<uint32_t>(i % kSliceElems), i / kSliceElems));
+    });
+#pragma unroll
+    for (int c = 0; c < kSampleCluster; ++c) st_dsmem_f32(mapa_shared(smem_addr(&sm.node_val[nd]), c), res);
+  }
+  cluster_sync_all();
+  const float S = tree_combine(sm);
+  uint64_t* X = cl_sort_buf(sm, 0);
+  uint32_t kand = 0xffffffffu, kor = 0u;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = t + r * kSamplerThreads;
+    if (j < nloc) {
+      const uint32_t key = ~__float_as_uint(__fdiv_rn(E[j], S));  // ascending keys = descending p
+      X[j] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i0 + j);
+      kand &= key;
+      kor |= key;
+    }
+  }
+  kand = __reduce_and_sync(0xffffffffu, kand);
+  kor = __reduce_or_sync(0xffffffffu, kor);
+  if (lane == 0) {
+    sm.red_and[warp] = kand;
+    sm.red_or[warp] = kor;
+  }
+  __syncthreads();  // X and the AND / OR partials are complete
+  stamp(2);
+
+  // ---- top-p (ref :53-63): stable radix sort by (descending p, ascending id) ----
+  const uint32_t below = (1u << lane) - 1u;
+  int cur = 0;
+  uint32_t skip = 0;  // passes whose digit every key shares (known after pass 0's exchange)
+  for (int pass = 0; pass < 8; ++pass) {
+    if ((skip >> pass) & 1u) continue;
+    const int sh = 4 * pass;
+    const uint64_t* src = cl_sort_buf(sm, cur);
+    const uint32_t dst_base = smem_addr(cl_sort_buf(sm, cur ^ 1));
+    // this warp's positions: 4 rounds of 32 consecutive ones, in order
+    uint64_t e[4];
+    if (lane < 16) sm.rs_cnt[warp][lane] = 0;
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = 128 * warp + 32 * r + lane;
+      e[r] = j < nloc ? src[j] : 0ull;
+      if (j < nloc) atomicAdd(&sm.rs_cnt[warp][static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {  // within the CTA: digit d's elements of warp w start at rs_off[w][d]
+      int tot = 0;
+      if (lane < 16)
+        for (int w = 0; w < kWarps; ++w) {
+          const int c = sm.rs_cnt[w][lane];
+          sm.rs_off[w][lane] = tot;
+          tot += c;
+        }
+      if (lane < 16) {
+#pragma unroll
+        for (int c = 0; c < kSampleCluster; ++c)
+          st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_cnt[rank][lane]), c), static_cast<uint32_t>(tot));
+      }
+      if (pass == 0 && lane >= 16 && lane < 16 + kSampleCluster) {
+        uint32_t ka = 0xffffffffu, ko = 0u;
+        for (int w = 0; w < kWarps; ++w) {
+          ka &= sm.red_and[w];
+          ko |= sm.red_or[w];
+        }
+        st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_and[rank]), lane - 16), ka);
+        st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_or[rank]), lane - 16), ko);
+      }
+    }
+    cluster_sync_all();  // every CTA's digit totals (and, at pass 0, AND / OR) have arrived
+    if (pass == 0) {
+      uint32_t ka = 0xffffffffu, ko = 0u;
+#pragma unroll
+      for (int c = 0; c < kSampleCluster; ++c) {
+        ka &= sm.cl_and[c];
+        ko |= sm.cl_or[c];
+      }
+      const uint32_t diff = ka ^ ko;  // bits that differ between some keys
+#pragma unroll
+      for (int q = 1; q < 8; ++q)
+        if (((diff >> (4 * q)) & 15u) == 0u) skip |= 1u << q;
+    }
+    if (warp == 0) {  // global start of digit d in this CTA: all smaller digits, then earlier CTAs
+      int before = 0, total = 0;
+      if (lane < 16)
+        for (int c = 0; c < kSampleCluster; ++c) {
+          const int n = sm.cl_cnt[c][lane];
+          if (c < rank) before += n;
+          total += n;
+        }
+      int incl = total;
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane < 16) {
+        const int base = incl - total + before;
+        for (int w = 0; w < kWarps; ++w) sm.rs_off[w][lane] += base;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {  // scatter in position order
+      const int j = 128 * warp + 32 * r + lane;
+      const bool ok = j < nloc;
+      const uint32_t d = static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u;
+      const uint32_t m = same_digit_lanes(d) & __ballot_sync(0xffffffffu, ok);
+      const int dst = ok ? sm.rs_off[warp][d] + __popc(m & below) : 0;
+      __syncwarp();
+      if (ok && (m & below) == 0) sm.rs_off[warp][d] += __popc(m);  // the group's lowest lane advances it
+      __syncwarp();
+      if (ok)
+        st_dsmem_u64(mapa_shared(dst_base + 8u * static_cast<uint32_t>(dst % kSliceElems), dst / kSliceElems), e[r]);
+    }
+    cluster_sync_all();  // the pass's output is complete in every CTA
+    cur ^= 1;
+  }
+
+  // ---- gather the sorted slices into CTA 0 ----
+  const uint64_t* fin = cl_sort_buf(sm, cur);
+  uint64_t g[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = t + r * kSamplerThreads;
+    g[r] = j < nloc ? fin[j] : 0ull;
+  }
+  cluster_sync_all();  // CTA 0's sort buffers are free from here
+  const uint32_t kb = smem_addr(sm.key), ib = smem_addr(sm.idx);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int j = t + r * kSamplerThreads;
+    if (j < nloc) {
+      const uint32_t i = static_cast<uint32_t>(i0 + j);
+      st_dsmem_u32(mapa_shared(kb + 4u * i, 0), static_cast<uint32_t>(g[r] >> 32));
+      st_dsmem_u16(mapa_shared(ib + 2u * i, 0), static_cast<uint32_t>(g[r]) & 0xffffu);
+    }
+  }
+  if (lead)
+    for (int i = V + t; i < kSamplerMaxVocab; i += kSamplerThreads) {
+      sm.key[i] = 0xffffffffu;  // decodes to p = 0
+      sm.idx[i] = 0xffff;
+    }
+  cluster_sync_all();  // CTA 0 holds every sorted key; the others are done
+  if (!lead) return;
+  stamp(3);
+  int n_rounds = 0;
+  const int cut = topp_cutoff(sm, V, a.top_p, a.trace != nullptr ? a.trace + static_cast<size_t>(b) * 8 + 7 : nullptr, n_rounds);
+  if (a.trace != nullptr && t == 0)
+    a.trace[static_cast<size_t>(b) * 8 + 6] = static_cast<uint64_t>(cut) | (static_cast<uint64_t>(n_rounds) << 32);
+  stamp(4);
+  const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
+  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
+  if (t == 0) a.out[b] = sm.idx[k];
+  stamp(5);
+}
+
+// Clusters of the cluster sampler that fit co-resident on the current device
+// (0 if none); cached per device.
+inline int sampler_cluster_capacity() {
+  static int cap[64];
+  static bool known[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (known[dev]) return cap[dev];
+  int n = 0;
+  if (cudaFuncSetAttribute(sample_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(sizeof(SamplerSmem))) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kSampleCluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(kSampleCluster * 32);
+    cfg.blockDim = dim3(kSamplerThreads);
+    cfg.dynamicSmemBytes = sizeof(SamplerSmem);
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, sample_cluster_kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cap[dev] = n;
+  known[dev] = true;
+  return n;
+}
+
 inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, const int32_t* history,
                                   int hist_cap, const int32_t* hist_len, const double* uniforms,
                                   double temperature, double top_p, double rep_penalty, int32_t* out,
-                                  cudaStream_t st, uint64_t* scratch, uint64_t* trace = nullptr) {
+                                  cudaStream_t st, uint64_t* scratch, uint64_t* trace = nullptr,
+                                  bool allow_cluster = true) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -584,6 +909,23 @@ inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, con
   a.top_p = top_p;
   a.trace = trace;
   a.scratch = scratch;
+  // top-p draws go to the cluster kernel when every sequence's cluster is
+  // co-resident (one wave); larger batches keep one CTA per sequence
+  if (allow_cluster && a.temperature > 0.0f && top_p < 1.0 && batch <= sampler_cluster_capacity()) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(batch * kSampleCluster));
+    cfg.blockDim = dim3(kSamplerThreads);
+    cfg.dynamicSmemBytes = sizeof(SamplerSmem);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = kSampleCluster;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, sample_cluster_kernel, a);
+  }
   sample_kernel<<<batch, kSamplerThreads, sizeof(SamplerSmem), st>>>(a);
   return cudaGetLastError();
 }
