@@ -76,13 +76,14 @@ struct SamplerSmem {
   int ch_k, ch_cut, ev_k, ev_kind;
   long long ev_s, ch_tot;
   long long scan64[kSamplerThreads / 32];
-  int rs_cnt[kSamplerThreads / 32][16];  // radix sort: digit counts / running offsets per warp
-  int rs_off[kSamplerThreads / 32][16];
+  int rs_cnt[kSamplerThreads / 32][17];  // radix sort: digit counts / running offsets per warp
+  int rs_off[kSamplerThreads / 32][17];  // (rows padded: a column read is conflict-free)
   // cluster sampler: values every CTA of the cluster pushes into every CTA
   // (slot = the pushing CTA's rank)
   float cl_max[kSampleCluster];
   uint32_t cl_and[kSampleCluster], cl_or[kSampleCluster];
   int cl_cnt[kSampleCluster][16];
+  int cl_tot[16], cl_lstart[16], cl_gofs[16];  // a sort pass's digit totals and starts: in the stage, stage -> global
   uint32_t red_and[kSamplerThreads / 32], red_or[kSamplerThreads / 32];
 };
 
@@ -371,58 +372,73 @@ __device__ int topp_cutoff(SamplerSmem& sm, int V, double top_p, uint64_t* diag,
   }
   __syncthreads();
   rounds = 0;
+  constexpr uint32_t kSat = 1u << 30;  // scans saturate here: any sum that large is past an event
   while (sm.ch_cut == 0) {
     ++rounds;
     const int k0 = sm.ch_k;
+    const int k0a = k0 & ~(kPer - 1);  // the chunk starts 8-aligned; keys before k0 count as p = 0
     const float c = sm.ch_c;  // > 0: it holds p_0, the largest probability
     int ex;
     frexpf(c, &ex);  // c in [2^(ex-1), 2^ex): ulp u = 2^(ex-24)
     const float scale = ldexpf(1.0f, 24 - ex);  // 1 / u, a power of two
-    const long long c0 = static_cast<long long>(__fmul_rn(c, scale));  // c / u, exact (< 2^24)
+    const uint32_t c0 = static_cast<uint32_t>(__fmul_rn(c, scale));  // c / u, exact (< 2^24)
     // T: the first running sum (in units of u) that reaches thr
-    const long long T = static_cast<long long>(ceil(static_cast<double>(thr) * static_cast<double>(scale)));
+    const double Td = ceil(static_cast<double>(thr) * static_cast<double>(scale));
+    const uint32_t T = Td >= 2147483648.0 ? 0x80000000u : static_cast<uint32_t>(Td);
+    const int kb = k0a + kPer * t;
+    uint32_t kw[kPer];
+    if (kb < kSamplerMaxVocab) {  // two 16-byte loads: 2-way bank conflicts instead of 8-way
+      const uint4 lo = *reinterpret_cast<const uint4*>(&sm.key[kb]);
+      const uint4 hi = *reinterpret_cast<const uint4*>(&sm.key[kb + 4]);
+      kw[0] = lo.x; kw[1] = lo.y; kw[2] = lo.z; kw[3] = lo.w;
+      kw[4] = hi.x; kw[5] = hi.y; kw[6] = hi.z; kw[7] = hi.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) kw[j] = 0xffffffffu;
+    }
     float y[kPer];
-    long long loc = 0;
+    uint32_t loc = 0;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int k = k0 + kPer * t + j;
-      const float p = k < V ? key_to_p(sm.key[k]) : 0.f;
+      const int k = kb + j;
+      const float p = (k >= k0 && k < V) ? key_to_p(kw[j]) : 0.f;
       y[j] = __fmul_rn(p, scale);  // p / u, exact, < 2^24
       const float q = floorf(y[j]);
-      loc += static_cast<long long>(q) + (y[j] - q > 0.5f ? 1 : 0);
+      loc += static_cast<uint32_t>(q) + (y[j] - q > 0.5f ? 1u : 0u);
     }
-    // exclusive block scan of the per-thread sums (64-bit)
-    long long inc = loc;
+    // block scan of the per-thread sums (32-bit, saturating)
+    uint32_t inc = loc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const long long v = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += v;
+      const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc = min(inc + v, kSat);
     }
+    const uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
     if (lane == 31) sm.scan64[warp] = inc;
     if (t == 0) sm.ev_k = 0x7fffffff;
     __syncthreads();
-    long long wt = lane < kWarps ? sm.scan64[lane] : 0;  // every warp scans the warp totals
+    uint32_t wt = lane < kWarps ? static_cast<uint32_t>(sm.scan64[lane]) : 0u;  // every warp scans the warp totals
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const long long v = __shfl_up_sync(0xffffffffu, wt, o);
-      if (lane >= o) wt += v;
+      const uint32_t v = __shfl_up_sync(0xffffffffu, wt, o);
+      if (lane >= o) wt = min(wt + v, kSat);
     }
-    const long long wbefore = warp > 0 ? __shfl_sync(0xffffffffu, wt, warp - 1) : 0;
-    long long S = c0 + wbefore + inc - loc;
+    const uint32_t wbefore = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
+    uint32_t S = min(c0 + (warp > 0 ? wbefore : 0u) + (lane > 0 ? excl : 0u), kSat);
     int ev = 0x7fffffff, kind = 0;
-    long long ev_s = 0;
+    uint32_t ev_s = 0;
 #pragma unroll
     for (int j = 0; j < kPer; ++j) {
-      const int k = k0 + kPer * t + j;
-      if (k >= V || ev != 0x7fffffff) continue;
+      const int k = kb + j;
+      if (k < k0 || k >= V || ev != 0x7fffffff) continue;
       const float q = floorf(y[j]);
       const float f = y[j] - q;
-      const long long qi = static_cast<long long>(q);
-      if (f == 0.5f || S + qi >= (1ll << 24) - 2) {  // exact tie, or the sum may leave the binade
+      const uint32_t qi = static_cast<uint32_t>(q);
+      if (f == 0.5f || S + qi >= (1u << 24) - 2) {  // exact tie, or the sum may leave the binade
         ev = k; kind = 1; ev_s = S;
         continue;
       }
-      S += qi + (f > 0.5f ? 1 : 0);
+      S += qi + (f > 0.5f ? 1u : 0u);
       if (S >= T) {  // threshold reached at k
         ev = k; kind = 2; ev_s = S;
       }
@@ -439,7 +455,7 @@ __device__ int topp_cutoff(SamplerSmem& sm, int V, double top_p, uint64_t* diag,
       const int k = sm.ev_k;
       const float u = ldexpf(1.0f, ex - 24);
       if (k == 0x7fffffff) {  // no event: the whole chunk stays in the binade, below thr
-        const int end = min(k0 + kChunk, V);
+        const int end = min(k0a + kChunk, V);
         sm.ch_c = __fmul_rn(static_cast<float>(sm.ch_tot), u);  // < 2^24 units: exact
         sm.ch_k = end;
         if (end >= V) sm.ch_cut = V;
@@ -585,7 +601,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
     a.trace[static_cast<size_t>(b) * 8 + 6] = static_cast<uint64_t>(cut) | (static_cast<uint64_t>(n_rounds) << 32);
   stamp(4);
   const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
-  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
+  for (int i = t; i < cut; i += kSamplerThreads)  // the renormalised kept p, once each
+    sm.key[i] = __float_as_uint(__fdiv_rn(key_to_p(sm.key[i]), S2));
+  __syncthreads();
+  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __uint_as_float(sm.key[i]); });
   if (t == 0) a.out[b] = sm.idx[k];
   stamp(5);
 }
@@ -602,8 +621,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
 //     each;
 //   * the stable LSD radix sort (4-bit digits) keeps sort positions [r *
 //     kSliceElems, ...) in CTA r: each pass counts digits per warp, exchanges
-//     the CTA's 16 totals, and scatters every element straight into the CTA
-//     that holds its destination position.  Digits that are equal for every
+//     the CTA's 16 totals, orders its elements by digit in a local stage, and
+//     sends each digit's run to its consecutive destination positions (in
+//     whichever CTAs hold them).  (4096 random 8-byte stores into other
+//     CTAs took ~5,900 cycles per CTA, ~900 into its own shared memory.)  Digits that are equal for every
 //     key (from the keys' AND / OR, exchanged with the first pass's counts)
 //     are skipped: such a pass is the identity;
 //   * the sorted keys and ids are gathered into CTA 0, which runs the top-p
@@ -728,6 +749,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     const int sh = 4 * pass;
     const uint64_t* src = cl_sort_buf(sm, cur);
     const uint32_t dst_base = smem_addr(cl_sort_buf(sm, cur ^ 1));
+    uint64_t* stage = cl_sort_buf(sm, 2);  // the exponentials' space, free from here
     // this warp's positions: 4 rounds of 32 consecutive ones, in order
     uint64_t e[4];
     if (lane < 16) sm.rs_cnt[warp][lane] = 0;
@@ -739,15 +761,28 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
       if (j < nloc) atomicAdd(&sm.rs_cnt[warp][static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u], 1);
     }
     __syncthreads();
-    if (warp == 0) {  // within the CTA: digit d's elements of warp w start at rs_off[w][d]
-      int tot = 0;
-      if (lane < 16)
-        for (int w = 0; w < kWarps; ++w) {
-          const int c = sm.rs_cnt[w][lane];
-          sm.rs_off[w][lane] = tot;
-          tot += c;
-        }
+    if (warp < 16) {  // digit d = warp: exclusive scan of the warps' counts (lane = warp index)
+      const int c = sm.rs_cnt[lane][warp];
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      sm.rs_off[lane][warp] = incl - c;
+      if (lane == 31) sm.cl_tot[warp] = incl;
+    }
+    __syncthreads();
+    if (warp == 0) {  // in the stage, digit d's elements of warp w start at cl_lstart[d] + rs_off[w][d]
+      const int tot = lane < 16 ? sm.cl_tot[lane] : 0;
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
       if (lane < 16) {
+        sm.cl_lstart[lane] = incl - tot;
 #pragma unroll
         for (int c = 0; c < kSampleCluster; ++c)
           st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_cnt[rank][lane]), c), static_cast<uint32_t>(tot));
@@ -762,7 +797,22 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
         st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_or[rank]), lane - 16), ko);
       }
     }
-    cluster_sync_all();  // every CTA's digit totals (and, at pass 0, AND / OR) have arrived
+    __syncthreads();
+    // stable counting sort of this CTA's elements by digit into the stage, so
+    // that each digit's elements leave as one run of consecutive positions
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int j = 128 * warp + 32 * r + lane;
+      const bool ok = j < nloc;
+      const uint32_t d = static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u;
+      const uint32_t m = same_digit_lanes(d) & __ballot_sync(0xffffffffu, ok);
+      const int pos = ok ? sm.cl_lstart[d] + sm.rs_off[warp][d] + __popc(m & below) : 0;
+      __syncwarp();
+      if (ok && (m & below) == 0) sm.rs_off[warp][d] += __popc(m);  // the group's lowest lane advances it
+      __syncwarp();
+      if (ok) stage[pos] = e[r];
+    }
+    cluster_sync_all();  // every CTA's digit totals (and, at pass 0, AND / OR) have arrived; the stage is complete
     if (pass == 0) {
       uint32_t ka = 0xffffffffu, ko = 0u;
 #pragma unroll
@@ -775,7 +825,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
       for (int q = 1; q < 8; ++q)
         if (((diff >> (4 * q)) & 15u) == 0u) skip |= 1u << q;
     }
-    if (warp == 0) {  // global start of digit d in this CTA: all smaller digits, then earlier CTAs
+    if (warp == 0) {  // global start of digit d from this CTA: all smaller digits, then earlier CTAs
       int before = 0, total = 0;
       if (lane < 16)
         for (int c = 0; c < kSampleCluster; ++c) {
@@ -789,24 +839,17 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      if (lane < 16) {
-        const int base = incl - total + before;
-        for (int w = 0; w < kWarps; ++w) sm.rs_off[w][lane] += base;
-      }
+      if (lane < 16) sm.cl_gofs[lane] = incl - total + before - sm.cl_lstart[lane];
     }
     __syncthreads();
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {  // scatter in position order
-      const int j = 128 * warp + 32 * r + lane;
-      const bool ok = j < nloc;
-      const uint32_t d = static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u;
-      const uint32_t m = same_digit_lanes(d) & __ballot_sync(0xffffffffu, ok);
-      const int dst = ok ? sm.rs_off[warp][d] + __popc(m & below) : 0;
-      __syncwarp();
-      if (ok && (m & below) == 0) sm.rs_off[warp][d] += __popc(m);  // the group's lowest lane advances it
-      __syncwarp();
-      if (ok)
-        st_dsmem_u64(mapa_shared(dst_base + 8u * static_cast<uint32_t>(dst % kSliceElems), dst / kSliceElems), e[r]);
+    for (int r = 0; r < 4; ++r) {  // consecutive stage positions -> consecutive global positions
+      const int j = t + r * kSamplerThreads;
+      if (j < nloc) {
+        const uint64_t x = stage[j];
+        const int dst = sm.cl_gofs[static_cast<uint32_t>(x >> (32 + sh)) & 15u] + j;
+        st_dsmem_u64(mapa_shared(dst_base + 8u * static_cast<uint32_t>(dst % kSliceElems), dst / kSliceElems), x);
+      }
     }
     cluster_sync_all();  // the pass's output is complete in every CTA
     cur ^= 1;
@@ -845,7 +888,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     a.trace[static_cast<size_t>(b) * 8 + 6] = static_cast<uint64_t>(cut) | (static_cast<uint64_t>(n_rounds) << 32);
   stamp(4);
   const float S2 = pairwise_sum(sm, cut, [&](int i) { return key_to_p(sm.key[i]); });
-  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __fdiv_rn(key_to_p(sm.key[i]), S2); });
+  for (int i = t; i < cut; i += kSamplerThreads)  // the renormalised kept p, once each
+    sm.key[i] = __float_as_uint(__fdiv_rn(key_to_p(sm.key[i]), S2));
+  __syncthreads();
+  const int k = cdf_search(sm, cut, a.uniforms[b], [&](int i) { return __uint_as_float(sm.key[i]); });
   if (t == 0) a.out[b] = sm.idx[k];
   stamp(5);
 }
