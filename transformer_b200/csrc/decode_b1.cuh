@@ -442,7 +442,7 @@ __device__ __forceinline__ bool gemv_phase(const DecodeArgs& A, Ring& ring, floa
 }
 
 // Same streaming for many units per warp (the logits): reduce per stage.
-template <int KI, int PITCH, int PS, class R, int GROUP = R::kN / 2, class Out>
+template <int KI, int PITCH, int PS, class R, int GROUP = R::kN / 2, bool TR = false, class Out>
 __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, R& ring, uint32_t flag, uint64_t t0,
                                                 int u_begin, int u_end, const XSmem x, Out out) {
   constexpr int kGroupStages = GROUP;  // stages waited for (and released) together
@@ -452,6 +452,7 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, R& ring, ui
     const int g1 = min(g0 + kGroupStages * PS, u_end);
     const int ns = (g1 - g0 + PS - 1) / PS;
     ok = wait_full_n(A, ring, ns, flag, t0);
+    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 1, ring.seq);
     if (ok) {
       const int first = g0 + ((warp - (g0 - u_begin)) % kConsumerWarps + kConsumerWarps) % kConsumerWarps;
       for (int u = first; u < g1; u += kConsumerWarps) {
@@ -464,6 +465,7 @@ __device__ __forceinline__ bool gemv_phase_wide(const DecodeArgs& A, R& ring, ui
         out(u, warp_sum(f2sum(a0) + f2sum(a1)), 0.f);
       }
     }
+    if (threadIdx.x == 0) stage_stamp<TR>(A, blockIdx.x, 2, ring.seq);
     release_n(ring, ns);
   }
   return ok;

@@ -1143,7 +1143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float best_v = -INFINITY;
       int best_i = 0x7fffffff;
       // released two stages at a time, so up to 10 of the 12 slots can be in flight
-      ok = gemv_phase_wide<S::KD, S::ROWB_D, S::RPS_D, RingC, 2>(A, ring, flag, t0, v0, v1, x, [&](int u, float v, float) {
+      ok = gemv_phase_wide<S::KD, S::ROWB_D, S::RPS_D, RingC, 2, TR>(A, ring, flag, t0, v0, v1, x, [&](int u, float v, float) {
         if (lane == 0 && A.logits) A.logits[u] = v;
         if (v > best_v) {
           best_v = v;
