@@ -18,6 +18,9 @@ rows in one ``b2d_prefill_rows`` call), the small case for its ncu captures.
 ``--mode serve`` runs the continuous batcher (``transformer_b200.serve``) on
 a stream of requests and reports generated tokens per second, wall-clock.
 
+``--mode paged-att-trace`` times the attention's phases per unit inside the
+captured batched step (its global-timer stamps).
+
 ``--mode paged`` runs the batched step over a paged KV pool with every
 sequence at ``--pos`` (the pool holds zeros: the step's work does not depend
 on the cached values), launched eagerly ``--warmup`` + ``--steps`` times; it is
@@ -223,6 +226,63 @@ def profile_paged(w, cfg, args, torch):
             "hbm_frac": alg / (us * 1e-6) / 1e9 / peak, "peak_gbs": peak, "peak_source": kind}
 
 
+def profile_paged_att_trace(w, cfg, args, torch):
+    """Per-unit phase times of the attention inside the captured batched step
+    (graph replay, every sequence at --pos): the units' global-timer stamps
+    (b2d_debug_tune knob 9), median over units, mean over layers 2..n-2.
+    Phases: issue (entry -> first pages requested), pdl_wait (-> the q/k/v
+    projection finished), query (-> query fragments and the new K/V row),
+    first_pair, rest_pairs, write, merge.  `after_input_us` is a unit's time
+    from the projection's end to its result; `kv_bytes` the pages read."""
+    import numpy as np
+    from transformer_b200.batched import BatchedDecoder
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    units = 8192
+    dec = BatchedDecoder(eng, args.batch, seed=args.batch)
+    dec.pos.fill_(args.pos)
+    dec.tok.copy_(torch.randint(0, cfg.vocab_size, (args.batch,), dtype=torch.int32))
+    buf = torch.zeros(cfg.n_layers * units * 8, dtype=torch.int64, device="cuda")
+    eng.debug_tune(att_trace=buf)
+    try:
+        dec.capture()
+        for _ in range(max(args.warmup, 1)):
+            dec.pos.fill_(args.pos)
+            dec.replay()
+        torch.cuda.synchronize()
+        buf.zero_()
+        dec.pos.fill_(args.pos)
+        dec.replay()
+        torch.cuda.synchronize()
+        eng.check_device()
+        t = buf.view(cfg.n_layers, units, 8).cpu().numpy().astype(np.int64)
+    finally:
+        eng.debug_tune(att_trace=torch.zeros(0, dtype=torch.int64))
+        dec.release()
+    names = ["issue", "pdl_wait", "query", "first_pair", "rest_pairs", "write", "merge"]
+    ph = {n: [] for n in names}
+    after, span, n_units = [], [], 0
+    for layer in range(2, cfg.n_layers - 1):
+        s = t[layer]
+        s = s[s[:, 0] > 0]
+        n_units = int(s.shape[0])
+        for k, n in enumerate(names):
+            ph[n].append(float(np.median(s[:, k + 1] - s[:, k])) / 1e3)
+        after.append(float(np.median(s[:, 7] - s[:, 2])) / 1e3)
+        span.append(float(s[:, 7].max() - s[:, 2].min()) / 1e3)
+    pages = (args.pos // 16 + 1) * 16
+    kv_bytes = args.batch * cfg.n_kv_heads * pages * 2 * cfg.d_head * 2
+    after_us = float(np.mean(after))
+    span_us = float(np.mean(span))
+    peak, kind = hbm_peak()
+    return {"mode": "paged-att-trace", "batch": args.batch, "pos": args.pos, "units": n_units,
+            "median_phase_us": {n: round(float(np.mean(v)), 2) for n, v in ph.items()},
+            "after_input_us": round(after_us, 2),
+            "first_input_to_last_result_us": round(span_us, 2), "kv_bytes": kv_bytes,
+            "hbm_frac_after_input": round(kv_bytes / (span_us * 1e-6) / 1e9 / peak, 3),
+            "peak_gbs": peak, "peak_source": kind}
+
+
 def profile_mixed(w, cfg, args, torch):
     """One fused pass of the continuous batcher, timed alone: ``--batch``
     decode rows at position ``--pos`` plus ``--prompts`` prompts of
@@ -324,7 +384,7 @@ def profile_serve(w, cfg, args, torch):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "serve", "mixed"], default="b1")
+    ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "paged-att-trace", "serve", "mixed"], default="b1")
     ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--att-splits", type=int, default=0, help="--mode paged: force 1, 2 or 4 attention units")
     ap.add_argument("--requests", type=int, default=1024)
@@ -360,8 +420,8 @@ def main():
         params = synth_params(cfg, 0)
     w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
     out = {"memory": compute_memory_stats(cfg)}
-    prof = {"b1": profile_b1, "b1-trace": profile_b1_trace, "paged": profile_paged, "serve": profile_serve,
-            "mixed": profile_mixed}[args.mode]
+    prof = {"b1": profile_b1, "b1-trace": profile_b1_trace, "paged": profile_paged,
+            "paged-att-trace": profile_paged_att_trace, "serve": profile_serve, "mixed": profile_mixed}[args.mode]
     out.update(prof(w, cfg, args, torch))
     print(json.dumps(out))
     return 0
