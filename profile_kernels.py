@@ -238,6 +238,8 @@ def profile_paged_att_trace(w, cfg, args, torch):
     from transformer_b200.batched import BatchedDecoder
     from transformer_b200.multi_sm_decode import DecodeEngine
     eng = DecodeEngine(w, max_batch=max(2, args.batch))
+    if args.att_splits:
+        eng.debug_tune(att_cpc=args.att_splits)  # attention units per (sequence, kv head); 0 = automatic
     units = 8192
     dec = BatchedDecoder(eng, args.batch, seed=args.batch)
     dec.pos.fill_(args.pos)
@@ -275,7 +277,8 @@ def profile_paged_att_trace(w, cfg, args, torch):
     after_us = float(np.mean(after))
     span_us = float(np.mean(span))
     peak, kind = hbm_peak()
-    return {"mode": "paged-att-trace", "batch": args.batch, "pos": args.pos, "units": n_units,
+    return {"mode": "paged-att-trace", "batch": args.batch, "pos": args.pos, "att_splits": args.att_splits,
+            "units": n_units,
             "median_phase_us": {n: round(float(np.mean(v)), 2) for n, v in ph.items()},
             "after_input_us": round(after_us, 2),
             "first_input_to_last_result_us": round(span_us, 2), "kv_bytes": kv_bytes,
@@ -386,7 +389,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "paged-att-trace", "serve", "mixed"], default="b1")
     ap.add_argument("--prompts", type=int, default=4)
-    ap.add_argument("--att-splits", type=int, default=0, help="--mode paged: force 1, 2 or 4 attention units")
+    ap.add_argument("--att-splits", type=int, default=0,
+                    help="--mode paged / paged-att-trace: force 1, 2 or 4 attention units")
     ap.add_argument("--requests", type=int, default=1024)
     ap.add_argument("--prompt-len", type=int, default=64)
     ap.add_argument("--gen-min", type=int, default=32)
