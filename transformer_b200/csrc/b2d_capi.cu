@@ -882,11 +882,13 @@ b2d_status run_rows(b2d_model* m, b2d_ws* ws, const int32_t* tok, const int32_t*
     int sp = ws->force_att_cpc ? ws->force_att_cpc : std::max(1, target / pairs);
     sp = std::min(sp, std::min(b2d::kPaMaxSplits, (c.context_len + 15) / 16));
     pa.cpc = sp >= 4 ? 4 : sp >= 2 ? 2 : 1;  // a row's units share one CTA of pa_warps(splits) warps
-    if (att_tma && pa.cpc == 1 && !ws->force_att_cpc && 2 * pairs > 8 * m->grid && 2 * pairs <= 22 * m->grid &&
-        c.context_len >= 2 * b2d::kPageTokens) {
+    // decode only: prompt rows keep the units of the contiguous-cache path,
+    // so a paged prefill equals a contiguous one bit for bit
+    if (att_tma && !prefill && pa.cpc == 1 && !ws->force_att_cpc && 2 * pairs > 8 * m->grid &&
+        2 * pairs <= 22 * m->grid && c.context_len >= 2 * b2d::kPageTokens) {
       pa.cpc = 2;
       att_stages = b2d::kPaStagesSplit;
-    } else if (att_tma && pa.cpc == 1 && pairs > 16 * m->grid) {
+    } else if (att_tma && !prefill && pa.cpc == 1 && pairs > 16 * m->grid) {
       att_stages = b2d::kPaStagesShallow;
     }
   }
