@@ -18,6 +18,9 @@ rows in one ``b2d_prefill_rows`` call), the small case for its ncu captures.
 ``--mode serve`` runs the continuous batcher (``transformer_b200.serve``) on
 a stream of requests and reports generated tokens per second, wall-clock.
 
+``--mode sample`` times B=--batch top-p draws of the device sampler (both
+kernels) with their phase stamps.
+
 ``--mode paged-att-trace`` times the attention's phases per unit inside the
 captured batched step (its global-timer stamps).
 
@@ -286,6 +289,54 @@ def profile_paged_att_trace(w, cfg, args, torch):
             "peak_gbs": peak, "peak_source": kind}
 
 
+def profile_sample(w, cfg, args, torch):
+    """B = --batch top-p draws (T 0.7, top-p 0.95, rep 1.2, 100-token
+    histories) on seeded N(0, s^2) logits, s = 0.3 (flat: ~28,400 tokens
+    kept), 1.0 and 3.0: microseconds per b2d_sample call (CUDA events, --steps
+    calls after --warmup) and the phase stamps (b2d_debug_tune knob 10) of
+    one more call, for the cluster kernel and the one-CTA kernel (knob 13)."""
+    import numpy as np
+    from transformer_b200.generate import Sampler
+    from transformer_b200.multi_sm_decode import DecodeEngine
+    B = args.batch
+    eng = DecodeEngine(w, max_batch=max(2, B))
+    smp = Sampler(eng, B, 256)
+    rng = np.random.default_rng(1)
+    hist = torch.from_numpy(rng.integers(0, cfg.vocab_size, (B, 100)).astype(np.int32))
+    smp.history[:, :100].copy_(hist)
+    smp.hist_len.fill_(100)
+    smp.uniforms.copy_(torch.from_numpy(rng.random(B)))
+    names = ["exp", "normalise", "sort", "cutoff", "draw"]
+    out = []
+    for single in (False, True):
+        eng.debug_tune(sample_single=single)
+        for sigma in (0.3, 1.0, 3.0):
+            lg = torch.from_numpy((rng.standard_normal((B, cfg.vocab_size)) * sigma).astype(np.float32)).cuda()
+            for _ in range(args.warmup):
+                smp.sample(lg, 0.7, 0.95, 1.2, B)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                smp.sample(lg, 0.7, 0.95, 1.2, B)
+            e1.record()
+            torch.cuda.synchronize()
+            buf = torch.zeros(B, 8, dtype=torch.int64, device="cuda")
+            eng.debug_tune(sample_trace=buf)
+            smp.sample(lg, 0.7, 0.95, 1.2, B)
+            torch.cuda.synchronize()
+            eng.debug_tune(sample_trace=torch.zeros(0, dtype=torch.int64))
+            t = buf.cpu().numpy().astype(np.int64)
+            out.append({"kernel": "one CTA per sequence" if single else "cluster of 8 CTAs per sequence",
+                        "sigma": sigma, "us_per_call": round(e0.elapsed_time(e1) * 1000 / args.steps, 1),
+                        "phases_us": {n: round(float(np.mean(t[:, i + 1] - t[:, i])) / 1e3, 1)
+                                      for i, n in enumerate(names)},
+                        "kept_mean": float(np.mean(t[:, 6] & 0xffffffff))})
+    eng.debug_tune(sample_single=False)
+    eng.check_device()
+    return {"mode": "sample", "batch": B, "results": out}
+
+
 def profile_mixed(w, cfg, args, torch):
     """One fused pass of the continuous batcher, timed alone: ``--batch``
     decode rows at position ``--pos`` plus ``--prompts`` prompts of
@@ -387,7 +438,8 @@ def profile_serve(w, cfg, args, torch):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "paged-att-trace", "serve", "mixed"], default="b1")
+    ap.add_argument("--mode", choices=["b1", "b1-trace", "paged", "paged-att-trace", "sample", "serve", "mixed"],
+                    default="b1")
     ap.add_argument("--prompts", type=int, default=4)
     ap.add_argument("--att-splits", type=int, default=0,
                     help="--mode paged / paged-att-trace: force 1, 2 or 4 attention units")
@@ -425,7 +477,8 @@ def main():
     w = prepare_decode_weights_nlayer(params, cfg, device="cuda")
     out = {"memory": compute_memory_stats(cfg)}
     prof = {"b1": profile_b1, "b1-trace": profile_b1_trace, "paged": profile_paged,
-            "paged-att-trace": profile_paged_att_trace, "serve": profile_serve, "mixed": profile_mixed}[args.mode]
+            "paged-att-trace": profile_paged_att_trace, "sample": profile_sample, "serve": profile_serve,
+            "mixed": profile_mixed}[args.mode]
     out.update(prof(w, cfg, args, torch))
     print(json.dumps(out))
     return 0
