@@ -120,28 +120,6 @@ __device__ void tree_split(SamplerSmem& sm, int n) {
   }
 }
 
-// numpy's block sum of get(s0 .. s0 + len - 1), len <= 128.
-template <class Get>
-__device__ float leaf_sum(int s0, int len, Get get) {
-  if (len < 8) {
-    float res = 0.f;
-    for (int i = 0; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
-    return res;
-  }
-  float r[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) r[j] = get(s0 + j);
-  int i = 8;
-  for (; i < len - (len % 8); i += 8) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], get(s0 + i + j));
-  }
-  float res = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                        __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
-  for (; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
-  return res;
-}
-
 // Bottom-up: internal node = left + right; returns 0 + root like np.sum.
 __device__ float tree_combine(SamplerSmem& sm) {
   const int t = threadIdx.x;
@@ -159,13 +137,52 @@ __device__ float tree_combine(SamplerSmem& sm) {
   return total;
 }
 
+// The leaves of the split tree, eight lanes per leaf (four leaves per warp):
+// lane j of a leaf's group runs numpy's accumulator j over elements
+// s0 + 8i + j, so the group reads 8 consecutive words per step (one thread
+// per leaf would read words 8 apart: 8-way bank conflicts).  The group then
+// adds ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) by shuffles and its
+// first lane the remainder, numpy's order exactly.  `mine(s0)` says whether
+// this CTA computes the leaf starting at s0; `store(nd, v)` (first lane of the
+// group) receives each leaf's sum.  Every warp of the block must call it.
+template <class Get, class Mine, class Store>
+__device__ void tree_leaves(const SamplerSmem& sm, Get get, Mine mine, Store store) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, j = lane & 7;
+  const int nwarps = static_cast<int>(blockDim.x) >> 5;
+  for (int base = 4 * warp; base < kTreeNodes; base += 4 * nwarps) {
+    const int nd = base + (lane >> 3);
+    const int len = sm.node_len[nd], s0 = sm.node_start[nd];
+    const bool leaf = len >= 0 && len <= 128 && mine(s0);
+    if (!__any_sync(0xffffffffu, leaf)) continue;
+    const int body = len - (len % 8);
+    float r = 0.f;
+    if (leaf && len >= 8) {
+      r = get(s0 + j);
+      for (int i = 8; i < body; i += 8) r = __fadd_rn(r, get(s0 + i + j));
+    }
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 4));
+    if (leaf && j == 0) {
+      float res;
+      if (len < 8) {
+        res = 0.f;
+        for (int i = 0; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+      } else {
+        res = r;
+        for (int i = body; i < len; ++i) res = __fadd_rn(res, get(s0 + i));
+      }
+      store(nd, res);
+    }
+  }
+}
+
 // numpy's pairwise float32 sum of get(0..n-1) (n <= 2^16, so the tree's leaves
 // are at most 128 long); all threads of the block must call it.
 template <class Get>
 __device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
   tree_split(sm, n);
-  for (int nd = 1 + threadIdx.x; nd < kTreeNodes; nd += blockDim.x)
-    if (sm.node_len[nd] >= 0 && sm.node_len[nd] <= 128) sm.node_val[nd] = leaf_sum(sm.node_start[nd], sm.node_len[nd], get);
+  tree_leaves(sm, get, [](int) { return true; }, [&](int nd, float v) { sm.node_val[nd] = v; });
   __syncthreads();
   return tree_combine(sm);
 }
@@ -176,7 +193,9 @@ __device__ float pairwise_sum(SamplerSmem& sm, int n, Get get) {
 template <class Get>
 __device__ int cdf_search(SamplerSmem& sm, int n, double u, Get get) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int per = (n + kSamplerThreads - 1) / kSamplerThreads;
+  // thread-contiguous chunks of an odd length: lanes' reads then fall in
+  // distinct banks (an even length such as 28 conflicts 4- to 8-way)
+  const int per = ((n + kSamplerThreads - 1) / kSamplerThreads) | 1;
   const int i0 = min(t * per, n), i1 = min(i0 + per, n);
   double local = 0.0;
   for (int i = i0; i < i1; ++i) local += static_cast<double>(get(i));
@@ -708,15 +727,16 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   // ---- normalise: p /= p.sum() (ref :51), the pairwise leaves spread ----
   tree_split(sm, V);
   const uint32_t e_base = smem_addr(E);
-  for (int nd = 1 + t; nd < kTreeNodes; nd += kSamplerThreads) {
-    const int len = sm.node_len[nd], s0 = sm.node_start[nd];
-    if (len < 0 || len > 128 || s0 < i0 || s0 >= i0 + nloc) continue;
-    const float res = leaf_sum(s0, len, [&](int i) {
-      return ld_dsmem_f32(mapa_shared(e_base + 4u * static_cast<uint32_t>(i % kSliceElems), i / kSliceElems));
-    });
+  tree_leaves(
+      sm,
+      [&](int i) {
+        return ld_dsmem_f32(mapa_shared(e_base + 4u * static_cast<uint32_t>(i % kSliceElems), i / kSliceElems));
+      },
+      [&](int s0) { return s0 >= i0 && s0 < i0 + nloc; },
+      [&](int nd, float v) {
 #pragma unroll
-    for (int c = 0; c < kSampleCluster; ++c) st_dsmem_f32(mapa_shared(smem_addr(&sm.node_val[nd]), c), res);
-  }
+        for (int c = 0; c < kSampleCluster; ++c) st_dsmem_f32(mapa_shared(smem_addr(&sm.node_val[nd]), c), v);
+      });
   cluster_sync_all();
   const float S = tree_combine(sm);
   uint64_t* X = cl_sort_buf(sm, 0);
