@@ -311,26 +311,18 @@ def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
 
 
 def measure_b1_e2e(eng, dev, stream, torch, prompt, n_steps):
-    """Config 1 through the public call with host buffers (pinned H2D of the
-    token and position, launch, D2H of the next token, sync per step)."""
+    """Config 1 through the public host-value call (``decode_token`` /
+    ``b2d_decode_token``): each step copies the token and position from
+    pinned host memory to the device, runs the step with the logits written,
+    copies the next token back and synchronises."""
     P0 = len(prompt)
     kv = eng.new_kv()
     eng.prefill(prompt, kv)
     tok = int(torch.argmax(eng.logits[0]).item())
-    h_in = torch.zeros(2, dtype=torch.int32, pin_memory=True)
-    h_out = torch.zeros(1, dtype=torch.int32, pin_memory=True)
-    d_in = torch.zeros(2, dtype=torch.int32, device=dev)
-    d_out = torch.zeros(1, dtype=torch.int32, device=dev)
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     for i in range(n_steps):
-        h_in[0] = tok
-        h_in[1] = P0 + (i % 128)
-        d_in.copy_(h_in, non_blocking=True)
-        eng.step(d_in[0:1], d_in[1:2], kv, eng.logits, d_out, stream)
-        h_out.copy_(d_out, non_blocking=True)
-        stream.synchronize()
-        tok = int(h_out[0])
+        tok = eng.decode_token(tok, P0 + (i % 128), kv, eng.logits, stream)
     dt = time.perf_counter() - t0
     return {"value": n_steps / dt, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
             "steps": n_steps}

@@ -298,3 +298,32 @@ def test_multi_step_range_and_timeout(engine_tiny):
     kv = eng.new_kv()
     toks = eng.decode_steps(tok, torch.zeros(1, dtype=torch.int32, device=dev), kv, 3)
     assert eng.last_error()[0] == _lib.B2D_OK and all(0 <= t < cfg.vocab_size for t in toks.cpu().tolist())
+
+
+def test_decode_token_host_values_equal_step(engine306):
+    """b2d_decode_token (host token / position in, host argmax out, through the
+    workspace's pinned staging) runs the same step as b2d_decode_step: the same
+    argmax and bit-identical logits and KV rows at every step of a short
+    greedy run; out-of-range arguments are rejected on the host."""
+    eng = engine306
+    dev = eng.device
+    prompt = [3, 141, 59, 265, 358, 979, 323]
+    kv_a, kv_b = eng.new_kv(), eng.new_kv()
+    lg_a = torch.empty(CONFIG_306M.vocab_size, dtype=torch.float32, device=dev)
+    lg_b = torch.empty_like(lg_a)
+    nt = torch.zeros(1, dtype=torch.int32, device=dev)
+    tok_a = tok_b = prompt[0]
+    for p in range(24):
+        fed_a = prompt[p] if p < len(prompt) else tok_a
+        fed_b = prompt[p] if p < len(prompt) else tok_b
+        tok_a = eng.decode_token(fed_a, p, kv_a, lg_a)
+        eng.step(torch.tensor([fed_b], dtype=torch.int32, device=dev), torch.tensor([p], dtype=torch.int32, device=dev),
+                 kv_b, lg_b, nt)
+        tok_b = int(nt.item())
+        assert tok_a == tok_b, p
+        assert torch.equal(lg_a, lg_b), p
+    assert torch.equal(kv_a, kv_b)
+    eng.check_device()
+    for bad_tok, bad_pos in ((-1, 0), (CONFIG_306M.vocab_size, 0), (5, -1), (5, CONFIG_306M.context_len)):
+        with pytest.raises(_lib.B2DError):
+            eng.decode_token(bad_tok, bad_pos, kv_a)

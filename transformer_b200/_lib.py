@@ -75,6 +75,8 @@ _SIGS = {
     "b2d_workspace_reset": (ctypes.c_int, [_P, _P]),
     "b2d_last_error": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_uint32)]),
     "b2d_decode_step": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, _P, _P]),
+    "b2d_decode_token": (ctypes.c_int, [_P, _P, ctypes.c_int32, ctypes.c_int32, _P, _P, ctypes.POINTER(ctypes.c_int32),
+                                        _P]),
     "b2d_decode_steps": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, _P, _P]),
     "b2d_decode_step_paged": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_int,
                                              _P, _P, _P]),

@@ -254,6 +254,8 @@ struct b2d_ws {
   uint64_t* sample_scratch;  // top-p sort buffer [sample_rows][kSamplerMaxVocab]
   int sample_rows;
   bool sample_single;      // diagnostics: top-p draws on one CTA per sequence even where clusters fit
+  int32_t* tok_host;       // b2d_decode_token: pinned [4] token, position, next token
+  int32_t* tok_dev;        // its device copy [4]
   int stage_stride;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[6], amap[6], actmap[6];  // box rows 16 / 32 / 64 / 96 / 128 / 256 (bn_index)
@@ -509,6 +511,8 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   for (auto& g : ws->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
   cudaFree(ws->sample_scratch);
+  cudaFreeHost(ws->tok_host);
+  cudaFree(ws->tok_dev);
   if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
   cudaFree(ws->H);
   cudaFree(ws->Hm);
@@ -710,6 +714,36 @@ b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, con
   B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
   return launch_b1(m, ws, tok_dev, pos_dev, kv_dev, logits_dev, next_tok_dev, 1, nullptr,
                    static_cast<cudaStream_t>(stream));
+}
+
+b2d_status b2d_decode_token(b2d_model* m, b2d_ws* ws, int32_t tok, int32_t pos, void* kv_dev, float* logits_dev,
+                            int32_t* next_tok, void* stream) {
+  if (!m || !ws || ws->m != m || !kv_dev || !next_tok || tok < 0 || tok >= m->cfg.vocab_size || pos < 0 ||
+      pos >= m->cfg.context_len)
+    return B2D_ERR_INVALID_ARG;
+  B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!ws->tok_host) {  // 16 pinned bytes and their device copy, on first use
+    B2D_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ws->tok_host), 4 * sizeof(int32_t), cudaHostAllocDefault),
+             "pinned token staging");
+    B2D_CUDA(cudaMalloc(reinterpret_cast<void**>(&ws->tok_dev), 4 * sizeof(int32_t)), "token staging");
+  }
+  // every call ends with the stream synchronised, so no earlier copy still reads the staging
+  ws->tok_host[0] = tok;
+  ws->tok_host[1] = pos;
+  b2d_status s = B2D_OK;
+  cudaError_t e = cudaMemcpyAsync(ws->tok_dev, ws->tok_host, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) s = cuda_fail(e, "token H2D");
+  if (s == B2D_OK) s = launch_b1(m, ws, ws->tok_dev, ws->tok_dev + 1, kv_dev, logits_dev, ws->tok_dev + 2, 1, nullptr, st);
+  if (s == B2D_OK) {
+    e = cudaMemcpyAsync(ws->tok_host + 2, ws->tok_dev + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) s = cuda_fail(e, "token D2H");
+  }
+  e = cudaStreamSynchronize(st);  // also on the error paths: no copy may still read the staging
+  if (s != B2D_OK) return s;
+  if (e != cudaSuccess) return cuda_fail(e, "sync");
+  *next_tok = ws->tok_host[2];
+  return B2D_OK;
 }
 
 b2d_status b2d_decode_steps(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev,

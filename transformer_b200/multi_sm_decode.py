@@ -110,6 +110,23 @@ class DecodeEngine:
                                       _ptr(logits), _ptr(next_tok), _stream_ptr(stream))
         _lib.check(st, "b2d_decode_step")
 
+    def decode_token(self, tok: int, pos: int, kv: torch.Tensor, logits: torch.Tensor | None = None,
+                     stream=None) -> int:
+        """One greedy step with host values (``b2d_decode_token``): copies the
+        token and position through pinned staging, runs the step, returns the
+        argmax as a Python int (the stream is synchronised)."""
+        if kv.dtype != torch.bfloat16 or kv.device != self.device or kv.numel() < self.kv_elems:
+            raise ValueError("kv must be a bf16 cache on the model device (see new_kv)")
+        if logits is not None and (logits.dtype != torch.float32 or logits.device != self.device or
+                                   logits.numel() < self.cfg.vocab_size):
+            raise ValueError("logits must be float32 [vocab] on the model device")
+        nt = ctypes.c_int32()
+        st = self.lib.b2d_decode_token(self.model, self.ws, int(tok), int(pos), _ptr(kv),
+                                       _ptr(logits) if logits is not None else None, ctypes.byref(nt),
+                                       _stream_ptr(stream))
+        _lib.check(st, "b2d_decode_token")
+        return int(nt.value)
+
     def decode_steps(self, tok: torch.Tensor, pos: torch.Tensor, kv: torch.Tensor, n_steps: int,
                      tokens: torch.Tensor | None = None, logits: torch.Tensor | None = None,
                      stream=None) -> torch.Tensor:
