@@ -1114,9 +1114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           float p[RPT];
 #pragma unroll
           for (int i = 0; i < RPT; ++i) p[i] = 0.f;
-#pragma unroll
-          for (int ch = 0; ch < C::MAXCH; ++ch) {
-            if (ch < nch) {
+          // (not unrolled over chunks: the persistent kernel's per-layer code
+          // competes for the instruction cache; measured 266.9 -> 265.1 us/token)
+#pragma unroll 1
+          for (int ch = 0; ch < nch; ++ch) {
+            {
               const uint8_t* stg = ring.stage[(ring.seq + static_cast<uint32_t>(ch)) % kStagesC];
               float a[8];
 #pragma unroll
