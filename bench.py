@@ -303,10 +303,9 @@ def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
                          "peak_source": f"{kind} hbm_gbs", "algorithmic_bytes_per_launch": alg,
                          "traffic": profile_traffic("decode_b1_cfg1.md"),
-                         "traffic_note": "ncu cannot replay the cooperative cluster launch (LaunchFailed), so "
-                                         "the cluster kernel has no DRAM counters; the flat kernel streaming "
-                                         "the same weights read 1.014x the algorithmic bytes "
-                                         "(profiles/decode_b1_flat_cfg1.md)"},
+                         "traffic_note": "ncu capture of the same grid as a plain cluster launch (ncu cannot "
+                                         "replay the cooperative one): mean DRAM read + write of three "
+                                         "one-token launches, profiles/decode_b1_cfg1.md"},
             "gpu_launches": n_steps}
 
 

@@ -335,7 +335,9 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * knob 12 = the B=1 step on the flat kernel (1) or on the cluster kernel
  * where it fits (0, default); knob 13 = b2d_sample's top-p draws on one CTA
  * per sequence (1) or on a cluster of 8 CTAs per sequence where the batch
- * fits one wave of clusters (0, default).
+ * fits one wave of clusters (0, default); knob 14 = the B=1 cluster grid
+ * launched without the cooperative attribute (1; for profilers, which cannot
+ * replay a cooperative launch) or with it (0, default).
  * Every b2d_debug_tune call drops the cached graphs' validity.
  */
 B2D_API b2d_status b2d_debug_trace(b2d_ws* ws, uint64_t* buf_dev, int stamps_per_cta);

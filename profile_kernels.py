@@ -129,6 +129,8 @@ def profile_b1(w, cfg, args, torch):
     from transformer_b200.multi_sm_decode import engine_for
     from transformer_b200.synth import prompt_cfg1, prompt_cfg2
     eng = engine_for(w)
+    if args.plain_launch:  # a profiler cannot replay the cooperative launch
+        eng.debug_tune(plain_launch=True)
     prefill_ms, _, _ = measure_prefill(w, cfg, prompt_cfg2(cfg)[:min(384, cfg.context_len - 1)], args.n_runs)
     prompt = prompt_cfg1(cfg)
     kv = eng.new_kv()
@@ -454,6 +456,8 @@ def main():
     ap.add_argument("--admit-batch", type=int, default=0, help="free slots that trigger an admission (0: default)")
     ap.add_argument("--sampled-frac", type=float, default=0.0,
                     help="--mode serve: fraction of requests sampled (T 0.7, top-p 0.95, rep 1.2)")
+    ap.add_argument("--plain-launch", action="store_true",
+                    help="--mode b1: launch the B=1 cluster grid without the cooperative attribute (for ncu)")
     ap.add_argument("--gen-len", type=int, default=128)
     ap.add_argument("--n-runs", type=int, default=10)
     ap.add_argument("--batch", type=int, default=64)

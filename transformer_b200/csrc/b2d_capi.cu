@@ -150,7 +150,7 @@ int b1c_grid(const ShapeOps* ops) {
 
 // One cooperative launch of the cluster kernel.
 cudaError_t launch_b1c(const void* kernel, int grid, size_t smem, cudaStream_t st, const b2d::MapsC& maps,
-                       const b2d::DecodeArgs& A) {
+                       const b2d::DecodeArgs& A, bool cooperative = true) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(b2d::kThreads);
@@ -164,7 +164,7 @@ cudaError_t launch_b1c(const void* kernel, int grid, size_t smem, cudaStream_t s
   at[1].id = cudaLaunchAttributeCooperative;
   at[1].val.cooperative = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = cooperative ? 2 : 1;
   void* args[] = {const_cast<b2d::MapsC*>(&maps), const_cast<b2d::DecodeArgs*>(&A)};
   return cudaLaunchKernelExC(&cfg, kernel, args);
 }
@@ -254,6 +254,7 @@ struct b2d_ws {
   uint64_t* sample_scratch;  // top-p sort buffer [sample_rows][kSamplerMaxVocab]
   int sample_rows;
   bool sample_single;      // diagnostics: top-p draws on one CTA per sequence even where clusters fit
+  bool b1_plain;           // diagnostics: the B=1 cluster grid launched without the cooperative attribute
   int32_t* tok_host;       // b2d_decode_token: pinned [4] token, position, next token
   int32_t* tok_dev;        // its device copy [4]
   int stage_stride;
@@ -624,6 +625,11 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
     case 10:  // sampler: phase stamp buffer (device address; 0 = off)
       ws->sample_trace = reinterpret_cast<uint64_t*>(static_cast<uintptr_t>(value));
       return B2D_OK;
+    case 14:  // B=1 cluster kernel: plain cluster launch (1) or cooperative (0, default).  The grid is the
+              // co-resident cluster count either way; profilers cannot replay a cooperative launch
+      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
+      ws->b1_plain = value == 1;
+      return B2D_OK;
     case 13:  // sampler: top-p draws on one CTA per sequence (1) or on clusters where they fit (0, default)
       if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
       ws->sample_single = value == 1;
@@ -692,7 +698,8 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   }
   ws->b1_kind = clustered ? 1 : 0;
   if (clustered) {
-    B2D_CUDA(launch_b1c(trace ? m->ops->kernel_c_trace : m->ops->kernel_c, grid, m->ops->smem_c, st, m->b1_maps, A),
+    B2D_CUDA(launch_b1c(trace ? m->ops->kernel_c_trace : m->ops->kernel_c, grid, m->ops->smem_c, st, m->b1_maps, A,
+                        !ws->b1_plain),
              "decode launch");
     return B2D_OK;
   }

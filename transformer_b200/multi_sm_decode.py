@@ -229,7 +229,7 @@ class DecodeEngine:
                    pdl: bool | None = None, ksplit: int | None = None, att_cpc: int | None = None,
                    gemm_trace: torch.Tensor | None = None, att_trace: torch.Tensor | None = None,
                    sample_trace: torch.Tensor | None = None, graphs: bool | None = None,
-                   flat: bool | None = None, sample_single: bool | None = None):
+                   flat: bool | None = None, sample_single: bool | None = None, plain_launch: bool | None = None):
         """Diagnostic knobs: back-off between failed polls (ns), weight copies
         in flight per CTA; batched step: programmatic dependent launch on/off,
         forced K split, forced attention units per (sequence, kv head) (0 =
@@ -238,7 +238,11 @@ class DecodeEngine:
         batched steps on / off; B=1 step on the flat one-CTA-per-SM kernel
         (True) or on the cluster kernel where it fits (False, default); top-p
         draws on one CTA per sequence (True) or on a cluster of CTAs per
-        sequence where the batch fits one wave (False, default)."""
+        sequence where the batch fits one wave (False, default); the B=1
+        cluster grid without the cooperative launch attribute (True: for
+        profilers) or with it (False, default)."""
+        if plain_launch is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 14, int(bool(plain_launch))), "b2d_debug_tune")
         if sample_single is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 13, int(bool(sample_single))), "b2d_debug_tune")
         if flat is not None:
