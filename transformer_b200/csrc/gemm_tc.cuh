@@ -271,8 +271,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__
   const uint32_t red_base = smem_addr(red);
   if (ks == 1) {  // the tile is local: 2 items' loads in flight per round
     // (measured, gate/up at B=256: U = 8 1.86 us, 2 1.42 us, 1 1.53 us per
-    // CTA; the epilogue runs once per launch from a cold instruction cache,
-    // so its code size counts as much as its load overlap)
+    // CTA; the epilogue runs once per CTA and launch, so its code size
+    // weighs against its load overlap)
     constexpr int U = 2;
 #pragma unroll 1
     for (int it0 = threadIdx.x; it0 < items; it0 += U * kGemmThreads) {
