@@ -311,9 +311,10 @@ def measure_b1(eng, cfg, dev, stream, torch, prompt, n_steps, label):
 
 def measure_b1_e2e(eng, dev, stream, torch, prompt, n_steps):
     """Config 1 through the public host-value call (``decode_token`` /
-    ``b2d_decode_token``): each step copies the token and position from
-    pinned host memory to the device, runs the step with the logits written,
-    copies the next token back and synchronises."""
+    ``b2d_decode_token``): each step passes the token and position from the
+    host (in the launch's arguments), runs the step with the logits written,
+    the kernel writes the next token to mapped pinned host memory, and the
+    host synchronises and reads it."""
     P0 = len(prompt)
     kv = eng.new_kv()
     eng.prefill(prompt, kv)

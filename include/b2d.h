@@ -151,13 +151,13 @@ B2D_API b2d_status b2d_decode_step(b2d_model* m, b2d_ws* ws, const int32_t* tok_
 
 /*
  * One greedy B=1 decode step with host values (no reference counterpart; the
- * reference's generate.py:112 loop reads the token back each step): copies
- * tok / pos (host ints, range-checked here) to the device through the
- * workspace's pinned staging, runs the step of b2d_decode_step, copies the
- * argmax back and synchronises `stream`; *next_tok (host) receives it.  The
- * staging (16 pinned bytes) is allocated on first use.  Device-side failures
- * (the status word) are read with b2d_last_error, as for b2d_decode_step.
- * Not capturable (it synchronises).
+ * reference's generate.py:112 loop reads the token back each step): tok / pos
+ * (host ints, range-checked here) travel in the launch's arguments, the step
+ * of b2d_decode_step runs, and the kernel writes the argmax into a mapped
+ * pinned word of the workspace (allocated on first use); the call
+ * synchronises `stream` and *next_tok (host) receives it.  Device-side
+ * failures (the status word) are read with b2d_last_error, as for
+ * b2d_decode_step.  Not capturable (it synchronises).
  */
 B2D_API b2d_status b2d_decode_token(b2d_model* m, b2d_ws* ws, int32_t tok, int32_t pos, void* kv_dev,
                                     float* logits_dev, int32_t* next_tok, void* stream);

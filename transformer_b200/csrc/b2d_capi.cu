@@ -255,8 +255,8 @@ struct b2d_ws {
   int sample_rows;
   bool sample_single;      // diagnostics: top-p draws on one CTA per sequence even where clusters fit
   bool b1_plain;           // diagnostics: the B=1 cluster grid launched without the cooperative attribute
-  int32_t* tok_host;       // b2d_decode_token: pinned [4] token, position, next token
-  int32_t* tok_dev;        // its device copy [4]
+  int32_t* tok_host;       // b2d_decode_token: mapped pinned word the kernel writes the argmax to
+  int32_t* tok_dev;        // its device address
   int stage_stride;
   __nv_bfloat16 *X, *A, *ACT;
   CUtensorMap xmap[6], amap[6], actmap[6];  // box rows 16 / 32 / 64 / 96 / 128 / 256 (bn_index)
@@ -512,8 +512,7 @@ b2d_status b2d_workspace_destroy(b2d_ws* ws) {
   for (auto& g : ws->graphs)
     if (g.exec) cudaGraphExecDestroy(g.exec);
   cudaFree(ws->sample_scratch);
-  cudaFreeHost(ws->tok_host);
-  cudaFree(ws->tok_dev);
+  cudaFreeHost(ws->tok_host);  // (tok_dev is its device alias)
   if (ws->cap_stream) cudaStreamDestroy(ws->cap_stream);
   cudaFree(ws->H);
   cudaFree(ws->Hm);
@@ -641,9 +640,10 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
 
 namespace {
 // One cooperative launch of the B=1 kernel: n_steps greedy tokens.
+// tok_dev / pos_dev null: the launch carries tok_val / pos_val instead.
 b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int32_t* pos_dev, void* kv_dev,
                      float* logits_dev, int32_t* next_tok_dev, int n_steps, int32_t* tok_out_dev,
-                     cudaStream_t st) {
+                     cudaStream_t st, int32_t tok_val = 0, int32_t pos_val = 0) {
   const b2d_config& c = m->cfg;
   b2d::DecodeArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -661,6 +661,8 @@ b2d_status launch_b1(b2d_model* m, b2d_ws* ws, const int32_t* tok_dev, const int
   A.rsin = reinterpret_cast<const float*>(m->w + m->lay.off_sin);
   A.tok = tok_dev;
   A.pos = pos_dev;
+  A.tok_val = tok_val;
+  A.pos_val = pos_val;
   A.kv = static_cast<__nv_bfloat16*>(kv_dev);
   A.logits = logits_dev;
   A.next_tok = next_tok_dev;
@@ -730,26 +732,21 @@ b2d_status b2d_decode_token(b2d_model* m, b2d_ws* ws, int32_t tok, int32_t pos, 
     return B2D_ERR_INVALID_ARG;
   B2D_CUDA(cudaSetDevice(m->device), "cudaSetDevice");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!ws->tok_host) {  // 16 pinned bytes and their device copy, on first use
-    B2D_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ws->tok_host), 4 * sizeof(int32_t), cudaHostAllocDefault),
-             "pinned token staging");
-    B2D_CUDA(cudaMalloc(reinterpret_cast<void**>(&ws->tok_dev), 4 * sizeof(int32_t)), "token staging");
+  if (!ws->tok_host) {  // one mapped pinned word the kernel writes the argmax to, on first use
+    B2D_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&ws->tok_host), 4 * sizeof(int32_t), cudaHostAllocMapped),
+             "mapped token word");
+    B2D_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&ws->tok_dev), ws->tok_host, 0),
+             "mapped token word address");
   }
-  // every call ends with the stream synchronised, so no earlier copy still reads the staging
-  ws->tok_host[0] = tok;
-  ws->tok_host[1] = pos;
-  b2d_status s = B2D_OK;
-  cudaError_t e = cudaMemcpyAsync(ws->tok_dev, ws->tok_host, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) s = cuda_fail(e, "token H2D");
-  if (s == B2D_OK) s = launch_b1(m, ws, ws->tok_dev, ws->tok_dev + 1, kv_dev, logits_dev, ws->tok_dev + 2, 1, nullptr, st);
-  if (s == B2D_OK) {
-    e = cudaMemcpyAsync(ws->tok_host + 2, ws->tok_dev + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) s = cuda_fail(e, "token D2H");
-  }
-  e = cudaStreamSynchronize(st);  // also on the error paths: no copy may still read the staging
+  // The token and position travel in the launch's arguments; the kernel
+  // writes the argmax straight into the mapped host word.  Every call ends
+  // with the stream synchronised, so no earlier step still writes it.
+  ws->tok_host[0] = -1;
+  b2d_status s = launch_b1(m, ws, nullptr, nullptr, kv_dev, logits_dev, ws->tok_dev, 1, nullptr, st, tok, pos);
+  const cudaError_t e = cudaStreamSynchronize(st);  // also on the error path
   if (s != B2D_OK) return s;
   if (e != cudaSuccess) return cuda_fail(e, "sync");
-  *next_tok = ws->tok_host[2];
+  *next_tok = *reinterpret_cast<volatile int32_t*>(ws->tok_host);
   return B2D_OK;
 }
 

@@ -65,8 +65,9 @@ struct DecodeArgs {
   const float* lnf;  // [D]
   const float* rcos; // [ctx][DH/2]
   const float* rsin;
-  const int32_t* tok;
-  const int32_t* pos;
+  const int32_t* tok;  // device token, or null: then tok_val
+  const int32_t* pos;  // device position, or null: then pos_val
+  int32_t tok_val, pos_val;  // the first step's token and position passed by value
   __nv_bfloat16* kv;  // [L][2][NKV][ctx][DH]
   float* logits;      // [V] or null
   int32_t* next_tok;
@@ -865,7 +866,7 @@ __device__ void producer_loop(const DecodeArgs& A, Smem<S>& sm, int cta, uint32_
     // A workspace holding an earlier device error stays halted until reset.
     if (ld_relaxed_u32(&A.ctl->status) != 0u) return;
     const int nsteps = A.n_steps > 1 ? A.n_steps : 1;
-    const int tok0 = __ldg(A.tok), pos0 = __ldg(A.pos);
+    const int tok0 = A.tok ? __ldg(A.tok) : A.tok_val, pos0 = A.pos ? __ldg(A.pos) : A.pos_val;
     if (tok0 < 0 || tok0 >= A.vocab || pos0 < 0 || pos0 + nsteps > A.ctx) {
       if (cta == 0 && t == 0)
         atomicCAS(&A.ctl->status, 0u, ST_BAD_INPUT | (tok0 < 0 || tok0 >= A.vocab ? 1u : 2u));

@@ -921,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // A workspace holding an earlier device error stays halted until reset.
   bool ok = ld_relaxed_u32(&A.ctl->status) == 0u;
   const int nsteps = A.n_steps > 1 ? A.n_steps : 1;
-  const int tok0 = __ldg(A.tok), pos0 = __ldg(A.pos);
+  const int tok0 = A.tok ? __ldg(A.tok) : A.tok_val, pos0 = A.pos ? __ldg(A.pos) : A.pos_val;
   if (ok && (tok0 < 0 || tok0 >= A.vocab || pos0 < 0 || pos0 + nsteps > A.ctx)) {
     if (cta == 0 && t == 0)
       atomicCAS(&A.ctl->status, 0u, ST_BAD_INPUT | (tok0 < 0 || tok0 >= A.vocab ? 1u : 2u));

@@ -112,9 +112,10 @@ class DecodeEngine:
 
     def decode_token(self, tok: int, pos: int, kv: torch.Tensor, logits: torch.Tensor | None = None,
                      stream=None) -> int:
-        """One greedy step with host values (``b2d_decode_token``): copies the
-        token and position through pinned staging, runs the step, returns the
-        argmax as a Python int (the stream is synchronised)."""
+        """One greedy step with host values (``b2d_decode_token``): the token
+        and position go in the launch's arguments, the kernel writes the
+        argmax to mapped pinned memory; returns it as a Python int (the stream
+        is synchronised)."""
         if kv.dtype != torch.bfloat16 or kv.device != self.device or kv.numel() < self.kv_elems:
             raise ValueError("kv must be a bf16 cache on the model device (see new_kv)")
         if logits is not None and (logits.dtype != torch.float32 or logits.device != self.device or
