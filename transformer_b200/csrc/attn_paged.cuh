@@ -241,6 +241,17 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
 
   // ---- query fragments (rows gid < GQA: head g*GQA + gid; hi part rows 0..7, lo part rows 8..15) ----
   const float* row = a.qkv + static_cast<size_t>(b) * (a.n_heads + 2 * a.n_kv) * 64;
+  // the new position's K / V row (owner unit), loaded beside the query so the
+  // two reads of the projection's output overlap
+  float nk0 = 0.f, nk1 = 0.f, nv0 = 0.f, nv1 = 0.f;
+  if (owner) {
+    const float* k = row + a.n_heads * 64 + g * 64;
+    const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
+    nk0 = k[lane];
+    nk1 = k[lane + 32];
+    nv0 = v[lane];
+    nv1 = v[lane + 32];
+  }
   uint32_t qa[4][4];  // [k-step][a0..a3]
   {
     float qv[4][4];   // [k-step][2tig, 2tig+1, 8+2tig, 9+2tig]
@@ -275,20 +286,19 @@ __global__ void __launch_bounds__(32 * W) paged_attn_mma_kernel(const __grid_con
   }
   if (owner) {  // the new position's K (post-RoPE) / V, bf16 as cached
     const float cs = cs_l, sn = sn_l;
-    const float* k = row + a.n_heads * 64 + g * 64;
-    const float* v = row + (a.n_heads + a.n_kv) * 64 + g * 64;
-    const float klo = k[lane], khi = k[lane + 32];
-    skn[lane] = __float2bfloat16_rn(klo * cs - khi * sn);
-    skn[lane + 32] = __float2bfloat16_rn(klo * sn + khi * cs);
-    svn[lane] = __float2bfloat16_rn(v[lane]);
-    svn[lane + 32] = __float2bfloat16_rn(v[lane + 32]);
+    const __nv_bfloat16 k0 = __float2bfloat16_rn(nk0 * cs - nk1 * sn), k1 = __float2bfloat16_rn(nk0 * sn + nk1 * cs);
+    const __nv_bfloat16 v0 = __float2bfloat16_rn(nv0), v1 = __float2bfloat16_rn(nv1);
+    skn[lane] = k0;
+    skn[lane + 32] = k1;
+    svn[lane] = v0;
+    svn[lane + 32] = v1;
     if (!bad && a.append) {
       __nv_bfloat16* kd = kv_row(a, tb, p, 0, g);
       __nv_bfloat16* vd = kv_row(a, tb, p, 1, g);
-      kd[lane] = skn[lane];
-      kd[lane + 32] = skn[lane + 32];
-      vd[lane] = svn[lane];
-      vd[lane + 32] = svn[lane + 32];
+      kd[lane] = k0;
+      kd[lane + 32] = k1;
+      vd[lane] = v0;
+      vd[lane + 32] = v1;
     }
     __syncwarp();
   }
