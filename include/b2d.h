@@ -333,9 +333,11 @@ B2D_API b2d_status b2d_debug_set(b2d_ws* ws, uint64_t wait_ns, int extra_ctas);
  * stamps (0 = off); knob 11 = b2d_decode_step_paged replays a cached CUDA
  * graph for repeated argument sets (1, default) or launches directly (0);
  * knob 12 = the B=1 step on the flat kernel (1) or on the cluster kernel
- * where it fits (0, default); knob 13 = b2d_sample's top-p draws on one CTA
- * per sequence (1) or on a cluster of 8 CTAs per sequence where the batch
- * fits one wave of clusters (0, default); knob 14 = the B=1 cluster grid
+ * where it fits (0, default); knob 13 = b2d_sample's top-p draws on a
+ * cluster of 16 CTAs per sequence where the batch fits one wave of such
+ * clusters, else of 8 where that fits, else one CTA per sequence (0,
+ * default); on one CTA per sequence (1); or on clusters of 8 where they fit
+ * one wave (2); knob 14 = the B=1 cluster grid
  * launched without the cooperative attribute (1; for profilers, which cannot
  * replay a cooperative launch) or with it (0, default).
  * Every b2d_debug_tune call drops the cached graphs' validity.

@@ -296,7 +296,8 @@ def profile_sample(w, cfg, args, torch):
     histories) on seeded N(0, s^2) logits, s = 0.3 (flat: ~28,400 tokens
     kept), 1.0 and 3.0: microseconds per b2d_sample call (CUDA events, --steps
     calls after --warmup) and the phase stamps (b2d_debug_tune knob 10) of
-    one more call, for the cluster kernel and the one-CTA kernel (knob 13)."""
+    one more call, for each kernel choice (knob 13: automatic, clusters of 8,
+    one CTA per sequence)."""
     import numpy as np
     from transformer_b200.generate import Sampler
     from transformer_b200.multi_sm_decode import DecodeEngine
@@ -310,8 +311,10 @@ def profile_sample(w, cfg, args, torch):
     smp.uniforms.copy_(torch.from_numpy(rng.random(B)))
     names = ["exp", "normalise", "sort", "cutoff", "draw"]
     out = []
-    for single in (False, True):
-        eng.debug_tune(sample_single=single)
+    labels = {0: "automatic (clusters of 16 where they fit, else 8)", 2: "cluster of 8 CTAs per sequence",
+              1: "one CTA per sequence"}
+    for mode in (0, 2, 1):
+        eng.debug_tune(sample_mode=mode)
         for sigma in (0.3, 1.0, 3.0):
             lg = torch.from_numpy((rng.standard_normal((B, cfg.vocab_size)) * sigma).astype(np.float32)).cuda()
             for _ in range(args.warmup):
@@ -329,12 +332,12 @@ def profile_sample(w, cfg, args, torch):
             torch.cuda.synchronize()
             eng.debug_tune(sample_trace=torch.zeros(0, dtype=torch.int64))
             t = buf.cpu().numpy().astype(np.int64)
-            out.append({"kernel": "one CTA per sequence" if single else "cluster of 8 CTAs per sequence",
+            out.append({"kernel": labels[mode],
                         "sigma": sigma, "us_per_call": round(e0.elapsed_time(e1) * 1000 / args.steps, 1),
                         "phases_us": {n: round(float(np.mean(t[:, i + 1] - t[:, i])) / 1e3, 1)
                                       for i, n in enumerate(names)},
                         "kept_mean": float(np.mean(t[:, 6] & 0xffffffff))})
-    eng.debug_tune(sample_single=False)
+    eng.debug_tune(sample_mode=0)
     eng.check_device()
     return {"mode": "sample", "batch": B, "results": out}
 

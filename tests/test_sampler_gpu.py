@@ -191,11 +191,12 @@ def test_topp_cutoff_equals_numpy_cumsum(engine306, scale, ties):
 
 @pytest.mark.parametrize("vocab", [32000, 32768, 5000, 4097, 100])
 def test_cluster_and_one_cta_samplers_agree(engine306, vocab):
-    """Top-p draws run on a cluster of 8 CTAs per sequence where the batch
-    fits one wave of clusters (the default), or on one CTA per sequence
-    (knob 13).  Both return the same tokens and the same top-p cutoff counts,
-    and the tokens equal the CPU restatement's.  The vocabularies leave
-    cluster CTAs full, partly filled and empty (a CTA holds 4096 ids)."""
+    """Top-p draws run on a cluster of 16 or 8 CTAs per sequence where the
+    batch fits one wave of clusters (the default picks 16 where the device
+    runs them), on clusters of 8, or on one CTA per sequence (knob 13).  All
+    return the same tokens and the same top-p cutoff counts, and the tokens
+    equal the CPU restatement's.  The vocabularies leave cluster CTAs full,
+    partly filled and empty (a CTA holds 2048 or 4096 ids)."""
     rng = np.random.default_rng(vocab)
     B = 4
     dev = engine306.device
@@ -217,15 +218,16 @@ def test_cluster_and_one_cta_samplers_agree(engine306, vocab):
             smp.uniforms[:B].copy_(torch.as_tensor(us))
             lg = torch.from_numpy(logits).to(dev)
             runs = {}
-            for single in (False, True):
-                engine306.debug_tune(sample_single=single)
+            for mode in (0, 2, 1):
+                engine306.debug_tune(sample_mode=mode)
                 buf.zero_()
                 tok = smp.sample(lg, temp, top_p, rp, B).cpu().numpy().copy()
-                runs[single] = (tok, buf[:, 6].cpu().numpy() & 0xffffffff)
-            assert (runs[False][0] == runs[True][0]).all(), (case, runs)
-            assert (runs[False][1] == runs[True][1]).all(), (case, runs)
+                runs[mode] = (tok, buf[:, 6].cpu().numpy() & 0xffffffff)
+            for mode in (2, 1):
+                assert (runs[0][0] == runs[mode][0]).all(), (case, mode, runs)
+                assert (runs[0][1] == runs[mode][1]).all(), (case, mode, runs)
             for b in range(B):
                 want = OS.sample_token(logits[b], temp, top_p, rp, list(hists[b]), us[b])
-                assert runs[False][0][b] == want or _boundary(logits[b], temp, top_p, rp, list(hists[b]), us[b])
+                assert runs[0][0][b] == want or _boundary(logits[b], temp, top_p, rp, list(hists[b]), us[b])
     finally:
-        engine306.debug_tune(sample_single=False, sample_trace=torch.zeros(0, dtype=torch.int64))
+        engine306.debug_tune(sample_mode=0, sample_trace=torch.zeros(0, dtype=torch.int64))

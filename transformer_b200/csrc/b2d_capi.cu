@@ -253,7 +253,7 @@ struct b2d_ws {
   uint64_t* sample_trace;  // diagnostics: sampler phase stamps [batch][8], or null
   uint64_t* sample_scratch;  // top-p sort buffer [sample_rows][kSamplerMaxVocab]
   int sample_rows;
-  bool sample_single;      // diagnostics: top-p draws on one CTA per sequence even where clusters fit
+  int sample_mode;         // diagnostics: top-p kernel choice (0 automatic, 1 one CTA, 2 clusters of 8)
   bool b1_plain;           // diagnostics: the B=1 cluster grid launched without the cooperative attribute
   int32_t* tok_host;       // b2d_decode_token: mapped pinned word the kernel writes the argmax to
   int32_t* tok_dev;        // its device address
@@ -629,9 +629,10 @@ b2d_status b2d_debug_tune(b2d_ws* ws, int knob, int64_t value) {
       if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
       ws->b1_plain = value == 1;
       return B2D_OK;
-    case 13:  // sampler: top-p draws on one CTA per sequence (1) or on clusters where they fit (0, default)
-      if (value < 0 || value > 1) return B2D_ERR_INVALID_ARG;
-      ws->sample_single = value == 1;
+    case 13:  // sampler: top-p draws automatic (0, default: clusters of 16, else 8, where they fit),
+              // on one CTA per sequence (1) or on clusters of 8 where they fit (2)
+      if (value < 0 || value > 2) return B2D_ERR_INVALID_ARG;
+      ws->sample_mode = static_cast<int>(value);
       return B2D_OK;
 
   }
@@ -785,7 +786,7 @@ b2d_status b2d_sample(b2d_ws* ws, const float* logits_dev, int batch, int vocab,
   }
   B2D_CUDA(b2d::launch_sampler(logits_dev, batch, vocab, history_dev, hist_cap, hist_len_dev, uniforms_dev,
                                params->temperature, params->top_p, params->rep_penalty, out_tok_dev, st,
-                               ws->sample_scratch, ws->sample_trace, !ws->sample_single),
+                               ws->sample_scratch, ws->sample_trace, ws->sample_mode),
            "sampler launch");
   return B2D_OK;
 }

@@ -1,5 +1,5 @@
 // sampler.cuh — device sampler: one CTA per sequence, or for top-p draws a
-// cluster of 8 CTAs per sequence while the batch fits one wave (sm_100a).
+// cluster of 16 or 8 CTAs per sequence while the batch fits one wave (sm_100a).
 //
 // Replaces the reference's host numpy sampler, generate.py:28-65 sample_token:
 // repetition penalty over the set of generated tokens, temperature, softmax,
@@ -38,11 +38,12 @@ namespace b2d {
 constexpr int kSamplerMaxVocab = 32768;
 constexpr int kSamplerThreads = 1024;
 constexpr int kTreeNodes = 1024;  // heap-indexed pairwise-sum tree (depth <= 9)
-// Cluster sampler: one cluster of kSampleCluster CTAs per sequence, CTA r
-// holding sort positions [r * kSliceElems, (r + 1) * kSliceElems).
-constexpr int kSampleCluster = 8;
-constexpr int kSliceElems = kSamplerMaxVocab / kSampleCluster;
-static_assert(kSliceElems == 4 * kSamplerThreads, "four positions per thread");
+// Cluster sampler: one cluster of CL (8 or 16) CTAs per sequence, CTA r
+// holding sort positions [r * slice, (r + 1) * slice), slice =
+// kSamplerMaxVocab / CL.
+constexpr int kSampleCluster = 8;      // the portable cluster size
+constexpr int kSampleClusterMax = 16;  // where the device runs clusters of 16
+static_assert(kSamplerMaxVocab / kSampleClusterMax >= kSamplerThreads, "at least one position per thread");
 
 struct SampleArgs {
   const float* logits;     // [batch][vocab]
@@ -80,9 +81,9 @@ struct SamplerSmem {
   int rs_off[kSamplerThreads / 32][17];  // (rows padded: a column read is conflict-free)
   // cluster sampler: values every CTA of the cluster pushes into every CTA
   // (slot = the pushing CTA's rank)
-  float cl_max[kSampleCluster];
-  uint32_t cl_and[kSampleCluster], cl_or[kSampleCluster];
-  int cl_cnt[kSampleCluster][16];
+  float cl_max[kSampleClusterMax];
+  uint32_t cl_and[kSampleClusterMax], cl_or[kSampleClusterMax];
+  int cl_cnt[kSampleClusterMax][16];
   int cl_tot[16], cl_lstart[16], cl_gofs[16];  // a sort pass's digit totals and starts: in the stage, stage -> global
   uint32_t red_and[kSamplerThreads / 32], red_or[kSamplerThreads / 32];
 };
@@ -651,18 +652,25 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_kernel(const Sample
 // Every thread of every CTA passes every cluster barrier (no early exit
 // before the gather), and no wait depends on data.  Before the gather, CTA
 // r's shared key array holds two sort buffers and its exponentials.
+template <int SLICE>
 __device__ __forceinline__ uint64_t* cl_sort_buf(SamplerSmem& sm, int which) {
-  return reinterpret_cast<uint64_t*>(sm.key) + which * kSliceElems;
+  return reinterpret_cast<uint64_t*>(sm.key) + which * SLICE;
 }
+template <int SLICE>
 __device__ __forceinline__ float* cl_exp_buf(SamplerSmem& sm) {
-  return reinterpret_cast<float*>(sm.key + 4 * kSliceElems);
+  return reinterpret_cast<float*>(sm.key + 4 * SLICE);
 }
 
+template <int CL>
 __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(const SampleArgs a) {
+  constexpr int kSliceElems = kSamplerMaxVocab / CL;       // positions per CTA
+  constexpr int PT = kSliceElems / kSamplerThreads;        // per thread
+  constexpr int WPOS = kSliceElems / (kSamplerThreads / 32);  // per warp
+  static_assert(PT * kSamplerThreads == kSliceElems && CL <= 16, "slice layout");
   extern __shared__ __align__(16) uint8_t sampler_smem_raw[];
   SamplerSmem& sm = *reinterpret_cast<SamplerSmem*>(sampler_smem_raw);
   const int rank = static_cast<int>(cluster_ctarank());
-  const int b = blockIdx.x / kSampleCluster, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int b = blockIdx.x / CL, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int V = a.vocab;
   const int i0 = rank * kSliceElems;
   const int nloc = max(0, min(kSliceElems, V - i0));  // positions (and ids) this CTA holds
@@ -687,10 +695,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     }
     __syncthreads();
   }
-  float v[4];
+  float v[PT];
   float mx = -INFINITY;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < PT; ++r) {
     const int j = t + r * kSamplerThreads;
     float x = -INFINITY;
     if (j < nloc) {
@@ -706,7 +714,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) sm.red_f[warp] = mx;
   __syncthreads();
-  if (t < kSampleCluster) {
+  if (t < CL) {
     float m = sm.red_f[0];
     for (int w = 1; w < kWarps; ++w) m = fmaxf(m, sm.red_f[w]);
     st_dsmem_f32(mapa_shared(smem_addr(&sm.cl_max[rank]), t), m);
@@ -714,10 +722,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   cluster_sync_all();
   mx = sm.cl_max[0];
 #pragma unroll
-  for (int c = 1; c < kSampleCluster; ++c) mx = fmaxf(mx, sm.cl_max[c]);
-  float* E = cl_exp_buf(sm);
+  for (int c = 1; c < CL; ++c) mx = fmaxf(mx, sm.cl_max[c]);
+  float* E = cl_exp_buf<kSliceElems>(sm);
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < PT; ++r) {
     const int j = t + r * kSamplerThreads;
     if (j < nloc) E[j] = __double2float_rn(exp(static_cast<double>(__fsub_rn(v[r], mx))));
   }
@@ -735,14 +743,14 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
       [&](int s0) { return s0 >= i0 && s0 < i0 + nloc; },
       [&](int nd, float v) {
 #pragma unroll
-        for (int c = 0; c < kSampleCluster; ++c) st_dsmem_f32(mapa_shared(smem_addr(&sm.node_val[nd]), c), v);
+        for (int c = 0; c < CL; ++c) st_dsmem_f32(mapa_shared(smem_addr(&sm.node_val[nd]), c), v);
       });
   cluster_sync_all();
   const float S = tree_combine(sm);
-  uint64_t* X = cl_sort_buf(sm, 0);
+  uint64_t* X = cl_sort_buf<kSliceElems>(sm, 0);
   uint32_t kand = 0xffffffffu, kor = 0u;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < PT; ++r) {
     const int j = t + r * kSamplerThreads;
     if (j < nloc) {
       const uint32_t key = ~__float_as_uint(__fdiv_rn(E[j], S));  // ascending keys = descending p
@@ -767,16 +775,16 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   for (int pass = 0; pass < 8; ++pass) {
     if ((skip >> pass) & 1u) continue;
     const int sh = 4 * pass;
-    const uint64_t* src = cl_sort_buf(sm, cur);
-    const uint32_t dst_base = smem_addr(cl_sort_buf(sm, cur ^ 1));
-    uint64_t* stage = cl_sort_buf(sm, 2);  // the exponentials' space, free from here
+    const uint64_t* src = cl_sort_buf<kSliceElems>(sm, cur);
+    const uint32_t dst_base = smem_addr(cl_sort_buf<kSliceElems>(sm, cur ^ 1));
+    uint64_t* stage = cl_sort_buf<kSliceElems>(sm, 2);  // the exponentials' space, free from here
     // this warp's positions: 4 rounds of 32 consecutive ones, in order
-    uint64_t e[4];
+    uint64_t e[PT];
     if (lane < 16) sm.rs_cnt[warp][lane] = 0;
     __syncwarp();
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int j = 128 * warp + 32 * r + lane;
+    for (int r = 0; r < PT; ++r) {
+      const int j = WPOS * warp + 32 * r + lane;
       e[r] = j < nloc ? src[j] : 0ull;
       if (j < nloc) atomicAdd(&sm.rs_cnt[warp][static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u], 1);
     }
@@ -804,10 +812,10 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
       if (lane < 16) {
         sm.cl_lstart[lane] = incl - tot;
 #pragma unroll
-        for (int c = 0; c < kSampleCluster; ++c)
+        for (int c = 0; c < CL; ++c)
           st_dsmem_u32(mapa_shared(smem_addr(&sm.cl_cnt[rank][lane]), c), static_cast<uint32_t>(tot));
       }
-      if (pass == 0 && lane >= 16 && lane < 16 + kSampleCluster) {
+      if (pass == 0 && lane >= 16 && lane < 16 + CL) {
         uint32_t ka = 0xffffffffu, ko = 0u;
         for (int w = 0; w < kWarps; ++w) {
           ka &= sm.red_and[w];
@@ -821,8 +829,8 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     // stable counting sort of this CTA's elements by digit into the stage, so
     // that each digit's elements leave as one run of consecutive positions
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int j = 128 * warp + 32 * r + lane;
+    for (int r = 0; r < PT; ++r) {
+      const int j = WPOS * warp + 32 * r + lane;
       const bool ok = j < nloc;
       const uint32_t d = static_cast<uint32_t>(e[r] >> (32 + sh)) & 15u;
       const uint32_t m = same_digit_lanes(d) & __ballot_sync(0xffffffffu, ok);
@@ -836,7 +844,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     if (pass == 0) {
       uint32_t ka = 0xffffffffu, ko = 0u;
 #pragma unroll
-      for (int c = 0; c < kSampleCluster; ++c) {
+      for (int c = 0; c < CL; ++c) {
         ka &= sm.cl_and[c];
         ko |= sm.cl_or[c];
       }
@@ -848,7 +856,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     if (warp == 0) {  // global start of digit d from this CTA: all smaller digits, then earlier CTAs
       int before = 0, total = 0;
       if (lane < 16)
-        for (int c = 0; c < kSampleCluster; ++c) {
+        for (int c = 0; c < CL; ++c) {
           const int n = sm.cl_cnt[c][lane];
           if (c < rank) before += n;
           total += n;
@@ -863,7 +871,7 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
     }
     __syncthreads();
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {  // consecutive stage positions -> consecutive global positions
+    for (int r = 0; r < PT; ++r) {  // consecutive stage positions -> consecutive global positions
       const int j = t + r * kSamplerThreads;
       if (j < nloc) {
         const uint64_t x = stage[j];
@@ -876,17 +884,17 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   }
 
   // ---- gather the sorted slices into CTA 0 ----
-  const uint64_t* fin = cl_sort_buf(sm, cur);
-  uint64_t g[4];
+  const uint64_t* fin = cl_sort_buf<kSliceElems>(sm, cur);
+  uint64_t g[PT];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < PT; ++r) {
     const int j = t + r * kSamplerThreads;
     g[r] = j < nloc ? fin[j] : 0ull;
   }
   cluster_sync_all();  // CTA 0's sort buffers are free from here
   const uint32_t kb = smem_addr(sm.key), ib = smem_addr(sm.idx);
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
+  for (int r = 0; r < PT; ++r) {
     const int j = t + r * kSamplerThreads;
     if (j < nloc) {
       const uint32_t i = static_cast<uint32_t>(i0 + j);
@@ -916,8 +924,11 @@ __global__ void __launch_bounds__(kSamplerThreads, 1) sample_cluster_kernel(cons
   stamp(5);
 }
 
-// Clusters of the cluster sampler that fit co-resident on the current device
-// (0 if none); cached per device.
+// Clusters of CL CTAs of the cluster sampler that fit co-resident on the
+// current device (0 if none, or if the device refuses the cluster size);
+// cached per device.  Clusters of 16 are a non-portable size: the device
+// decides whether it runs them.
+template <int CL>
 inline int sampler_cluster_capacity() {
   static int cap[64];
   static bool known[64] = {};
@@ -925,20 +936,24 @@ inline int sampler_cluster_capacity() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (known[dev]) return cap[dev];
   int n = 0;
-  if (cudaFuncSetAttribute(sample_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(sizeof(SamplerSmem))) == cudaSuccess) {
+  bool ok = cudaFuncSetAttribute(sample_cluster_kernel<CL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(SamplerSmem))) == cudaSuccess;
+  if (ok && CL > 8)
+    ok = cudaFuncSetAttribute(sample_cluster_kernel<CL>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+         cudaSuccess;
+  if (ok) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = kSampleCluster;
+    at[0].val.clusterDim.x = CL;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(kSampleCluster * 32);
+    cfg.gridDim = dim3(CL * 32);
     cfg.blockDim = dim3(kSamplerThreads);
     cfg.dynamicSmemBytes = sizeof(SamplerSmem);
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, sample_cluster_kernel, &cfg) != cudaSuccess) n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, sample_cluster_kernel<CL>, &cfg) != cudaSuccess) n = 0;
   }
   cudaGetLastError();
   cap[dev] = n;
@@ -946,11 +961,31 @@ inline int sampler_cluster_capacity() {
   return n;
 }
 
+template <int CL>
+inline cudaError_t launch_sampler_cluster(const SampleArgs& a, int batch, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(batch * CL));
+  cfg.blockDim = dim3(kSamplerThreads);
+  cfg.dynamicSmemBytes = sizeof(SamplerSmem);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CL;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, sample_cluster_kernel<CL>, a);
+}
+
+// Kernel choice for top-p draws (mode): 0 automatic, clusters of 16 CTAs per
+// sequence where every cluster of the batch is co-resident, else of 8, else one
+// CTA per sequence; 1 one CTA per sequence; 2 clusters of 8 where they fit.
 inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, const int32_t* history,
                                   int hist_cap, const int32_t* hist_len, const double* uniforms,
                                   double temperature, double top_p, double rep_penalty, int32_t* out,
                                   cudaStream_t st, uint64_t* scratch, uint64_t* trace = nullptr,
-                                  bool allow_cluster = true) {
+                                  int mode = 0) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -975,22 +1010,11 @@ inline cudaError_t launch_sampler(const float* logits, int batch, int vocab, con
   a.top_p = top_p;
   a.trace = trace;
   a.scratch = scratch;
-  // top-p draws go to the cluster kernel when every sequence's cluster is
+  // top-p draws go to a cluster kernel when every sequence's cluster is
   // co-resident (one wave); larger batches keep one CTA per sequence
-  if (allow_cluster && a.temperature > 0.0f && top_p < 1.0 && batch <= sampler_cluster_capacity()) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(batch * kSampleCluster));
-    cfg.blockDim = dim3(kSamplerThreads);
-    cfg.dynamicSmemBytes = sizeof(SamplerSmem);
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = kSampleCluster;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, sample_cluster_kernel, a);
+  if (mode != 1 && a.temperature > 0.0f && top_p < 1.0) {
+    if (mode == 0 && batch <= sampler_cluster_capacity<16>()) return launch_sampler_cluster<16>(a, batch, st);
+    if (batch <= sampler_cluster_capacity<8>()) return launch_sampler_cluster<8>(a, batch, st);
   }
   sample_kernel<<<batch, kSamplerThreads, sizeof(SamplerSmem), st>>>(a);
   return cudaGetLastError();

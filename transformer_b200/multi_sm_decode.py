@@ -230,22 +230,23 @@ class DecodeEngine:
                    pdl: bool | None = None, ksplit: int | None = None, att_cpc: int | None = None,
                    gemm_trace: torch.Tensor | None = None, att_trace: torch.Tensor | None = None,
                    sample_trace: torch.Tensor | None = None, graphs: bool | None = None,
-                   flat: bool | None = None, sample_single: bool | None = None, plain_launch: bool | None = None):
+                   flat: bool | None = None, sample_mode: int | None = None, plain_launch: bool | None = None):
         """Diagnostic knobs: back-off between failed polls (ns), weight copies
         in flight per CTA; batched step: programmatic dependent launch on/off,
         forced K split, forced attention units per (sequence, kv head) (0 =
         automatic); device stamp buffers for the projections, the attention
         and the sampler (empty tensor = off); graph replay of repeated
         batched steps on / off; B=1 step on the flat one-CTA-per-SM kernel
-        (True) or on the cluster kernel where it fits (False, default); top-p
-        draws on one CTA per sequence (True) or on a cluster of CTAs per
-        sequence where the batch fits one wave (False, default); the B=1
+        (True) or on the cluster kernel where it fits (False, default); the
+        top-p sampler's kernel (0, default: a cluster of 16 CTAs per sequence
+        where the batch's clusters fit one wave, else of 8; 1: one CTA per
+        sequence; 2: clusters of 8 where they fit); the B=1
         cluster grid without the cooperative launch attribute (True: for
         profilers) or with it (False, default)."""
         if plain_launch is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 14, int(bool(plain_launch))), "b2d_debug_tune")
-        if sample_single is not None:
-            _lib.check(self.lib.b2d_debug_tune(self.ws, 13, int(bool(sample_single))), "b2d_debug_tune")
+        if sample_mode is not None:
+            _lib.check(self.lib.b2d_debug_tune(self.ws, 13, int(sample_mode)), "b2d_debug_tune")
         if flat is not None:
             _lib.check(self.lib.b2d_debug_tune(self.ws, 12, int(bool(flat))), "b2d_debug_tune")
         if graphs is not None:
