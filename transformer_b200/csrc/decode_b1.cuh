@@ -242,6 +242,36 @@ struct Waiter {
   }
 };
 
+// The same bookkeeping with the clock check out of line, so that a wait site
+// keeps only the poll counter inline.  Returns the wait's start time (set by
+// the first check), or 0 when the wait must give up; every site using it
+// stops waiting once expired() returns true.  The cluster kernel's producer
+// warp uses it: its poll loops stay small, and it issues the weight stream
+// faster (measured: config 1 263.4 -> 236.8 us/token, config 2 271.6 ->
+// 269.5 us/token).  The consumers' waits keep the inline form, which measured
+// the same or faster there.
+__device__ __noinline__ uint64_t waiter_check(uint64_t start, Control* ctl, uint64_t wait_ns, uint32_t flag,
+                                              uint64_t t0, uint32_t site) {
+  const uint64_t now = globaltimer_ns();
+  if (start == 0) return now;
+  if (now - start < 20000u) return start;
+  if (ld_relaxed_u32(&ctl->abort_flag) == flag) return 0;
+  if (now - t0 > wait_ns) {
+    raise_error(ctl, ST_TIMEOUT | site, flag);
+    return 0;
+  }
+  return start;
+}
+struct ProducerWaiter {
+  uint64_t start = 0;
+  uint32_t spins = 0;
+  __device__ __forceinline__ bool expired(const DecodeArgs& A, uint32_t flag, uint64_t t0, uint32_t site) {
+    if ((++spins & 127u) != 0) return false;
+    start = waiter_check(start, A.ctl, A.wait_ns, flag, t0, site);
+    return start == 0;
+  }
+};
+
 // Gather up to N word pairs per thread.  addr(i) -> pointer to pair i (16-B
 // aligned); valid(i) says whether this thread owns item i; store(i, a, b)
 // receives the payloads.  All owned loads are issued together, then the

@@ -293,7 +293,7 @@ __device__ void producer_c(const DecodeArgs& A, SmemC<S>& sm, const MapsC& maps,
     bool good = true;
     if (lane == 0) {
       while (good && seq - landed >= cap) {
-        Waiter wt;
+        ProducerWaiter wt;
         while (!mbar_test(&sm.full[landed % kStagesC], (landed / kStagesC) & 1u)) {
           if (*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_FULL)) {
             good = false;
@@ -304,7 +304,7 @@ __device__ void producer_c(const DecodeArgs& A, SmemC<S>& sm, const MapsC& maps,
       }
       if (good && seq >= kStagesC) {
         const uint32_t par = ((seq / kStagesC) - 1) & 1u;
-        Waiter wt;
+        ProducerWaiter wt;
         while (!mbar_test(&sm.empty[slot], par)) {
           if (*reinterpret_cast<volatile int*>(&sm.abort) || wt.expired(A, flag, t0, SITE_EMPTY)) {
             good = false;
