@@ -475,6 +475,9 @@ inline GemmPlan gemm_plan(int M, int N, int K, int bn_cap) {
   int ks = 1;
   for (int k = 2; k <= kGemmMaxSplit && k <= K / kGemmBK; ++k)
     if (tiles <= gemm_max_clusters(bn, k)) ks = k;
+  // 16-row tiles already split: one split deeper than one wave allows
+  // (B=8 step, gate/up split 4 instead of 3: 653 -> 623 us)
+  if (bn == 16 && ks > 1 && ks < kGemmMaxSplit && ks < K / kGemmBK) ++ks;
   return {bn, ks};
 }
 
